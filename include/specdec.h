@@ -1,0 +1,253 @@
+/*
+ * specdec.h -- C ABI of libspecdec_sm100.so, the B200 (sm_100a) speculative-
+ * decoding hot path of the sme-llm-edge server.
+ *
+ * Two groups of entry points:
+ *
+ *  1. The reference's FFI symbols, with the reference's exact signatures and
+ *     host-pointer semantics, so the unchanged reference C++ operator classes
+ *     (server/speculative_decoder.cpp, server/mtp_heads.cpp,
+ *     server/paged_kv_cache.cpp) link against this library instead of the Rust
+ *     SVE2/SME library (src/sme_kernel/rust_sme/src/lib.rs).  They stage their
+ *     inputs to the GPU, run a CUDA kernel and copy results back.  They return
+ *     void like the reference; failures leave the reference's default outputs
+ *     and are reported through specdec_last_error().
+ *
+ *  2. Device-resident entry points (specdec_*): device pointers, an explicit
+ *     cudaStream_t (passed as void*), int status return.  These are the fast
+ *     path used by the step engine.
+ *
+ * No torch types appear here; plain pointers and sizes only.
+ */
+#ifndef SPECDEC_H
+#define SPECDEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------- status */
+enum {
+    SPECDEC_OK = 0,
+    SPECDEC_EINVAL = 1,   /* bad argument / shape */
+    SPECDEC_ENOMEM = 2,   /* device memory or KV block pool exhausted */
+    SPECDEC_ECUDA = 3,    /* CUDA runtime / launch error */
+    SPECDEC_ETIMEOUT = 4, /* a bounded device-side wait gave up */
+    SPECDEC_ENOTSUP = 5   /* feature not available on this device */
+};
+/* Last error message of the calling thread ("" if none). */
+const char* specdec_last_error(void);
+int specdec_abi_version(void);
+
+/* ===================================================================== */
+/* 1. Reference FFI symbols (host pointers).                               */
+/* ===================================================================== */
+
+/* Replaces sve2_speculative_verify_f32, src/sme_kernel/rust_sme/src/lib.rs:696-779
+ * (declared by the reference at server/speculative_decoder.cpp:5-16).
+ * logits [batch, max_draft_length, vocab]; drafts [batch, max_draft_length];
+ * accepted = number of positions i < len[b] whose argmax equals the draft
+ * (count, not prefix); replacement = argmax at index `accepted` when any
+ * position mismatches, else -1.  Argmax ties follow the reference's 128-bit
+ * SVE lane rule (4 fp32 lanes). */
+void sve2_speculative_verify_f32(const float* logits_ptr, const int32_t* draft_tokens_ptr,
+                                 const int32_t* draft_lengths_ptr, uint32_t vocab_size, uint32_t max_draft_length,
+                                 uint32_t batch_size, int32_t* accepted_counts_ptr, int32_t* replacement_tokens_ptr);
+
+/* Replaces rust_sme_mtp_predict_f32, lib.rs:1792-1831 (declared at
+ * server/mtp_heads.h:6-13): logits[k, j] = sum_d h[d] * W[k, d, j]. */
+void rust_sme_mtp_predict_f32(const float* hidden_state_ptr, const float* weights_ptr, float* logits_out_ptr,
+                              uint32_t hidden_dim, uint32_t vocab_size, uint32_t k_heads);
+
+/* Replaces rust_sme_mtp_sample_f32, lib.rs:1840-1886 (server/mtp_heads.h:15-20):
+ * per-head argmax with the SVE lane tie rule, default 0. */
+void rust_sme_mtp_sample_f32(const float* logits_ptr, int32_t* draft_tokens_out, uint32_t vocab_size,
+                             uint32_t k_heads);
+
+/* Replaces sme_sm_prefetch_kv_blocks, lib.rs:670-689 (server/paged_kv_cache.cpp:6-8).
+ * A no-op: on the GPU the attention kernel stages KV blocks with bulk async
+ * copies, so a host-side prefetch hint has nothing to do. */
+void sme_sm_prefetch_kv_blocks(const int8_t** k_ptrs, const int8_t** v_ptrs, uint32_t num_blocks);
+
+/* Replaces rust_sme_flashdecoding_chunk_f32 / rust_sve2_flashdecoding_reduce_f32
+ * (lib.rs:1638-1783; declared by server/flash_decoding_tracker.cpp). */
+void rust_sme_flashdecoding_chunk_f32(const float* q_ptr, const float* k_chunk_ptr, const float* v_chunk_ptr,
+                                      uint32_t chunk_len, uint32_t head_dim, float softmax_scale,
+                                      float* partial_o_out, float* partial_max_out, float* partial_sum_exp_out);
+void rust_sve2_flashdecoding_reduce_f32(const float* partial_o_ptr, const float* partial_max_ptr,
+                                        const float* partial_sum_exp_ptr, uint32_t num_chunks, uint32_t head_dim,
+                                        float* final_o_out);
+
+/* C-ABI form of compute_paged_attention (server/paged_attention.h:10-19,
+ * server/paged_attention.cpp:16-111), host pointers.  The std::vector
+ * arguments are flattened: request m owns tables[table_off[m] .. table_off[m+1]).
+ * Adds exp(q.k/sqrt(hidden))/seq_len * v into o, exactly the reference formula
+ * (no max subtraction, no normalisation).  Returns a status. */
+int specdec_paged_attention_compat_f32(const float* q, const float* k_pool, const float* v_pool, size_t pool_floats,
+                                       const int32_t* table_off, const int32_t* tables, const int32_t* seq_lens,
+                                       float* o, int M, int hidden_dim, int block_size);
+
+/* ===================================================================== */
+/* 2. Device-resident kernels (device pointers, stream as void*).          */
+/* ===================================================================== */
+
+/* Sampling parameters.  temperature <= 0 selects greedy decisions; top_p >= 1
+ * disables the nucleus.  Uniforms come from Philox4x32-10 with
+ * counter {b, i, purpose, step} and key {seed_lo, seed_hi}. */
+typedef struct {
+    float temperature;
+    float top_p;
+    uint64_t seed;
+    uint32_t step;
+} specdec_sampling;
+
+/* Bytes of device scratch the acceptance / sampling kernels need for `rows`
+ * logits rows. */
+size_t specdec_accept_workspace_bytes(int rows);
+
+/* Chain acceptance (speculative sampling, min(1,p/q) test, residual
+ * max(0,p-q) draw, bonus token).  Replaces the reference's greedy verify
+ * (lib.rs:696-779) with the standard algorithm; temperature <= 0 gives
+ * greedy longest-prefix acceptance.
+ *   target [B, k+1, V] fp32, draft [B, k, V] fp32 (unused when greedy),
+ *   drafts [B, k] int32 -> accepted_len [B], out_tokens [B, k+1]. */
+int specdec_accept_chain(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
+                         const specdec_sampling* sp, int32_t* accepted_len, int32_t* out_tokens, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Tree acceptance over R BFS-ordered nodes (node 0 = root / pending token).
+ * target [B, R, V]; node_tokens [B, R]; parent [R] (device).  Outputs
+ * accepted_len [B], path_nodes [B, R], out_tokens [B, R]. */
+int specdec_accept_tree(const float* target, const int32_t* node_tokens, const int32_t* parent, int B, int R, int V,
+                        const specdec_sampling* sp, int32_t* accepted_len, int32_t* path_nodes, int32_t* out_tokens,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Draft-token sampling of logits rows [rows, V]; row r uses stream (r/k, r%k). */
+int specdec_sample_rows(const float* logits, int rows, int k, int V, const specdec_sampling* sp, int32_t* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reference-semantics greedy verify on device pointers (see
+ * sve2_speculative_verify_f32 above). */
+int specdec_compat_verify(const float* logits, const int32_t* drafts, const int32_t* lens, int V, int max_draft,
+                          int B, int32_t* accepted, int32_t* replacement, void* stream);
+
+/* W4A16 weights in the device tiled layout: for every 128-row x 128-column
+ * unit, 8192 bytes of nibbles then 128 fp16 group scales (8448 bytes). */
+size_t specdec_w4_tiled_bytes(int N, int K);
+/* Converts reference-format int4 (packed [N, K/2], low nibble = even k,
+ * u4 = q + 8, server/sve_packing.cpp:8-30) plus fp16 group-128 scales
+ * [N, K/128] (device pointers) into the tiled layout. */
+int specdec_w4_tile(const uint8_t* packed, const uint16_t* scales, int N, int K, void* tiled, void* stream);
+int specdec_w4_untile(const void* tiled, int N, int K, uint8_t* packed, uint16_t* scales, void* stream);
+/* Y[m, n] = sum_k X[m, k] * W[n, k] (mode 0 store, 1 add).  X fp16 [M, K]
+ * (row stride ldx elements, 16-byte aligned), Y fp32 with row stride ldy.
+ * The int4 weights are dequantised in registers and multiplied on the tcgen05
+ * tensor cores with TMEM accumulators.  The workspace (size from
+ * specdec_w4a16_workspace_bytes) holds partial tiles of k-ranges split across
+ * CTAs; the result is deterministic (parts are summed in a fixed order). */
+size_t specdec_w4a16_workspace_bytes(int M, int N, int K);
+int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
+                       int mode, void* workspace, size_t workspace_bytes, void* stream);
+/* Same contraction on the CUDA cores (used to cross-check the tensor path). */
+int specdec_w4a16_gemm_simt(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
+                            int mode, void* stream);
+
+/* Verify attention over a paged fp16 KV pool [num_blocks, 2, Hkv, 16, hd]
+ * (one layer).  q/out [B*R, Hq, hd] fp16.  Row r of sequence b sees slots
+ * 0..ctx_len[b]-1 and new slot ctx_len[b]+j iff bit j of mask[r].
+ * tables [B, max_blocks] int32.  The workspace is zero-filled by the call. */
+size_t specdec_attention_workspace_bytes(int B, int R, int n_q_heads, int n_kv_heads, int head_dim, int max_blocks);
+int specdec_attention(const uint16_t* q, const uint16_t* kv_layer, int num_blocks, int n_kv_heads, int head_dim,
+                      const int32_t* tables, int max_blocks, const int32_t* ctx_len, const uint64_t* mask, int B,
+                      int R, int n_q_heads, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ===================================================================== */
+/* 3. Paged KV block manager (device resident).  Mirrors PagedKVCache      */
+/*    (server/paged_kv_cache.h:28-63): lowest-free-index allocation with   */
+/*    reference counts; tables live in device memory.                     */
+/* ===================================================================== */
+typedef struct specdec_kv specdec_kv;
+int specdec_kv_create(int num_blocks, int block_size, int max_reqs, int max_blocks_per_req, specdec_kv** out);
+int specdec_kv_destroy(specdec_kv* kv);
+/* Appends n_tokens[i] tokens to request reqs[i] for i < n, in order
+ * (PagedKVCache::append_tokens).  last_block[i] receives the reference's
+ * return value. Host arrays. */
+int specdec_kv_append(specdec_kv* kv, const int32_t* reqs, const int32_t* n_tokens, int n, int32_t* last_block,
+                      void* stream);
+int specdec_kv_free_request(specdec_kv* kv, int req, void* stream);
+int specdec_kv_share_prefix(specdec_kv* kv, int new_req, int src_req, int shared_len, void* stream);
+int specdec_kv_free_merged_blocks(specdec_kv* kv, int req, int n_blocks, void* stream);
+int specdec_kv_evict_tokens(specdec_kv* kv, int req, int n_tokens, int* evicted, void* stream);
+/* Token-granular rollback: new lengths (host array, -1 = unchanged); tail
+ * blocks past the new length are released. */
+int specdec_kv_truncate(specdec_kv* kv, const int32_t* new_len, int n, void* stream);
+float specdec_kv_utilization(specdec_kv* kv, void* stream);
+/* Copies tables [max_reqs, max_blocks_per_req] (-1 padded), lengths and
+ * reference counts to host buffers (any may be NULL). */
+int specdec_kv_read(specdec_kv* kv, int32_t* tables, int32_t* lens, int32_t* refcounts, void* stream);
+/* Device pointers to the table state (for kernels that read block tables). */
+int32_t* specdec_kv_tables_dev(specdec_kv* kv);
+int32_t* specdec_kv_lens_dev(specdec_kv* kv);
+
+/* ===================================================================== */
+/* 4. Step engine: the whole speculative step on device.                  */
+/* ===================================================================== */
+typedef struct {
+    int hidden, layers, n_q_heads, n_kv_heads, head_dim, ffn, vocab;
+    int n_mtp_heads;
+    int block_size;     /* 16 */
+    float rms_eps;      /* 1e-5 */
+    float rope_theta;   /* 10000 */
+} specdec_model_config;
+
+typedef struct {
+    int batch;          /* sequences held by this engine (one GPU) */
+    int draft_len;      /* chain draft length k (tree: ignored) */
+    int tree_nodes;     /* 0 = chain; else nodes of the draft tree incl. root */
+    int tree_branching[8];
+    int tree_levels;
+    int max_ctx;        /* maximum tokens per sequence */
+    int num_blocks;     /* KV pool blocks (0 = derive from batch * max_ctx) */
+    int use_graph;      /* capture the step in a CUDA graph */
+    specdec_sampling sampling;
+} specdec_run_config;
+
+typedef struct specdec_engine specdec_engine;
+int specdec_engine_create(const specdec_model_config* mc, const specdec_run_config* rc, int device,
+                          specdec_engine** out);
+int specdec_engine_destroy(specdec_engine* e);
+/* Synthesises all weights on the device (bit-identical to the oracle's
+ * host-side generator for the same seed). */
+int specdec_engine_init_weights(specdec_engine* e, uint32_t seed);
+/* Chunked prefill of host prompts [batch, prompt_len] (all but the last
+ * token enter the KV; the last becomes the pending token). */
+int specdec_engine_prefill(specdec_engine* e, const int32_t* prompts, int prompt_len);
+/* Synthetic state: every sequence gets ctx_len[b] tokens of seeded random
+ * fp16 K/V, a random pending token and a random draft hidden state. */
+int specdec_engine_seed_state(specdec_engine* e, const int32_t* ctx_len, uint32_t seed);
+/* One speculative step on device: draft -> verify forward -> acceptance ->
+ * KV commit / rollback.  No host synchronisation. */
+int specdec_engine_step(specdec_engine* e);
+/* Same step with the host boundary: copies per-sequence control inputs
+ * (step counter) from host, runs the step, copies accepted lengths and
+ * emitted tokens back (out_len [batch], out_tokens [batch, rows]). */
+int specdec_engine_step_host(specdec_engine* e, int32_t* out_len, int32_t* out_tokens);
+/* Per-sequence active flags used by the next specdec_engine_step_host
+ * (inactive sequences keep their state; their reserved slots roll back). */
+int specdec_engine_set_active(specdec_engine* e, const int32_t* active);
+void* specdec_engine_stream(specdec_engine* e);
+/* Read back state / intermediate buffers ("logits", "draft_logits", "drafts",
+ * "accepted", "out_tokens", "pending", "h0", "hidden", "lens", "tables", "kv",
+ * "step", "emitted", ...) and overwrite state ("h0", "pending", "drafts",
+ * "kv").  Both synchronise the engine stream. */
+int specdec_engine_read(specdec_engine* e, const char* what, void* host, size_t bytes);
+int specdec_engine_write(specdec_engine* e, const char* what, const void* host, size_t bytes);
+int specdec_engine_info(specdec_engine* e, const char* what, int64_t* value);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,44 @@
+#!/usr/bin/env bash
+# Builds oracle/_ref/libref.so from the reference's own C++ sources (test
+# infrastructure: the result is a checker, never part of the product).
+#
+#   server/paged_attention.cpp, server/speculative_decoder.cpp,
+#   server/mtp_heads.cpp                 compiled in place, unmodified;
+#   server/paged_kv_cache.cpp            compiled unmodified from a scratch copy
+#                                        under oracle/_ref/src whose header has
+#                                        the one-word shim the reference needs
+#                                        to compile (`mutable` on cache_mutex,
+#                                        required by get_utilization() const);
+#   oracle/ref_shim.cpp + oracle C files provide the Rust kernel symbols those
+#                                        files call (C restatements of lib.rs).
+#
+# Outputs only into oracle/_ref/ (git-ignored).  Needs the reference tree at
+# $REF (default /root/reference); without it the script exits 0 and leaves any
+# previously built library in place.
+set -euo pipefail
+HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+REF="${REF:-/root/reference}"
+OUT="$HERE/_ref"
+if [ ! -d "$REF/server" ]; then
+  echo "build_ref: reference tree not found at $REF; skipping" >&2
+  exit 0
+fi
+CXX=/usr/bin/g++
+CC=/usr/bin/gcc
+mkdir -p "$OUT/src" "$OUT/obj"
+cp "$REF/server/paged_kv_cache.cpp" "$OUT/src/paged_kv_cache.cpp"
+sed 's/^\(\s*\)std::mutex cache_mutex;/\1mutable std::mutex cache_mutex;/' "$REF/server/paged_kv_cache.h" > "$OUT/src/paged_kv_cache.h"
+grep -q "mutable std::mutex cache_mutex" "$OUT/src/paged_kv_cache.h"
+
+CXXFLAGS="-std=c++20 -O2 -fPIC -fopenmp -ffp-contract=off -w"
+CFLAGS="-O2 -fPIC -fopenmp -ffp-contract=off -std=gnu11 -w"
+$CXX $CXXFLAGS -c "$REF/server/paged_attention.cpp" -o "$OUT/obj/paged_attention.o"
+$CXX $CXXFLAGS -c "$REF/server/speculative_decoder.cpp" -o "$OUT/obj/speculative_decoder.o"
+$CXX $CXXFLAGS -c "$REF/server/mtp_heads.cpp" -o "$OUT/obj/mtp_heads.o"
+$CXX $CXXFLAGS -c "$OUT/src/paged_kv_cache.cpp" -o "$OUT/obj/paged_kv_cache.o"
+$CXX $CXXFLAGS -I"$OUT/src" -I"$REF/server" -I"$HERE" -c "$HERE/ref_shim.cpp" -o "$OUT/obj/ref_shim.o"
+for f in orc_sample orc_model orc_kv; do
+  $CC $CFLAGS -c "$HERE/$f.c" -o "$OUT/obj/$f.o"
+done
+$CXX -shared -fopenmp -o "$OUT/libref.so" "$OUT"/obj/*.o -lm
+echo "build_ref: built $OUT/libref.so"

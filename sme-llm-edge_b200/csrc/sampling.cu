@@ -1,0 +1,784 @@
+// sampling.cu -- fused acceptance / sampling kernels (sm_100a).
+//
+// Row statistics, rejection-sampling acceptance (min(1, p/q) test, residual
+// max(0, p - q) redraw, bonus token), tree acceptance, draft sampling, top-k,
+// and the reference-compatible greedy verify (lib.rs:696-779).
+//
+// Every decision is taken on exact integers: a token's probability mass is
+// E_j = floor(2^((z_j - max) * log2(e) / T) * 2^31) (deterministic exp2), sums
+// are integer, the min(1, p/q) test and the residual are integer
+// cross-multiplications, so the result does not depend on reduction order.
+#include <cfloat>
+#include <climits>
+
+#include "common.cuh"
+
+namespace specdec {
+
+struct DevRowStats {
+    float max;
+    uint32_t tau;
+    uint64_t sum;
+    uint64_t nuc;
+    int32_t argmax;
+    int32_t pad;
+};
+static_assert(sizeof(DevRowStats) == 32, "row stats layout");
+
+constexpr int kRowThreads = 1024;
+
+struct RowSmem {
+    uint64_t hist[256];
+    u128 scan[32];
+    uint64_t red64[32];
+    float redf[32];
+    int redi[32];
+    DevRowStats st;
+    int result;
+    u128 big;
+};
+
+__device__ __forceinline__ uint32_t mass_of(float z, float m, float c) {
+    return exp2_fx31(__fmul_rn(__fsub_rn(z, m), c));
+}
+
+// (value desc, index asc) arg-max reduction; NaN never wins.
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
+    if (i2 < 0) return;
+    if (i < 0 || v2 > v || (v2 == v && i2 < i)) {
+        v = v2;
+        i = i2;
+    }
+}
+
+__device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, float* out_max, int* out_idx) {
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        float v = z[j];
+        if (v > bv || (bi < 0 && v == bv)) {
+            bv = v;
+            bi = j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, v2, i2);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) {
+        sm.redf[wid] = bv;
+        sm.redi[wid] = bi;
+    }
+    __syncthreads();
+    if (wid == 0) {
+        bv = lane < nw ? sm.redf[lane] : -INFINITY;
+        bi = lane < nw ? sm.redi[lane] : -1;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+            int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            argmax_merge(bv, bi, v2, i2);
+        }
+        if (lane == 0) {
+            sm.redf[0] = bv;
+            sm.redi[0] = bi;
+        }
+    }
+    __syncthreads();
+    *out_max = sm.redf[0];
+    *out_idx = sm.redi[0];
+    __syncthreads();
+}
+
+// Adds e into H[bin] for every valid lane; whole warp must call together.
+__device__ __forceinline__ void warp_hist_add(uint64_t* H, uint32_t bin, uint32_t e, bool valid) {
+    const int lane = threadIdx.x & 31;
+    unsigned active = __ballot_sync(0xffffffffu, valid && e != 0);
+    while (active) {
+        const int leader = __ffs(active) - 1;
+        const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
+        const unsigned grp = __ballot_sync(0xffffffffu, valid && e != 0 && bin == lb);
+        uint64_t v = ((grp >> lane) & 1u) ? (uint64_t)e : 0ull;
+        v = warp_sum(v);
+        if (lane == leader) atomicAdd((unsigned long long*)&H[lb], (unsigned long long)v);
+        active &= ~grp;
+    }
+}
+
+// Warp 0 picks the highest digit whose cumulative mass (from the top) reaches thr.
+__device__ void select_digit(RowSmem& sm, uint64_t thr, uint64_t* G, uint32_t* digit, uint64_t* last_bin) {
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        uint64_t local = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) local += sm.hist[255 - 8 * lane - i];
+        uint64_t incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const uint64_t g0 = *G;
+        const unsigned hit = __ballot_sync(0xffffffffu, g0 + incl >= thr);
+        const int f = hit ? (__ffs(hit) - 1) : 31;
+        if (lane == f) {
+            uint64_t cum = g0 + incl - local;
+            int chosen = 255 - 8 * f - 7;
+            for (int i = 0; i < 8; ++i) {
+                const int bin = 255 - 8 * f - i;
+                if (cum + sm.hist[bin] >= thr) {
+                    chosen = bin;
+                    break;
+                }
+                cum += sm.hist[bin];
+            }
+            sm.red64[0] = cum;
+            sm.red64[1] = sm.hist[chosen];
+            sm.redi[0] = chosen;
+        }
+    }
+    __syncthreads();
+    *G = sm.red64[0];
+    *last_bin = sm.red64[1];
+    *digit = (uint32_t)sm.redi[0];
+    __syncthreads();
+}
+
+// Full row statistics (max, argmax, mass sum, top-p threshold, nucleus mass).
+__device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint64_t tp, bool need_mass, RowSmem& sm,
+                              DevRowStats* st) {
+    float m;
+    int am;
+    cta_argmax(z, V, sm, &m, &am);
+    DevRowStats r;
+    r.max = m;
+    r.argmax = am;
+    r.pad = 0;
+    r.tau = 0;
+    r.sum = 0;
+    r.nuc = 0;
+    if (need_mass) {
+        const bool nucleus = tp < (1ull << 32);
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
+        __syncthreads();
+        uint64_t s = 0;
+        const int lane = threadIdx.x & 31;
+        const int warp_base = (threadIdx.x >> 5) * 32, stride = blockDim.x;
+        for (int base = warp_base; base < V; base += stride) {
+            const int j = base + lane;
+            const bool valid = j < V;
+            const float zj = valid ? z[j] : 0.0f;
+            const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
+            s += e;
+            if (nucleus) warp_hist_add(sm.hist, logit_key(zj) >> 24, e, valid);
+        }
+        s = block_sum<uint64_t>(s, sm.red64);
+        r.sum = s;
+        r.nuc = s;
+        if (nucleus) {
+            uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
+            if (thr < 1) thr = 1;
+            __syncthreads();
+            uint64_t G = 0, last = 0;
+            uint32_t prefix = 0, dg = 0;
+            select_digit(sm, thr, &G, &dg, &last);
+            prefix = dg << 24;
+            for (int d = 2; d >= 0; --d) {
+                const int shift = 8 * d;
+                for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
+                __syncthreads();
+                for (int base = warp_base; base < V; base += stride) {
+                    const int j = base + lane;
+                    bool valid = j < V;
+                    const float zj = valid ? z[j] : 0.0f;
+                    const uint32_t key = logit_key(zj);
+                    valid = valid && ((key >> (shift + 8)) == (prefix >> (shift + 8)));
+                    const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
+                    warp_hist_add(sm.hist, (key >> shift) & 255u, e, valid);
+                }
+                __syncthreads();
+                select_digit(sm, thr, &G, &dg, &last);
+                prefix |= dg << shift;
+            }
+            r.tau = prefix;
+            r.nuc = G + last;
+        }
+    }
+    *st = r;
+}
+
+__device__ __forceinline__ uint32_t nucleus_mass(const float* z, const DevRowStats& st, float c, int x) {
+    const float zx = z[x];
+    if (logit_key(zx) < st.tau) return 0u;
+    return mass_of(zx, st.max, c);
+}
+
+// Block-wide inclusive scan of u128 (blockDim.x multiple of 32, <= 1024).
+__device__ u128 block_incl_scan_u128(u128 v, RowSmem& sm, u128* total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t lo = __shfl_up_sync(0xffffffffu, (uint64_t)v, o);
+        uint64_t hi = __shfl_up_sync(0xffffffffu, (uint64_t)(v >> 64), o);
+        if (lane >= o) v += ((u128)hi << 64) | lo;
+    }
+    __syncthreads();
+    if (lane == 31) sm.scan[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+        u128 w = lane < nw ? sm.scan[lane] : (u128)0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint64_t lo = __shfl_up_sync(0xffffffffu, (uint64_t)w, o);
+            uint64_t hi = __shfl_up_sync(0xffffffffu, (uint64_t)(w >> 64), o);
+            if (lane >= o) w += ((u128)hi << 64) | lo;
+        }
+        if (lane < nw) sm.scan[lane] = w;
+    }
+    __syncthreads();
+    const u128 before = wid ? sm.scan[wid - 1] : (u128)0;
+    *total = sm.scan[nw - 1];
+    return v + before;
+}
+
+// Smallest j (index order) whose running mass exceeds `target`.
+template <class MassFn>
+__device__ int cta_inverse_cdf(int V, u128 target, MassFn mass, RowSmem& sm) {
+    u128 running = 0;
+    if (threadIdx.x == 0) sm.result = -1;
+    const int per_tile = blockDim.x * 4;
+    for (int tile = 0; tile < V; tile += per_tile) {
+        const int j0 = tile + threadIdx.x * 4;
+        u128 mv[4];
+        u128 local = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int j = j0 + q;
+            mv[q] = j < V ? mass(j) : (u128)0;
+            local += mv[q];
+        }
+        u128 total;
+        const u128 incl = block_incl_scan_u128(local, sm, &total);
+        if (running + total > target) {
+            u128 before = running + incl - local;
+            if (before <= target && target < running + incl) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    before += mv[q];
+                    if (before > target) {
+                        sm.result = j0 + q;
+                        break;
+                    }
+                }
+            }
+            __syncthreads();
+            const int r = sm.result;
+            __syncthreads();
+            return r;
+        }
+        running += total;
+        __syncthreads();
+    }
+    __syncthreads();
+    const int r = sm.result;
+    __syncthreads();
+    return r;
+}
+
+__device__ int cta_sample_nucleus(const float* z, int V, float c, const DevRowStats& st, uint64_t u64, RowSmem& sm) {
+    const u128 target = (u128)mulhi64(u64, st.nuc);
+    return cta_inverse_cdf(V, target, [&](int j) -> u128 { return (u128)nucleus_mass(z, st, c, j); }, sm);
+}
+
+// --------------------------------------------------------------- kernels
+struct RowSet {
+    const float* base;  // rows of length V, row r at base + r * V
+    int rows;
+};
+
+__global__ void __launch_bounds__(kRowThreads) row_stats_kernel(RowSet a, RowSet b, int V, float c, uint64_t tp,
+                                                                bool need_mass_a, bool need_mass_b,
+                                                                DevRowStats* out) {
+    __shared__ RowSmem sm;
+    const int r = blockIdx.x;
+    const bool in_a = r < a.rows;
+    const float* z = in_a ? a.base + (size_t)r * V : b.base + (size_t)(r - a.rows) * V;
+    DevRowStats st;
+    cta_row_stats(z, V, c, tp, in_a ? need_mass_a : need_mass_b, sm, &st);
+    if (threadIdx.x == 0) out[r] = st;
+}
+
+// One CTA per sequence: sequential min(1, p/q) tests over the draft positions,
+// then the residual (or bonus) draw on the first rejected (or last) row.
+__global__ void __launch_bounds__(kRowThreads) accept_chain_kernel(const float* __restrict__ target,
+                                                                   const float* __restrict__ draft,
+                                                                   const int32_t* __restrict__ drafts, int k, int V,
+                                                                   float c, bool greedy, uint64_t seed, const uint32_t* step_dev, uint32_t step_host,
+                                                                   const DevRowStats* __restrict__ stats, int B,
+                                                                   int32_t* __restrict__ accepted_len,
+                                                                   int32_t* __restrict__ out_tokens) {
+    __shared__ RowSmem sm;
+    const uint32_t step = step_dev ? *step_dev : step_host;
+    const int b = blockIdx.x;
+    const DevRowStats* sp = stats + (size_t)b * (k + 1);
+    const DevRowStats* sq = stats + (size_t)B * (k + 1) + (size_t)b * k;
+    const float* P = target + (size_t)b * (k + 1) * V;
+    const float* Q = draft + (size_t)b * k * V;
+    const int32_t* D = drafts + (size_t)b * k;
+    if (threadIdx.x == 0) {
+        int a = 0;
+        if (greedy) {
+            while (a < k && sp[a].argmax == D[a]) ++a;
+        } else {
+            while (a < k) {
+                const int x = D[a];
+                uint64_t ep = 0, eq = 0;
+                if (x >= 0 && x < V) {
+                    ep = nucleus_mass(P + (size_t)a * V, sp[a], c, x);
+                    eq = nucleus_mass(Q + (size_t)a * V, sq[a], c, x);
+                }
+                const uint32_t u = uniform_u32(seed, step, (uint32_t)b, (uint32_t)a, U_ACCEPT);
+                const u128 lhs = (u128)u * eq * sp[a].nuc;
+                const u128 rhs = ((u128)ep * sq[a].nuc) << 32;
+                if (!(lhs < rhs)) break;
+                ++a;
+            }
+        }
+        sm.redi[0] = a;
+    }
+    __syncthreads();
+    const int a = sm.redi[0];
+    __syncthreads();
+    int tok;
+    if (greedy) {
+        tok = sp[a].argmax;
+    } else {
+        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)a, U_RESAMPLE);
+        const float* zp = P + (size_t)a * V;
+        if (a == k) {
+            tok = cta_sample_nucleus(zp, V, c, sp[a], u64, sm);
+        } else {
+            const float* zq = Q + (size_t)a * V;
+            const DevRowStats stp = sp[a], stq = sq[a];
+            auto resid = [&](int j) -> u128 {
+                const u128 x = (u128)nucleus_mass(zp, stp, c, j) * stq.nuc;
+                const u128 y = (u128)nucleus_mass(zq, stq, c, j) * stp.nuc;
+                return x > y ? x - y : (u128)0;
+            };
+            // total residual mass
+            u128 part = 0;
+            for (int j = threadIdx.x; j < V; j += blockDim.x) part += resid(j);
+            u128 R = 0;
+            {
+                u128 tot;
+                (void)block_incl_scan_u128(part, sm, &tot);
+                R = tot;
+            }
+            __syncthreads();
+            if (R == 0) {
+                tok = cta_sample_nucleus(zp, V, c, stp, u64, sm);
+            } else {
+                const uint64_t rh = (uint64_t)(R >> 64), rl = (uint64_t)R;
+                const u128 tgt = (u128)u64 * rh + (u128)mulhi64(u64, rl);
+                tok = cta_inverse_cdf(V, tgt, resid, sm);
+            }
+        }
+    }
+    if (threadIdx.x == 0) {
+        int32_t* out = out_tokens + (size_t)b * (k + 1);
+        for (int i = 0; i < a; ++i) out[i] = D[i];
+        out[a] = tok;
+        for (int i = a + 1; i <= k; ++i) out[i] = -1;
+        accepted_len[b] = a;
+    }
+}
+
+// Tree acceptance, one CTA per sequence; statistics of the visited rows are
+// computed on demand (a path visits at most depth+1 of the R rows).
+__global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* __restrict__ target,
+                                                                  const int32_t* __restrict__ node_tokens,
+                                                                  const int32_t* __restrict__ parent, int R, int V,
+                                                                  float c, uint64_t tp, bool greedy, uint64_t seed,
+                                                                  const uint32_t* step_dev, uint32_t step_host,
+                                                                  int32_t* __restrict__ accepted_len,
+                                                                  int32_t* __restrict__ path_nodes,
+                                                                  int32_t* __restrict__ out_tokens) {
+    __shared__ RowSmem sm;
+    __shared__ int s_removed[64];
+    __shared__ int s_nremoved, s_next, s_emit_mode;
+    __shared__ uint64_t s_remaining;
+    const uint32_t step = step_dev ? *step_dev : step_host;
+    const int b = blockIdx.x;
+    const float* P = target + (size_t)b * R * V;
+    const int32_t* tok = node_tokens + (size_t)b * R;
+    int32_t* path = path_nodes + (size_t)b * R;
+    int32_t* out = out_tokens + (size_t)b * R;
+    for (int i = threadIdx.x; i < R; i += blockDim.x) {
+        path[i] = -1;
+        out[i] = -1;
+    }
+    int cur = 0, a = 0, emit = -1;
+    for (;;) {
+        const float* z = P + (size_t)cur * V;
+        DevRowStats st;
+        cta_row_stats(z, V, c, tp, !greedy, sm, &st);
+        if (threadIdx.x == 0) {
+            int next = -1;
+            s_nremoved = 0;
+            s_emit_mode = 0;
+            if (greedy) {
+                for (int ch = cur + 1; ch < R; ++ch)
+                    if (parent[ch] == cur && tok[ch] == st.argmax) {
+                        next = ch;
+                        break;
+                    }
+            } else {
+                uint64_t remaining = st.nuc;
+                for (int ch = cur + 1; ch < R && next < 0; ++ch) {
+                    if (parent[ch] != cur) continue;
+                    const int x = tok[ch];
+                    uint64_t e = (x >= 0 && x < V) ? nucleus_mass(z, st, c, x) : 0;
+                    bool dup = false;
+                    for (int t = 0; t < s_nremoved; ++t) dup |= s_removed[t] == x;
+                    if (dup) e = 0;
+                    const uint32_t u = uniform_u32(seed, step, (uint32_t)b, (uint32_t)ch, U_ACCEPT);
+                    if ((u128)u * remaining < ((u128)e << 32)) {
+                        next = ch;
+                        break;
+                    }
+                    if (!dup && s_nremoved < 64) s_removed[s_nremoved++] = x;
+                    remaining -= e;
+                }
+                s_remaining = remaining;
+            }
+            s_next = next;
+        }
+        __syncthreads();
+        const int next = s_next;
+        if (next < 0) {
+            if (greedy) {
+                emit = st.argmax;
+            } else {
+                const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)cur, U_RESAMPLE);
+                const uint64_t remaining = s_remaining;
+                const int nrem = s_nremoved;
+                if (remaining == 0) {
+                    emit = cta_sample_nucleus(z, V, c, st, u64, sm);
+                } else {
+                    const u128 tgt = (u128)mulhi64(u64, remaining);
+                    emit = cta_inverse_cdf(
+                        V, tgt,
+                        [&](int j) -> u128 {
+                            for (int t = 0; t < nrem; ++t)
+                                if (s_removed[t] == j) return (u128)0;
+                            return (u128)nucleus_mass(z, st, c, j);
+                        },
+                        sm);
+                }
+            }
+            break;
+        }
+        if (threadIdx.x == 0) {
+            path[a] = next;
+            out[a] = tok[next];
+        }
+        ++a;
+        cur = next;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        out[a] = emit;
+        accepted_len[b] = a;
+    }
+}
+
+// Draft sampling: one CTA per row.
+__global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* __restrict__ logits, int k, int V,
+                                                                  float c, uint64_t tp, bool greedy, uint64_t seed,
+                                                                  const uint32_t* step_dev, uint32_t step_host,
+                                                                  int32_t* __restrict__ out) {
+    __shared__ RowSmem sm;
+    const uint32_t step = step_dev ? *step_dev : step_host;
+    const int r = blockIdx.x;
+    const float* z = logits + (size_t)r * V;
+    DevRowStats st;
+    cta_row_stats(z, V, c, tp, !greedy, sm, &st);
+    int tok = st.argmax;
+    if (!greedy)
+        tok = cta_sample_nucleus(z, V, c, st,
+                                 uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k), U_DRAFT), sm);
+    if (threadIdx.x == 0) out[r] = tok;
+}
+
+// Top-k (descending value, ascending index) per row: k rounds of arg-max with
+// the already chosen indices excluded.
+__global__ void __launch_bounds__(kRowThreads) topk_kernel(const float* __restrict__ logits, int V, int k,
+                                                           int32_t* __restrict__ out) {
+    __shared__ RowSmem sm;
+    __shared__ int chosen[16];
+    const int r = blockIdx.x;
+    const float* z = logits + (size_t)r * V;
+    for (int t = 0; t < k; ++t) {
+        float bv = -INFINITY;
+        int bi = -1;
+        for (int j = threadIdx.x; j < V; j += blockDim.x) {
+            bool ex = false;
+            for (int u = 0; u < t; ++u) ex |= chosen[u] == j;
+            if (ex) continue;
+            const float v = z[j];
+            if (bi < 0 || v > bv) {
+                bv = v;
+                bi = j;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+            int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            argmax_merge(bv, bi, v2, i2);
+        }
+        const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+        __syncthreads();
+        if (lane == 0) {
+            sm.redf[wid] = bv;
+            sm.redi[wid] = bi;
+        }
+        __syncthreads();
+        if (wid == 0) {
+            bv = lane < nw ? sm.redf[lane] : -INFINITY;
+            bi = lane < nw ? sm.redi[lane] : -1;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+                int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+                argmax_merge(bv, bi, v2, i2);
+            }
+            if (lane == 0) {
+                chosen[t] = bi;
+                out[(size_t)r * k + t] = bi;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------- reference-compatible verify
+// Arg-max as a 4-lane (128-bit SVE) scan computes it: per lane strict '>' keeps
+// the earliest index, the lowest lane holding the global max wins.
+__device__ __forceinline__ bool compat_better(float v, int i, float bv, int bi) {
+    if (bi < 0) return true;
+    if (v > bv) return true;
+    if (v < bv) return false;
+    const int l = i & 3, bl = bi & 3;
+    return l < bl || (l == bl && i < bi);
+}
+
+__global__ void compat_argmax_kernel(const float* __restrict__ logits, const int32_t* __restrict__ lens, int V,
+                                     int max_draft, int32_t* __restrict__ best) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int b = blockIdx.x / max_draft, i = blockIdx.x % max_draft;
+    const int d = lens ? min(lens[b], 8) : max_draft;
+    if (i >= d) {
+        if (threadIdx.x == 0) best[blockIdx.x] = 0;
+        return;
+    }
+    const float* z = logits + (size_t)blockIdx.x * V;
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float v = z[j];
+        if (v != v) continue;  // NaN never compares greater
+        if (compat_better(v, j, bv, bi)) {
+            bv = v;
+            bi = j;
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (i2 >= 0 && compat_better(v2, i2, bv, bi)) {
+            bv = v2;
+            bi = i2;
+        }
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) {
+        sv[wid] = bv;
+        si[wid] = bi;
+    }
+    __syncthreads();
+    if (wid == 0) {
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : -1;
+        for (int o = 16; o; o >>= 1) {
+            float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+            int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (i2 >= 0 && compat_better(v2, i2, bv, bi)) {
+                bv = v2;
+                bi = i2;
+            }
+        }
+        if (lane == 0) best[blockIdx.x] = bi < 0 ? 0 : bi;
+    }
+}
+
+__global__ void compat_count_kernel(const int32_t* __restrict__ best, const int32_t* __restrict__ drafts,
+                                    const int32_t* __restrict__ lens, int max_draft, int B, int32_t* accepted,
+                                    int32_t* replacement) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    int d = lens[b];
+    if (d <= 0) {
+        accepted[b] = 0;
+        replacement[b] = -1;
+        return;
+    }
+    d = min(d, min(8, max_draft));
+    int cnt = 0;
+    bool mism = false;
+    for (int i = 0; i < d; ++i) {
+        if (best[(size_t)b * max_draft + i] == drafts[(size_t)b * max_draft + i]) ++cnt;
+        else mism = true;
+    }
+    accepted[b] = cnt;
+    replacement[b] = mism ? best[(size_t)b * max_draft + cnt] : -1;
+}
+
+// ------------------------------------------------------------ host side
+float temp_coeff(float temperature) { return (float)(1.4426950408889634 / (double)temperature); }
+uint64_t top_p_q32(float top_p) {
+    if (!(top_p < 1.0f)) return 1ull << 32;
+    if (top_p <= 0.0f) return 0;
+    return (uint64_t)llround((double)top_p * 4294967296.0);
+}
+
+int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaStream_t s) {
+    SD_CHECK(k >= 1 && k <= 16, SPECDEC_EINVAL, "topk: k must be in [1,16]");
+    topk_kernel<<<rows, kRowThreads, 0, s>>>(logits, V, k, out);
+    SD_LAUNCH_CHECK("topk_kernel");
+    return SPECDEC_OK;
+}
+
+int launch_accept_chain_dev(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
+                            float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
+                            int32_t* accepted_len, int32_t* out_tokens, void* ws, cudaStream_t s) {
+    const bool greedy = !(temperature > 0.0f);
+    const float c = greedy ? 0.0f : temp_coeff(temperature);
+    const uint64_t tp = top_p_q32(top_p);
+    const int rows = B * (k + 1) + (greedy ? 0 : B * k);
+    RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
+    DevRowStats* st = reinterpret_cast<DevRowStats*>(ws);
+    row_stats_kernel<<<rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
+    SD_LAUNCH_CHECK("row_stats_kernel");
+    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, seed,
+                                                  step_dev, 0u, st, B, accepted_len, out_tokens);
+    SD_LAUNCH_CHECK("accept_chain_kernel");
+    return SPECDEC_OK;
+}
+
+int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, const int32_t* parent, int B, int R, int V,
+                           float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
+                           int32_t* accepted_len, int32_t* path, int32_t* out_tokens, cudaStream_t s) {
+    const bool greedy = !(temperature > 0.0f);
+    accept_tree_kernel<<<B, kRowThreads, 0, s>>>(target, node_tokens, parent, R, V, greedy ? 0.0f : temp_coeff(temperature),
+                                                 top_p_q32(top_p), greedy, seed, step_dev, 0u, accepted_len, path,
+                                                 out_tokens);
+    SD_LAUNCH_CHECK("accept_tree_kernel");
+    return SPECDEC_OK;
+}
+
+int launch_sample_rows_dev(const float* logits, int rows, int k, int V, float temperature, float top_p, uint64_t seed,
+                           const uint32_t* step_dev, int32_t* out, cudaStream_t s) {
+    const bool greedy = !(temperature > 0.0f);
+    sample_rows_kernel<<<rows, kRowThreads, 0, s>>>(logits, k, V, greedy ? 0.0f : temp_coeff(temperature),
+                                                    top_p_q32(top_p), greedy, seed, step_dev, 0u, out);
+    SD_LAUNCH_CHECK("sample_rows_kernel");
+    return SPECDEC_OK;
+}
+
+}  // namespace specdec
+
+using namespace specdec;
+
+extern "C" size_t specdec_accept_workspace_bytes(int rows) { return (size_t)(rows > 0 ? rows : 0) * sizeof(DevRowStats); }
+
+extern "C" int specdec_accept_chain(const float* target, const float* draft, const int32_t* drafts, int B, int k,
+                                    int V, const specdec_sampling* sp, int32_t* accepted_len, int32_t* out_tokens,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    SD_CHECK(sp && target && drafts && accepted_len && out_tokens, SPECDEC_EINVAL, "accept_chain: null argument");
+    SD_CHECK(B >= 0 && k >= 0 && V > 0, SPECDEC_EINVAL, "accept_chain: bad shape");
+    if (B == 0) return SPECDEC_OK;
+    const bool greedy = !(sp->temperature > 0.0f);
+    SD_CHECK(greedy || draft, SPECDEC_EINVAL, "accept_chain: draft logits required when sampling");
+    const int rows = B * (k + 1) + (greedy ? 0 : B * k);
+    SD_CHECK(workspace && workspace_bytes >= specdec_accept_workspace_bytes(B * (2 * k + 1)), SPECDEC_EINVAL,
+             "accept_chain: workspace too small");
+    cudaStream_t s = as_stream(stream);
+    const float c = greedy ? 0.0f : temp_coeff(sp->temperature);
+    const uint64_t tp = top_p_q32(sp->top_p);
+    RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
+    DevRowStats* st = reinterpret_cast<DevRowStats*>(workspace);
+    row_stats_kernel<<<rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
+    SD_LAUNCH_CHECK("row_stats_kernel");
+    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, sp->seed,
+                                                  nullptr, sp->step, st, B, accepted_len, out_tokens);
+    SD_LAUNCH_CHECK("accept_chain_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_accept_tree(const float* target, const int32_t* node_tokens, const int32_t* parent, int B,
+                                   int R, int V, const specdec_sampling* sp, int32_t* accepted_len,
+                                   int32_t* path_nodes, int32_t* out_tokens, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    (void)workspace;
+    (void)workspace_bytes;
+    SD_CHECK(sp && target && node_tokens && parent && accepted_len && path_nodes && out_tokens, SPECDEC_EINVAL,
+             "accept_tree: null argument");
+    SD_CHECK(R >= 1 && R <= 64 && V > 0 && B >= 0, SPECDEC_EINVAL, "accept_tree: bad shape (R must be 1..64)");
+    if (B == 0) return SPECDEC_OK;
+    const bool greedy = !(sp->temperature > 0.0f);
+    const float c = greedy ? 0.0f : temp_coeff(sp->temperature);
+    accept_tree_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(target, node_tokens, parent, R, V, c,
+                                                                 top_p_q32(sp->top_p), greedy, sp->seed, nullptr,
+                                                                 sp->step, accepted_len, path_nodes, out_tokens);
+    SD_LAUNCH_CHECK("accept_tree_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_sample_rows(const float* logits, int rows, int k, int V, const specdec_sampling* sp,
+                                   int32_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+    (void)workspace;
+    (void)workspace_bytes;
+    SD_CHECK(sp && logits && out && rows >= 0 && k >= 1 && V > 0, SPECDEC_EINVAL, "sample_rows: bad argument");
+    if (rows == 0) return SPECDEC_OK;
+    const bool greedy = !(sp->temperature > 0.0f);
+    sample_rows_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(
+        logits, k, V, greedy ? 0.0f : temp_coeff(sp->temperature), top_p_q32(sp->top_p), greedy, sp->seed, nullptr, sp->step,
+        out);
+    SD_LAUNCH_CHECK("sample_rows_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_compat_verify(const float* logits, const int32_t* drafts, const int32_t* lens, int V,
+                                     int max_draft, int B, int32_t* accepted, int32_t* replacement, void* stream) {
+    SD_CHECK(logits && drafts && lens && accepted && replacement, SPECDEC_EINVAL, "compat_verify: null argument");
+    SD_CHECK(V > 0 && max_draft > 0 && B >= 0, SPECDEC_EINVAL, "compat_verify: bad shape");
+    if (B == 0) return SPECDEC_OK;
+    cudaStream_t s = as_stream(stream);
+    int32_t* best = nullptr;
+    SD_CUDA(cudaMallocAsync(&best, sizeof(int32_t) * (size_t)B * max_draft, s));
+    compat_argmax_kernel<<<B * max_draft, 256, 0, s>>>(logits, lens, V, max_draft, best);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        compat_count_kernel<<<(B + 127) / 128, 128, 0, s>>>(best, drafts, lens, max_draft, B, accepted, replacement);
+        e = cudaGetLastError();
+    }
+    cudaFreeAsync(best, s);
+    if (e != cudaSuccess) return cuda_status(e, "compat_verify");
+    return SPECDEC_OK;
+}

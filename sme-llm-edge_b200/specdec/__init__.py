@@ -1,0 +1,408 @@
+"""Host-side mirror of the sme-llm-edge speculative-decoding operator surface,
+backed by libspecdec_sm100.so (CUDA, sm_100a).
+
+The classes keep the reference's names and argument meanings:
+
+  SpeculativeDecoder   server/speculative_decoder.h:12-35
+  MTPHeads             server/mtp_heads.h:23-41
+  compute_paged_attention  server/paged_attention.h:10-19
+  PagedKVCache         server/paged_kv_cache.h:28-63
+
+plus the device-resident step engine (`Engine`).  Every compute call runs a
+CUDA kernel of libspecdec_sm100.so; there is no CPU path.  Importing this
+module loads the library and raises if it is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libspecdec_sm100.so")
+
+OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, ENOTSUP = range(6)
+
+
+class SpecdecError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"specdec error {code}: {msg}")
+        self.code = code
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} not built; run `python sme-llm-edge_b200/build.py`")
+    return C.CDLL(LIB_PATH)
+
+
+_lib = _load()
+
+P = C.c_void_p
+I = C.c_int
+F = C.c_float
+SZ = C.c_size_t
+U32 = C.c_uint32
+U64 = C.c_uint64
+
+
+class Sampling(C.Structure):
+    _fields_ = [("temperature", F), ("top_p", F), ("seed", U64), ("step", U32)]
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("hidden", I), ("layers", I), ("n_q_heads", I), ("n_kv_heads", I), ("head_dim", I), ("ffn", I),
+                ("vocab", I), ("n_mtp_heads", I), ("block_size", I), ("rms_eps", F), ("rope_theta", F)]
+
+
+class RunConfig(C.Structure):
+    _fields_ = [("batch", I), ("draft_len", I), ("tree_nodes", I), ("tree_branching", I * 8), ("tree_levels", I),
+                ("max_ctx", I), ("num_blocks", I), ("use_graph", I), ("sampling", Sampling)]
+
+
+_SIGS = {
+    "specdec_last_error": (C.c_char_p, []),
+    "specdec_abi_version": (I, []),
+    "sve2_speculative_verify_f32": (None, [P, P, P, U32, U32, U32, P, P]),
+    "rust_sme_mtp_predict_f32": (None, [P, P, P, U32, U32, U32]),
+    "rust_sme_mtp_sample_f32": (None, [P, P, U32, U32]),
+    "sme_sm_prefetch_kv_blocks": (None, [P, P, U32]),
+    "rust_sme_flashdecoding_chunk_f32": (None, [P, P, P, U32, U32, F, P, P, P]),
+    "rust_sve2_flashdecoding_reduce_f32": (None, [P, P, P, U32, U32, P]),
+    "specdec_paged_attention_compat_f32": (I, [P, P, P, SZ, P, P, P, P, I, I, I]),
+    "specdec_accept_workspace_bytes": (SZ, [I]),
+    "specdec_accept_chain": (I, [P, P, P, I, I, I, C.POINTER(Sampling), P, P, P, SZ, P]),
+    "specdec_accept_tree": (I, [P, P, P, I, I, I, C.POINTER(Sampling), P, P, P, P, SZ, P]),
+    "specdec_sample_rows": (I, [P, I, I, I, C.POINTER(Sampling), P, P, SZ, P]),
+    "specdec_compat_verify": (I, [P, P, P, I, I, I, P, P, P]),
+    "specdec_w4_tiled_bytes": (SZ, [I, I]),
+    "specdec_w4_tile": (I, [P, P, I, I, P, P]),
+    "specdec_w4_untile": (I, [P, I, I, P, P, P]),
+    "specdec_w4a16_workspace_bytes": (SZ, [I, I, I]),
+    "specdec_w4a16_gemm": (I, [P, I, I, P, I, I, P, I, I, P, SZ, P]),
+    "specdec_w4a16_gemm_simt": (I, [P, I, I, P, I, I, P, I, I, P]),
+    "specdec_attention_workspace_bytes": (SZ, [I, I, I, I, I, I]),
+    "specdec_attention": (I, [P, P, I, I, I, P, I, P, P, I, I, I, P, P, SZ, P]),
+    "specdec_kv_create": (I, [I, I, I, I, C.POINTER(P)]),
+    "specdec_kv_destroy": (I, [P]),
+    "specdec_kv_append": (I, [P, P, P, I, P, P]),
+    "specdec_kv_free_request": (I, [P, I, P]),
+    "specdec_kv_share_prefix": (I, [P, I, I, I, P]),
+    "specdec_kv_free_merged_blocks": (I, [P, I, I, P]),
+    "specdec_kv_evict_tokens": (I, [P, I, I, C.POINTER(I), P]),
+    "specdec_kv_truncate": (I, [P, P, I, P]),
+    "specdec_kv_utilization": (F, [P, P]),
+    "specdec_kv_read": (I, [P, P, P, P, P]),
+    "specdec_kv_tables_dev": (P, [P]),
+    "specdec_kv_lens_dev": (P, [P]),
+    "specdec_engine_create": (I, [C.POINTER(ModelConfig), C.POINTER(RunConfig), I, C.POINTER(P)]),
+    "specdec_engine_destroy": (I, [P]),
+    "specdec_engine_init_weights": (I, [P, U32]),
+    "specdec_engine_prefill": (I, [P, P, I]),
+    "specdec_engine_seed_state": (I, [P, P, U32]),
+    "specdec_engine_step": (I, [P]),
+    "specdec_engine_step_host": (I, [P, P, P]),
+    "specdec_engine_set_active": (I, [P, P]),
+    "specdec_engine_stream": (P, [P]),
+    "specdec_engine_read": (I, [P, C.c_char_p, P, SZ]),
+    "specdec_engine_write": (I, [P, C.c_char_p, P, SZ]),
+    "specdec_engine_info": (I, [P, C.c_char_p, C.POINTER(C.c_int64)]),
+}
+for _name, (_res, _args) in _SIGS.items():
+    _fn = getattr(_lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+EXPORTED_SYMBOLS = tuple(_SIGS)
+
+
+def lib():
+    return _lib
+
+
+def last_error() -> str:
+    return (_lib.specdec_last_error() or b"").decode()
+
+
+def check(rc: int):
+    if rc != OK:
+        raise SpecdecError(rc, last_error())
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def sampling(temperature: float, top_p: float = 1.0, seed: int = 0, step: int = 0) -> Sampling:
+    return Sampling(float(temperature), float(top_p), int(seed), int(step))
+
+
+# ======================================================================
+# Reference operator surface
+# ======================================================================
+class SpeculativeDecoder:
+    """server/speculative_decoder.h: n-gram drafting on the host, verification on the GPU."""
+
+    def __init__(self, max_draft: int = 3):
+        self.max_draft_length = int(max_draft)
+        self.ngram_table: dict[tuple[int, int], int] = {}
+
+    def generate_draft(self, recent_tokens):
+        # speculative_decoder.cpp:24-51 (bigram table lookup)
+        out = []
+        if len(recent_tokens) < 2:
+            return out
+        t1, t2 = int(recent_tokens[-2]), int(recent_tokens[-1])
+        for _ in range(self.max_draft_length):
+            nxt = self.ngram_table.get((t1, t2))
+            if nxt is None:
+                break
+            out.append(nxt)
+            t1, t2 = t2, nxt
+        return out
+
+    def update_ngram(self, t1: int, t2: int, next_token: int):
+        self.ngram_table[(int(t1), int(t2))] = int(next_token)
+
+    def verify_drafts_sve2(self, model_logits, draft_tokens, draft_lengths, vocab_size: int, batch_size: int):
+        """speculative_decoder.cpp:53-77 -> sve2_speculative_verify_f32 on the GPU.
+
+        model_logits is [batch, max_draft_length, vocab] (the decoder's own
+        max_draft_length is the stride, as in the reference)."""
+        acc = np.zeros(batch_size, np.int32)
+        rep = np.full(batch_size, -1, np.int32)
+        logits = np.ascontiguousarray(model_logits, dtype=np.float32).reshape(-1)
+        drafts = np.ascontiguousarray(draft_tokens, dtype=np.int32).reshape(-1)
+        lens = np.ascontiguousarray(draft_lengths, dtype=np.int32).reshape(-1)
+        if logits.size == 0 or drafts.size == 0 or lens.size == 0:
+            return acc, rep
+        _lib.sve2_speculative_verify_f32(_p(logits), _p(drafts), _p(lens), vocab_size, self.max_draft_length,
+                                         batch_size, _p(acc), _p(rep))
+        return acc, rep
+
+
+class MTPHeads:
+    """server/mtp_heads.h: K draft heads of fp32 [K, hidden, vocab] weights."""
+
+    def __init__(self, k_heads: int, hidden_dim: int, vocab_size: int):
+        self.k_heads, self.hidden_dim, self.vocab_size = int(k_heads), int(hidden_dim), int(vocab_size)
+        self.mtp_weights = np.zeros(self.k_heads * self.hidden_dim * self.vocab_size, np.float32)
+        self.mtp_logits = np.zeros(self.k_heads * self.vocab_size, np.float32)
+
+    def load_weights(self, weights_data):
+        if weights_data is None:
+            return
+        self.mtp_weights[:] = np.asarray(weights_data, dtype=np.float32).reshape(-1)
+
+    def generate_drafts(self, hidden_state):
+        if hidden_state is None or not (self.hidden_dim and self.vocab_size and self.k_heads):
+            return [-1] * self.k_heads
+        h = np.ascontiguousarray(hidden_state, dtype=np.float32).reshape(-1)
+        _lib.rust_sme_mtp_predict_f32(_p(h), _p(self.mtp_weights), _p(self.mtp_logits), self.hidden_dim,
+                                      self.vocab_size, self.k_heads)
+        out = np.zeros(self.k_heads, np.int32)
+        _lib.rust_sme_mtp_sample_f32(_p(self.mtp_logits), _p(out), self.vocab_size, self.k_heads)
+        return out.tolist()
+
+
+def compute_paged_attention(batch_q, k_cache_pool, v_cache_pool, batch_block_tables, batch_seq_lens, batch_o,
+                            hidden_dim: int, block_size: int):
+    """server/paged_attention.cpp:16-111 semantics on the GPU; accumulates into batch_o (in place)."""
+    q = np.ascontiguousarray(batch_q, dtype=np.float32).reshape(-1)
+    kp = np.ascontiguousarray(k_cache_pool, dtype=np.float32).reshape(-1)
+    vp = np.ascontiguousarray(v_cache_pool, dtype=np.float32).reshape(-1)
+    M = len(batch_seq_lens)
+    off = np.zeros(M + 1, np.int32)
+    for m in range(M):
+        off[m + 1] = off[m] + len(batch_block_tables[m])
+    flat = np.zeros(max(1, int(off[-1])), np.int32)
+    for m in range(M):
+        flat[off[m]:off[m + 1]] = batch_block_tables[m]
+    lens = np.ascontiguousarray(batch_seq_lens, dtype=np.int32)
+    o = batch_o if isinstance(batch_o, np.ndarray) and batch_o.dtype == np.float32 else np.asarray(batch_o, np.float32)
+    assert o.flags["C_CONTIGUOUS"]
+    check(_lib.specdec_paged_attention_compat_f32(_p(q), _p(kp), _p(vp), kp.size, _p(off), _p(flat), _p(lens), _p(o),
+                                                  M, hidden_dim, block_size))
+    return o
+
+
+class PagedKVCache:
+    """server/paged_kv_cache.h: block tables kept in device memory.
+
+    Allocation is lowest-free-index with reference counts, as the reference
+    (paged_kv_cache.cpp:68-77); the K/V payload lives in the engine's fp16 pool."""
+
+    def __init__(self, num_blocks: int, block_size: int, hidden_dim: int = 0, max_requests: int = 256,
+                 max_blocks_per_request: int = 1024):
+        self.num_blocks, self.block_size, self.hidden_dim = num_blocks, block_size, hidden_dim
+        self.max_requests, self.max_bpr = max_requests, max_blocks_per_request
+        h = P()
+        check(_lib.specdec_kv_create(num_blocks, block_size, max_requests, max_blocks_per_request, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            _lib.specdec_kv_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def append_tokens(self, request_id: int, n_tokens) -> int:
+        """Appends tokens (a count, or K/V rows whose first dim is the count)."""
+        n = int(n_tokens) if np.isscalar(n_tokens) else (np.asarray(n_tokens).size // max(1, self.hidden_dim))
+        return self.append_batch([request_id], [n])[0]
+
+    def append_batch(self, request_ids, n_tokens):
+        reqs = np.ascontiguousarray(request_ids, dtype=np.int32)
+        ns = np.ascontiguousarray(n_tokens, dtype=np.int32)
+        last = np.zeros(reqs.size, np.int32)
+        rc = _lib.specdec_kv_append(self._h, _p(reqs), _p(ns), reqs.size, _p(last), None)
+        if rc not in (OK, ENOMEM):
+            check(rc)
+        return last.tolist()
+
+    def get_cache_for_batch(self, request_ids):
+        tabs, lens, _ = self.read()
+        out_t, out_l = [], []
+        for r in request_ids:
+            row = tabs[r]
+            out_t.append([int(x) for x in row[row >= 0]])
+            out_l.append(int(lens[r]))
+        return out_t, out_l
+
+    def free_request(self, request_id: int):
+        check(_lib.specdec_kv_free_request(self._h, request_id, None))
+
+    def share_prefix(self, new_request_id: int, source_request_id: int, shared_length: int):
+        check(_lib.specdec_kv_share_prefix(self._h, new_request_id, source_request_id, shared_length, None))
+
+    def free_merged_blocks(self, request_id: int, num_blocks_to_free: int):
+        check(_lib.specdec_kv_free_merged_blocks(self._h, request_id, num_blocks_to_free, None))
+
+    def evict_least_important_blocks(self, request_id: int, num_tokens_to_evict: int) -> bool:
+        ev = I(0)
+        check(_lib.specdec_kv_evict_tokens(self._h, request_id, num_tokens_to_evict, C.byref(ev), None))
+        return bool(ev.value)
+
+    def truncate(self, new_lengths):
+        nl = np.ascontiguousarray(new_lengths, dtype=np.int32)
+        check(_lib.specdec_kv_truncate(self._h, _p(nl), nl.size, None))
+
+    def get_utilization(self) -> float:
+        return float(_lib.specdec_kv_utilization(self._h, None))
+
+    def prefetch_kv_blocks(self, physical_block_indices):
+        """No-op on the GPU (kept for interface parity with paged_kv_cache.cpp:156-176)."""
+        return None
+
+    def read(self):
+        tabs = np.zeros((self.max_requests, self.max_bpr), np.int32)
+        lens = np.zeros(self.max_requests, np.int32)
+        refs = np.zeros(self.num_blocks, np.int32)
+        check(_lib.specdec_kv_read(self._h, _p(tabs), _p(lens), _p(refs), None))
+        return tabs, lens, refs
+
+
+# ======================================================================
+# Step engine
+# ======================================================================
+MODEL_SHAPES = {
+    "tiny": dict(hidden=512, layers=4, n_q_heads=8, n_kv_heads=2, head_dim=64, ffn=1376, vocab=32000, n_mtp_heads=3),
+    "llama3-8b": dict(hidden=4096, layers=32, n_q_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
+                      n_mtp_heads=3),
+    "14b": dict(hidden=5120, layers=48, n_q_heads=40, n_kv_heads=8, head_dim=128, ffn=13824, vocab=152064,
+                n_mtp_heads=3),
+}
+
+
+def model_config(shape: dict) -> ModelConfig:
+    return ModelConfig(shape["hidden"], shape["layers"], shape["n_q_heads"], shape["n_kv_heads"], shape["head_dim"],
+                       shape["ffn"], shape["vocab"], shape["n_mtp_heads"], 16, shape.get("rms_eps", 1e-5),
+                       shape.get("rope_theta", 10000.0))
+
+
+class Engine:
+    """One GPU's speculative-decoding engine (weights, paged KV, step graph)."""
+
+    def __init__(self, shape: dict, batch: int, draft_len: int = 4, max_ctx: int = 2048, temperature: float = 0.8,
+                 top_p: float = 1.0, seed: int = 0, tree_branching=None, tree_nodes: int = 0, use_graph: bool = True,
+                 device: int = 0, num_blocks: int = 0):
+        self.shape = dict(shape)
+        self.mc = model_config(shape)
+        br = list(tree_branching or [])
+        rc = RunConfig()
+        rc.batch = batch
+        rc.draft_len = draft_len
+        rc.tree_nodes = tree_nodes
+        for i, b in enumerate(br[:8]):
+            rc.tree_branching[i] = b
+        rc.tree_levels = len(br)
+        rc.max_ctx = max_ctx
+        rc.num_blocks = num_blocks
+        rc.use_graph = 1 if use_graph else 0
+        rc.sampling = sampling(temperature, top_p, seed, 0)
+        self.rc = rc
+        h = P()
+        check(_lib.specdec_engine_create(C.byref(self.mc), C.byref(rc), device, C.byref(h)))
+        self._h = h
+        self.batch = batch
+        self.rows = self.info("rows")
+        self.draft_len = self.info("draft_len")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.specdec_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self, key: str) -> int:
+        v = C.c_int64(0)
+        check(_lib.specdec_engine_info(self._h, key.encode(), C.byref(v)))
+        return int(v.value)
+
+    def init_weights(self, seed: int):
+        check(_lib.specdec_engine_init_weights(self._h, seed))
+
+    def prefill(self, prompts):
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        check(_lib.specdec_engine_prefill(self._h, _p(p), p.shape[1]))
+
+    def seed_state(self, ctx_len, seed: int):
+        c = np.ascontiguousarray(ctx_len, dtype=np.int32)
+        check(_lib.specdec_engine_seed_state(self._h, _p(c), seed))
+
+    def step(self):
+        check(_lib.specdec_engine_step(self._h))
+
+    def step_host(self):
+        acc = np.zeros(self.batch, np.int32)
+        out = np.zeros((self.batch, self.rows), np.int32)
+        check(_lib.specdec_engine_step_host(self._h, _p(acc), _p(out)))
+        return acc, out
+
+    def set_active(self, active):
+        a = np.ascontiguousarray(active, dtype=np.int32)
+        check(_lib.specdec_engine_set_active(self._h, _p(a)))
+
+    def stream(self) -> int:
+        return int(_lib.specdec_engine_stream(self._h) or 0)
+
+    def read(self, what: str, dtype, shape):
+        out = np.zeros(shape, dtype)
+        check(_lib.specdec_engine_read(self._h, what.encode(), _p(out), out.nbytes))
+        return out
+
+    def write(self, what: str, arr):
+        a = np.ascontiguousarray(arr)
+        check(_lib.specdec_engine_write(self._h, what.encode(), _p(a), a.nbytes))

@@ -1,0 +1,49 @@
+"""CPU checks of the C-ABI boundary: the library loads without a GPU and
+exports every function declared in include/specdec.h."""
+import os
+import re
+import subprocess
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "specdec.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = set()
+    for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", src):
+        name = m.group(1)
+        if name in ("if", "sizeof", "defined", "extern"):
+            continue
+        names.add(name)
+    return sorted(n for n in names if n.startswith(("specdec_", "sve2_", "rust_", "sme_")))
+
+
+def test_library_exports_every_declared_symbol():
+    import specdec
+
+    out = subprocess.run(["nm", "-D", "--defined-only", specdec.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+    assert len(declared_functions()) >= 40
+
+
+def test_python_binding_covers_header():
+    import specdec
+
+    assert set(declared_functions()) <= set(specdec.EXPORTED_SYMBOLS)
+    assert specdec.lib().specdec_abi_version() == 1
+
+
+def test_invalid_arguments_fail_loudly_without_gpu():
+    import ctypes as C
+
+    import specdec
+
+    rc = specdec.lib().specdec_w4a16_gemm(None, 4, 8, None, 8, 8, None, 8, 0, None, 0, None)
+    assert rc == specdec.EINVAL and "bad argument" in specdec.last_error()
+    h = C.c_void_p()
+    assert specdec.lib().specdec_kv_create(0, 16, 1, 1, C.byref(h)) == specdec.EINVAL
