@@ -1,0 +1,363 @@
+"""Benchmark of the speculative-decoding step (MTP draft -> verify forward ->
+acceptance -> KV commit/rollback) on B200.
+
+Default workload: Llama-3-8B-shape W4A16 chain speculative decoding, batch 32
+sequences per GPU, 2048-token contexts, draft length 4 (3 MTP heads),
+temperature 0.8, seed 1.  Weights are synthetic int4 (group 128, fp16 scales,
+N(0, 0.02) draws); the KV cache is seeded with random fp16 values (no prefill
+in the timed setup).  Sequences are sharded by request: every rank holds a
+full weight replica and its own sequences (weak scaling, no collective on
+the data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 8b|tree|14b|tiny]
+    python bench.py --impl reference ...   # CPU restatement on the host cores
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sme-llm-edge_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+CONFIGS = {
+    "8b": dict(shape="llama3-8b", batch=32, ctx=2048, draft_len=4, temperature=0.8, seed=1, tree=None),
+    "tree": dict(shape="llama3-8b", batch=16, ctx=4096, draft_len=0, temperature=1.0, seed=2, tree=[4, 4, 2, 2]),
+    "14b": dict(shape="14b", batch=64, ctx=8192, draft_len=4, temperature=0.8, seed=3, tree=None, ragged=(1024, 8192)),
+    "tiny": dict(shape="tiny", batch=1, ctx=512, draft_len=3, temperature=1.0, seed=0, tree=None),
+}
+METRIC = "accepted tokens/s, 8B-shape W4A16 MTP spec-decode, 1/2/4/8 B200; verify µs"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return world, rank, local, pg
+
+
+def reduce_max(pg, x: float, local: int) -> float:
+    if pg is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(pg, x: float, local: int) -> float:
+    if pg is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+    pg.all_reduce(t, op=pg.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(pg, local):
+    if pg is not None:
+        import torch
+
+        pg.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+
+def ctx_lengths(cfg, rank):
+    B = cfg["batch"]
+    if cfg.get("ragged"):
+        lo, hi = cfg["ragged"]
+        rng = np.random.default_rng(cfg["seed"] * 1000 + rank)
+        return rng.integers(lo, hi + 1, B).astype(np.int32)
+    return np.full(B, cfg["ctx"], np.int32)
+
+
+def workload_bytes_flops(shape, ctx, rows, weight_bytes):
+    """Algorithmic bytes of one verify step: W4 weights + scales of all layers and
+    lm_head read once, fp16 K/V of every context token of every sequence read once."""
+    kv_per_tok = shape["layers"] * shape["n_kv_heads"] * shape["head_dim"] * 2 * 2
+    kv_bytes = float(np.sum(ctx.astype(np.float64) + rows)) * kv_per_tok
+    H, F, V, L = shape["hidden"], shape["ffn"], shape["vocab"], shape["layers"]
+    qd, kd = shape["n_q_heads"] * shape["head_dim"], shape["n_kv_heads"] * shape["head_dim"]
+    params = L * (H * (qd + 2 * kd) + qd * H + 2 * H * F + F * H) + H * V
+    return weight_bytes + kv_bytes, kv_bytes, 2.0 * params
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline(cfg, budget_s=20.0, max_seqs=2):
+    """Oracle restatement of the step on the host cores (OpenMP, all threads):
+    a bounded sample of sequences through the full model, extrapolated per token."""
+    import oracle as O
+    import specdec as S
+
+    shape = S.MODEL_SHAPES[cfg["shape"]]
+    ocfg = dict(shape, block_size=16, rms_eps=1e-5, rope_theta=10000.0)
+    k = cfg["draft_len"] if not cfg["tree"] else 4
+    R = k + 1
+    ctx = int(cfg["ctx"])
+    t0 = time.time()
+    m = O.OracleModel(ocfg, seed=cfg["seed"], rope_max_pos=ctx + 80)
+    setup = time.time() - t0
+    H, V = shape["hidden"], shape["vocab"]
+    mbpr = (ctx + R + 15) // 16 + 1
+    rng = np.random.default_rng(7)
+    tokens_done, t_spent, seqs = 0, 0.0, 0
+    while seqs < max_seqs and t_spent < budget_s:
+        kv = O.OracleKV(shape["layers"], mbpr, shape["n_kv_heads"], 16, shape["head_dim"])
+        kv.pool[:] = O.f16_bits(rng.uniform(-1, 1, kv.pool.shape).astype(np.float32))
+        tables = np.arange(mbpr, dtype=np.int32)[None, :]
+        h0 = rng.standard_normal((1, H)).astype(np.float32)
+        pend = int(rng.integers(0, V))
+        t1 = time.time()
+        dl, drafts, _ = O.draft_chain(m, h0, k, cfg["temperature"], 1.0, cfg["seed"], 0)
+        toks = np.concatenate([[pend], drafts[0]]).astype(np.int32)
+        pos = np.arange(ctx, ctx + R, dtype=np.int32)
+        mask = np.array([(1 << (r + 1)) - 1 for r in range(R)], np.uint64)
+        lg, _ = O.forward(m, kv, tables, [ctx], toks, pos, pos, mask, 1, R, want_hidden=False)
+        acc, out = O.accept_chain(lg.reshape(1, R, V), dl, drafts, cfg["temperature"], 1.0, cfg["seed"], 0)
+        t_spent += time.time() - t1
+        tokens_done += int(acc[0]) + 1
+        seqs += 1
+    m.close()
+    value = tokens_done / t_spent
+    return {"value": value, "unit": "accepted tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{seqs} sequence-step(s) of the full {cfg['shape']} model ({R} verify rows, ctx {ctx}, "
+                      f"draft {k}); the CPU per-sequence cost is linear in sequences, so tokens/s is reported "
+                      f"as measured; OpenMP threads = {os.cpu_count()}; x86-64 scalar/auto-vectorised C, "
+                      f"ARM SVE2/SME unavailable; weight synthesis {setup:.1f}s not timed",
+            "seconds": round(t_spent, 2)}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cfg = dict(CONFIGS[args.config])
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(cfg, budget_s=15.0, max_seqs=1)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    v = float(np.mean(vals))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "accepted tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{cfg['shape']} W4A16 chain spec-decode step (CPU oracle restatement)",
+                       "batch_per_gpu": cfg["batch"], "ctx": cfg["ctx"], "draft_len": cfg["draft_len"]},
+            "cpu_baseline": {"kind": cb["kind"], "cores": cb["cores"], "sample": cb["sample"], "value": v,
+                             "unit": "accepted tokens/s"},
+            "e2e": {"value": v, "unit": "accepted tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ GPU arm
+def run_gpu(args, world, rank, local, pg):
+    import torch
+
+    import specdec as S
+
+    torch.cuda.set_device(local)
+    cfg = dict(CONFIGS[args.config])
+    shape = S.MODEL_SHAPES[cfg["shape"]]
+    ctx = ctx_lengths(cfg, rank)
+    extra = (args.warmup + 2 * args.steps + 8) * 65
+    eng = S.Engine(shape, batch=cfg["batch"], draft_len=cfg["draft_len"] or 4, max_ctx=int(ctx.max()) + extra,
+                   temperature=cfg["temperature"], top_p=1.0, seed=cfg["seed"] + 1000 * rank,
+                   tree_branching=cfg["tree"], tree_nodes=64 if cfg["tree"] else 0, use_graph=True, device=local)
+    eng.init_weights(cfg["seed"])
+    eng.seed_state(ctx, cfg["seed"] * 7 + rank)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=f"cuda:{local}")
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+    emitted0 = int(eng.read("emitted", np.int64, (1,))[0])
+    clocks = ClockSampler(local)
+    barrier(pg, local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        eng.step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier(pg, local)
+    ms = ev0.elapsed_time(ev1)
+    emitted1 = int(eng.read("emitted", np.int64, (1,))[0])
+    tokens = emitted1 - emitted0
+    ms_max = reduce_max(pg, ms, local)
+    tokens_all = reduce_sum(pg, tokens, local)
+    value = tokens_all / (ms_max / 1e3)
+    kps = eng.info("kernels_per_step")
+
+    # end to end through the host boundary: per step H2D of the control block,
+    # graph launch, D2H of accepted lengths + emitted tokens, host sync
+    B, R = cfg["batch"], eng.rows
+    eng.set_active(np.ones(B, np.int32))
+    e0 = int(eng.read("emitted", np.int64, (1,))[0])
+    barrier(pg, local)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        eng.step_host()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = reduce_max(pg, t0.elapsed_time(t1), local)
+    e_tok = reduce_sum(pg, int(eng.read("emitted", np.int64, (1,))[0]) - e0, local)
+    e2e = {"value": e_tok / (e_ms / 1e3), "unit": "accepted tokens/s", "h2d_bytes_per_step": 4 * B,
+           "d2h_bytes_per_step": 4 * B + 4 * B * R}
+
+    # per-kernel device time (eager steps with an event after every launch)
+    prof = eng.profile(3)
+    peaks, peak_src = load_peaks()
+    ctx_now = eng.read("lens", np.int32, (B,)) - 0
+    wbytes = eng.info("weight_bytes")
+    vbytes, kvbytes, flops_per_row = workload_bytes_flops(shape, ctx_now, R, wbytes)
+    M = B * R
+    gemm_flops = flops_per_row * M
+    verify_ms = prof["gemm_verify"] + prof["attention"] + prof["other"]
+    gemm_tflops = gemm_flops / (prof["gemm_verify"] * 1e-3) / 1e12
+    attn_gbs = kvbytes / (prof["attention"] * 1e-3) / 1e9
+    if prof["gemm_verify"] >= prof["attention"]:
+        roof = {"kernel": "w4a16_tc_kernel (verify projections + lm_head)", "bound": "tensor",
+                "achieved": round(gemm_tflops, 1), "peak": peaks.get("bf16_tflops_sustained", 1400.0),
+                "unit": "TFLOP/s", "peak_source": f"{peak_src} bf16 sustained"}
+    else:
+        roof = {"kernel": "attn_kernel (verify attention)", "bound": "hbm", "achieved": round(attn_gbs, 1),
+                "peak": peaks.get("hbm_gbs", 6650.0), "unit": "GB/s", "peak_source": f"{peak_src} hbm copy"}
+    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    roof["traffic"] = None
+    verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_bytes": vbytes,
+              "verify_hbm_frac_of_measured": round(vbytes / (verify_ms * 1e-3) / 1e9 / peaks.get("hbm_gbs", 6650.0), 4),
+              "verify_hbm_frac_of_8tbs": round(vbytes / (verify_ms * 1e-3) / 1e9 / 8000.0, 4),
+              "gemm_verify_tflops": round(gemm_tflops, 1), "attention_gbs": round(attn_gbs, 1),
+              "profile_ms_per_step": {k: round(v, 4) for k, v in prof.items()}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and cfg["shape"] != "14b" and not cfg["tree"]:
+        try:
+            cpu = cpu_baseline(cfg)
+        except Exception as exc:  # the CPU leg must not hide the GPU number
+            cpu = {"value": None, "error": str(exc)[:200]}
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "accepted tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp16 act, fp32 acc)",
+            "data": "synthetic (random int4 weights, seeded random fp16 KV)",
+            "config": {"workload": f"{cfg['shape']} W4A16 MTP spec-decode step", "batch_per_gpu": B,
+                       "global_batch": B * world, "ctx": int(cfg["ctx"]),
+                       "draft": f"tree {cfg['tree']} 64 nodes" if cfg["tree"] else f"chain {cfg['draft_len']}",
+                       "temperature": cfg["temperature"], "parallelism": f"request-sharded x{world}",
+                       "l2": "inputs larger than L2 (weights + KV ~ {:.1f} GB per step)".format(vbytes / 1e9)},
+            "mean_tokens_per_seq_step": round(tokens_all / (args.steps * B * world), 3),
+            "e2e": e2e, "gpu_launches": kps * args.steps, "clocks": clk, "roofline": roof, "verify": verify,
+            "cpu_baseline": cpu}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        # CPU arm: rank 0 alone measures; other ranks exit without work
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local, pg = dist_setup()
+    try:
+        run_gpu(args, world, rank, local, pg)
+    finally:
+        if pg is not None:
+            pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -246,6 +246,11 @@ void* specdec_engine_stream(specdec_engine* e);
 int specdec_engine_read(specdec_engine* e, const char* what, void* host, size_t bytes);
 int specdec_engine_write(specdec_engine* e, const char* what, const void* host, size_t bytes);
 int specdec_engine_info(specdec_engine* e, const char* what, int64_t* value);
+/* Runs `steps` eager steps with an event after every kernel and writes the
+ * mean device ms per step of: [0] verify GEMMs, [1] verify attention,
+ * [2] draft GEMMs, [3] sampling / acceptance, [4] other kernels, [5] whole
+ * step, [6] verify GEMM launches per step.  ms_out holds 7 floats. */
+int specdec_engine_profile(specdec_engine* e, int steps, float* ms_out);
 
 #ifdef __cplusplus
 }

@@ -387,11 +387,20 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
     a.QRP = p.QRP;
     a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)HD));
     const unsigned grid = (unsigned)(pairs * p.S);
+    // opt in once to the largest dynamic shared memory any plan uses
+    static bool attr128 = false, attr64 = false;
+    const int kMaxSmem = 227 * 1024;
     if (HD == 128) {
-        SD_CUDA(cudaFuncSetAttribute(attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+        if (!attr128) {
+            SD_CUDA(cudaFuncSetAttribute(attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+            attr128 = true;
+        }
         attn_kernel<128><<<grid, p.threads, p.smem, s>>>(a, p.MT, p.KG);
     } else {
-        SD_CUDA(cudaFuncSetAttribute(attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+        if (!attr64) {
+            SD_CUDA(cudaFuncSetAttribute(attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+            attr64 = true;
+        }
         attn_kernel<64><<<grid, p.threads, p.smem, s>>>(a, p.MT, p.KG);
     }
     SD_LAUNCH_CHECK("attn_kernel");

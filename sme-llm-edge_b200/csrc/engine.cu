@@ -430,7 +430,28 @@ struct specdec_engine {
     cudaGraphExec_t gexec = nullptr;
     int kernels_per_step = 0;
     std::vector<int> host_parent;
+    // profiler: an event after every launch; the interval since the previous
+    // event is that launch's device time (one stream, in-order execution)
+    bool prof_on = false;
+    int gemm_cat = 0;
+    std::vector<cudaEvent_t> prof_pool;
+    std::vector<int> prof_cat;
+    size_t prof_used = 0;
 };
+
+enum { CAT_GEMM_VERIFY = 0, CAT_ATTENTION = 1, CAT_GEMM_DRAFT = 2, CAT_ACCEPT = 3, CAT_OTHER = 4, CAT_N = 5 };
+
+static void prof_mark(specdec_engine* e, int cat) {
+    if (!e->prof_on) return;
+    if (e->prof_used == e->prof_pool.size()) {
+        cudaEvent_t ev;
+        cudaEventCreate(&ev);
+        e->prof_pool.push_back(ev);
+    }
+    cudaEventRecord(e->prof_pool[e->prof_used], e->stream);
+    e->prof_cat.push_back(cat);
+    ++e->prof_used;
+}
 
 namespace {
 
@@ -451,7 +472,9 @@ int gemm(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int
     int rc = make_x_tmap(&map, X, M, K, K, p.MT);
     if (rc) return rc;
     ++e->kernels_per_step;
-    return gemm_launch(map, p, w, M, N, Y, ldy, mode, e->gemm_ws, e->stream);
+    rc = gemm_launch(map, p, w, M, N, Y, ldy, mode, e->gemm_ws, e->stream);
+    prof_mark(e, e->gemm_cat);
+    return rc;
 }
 
 #define ENG_TRY(x)              \
@@ -459,11 +482,14 @@ int gemm(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int
         int _rc = (x);          \
         if (_rc) return _rc;    \
     } while (0)
-#define ENG_LAUNCH(name)                 \
+// one kernel launched: count it, check the launch, close its profiler interval
+#define ENG_LAUNCH_CAT(name, cat)        \
     do {                                 \
         ++e->kernels_per_step;           \
         SD_LAUNCH_CHECK(name);           \
+        prof_mark(e, cat);               \
     } while (0)
+#define ENG_LAUNCH(name) ENG_LAUNCH_CAT(name, CAT_OTHER)
 
 // Verify forward over Rrows rows per sequence (Rrows * B rows in total).
 int forward(specdec_engine* e, int Rrows, bool want_logits) {
@@ -471,6 +497,7 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
     const int B = e->B, M = B * Rrows, H = c.hidden, F = c.ffn, hd = c.head_dim;
     cudaStream_t s = e->stream;
     KVState& kvs = kv_state(e->kvm);
+    e->gemm_cat = CAT_GEMM_VERIFY;
     embed_kernel<<<M, 256, 0, s>>>(e->tokens, e->emb, H, c.vocab, e->x);
     ENG_LAUNCH("embed_kernel");
     for (int l = 0; l < c.layers; ++l) {
@@ -486,6 +513,7 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
         ENG_TRY(launch_attention(e->q16, kv_l, e->num_blocks, c.n_kv_heads, hd, kvs.tables, e->max_blocks, kvs.ctx,
                                  e->mask, B, Rrows, c.n_q_heads, e->att, e->attn_ws, e->attn_ws_bytes,
                                  e->rc.max_ctx, s));
+        prof_mark(e, CAT_ATTENTION);
         ENG_TRY(gemm(e, e->att, M, e->qd, w.o, H, e->x, H, 1));
         rmsnorm_kernel<<<M, 256, 0, s>>>(e->x, H, H, c.rms_eps, e->xn, H);
         ENG_LAUNCH("rmsnorm_kernel");
@@ -507,6 +535,7 @@ int draft_hidden_and_logits(specdec_engine* e, int levels) {
     const auto& c = e->mc;
     const int B = e->B, H = c.hidden;
     cudaStream_t s = e->stream;
+    e->gemm_cat = CAT_GEMM_DRAFT;
     for (int i = 0; i < levels; ++i) {
         const int head = i < c.n_mtp_heads ? i : c.n_mtp_heads - 1;
         const float* src = i == 0 ? e->h0 : e->dh + (size_t)(i - 1) * H;
@@ -528,14 +557,17 @@ int record_step(specdec_engine* e) {
     KVState& kvs = kv_state(e->kvm);
     const auto& sp = e->rc.sampling;
     e->kernels_per_step = 0;
+    prof_mark(e, CAT_OTHER);  // step start
     if (!e->tree) {
         const int k = e->k;
         ENG_TRY(draft_hidden_and_logits(e, k));
         ++e->kernels_per_step;
         ENG_TRY(launch_sample_rows_dev(e->dlogits, B * k, k, V, sp.temperature, sp.top_p, sp.seed, e->step, e->drafts,
                                        s));
+        prof_mark(e, CAT_ACCEPT);
         ++e->kernels_per_step;
         ENG_TRY(kv_append_uniform(e->kvm, B, R, s));
+        prof_mark(e, CAT_OTHER);
         build_chain_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->drafts, kvs.ctx, B, k, e->tokens,
                                                                    e->pos, e->slot);
         ENG_LAUNCH("build_chain_rows_kernel");
@@ -543,6 +575,7 @@ int record_step(specdec_engine* e) {
         e->kernels_per_step += 2;
         ENG_TRY(launch_accept_chain_dev(e->logits, e->dlogits, e->drafts, B, k, V, sp.temperature, sp.top_p, sp.seed,
                                         e->step, e->acc, e->out_tokens, e->acc_ws, s));
+        prof_mark(e, CAT_ACCEPT);
         commit_chain_kernel<<<B, 256, 0, s>>>(e->acc, e->out_tokens, R, kvs.ctx, e->active, e->x, c.hidden, e->new_len,
                                               e->pending, e->h0, e->emitted, e->step);
         ENG_LAUNCH("commit_chain_kernel");
@@ -551,8 +584,10 @@ int record_step(specdec_engine* e) {
         ENG_TRY(draft_hidden_and_logits(e, levels));
         ++e->kernels_per_step;
         ENG_TRY(launch_topk(e->dlogits, B * levels, V, e->topk_w, e->topk, s));
+        prof_mark(e, CAT_ACCEPT);
         ++e->kernels_per_step;
         ENG_TRY(kv_append_uniform(e->kvm, B, R, s));
+        prof_mark(e, CAT_OTHER);
         build_tree_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->topk, e->topk_w, levels, e->depth,
                                                                   e->rank, kvs.ctx, B, R, e->tokens, e->node_tokens,
                                                                   e->pos, e->slot);
@@ -561,6 +596,7 @@ int record_step(specdec_engine* e) {
         ++e->kernels_per_step;
         ENG_TRY(launch_accept_tree_dev(e->logits, e->node_tokens, e->parent, B, R, V, sp.temperature, sp.top_p,
                                        sp.seed, e->step, e->acc, e->path, e->out_tokens, s));
+        prof_mark(e, CAT_ACCEPT);
         const int per = 2 * c.n_kv_heads * c.head_dim;
         const size_t sm = sizeof(__half) * (size_t)levels * per;
         tree_compact_kernel<<<dim3(B, c.layers), 256, sm, s>>>(e->acc, e->path, R, kvs.ctx, kvs.tables, e->max_blocks,
@@ -572,6 +608,7 @@ int record_step(specdec_engine* e) {
     }
     ++e->kernels_per_step;
     ENG_TRY(kv_truncate_dev(e->kvm, e->new_len, B, s));
+    prof_mark(e, CAT_OTHER);
     return SPECDEC_OK;
 }
 
@@ -579,6 +616,7 @@ int record_step(specdec_engine* e) {
 
 extern "C" int specdec_engine_destroy(specdec_engine* e) {
     if (!e) return SPECDEC_OK;
+    for (cudaEvent_t ev : e->prof_pool) cudaEventDestroy(ev);
     if (e->gexec) cudaGraphExecDestroy(e->gexec);
     if (e->graph) cudaGraphDestroy(e->graph);
     if (e->kvm) specdec_kv_destroy(e->kvm);
@@ -979,6 +1017,38 @@ extern "C" int specdec_engine_write(specdec_engine* e, const char* what, const v
     SD_CHECK(bytes <= v.bytes, SPECDEC_EINVAL, "engine_write: too many bytes");
     SD_CUDA(cudaStreamSynchronize(e->stream));
     SD_CUDA(cudaMemcpy(const_cast<void*>(v.ptr), host, bytes, cudaMemcpyHostToDevice));
+    return SPECDEC_OK;
+}
+
+// Runs `steps` eager steps with an event after every launch and returns the
+// device time per step of each kernel category (ms): [0] verify GEMMs,
+// [1] attention, [2] draft GEMMs, [3] sampling / acceptance, [4] the rest,
+// [5] whole step.  Also returns the verify GEMM launch count per step in [6].
+extern "C" int specdec_engine_profile(specdec_engine* e, int steps, float* ms_out) {
+    SD_CHECK(e && ms_out && steps > 0, SPECDEC_EINVAL, "engine_profile: bad argument");
+    SD_CUDA(cudaStreamSynchronize(e->stream));
+    double acc[CAT_N + 2] = {0};
+    for (int it = 0; it < steps; ++it) {
+        e->prof_on = true;
+        e->prof_used = 0;
+        e->prof_cat.clear();
+        int rc = record_step(e);
+        e->prof_on = false;
+        if (rc) return rc;
+        SD_CUDA(cudaStreamSynchronize(e->stream));
+        int ngemm = 0;
+        for (size_t i = 1; i < e->prof_used; ++i) {
+            float ms = 0.f;
+            SD_CUDA(cudaEventElapsedTime(&ms, e->prof_pool[i - 1], e->prof_pool[i]));
+            acc[e->prof_cat[i]] += ms;
+            ngemm += e->prof_cat[i] == CAT_GEMM_VERIFY;
+        }
+        float total = 0.f;
+        SD_CUDA(cudaEventElapsedTime(&total, e->prof_pool[0], e->prof_pool[e->prof_used - 1]));
+        acc[CAT_N] += total;
+        acc[CAT_N + 1] += ngemm;
+    }
+    for (int i = 0; i < CAT_N + 2; ++i) ms_out[i] = (float)(acc[i] / steps);
     return SPECDEC_OK;
 }
 

@@ -108,6 +108,7 @@ _SIGS = {
     "specdec_engine_read": (I, [P, C.c_char_p, P, SZ]),
     "specdec_engine_write": (I, [P, C.c_char_p, P, SZ]),
     "specdec_engine_info": (I, [P, C.c_char_p, C.POINTER(C.c_int64)]),
+    "specdec_engine_profile": (I, [P, I, P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(_lib, _name)
@@ -402,6 +403,13 @@ class Engine:
         out = np.zeros(shape, dtype)
         check(_lib.specdec_engine_read(self._h, what.encode(), _p(out), out.nbytes))
         return out
+
+    def profile(self, steps: int) -> dict:
+        """Mean device ms per step by kernel category (eager steps, event after every launch)."""
+        out = np.zeros(7, np.float32)
+        check(_lib.specdec_engine_profile(self._h, steps, _p(out)))
+        keys = ("gemm_verify", "attention", "gemm_draft", "accept", "other", "step", "verify_gemm_launches")
+        return {k: float(v) for k, v in zip(keys, out)}
 
     def write(self, what: str, arr):
         a = np.ascontiguousarray(arr)

@@ -64,7 +64,8 @@ def test_accept_tree_bit_exact(cuda_device, T):
 
     acc, path, out = _i32(B), _i32((B, R)), _i32((B, R))
     sp = S.sampling(T, 1.0, 55, 3)
-    S.check(S.lib().specdec_accept_tree(ptr(dev(tgt)), ptr(dev(tok)), ptr(dev(parent)), B, R, V, C.byref(sp),
+    d_tgt, d_tok, d_par = dev(tgt), dev(tok), dev(parent)  # keep the device buffers alive across the launch
+    S.check(S.lib().specdec_accept_tree(ptr(d_tgt), ptr(d_tok), ptr(d_par), B, R, V, C.byref(sp),
                                         ptr(acc), ptr(path), ptr(out), None, 0, stream_ptr()))
     sync()
     assert acc.cpu().numpy().tolist() == acc_o.tolist()
@@ -80,7 +81,8 @@ def test_sample_rows_bit_exact(cuda_device, T, tp):
     ref = O.sample_rows(z, k, T, tp, 99, 5)
     out = _i32(rows)
     sp = S.sampling(T, tp, 99, 5)
-    S.check(S.lib().specdec_sample_rows(ptr(dev(z)), rows, k, V, C.byref(sp), ptr(out), None, 0, stream_ptr()))
+    d_z = dev(z)
+    S.check(S.lib().specdec_sample_rows(ptr(d_z), rows, k, V, C.byref(sp), ptr(out), None, 0, stream_ptr()))
     sync()
     assert out.cpu().numpy().tolist() == ref.tolist()
 
@@ -201,7 +203,8 @@ def _gemm_case(M, N, K, seed=0):
     nbytes = S.lib().specdec_w4_tiled_bytes(N, K)
     assert nbytes == tiled_ref.size
     d_tiled = zeros(nbytes, torch.uint8)
-    S.check(S.lib().specdec_w4_tile(ptr(dev(packed)), ptr(dev(scales)), N, K, ptr(d_tiled), stream_ptr()))
+    d_packed, d_scales = dev(packed), dev(scales)
+    S.check(S.lib().specdec_w4_tile(ptr(d_packed), ptr(d_scales), N, K, ptr(d_tiled), stream_ptr()))
     sync()
     np.testing.assert_array_equal(d_tiled.cpu().numpy(), tiled_ref)
     return packed, scales, X16, d_tiled
@@ -229,7 +232,6 @@ def test_w4a16_gemm_tcgen05_matches_oracle(cuda_device, M, N, K):
     sync()
     np.testing.assert_array_equal(Y2.cpu().numpy(), y)
     np.testing.assert_allclose(Y.cpu().numpy(), 2 * y, rtol=1e-6, atol=1e-6)
-    st = C.c_int64(0)
 
 
 def test_w4a16_simt_matches_tcgen05(cuda_device):
@@ -278,8 +280,9 @@ def test_attention_matches_oracle(cuda_device, B, R, Hq, Hkv, hd, ctx_max, tree)
     ws = zeros(ws_b, torch.uint8)
     out = zeros((B * R, Hq, hd), torch.float16)
     d_kv = dev(kv.pool[0])
-    S.check(S.lib().specdec_attention(ptr(dev(q)), ptr(d_kv), nblk, Hkv, hd, ptr(dev(tables)), max_blocks,
-                                      ptr(dev(ctx)), ptr(dev(mask)), B, R, Hq, ptr(out), ptr(ws), ws_b, stream_ptr()))
+    d_q, d_tab, d_ctx, d_mask = dev(q), dev(tables), dev(ctx), dev(mask)
+    S.check(S.lib().specdec_attention(ptr(d_q), ptr(d_kv), nblk, Hkv, hd, ptr(d_tab), max_blocks,
+                                      ptr(d_ctx), ptr(d_mask), B, R, Hq, ptr(out), ptr(ws), ws_b, stream_ptr()))
     sync()
     got = out.cpu().numpy().astype(np.float32)
     np.testing.assert_allclose(got, O.f16_vals(out_o), rtol=1e-2, atol=1e-2)
