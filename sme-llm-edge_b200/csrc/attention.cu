@@ -348,10 +348,14 @@ static AttnPlan plan_attention(int B, int R, int G, int Hkv, int HD, int max_ctx
 using namespace specdec;
 
 namespace specdec {
+// Workspace: split tickets first (fixed offset, so plans with different row
+// counts sharing one workspace never overlap each other's tickets), then the
+// partial O and (m, l) of every split.
+static size_t ticket_bytes(size_t pairs) { return (pairs * 4 + 255) / 256 * 256; }
 size_t attention_workspace(int B, int R, int Hq, int Hkv, int HD, int max_ctx) {
     AttnPlan p = plan_attention(B, R, Hq / Hkv, Hkv, HD, max_ctx);
     const size_t pairs = (size_t)B * Hkv;
-    return pairs * p.S * p.QRP * HD * 4 + pairs * p.S * p.QRP * 2 * 4 + pairs * 4 + 256;
+    return ticket_bytes(pairs) + pairs * p.S * p.QRP * HD * 4 + pairs * p.S * p.QRP * 2 * 4;
 }
 
 int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, int Hkv, int HD, const int32_t* tables,
@@ -380,25 +384,35 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
     a.out = out;
     const size_t pairs = (size_t)B * Hkv;
     char* w = reinterpret_cast<char*>(ws);
-    a.part_o = reinterpret_cast<float*>(w);
-    a.part_ml = reinterpret_cast<float*>(w + pairs * p.S * p.QRP * HD * 4);
-    a.tickets = reinterpret_cast<int*>(w + pairs * p.S * p.QRP * HD * 4 + pairs * p.S * p.QRP * 2 * 4);
+    a.tickets = reinterpret_cast<int*>(w);
+    a.part_o = reinterpret_cast<float*>(w + ticket_bytes(pairs));
+    a.part_ml = reinterpret_cast<float*>(w + ticket_bytes(pairs) + pairs * p.S * p.QRP * HD * 4);
     a.S = p.S;
     a.QRP = p.QRP;
     a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)HD));
     const unsigned grid = (unsigned)(pairs * p.S);
-    // opt in once to the largest dynamic shared memory any plan uses
+    // opt in once to the largest dynamic shared memory the device allows next
+    // to the kernel's static shared memory
     static bool attr128 = false, attr64 = false;
-    const int kMaxSmem = 227 * 1024;
+    auto opt_in = [](const void* fn) -> cudaError_t {
+        int dev = 0, optin = 0;
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, fn);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+        return e;
+    };
     if (HD == 128) {
         if (!attr128) {
-            SD_CUDA(cudaFuncSetAttribute(attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+            SD_CUDA(opt_in(reinterpret_cast<const void*>(attn_kernel<128>)));
             attr128 = true;
         }
         attn_kernel<128><<<grid, p.threads, p.smem, s>>>(a, p.MT, p.KG);
     } else {
         if (!attr64) {
-            SD_CUDA(cudaFuncSetAttribute(attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+            SD_CUDA(opt_in(reinterpret_cast<const void*>(attn_kernel<64>)));
             attr64 = true;
         }
         attn_kernel<64><<<grid, p.threads, p.smem, s>>>(a, p.MT, p.KG);

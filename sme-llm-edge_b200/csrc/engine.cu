@@ -778,6 +778,7 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
     cudaMemset(e->attn_ws, 0, e->attn_ws_bytes);
     if ((rcode = dalloc(e, reinterpret_cast<char**>(&e->acc_ws), (size_t)e->B * (2 * e->R + 1) * 32))) return fail(rcode);
     if (cudaMallocHost(&e->h_ctrl, sizeof(int32_t) * (e->B + 8)) != cudaSuccess) return fail(SPECDEC_ENOMEM);
+    for (int b = 0; b < e->B; ++b) e->h_ctrl[b] = 1;  // every sequence starts active
     if (cudaMallocHost(&e->h_out, sizeof(int32_t) * (e->B * (e->R + 1) + 8)) != cudaSuccess) return fail(SPECDEC_ENOMEM);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(cuda_status(cudaGetLastError(), "engine_create"));
     *out = e;

@@ -9,8 +9,9 @@
 //   deq(w) = fp16((u4 - 8) * scale)   (offset-binary nibbles as written by the
 //            reference packer, server/sve_packing.cpp:8-30)
 //
-// CTA = 14 warps, warp-specialised:
-//   warp 0      bulk-copy producer (int4 units) + TMA producer (X tiles)
+// CTA = 15 warps, warp-specialised:
+//   warp 0      bulk-copy producer of the int4 units (runs 4 k-steps ahead)
+//   warp 14     TMA producer of the activation tiles
 //   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, fp32 store / add
 //   warps 6-13  dequant: int4 -> fp16 in registers, stored in the K-major
@@ -30,15 +31,17 @@ namespace specdec {
 
 constexpr int kUnitBytes = 8448;   // 8192 nibble bytes + 128 fp16 scales
 constexpr int kRawStageBytes = 2 * kUnitBytes;
-constexpr int kRawStages = 4;
-constexpr int kGemmThreads = 448;
+constexpr int kGemmThreads = 480;
 constexpr int kASlotBytes = 32768;  // 256 rows x 64 k fp16
 constexpr int kSmemBudget = 227 * 1024;
 
+// int4 prefetch depth (k128 items): deeper for small token tiles, whose
+// A/B slots are cheap and whose step is bound by the weight stream.
+__host__ __device__ constexpr int raw_stages_for(int MT) { return MT <= 64 ? 6 : 4; }
 __host__ __device__ constexpr int ab_stages_for(int MT) {
-    return (kSmemBudget - kRawStages * kRawStageBytes - 2048 - 1024) / (kASlotBytes + MT * 128) > 4
+    return (kSmemBudget - raw_stages_for(MT) * kRawStageBytes - 2048 - 1024) / (kASlotBytes + MT * 128) > 4
                ? 4
-               : (kSmemBudget - kRawStages * kRawStageBytes - 2048 - 1024) / (kASlotBytes + MT * 128);
+               : (kSmemBudget - raw_stages_for(MT) * kRawStageBytes - 2048 - 1024) / (kASlotBytes + MT * 128);
 }
 __host__ __device__ constexpr int tmem_cols_for(int MT) {
     return 2 * MT <= 32 ? 32 : (2 * MT <= 64 ? 64 : (2 * MT <= 128 ? 128 : (2 * MT <= 256 ? 256 : 512)));
@@ -46,7 +49,7 @@ __host__ __device__ constexpr int tmem_cols_for(int MT) {
 template <int MT>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
     return 1024 /*align slack*/ + (size_t)ab_stages_for(MT) * (kASlotBytes + MT * 128) +
-           (size_t)kRawStages * kRawStageBytes + 2048;
+           (size_t)raw_stages_for(MT) * kRawStageBytes + 2048;
 }
 
 // ------------------------------------------------------------ PTX helpers
@@ -73,18 +76,31 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that lets the thread sleep (up to hint_ns) until the phase completes,
+// so waiting warps do not take issue slots from the working ones.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t a, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t gtimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait: ~2 s of wall time at most.
+// Bounded wait: ~2 s of wall time at most.  The first probe is a plain
+// try_wait; after that the thread sleeps in the barrier between probes.
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
-    for (int i = 0; i < 256; ++i)
-        if (mbar_try(a, parity)) return true;
+    if (mbar_try(a, parity)) return true;
     const uint64_t t0 = gtimer();
     for (;;) {
-        if (mbar_try(a, parity)) return true;
+        if (mbar_try_sleep(a, parity, 20000u)) return true;
         if (gtimer() - t0 > 2000000000ull) return false;
     }
 }
@@ -170,6 +186,7 @@ template <int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, GemmArgs args) {
     constexpr int AB = ab_stages_for(MT);
+    constexpr int RS = raw_stages_for(MT);
     constexpr int BSLOT = MT * 128;
     constexpr int TMEM_COLS = tmem_cols_for(MT);
     constexpr uint32_t IDESC = idesc_f16(128, MT);
@@ -179,10 +196,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     unsigned char* sA = base;                                   // AB x 32 KB
     unsigned char* sB = sA + AB * kASlotBytes;                  // AB x MT*128
     unsigned char* sRaw = sB + AB * BSLOT;                      // 4 x 16896
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + kRawStages * kRawStageBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + RS * kRawStageBytes);
     uint64_t* raw_full = bars;
-    uint64_t* raw_empty = bars + kRawStages;
-    uint64_t* a_full = bars + 2 * kRawStages;
+    uint64_t* raw_empty = bars + RS;
+    uint64_t* a_full = bars + 2 * RS;
     uint64_t* b_full = a_full + AB;
     uint64_t* ab_empty = b_full + AB;
     uint64_t* acc_full = ab_empty + AB;
@@ -195,7 +212,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int g1 = (int)(((long long)(blockIdx.x + 1) * args.total) / gridDim.x);
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kRawStages; ++i) {
+        for (int i = 0; i < RS; ++i) {
             mbar_init(s_addr(&raw_full[i]), 1);
             mbar_init(s_addr(&raw_empty[i]), 8);
         }
@@ -225,12 +242,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // ------------------------------------------------ producer
         if (lane == 0 && g0 < g1) {
             int r_it = 0, ab_it = 0;
+            // int4 units only: runs up to RS items ahead of the dequant warps
             bool ok = true;
             for (int g = g0; g < g1 && ok; ++g) {
                 const int tile = g / KG, kg = g % KG;
-                const int n_tile = tile / args.m_tiles, m_tile = tile % args.m_tiles;
-                const int rs = r_it % kRawStages;
-                if (r_it >= kRawStages) ok = mbar_wait(s_addr(&raw_empty[rs]), ((r_it / kRawStages) - 1) & 1);
+                const int n_tile = tile / args.m_tiles;
+                const int rs = r_it % RS;
+                if (r_it >= RS) ok = mbar_wait(s_addr(&raw_empty[rs]), ((r_it / RS) - 1) & 1);
                 if (!ok || *abort_flag) break;
                 const uint32_t rf = s_addr(&raw_full[rs]);
                 mbar_expect_tx(rf, kRawStageBytes);
@@ -239,10 +257,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     bulk_g2s(s_addr(sRaw + rs * kRawStageBytes + u * kUnitBytes), src, kUnitBytes, rf);
                 }
                 ++r_it;
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                record_timeout(args.status, 1);
+            }
+            // drain: every copy issued above completes on its barrier before the CTA exits
+            if (r_it > 0) (void)mbar_wait(s_addr(&raw_full[(r_it - 1) % RS]), ((r_it - 1) / RS) & 1);
+        }
+    } else if (warp == 14) {
+        // ------------------------------------------------ activation (B operand) producer
+        if (lane == 0 && g0 < g1) {
+            int ab_it = 0;
+            bool ok = true;
+            for (int g = g0; g < g1 && ok; ++g) {
+                const int tile = g / KG, kg = g % KG;
+                const int m_tile = tile % args.m_tiles;
                 for (int hk = 0; hk < 2; ++hk) {
                     const int s = ab_it % AB;
                     if (ab_it >= AB) ok = mbar_wait(s_addr(&ab_empty[s]), ((ab_it / AB) - 1) & 1);
-                    if (!ok || *abort_flag) break;
+                    if (!ok || *abort_flag) {
+                        ok = false;
+                        break;
+                    }
                     const uint32_t bf = s_addr(&b_full[s]);
                     mbar_expect_tx(bf, BSLOT);
                     tma_load_2d(s_addr(sB + s * BSLOT), &tmap_x, kg * 128 + hk * 64, m_tile * MT, bf);
@@ -251,10 +288,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             if (!ok) {
                 *abort_flag = 1;
-                record_timeout(args.status, 1);
+                record_timeout(args.status, 5);
             }
-            // drain: every copy issued above completes on its barrier before the CTA exits
-            if (r_it > 0) (void)mbar_wait(s_addr(&raw_full[(r_it - 1) % kRawStages]), ((r_it - 1) / kRawStages) & 1);
             if (ab_it > 0) (void)mbar_wait(s_addr(&b_full[(ab_it - 1) % AB]), ((ab_it - 1) / AB) & 1);
         }
     } else if (warp == 1) {
@@ -362,23 +397,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         uint32_t v[16];
                         tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
                         tc_wait_ld();
+                        float acc[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            float val = 0.f;
-                            for (int p = c_lo; p <= c_hi; ++p) {
-                                if (p == (int)blockIdx.x) {
-                                    val += __uint_as_float(v[j]);
-                                } else {
-                                    const int ps = (((long long)p * args.total) / gridDim.x) / KG == tile ? 0 : 1;
-                                    val += __ldcg(args.part + ((size_t)p * 2 + ps) * slot_floats +
-                                                  ((size_t)q * MT + c * 16 + j) * 128 + quad * 32 + lane);
-                                }
+                        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+                        // parts in CTA order (deterministic sum); the first part of
+                        // CTA p is its slot 0, a later tile of p its slot 1
+                        const size_t off = ((size_t)q * MT + c * 16) * 128 + quad * 32 + lane;
+                        for (int p = c_lo; p <= c_hi; ++p) {
+                            if (p == (int)blockIdx.x) {
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(v[j]);
+                            } else {
+                                const int ps = ((((long long)p * args.total) / gridDim.x) / KG == tile) ? 0 : 1;
+                                const float* src = args.part + ((size_t)p * 2 + ps) * slot_floats + off;
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) acc[j] += __ldcg(src + (size_t)j * 128);
                             }
-                            const int m = m_tile * MT + c * 16 + j;
-                            if (n < args.N && m < args.M) {
-                                float* y = args.Y + (size_t)m * args.ldy + n;
-                                if (args.mode) *y += val;
-                                else *y = val;
+                        }
+                        if (n < args.N) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const int m = m_tile * MT + c * 16 + j;
+                                if (m < args.M) {
+                                    float* y = args.Y + (size_t)m * args.ldy + n;
+                                    if (args.mode) *y += acc[j];
+                                    else *y = acc[j];
+                                }
                             }
                         }
                     }
@@ -396,13 +440,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int r_it = 0, ab_it = 0;
         bool ok = true;
         for (int g = g0; g < g1 && ok; ++g) {
-            const int rs = r_it % kRawStages;
-            ok = mbar_wait(s_addr(&raw_full[rs]), (r_it / kRawStages) & 1);
+            const int rs = r_it % RS;
+            ok = mbar_wait(s_addr(&raw_full[rs]), (r_it / RS) & 1);
             if (!ok || *abort_flag) {
                 ok = false;
                 break;
             }
             const unsigned char* raw = sRaw + rs * kRawStageBytes;
+            // this thread's row r and its two units' group scales are fixed for the item
+            const int r = dt & 127;
+            const __half2 s2u0 = __half2half2(*reinterpret_cast<const __half*>(raw + 8192 + r * 2));
+            const __half2 s2u1 = __half2half2(*reinterpret_cast<const __half*>(raw + kUnitBytes + 8192 + r * 2));
+            const __half2 bias = __float2half2_rn(1032.0f);
             for (int hk = 0; hk < 2; ++hk) {
                 const int s = ab_it % AB;
                 if (ab_it >= AB) ok = mbar_wait(s_addr(&ab_empty[s]), ((ab_it / AB) - 1) & 1);
@@ -411,22 +460,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     break;
                 }
                 unsigned char* a_slot = sA + s * kASlotBytes;
+                uint32_t wv[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {  // all loads first: 8 independent shared loads in flight
+                    const int u = i >> 2, kcl = 2 * (i & 3) + (dt >> 7);
+                    wv[i] = *reinterpret_cast<const uint32_t*>(raw + u * kUnitBytes + (((hk * 8 + kcl) * 128 + r) << 2));
+                }
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int idx = i * 256 + dt;
-                    const int u = idx >> 10, rem = idx & 1023;
-                    const int kcl = rem >> 7, r = rem & 127;
-                    const unsigned char* unit = raw + u * kUnitBytes;
-                    const uint32_t w = *reinterpret_cast<const uint32_t*>(unit + (((hk * 8 + kcl) * 128 + r) << 2));
-                    const __half sc = *reinterpret_cast<const __half*>(unit + 8192 + r * 2);
-                    const __half2 s2 = __half2half2(sc);
-                    const __half2 bias = __float2half2_rn(1032.0f);
+                    const int u = i >> 2, kcl = 2 * (i & 3) + (dt >> 7);
+                    const __half2 s2 = u ? s2u1 : s2u0;
                     uint32_t outw[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const uint32_t t = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t t = ((wv[i] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
                         __half2 hv = *reinterpret_cast<const __half2*>(&t);
-                        hv = __hmul2(__hsub2(hv, bias), s2);
+                        hv = __hmul2(__hsub2(hv, bias), s2);  // exact (u - 8), then one rounding of (u - 8) * s
                         outw[j] = *reinterpret_cast<uint32_t*>(&hv);
                     }
                     unsigned char* dst = a_slot + u * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + ((kcl ^ (r & 7)) << 4);
@@ -631,25 +680,20 @@ GemmPlan plan_gemm(int M, int N, int K) {
     return p;
 }
 
-// Workspace of one launch: parked partial tiles + per-tile tickets.  The
-// tickets must be zero before the first launch; every launch leaves them zero.
+// Workspace of one launch: per-tile tickets at a fixed offset (the front, so
+// that launches with different token tiles sharing one workspace never
+// overlap each other's tickets), then the parked partial tiles.  The tickets
+// must be zero before the first launch; every launch leaves them zero.
+constexpr size_t kTicketBytes = 1 << 18;  // 65536 tiles
 size_t gemm_workspace_bytes(const GemmPlan& p) {
-    return (size_t)p.grid * 2 * 2 * p.MT * 128 * sizeof(float) + (size_t)p.m_tiles * p.n_tiles * sizeof(int) + 256;
+    return kTicketBytes + (size_t)p.grid * 2 * 2 * p.MT * 128 * sizeof(float);
 }
 size_t gemm_workspace_bound(int max_m, int max_n, int max_k) {
-    size_t worst = 0;
-    for (int m = 1; m <= max_m; m = (m < 16 ? 16 : m * 2)) {
-        GemmPlan p = plan_gemm(m, max_n, max_k);
-        size_t b = gemm_workspace_bytes(p);
-        if (b > worst) worst = b;
-    }
-    GemmPlan p = plan_gemm(max_m, max_n, max_k);
-    size_t b = gemm_workspace_bytes(p);
-    if (b > worst) worst = b;
-    // tile counts grow with N; the partial area only with grid and MT (<= 256)
-    const size_t bound = (size_t)num_sms() * 2 * 2 * 256 * 128 * sizeof(float) +
-                         (size_t)((max_m + 15) / 16) * ((max_n + 255) / 256) * sizeof(int) + 256;
-    return worst > bound ? worst : bound;
+    (void)max_m;
+    (void)max_n;
+    (void)max_k;
+    // the partial area depends only on the grid and the token tile (<= 256)
+    return kTicketBytes + (size_t)num_sms() * 2 * 2 * 256 * 128 * sizeof(float);
 }
 
 // Launch with a prebuilt tensor map (built for this plan's MT).
@@ -666,8 +710,12 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
     a.Y = Y;
     a.ldy = ldy;
     a.mode = mode;
-    a.part = reinterpret_cast<float*>(ws);
-    a.tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (size_t)p.grid * 2 * 2 * p.MT * 128 * sizeof(float));
+    if ((size_t)p.m_tiles * p.n_tiles * sizeof(int) > kTicketBytes) {
+        set_error("w4a16_gemm: too many output tiles for the ticket area");
+        return SPECDEC_EINVAL;
+    }
+    a.tickets = reinterpret_cast<int*>(ws);
+    a.part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kTicketBytes);
     a.status = device_status_ptr();
     switch (p.MT) {
         case 16: return launch_tc<16>(map, a, p.grid, s);
@@ -733,8 +781,7 @@ extern "C" int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void*
     int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
     if (rc) return rc;
     // tickets must start at zero; clear them (the kernel leaves them zero again)
-    SD_CUDA(cudaMemsetAsync(reinterpret_cast<char*>(workspace) + (size_t)p.grid * 2 * 2 * p.MT * 128 * sizeof(float), 0,
-                            (size_t)p.m_tiles * p.n_tiles * sizeof(int), s));
+    SD_CUDA(cudaMemsetAsync(workspace, 0, (size_t)p.m_tiles * p.n_tiles * sizeof(int), s));
     return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, workspace, s);
 }
 

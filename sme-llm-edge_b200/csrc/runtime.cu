@@ -12,6 +12,7 @@ void set_error(const std::string& msg) { g_last_error = msg; }
 
 int cuda_status(cudaError_t e, const char* what) {
     set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    (void)cudaGetLastError();  // clear a non-sticky error so it does not resurface at the next launch check
     return e == cudaErrorMemoryAllocation ? SPECDEC_ENOMEM : SPECDEC_ECUDA;
 }
 

@@ -252,7 +252,8 @@ def test_w4a16_simt_matches_tcgen05(cuda_device):
 # ---------------------------------------------------------------- attention
 @pytest.mark.parametrize("B,R,Hq,Hkv,hd,ctx_max,tree", [(2, 5, 8, 2, 64, 100, False), (3, 5, 32, 8, 128, 700, False),
                                                         (2, 64, 8, 2, 64, 300, True), (1, 64, 32, 8, 128, 200, True),
-                                                        (4, 1, 8, 8, 128, 50, False), (2, 40, 4, 1, 64, 0, False)])
+                                                        (4, 1, 8, 8, 128, 50, False), (2, 40, 4, 1, 64, 0, False),
+                                                        (1, 4, 8, 2, 64, 511, False), (1, 5, 32, 8, 128, 2100, False)])
 def test_attention_matches_oracle(cuda_device, B, R, Hq, Hkv, hd, ctx_max, tree):
     import torch
 
@@ -286,3 +287,22 @@ def test_attention_matches_oracle(cuda_device, B, R, Hq, Hkv, hd, ctx_max, tree)
     sync()
     got = out.cpu().numpy().astype(np.float32)
     np.testing.assert_allclose(got, O.f16_vals(out_o), rtol=1e-2, atol=1e-2)
+
+
+def test_w4a16_shared_workspace_across_token_tiles(cuda_device):
+    """One workspace reused by GEMMs with different token tiles (as the engine
+    does): every launch must still finish every split tile."""
+    import torch
+
+    shapes = [(64, 768, 512), (4, 768, 512), (160, 768, 512), (16, 768, 512), (64, 768, 512), (300, 768, 512)]
+    packed, scales, _, d_tiled = _gemm_case(8, 768, 512)
+    ws_b = max(S.lib().specdec_w4a16_workspace_bytes(M, N, K) for M, N, K in shapes)
+    ws = zeros(ws_b, torch.uint8)
+    for M, N, K in shapes:
+        X16 = O.f16_bits(np.random.default_rng(M).standard_normal((M, K)) * 0.5)
+        dX = dev(X16)
+        Y = zeros((M, N), torch.float32)
+        S.check(S.lib().specdec_w4a16_gemm(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y), N, 0, ptr(ws), ws_b,
+                                           stream_ptr()))
+        sync()
+        np.testing.assert_allclose(Y.cpu().numpy(), O.w4a16_gemm(X16, packed, scales), rtol=2e-3, atol=2e-3)
