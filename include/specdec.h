@@ -118,6 +118,21 @@ int specdec_accept_chain(const float* target, const float* draft, const int32_t*
                          const specdec_sampling* sp, int32_t* accepted_len, int32_t* out_tokens, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Same chain acceptance as specdec_accept_chain, for callers that may not
+ * allocate device memory when they accept drafts (a serving loop that reserves
+ * its whole memory budget up front, or a host program that owns the GPU
+ * allocator).  No counterpart exists in the reference.  The row statistics
+ * live in a fixed array compiled into the library: 8192 rows of 32 bytes
+ * (256 KB on every GPU that loads the library, held until exit), so
+ * B*(k+1) + B*k must not exceed 8192 (B*(k+1) when greedy); larger calls fail
+ * with SPECDEC_EINVAL.  The first call on a device looks up the array's
+ * address with that device current and should come before any stream
+ * capture.  All calls share the array: calls whose kernels overlap on the
+ * GPU race.  No cudaMalloc, cudaFree or allocating library routine is used. */
+int specdec_accept_chain_noalloc(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
+                                 const specdec_sampling* sp, int32_t* accepted_len, int32_t* out_tokens,
+                                 void* stream);
+
 /* Tree acceptance over R BFS-ordered nodes (node 0 = root / pending token).
  * target [B, R, V]; node_tokens [B, R]; parent [R] (device).  Outputs
  * accepted_len [B], path_nodes [B, R], out_tokens [B, R]. */

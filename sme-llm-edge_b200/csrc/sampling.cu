@@ -10,6 +10,7 @@
 // cross-multiplications, so the result does not depend on reduction order.
 #include <cfloat>
 #include <climits>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -724,6 +725,78 @@ extern "C" int specdec_accept_chain(const float* target, const float* draft, con
     RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
     DevRowStats* st = reinterpret_cast<DevRowStats*>(workspace);
     row_stats_kernel<<<rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
+    SD_LAUNCH_CHECK("row_stats_kernel");
+    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, sp->seed,
+                                                  nullptr, sp->step, st, B, accepted_len, out_tokens);
+    SD_LAUNCH_CHECK("accept_chain_kernel");
+    return SPECDEC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Chain acceptance without any allocation.
+//
+// Some callers cannot allocate device memory at the point where they accept
+// drafts: a serving loop that reserves its whole device-memory budget at
+// start-up and must not grow it per step, or a host program that owns the
+// GPU allocator and forbids plug-ins from calling it.  For them this variant
+// keeps the per-row statistics in a fixed array compiled into the library
+// (kStaticAcceptRows rows of 32 bytes, 256 KB on every GPU that loads the
+// library, held until the process exits) instead of a caller workspace.
+//
+// The array's device address is looked up once per device, on the first call
+// made with that device current (cudaGetSymbolAddress); that first call should
+// come before any stream capture.  Every call shares the array: two calls
+// whose kernels overlap on the GPU (different streams, no ordering between
+// them) race on it.  Nothing in it needs to start at zero: the statistics
+// kernel overwrites every row it later reads.
+namespace specdec {
+constexpr int kStaticAcceptRows = 8192;
+static __device__ __align__(256) DevRowStats g_static_accept_rows[kStaticAcceptRows];
+
+static std::mutex g_static_accept_mu;
+static DevRowStats* g_static_accept_ptr[64] = {};
+
+// Device address of the fixed scratch for the current device (looked up once).
+static int static_accept_rows(DevRowStats** out) {
+    int dev = 0;
+    SD_CUDA(cudaGetDevice(&dev));
+    SD_CHECK(dev >= 0 && dev < 64, SPECDEC_EINVAL, "accept_chain_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lk(g_static_accept_mu);
+    if (!g_static_accept_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_accept_rows);
+        if (e != cudaSuccess) return cuda_status(e, "accept_chain_noalloc: cudaGetSymbolAddress");
+        g_static_accept_ptr[dev] = reinterpret_cast<DevRowStats*>(p);
+    }
+    *out = g_static_accept_ptr[dev];
+    return SPECDEC_OK;
+}
+}  // namespace specdec
+
+extern "C" int specdec_accept_chain_noalloc(const float* target, const float* draft, const int32_t* drafts, int B,
+                                            int k, int V, const specdec_sampling* sp, int32_t* accepted_len,
+                                            int32_t* out_tokens, void* stream) {
+    SD_CHECK(sp && target && drafts && accepted_len && out_tokens, SPECDEC_EINVAL,
+             "accept_chain_noalloc: null argument");
+    SD_CHECK(B >= 0 && k >= 0 && V > 0, SPECDEC_EINVAL, "accept_chain_noalloc: bad shape");
+    if (B == 0) return SPECDEC_OK;
+    const bool greedy = !(sp->temperature > 0.0f);
+    SD_CHECK(greedy || draft, SPECDEC_EINVAL, "accept_chain_noalloc: draft logits required when sampling");
+    const long long rows = (long long)B * (k + 1) + (greedy ? 0 : (long long)B * k);
+    if (rows > kStaticAcceptRows) {
+        set_error("accept_chain_noalloc: batch*(k+1) + batch*k logits rows (" + std::to_string(rows) +
+                  ") exceed the fixed scratch of " + std::to_string(kStaticAcceptRows) +
+                  " rows; use specdec_accept_chain with a caller workspace");
+        return SPECDEC_EINVAL;
+    }
+    DevRowStats* st = nullptr;
+    int rc = static_accept_rows(&st);
+    if (rc) return rc;
+    cudaStream_t s = as_stream(stream);
+    const float c = greedy ? 0.0f : temp_coeff(sp->temperature);
+    const uint64_t tp = top_p_q32(sp->top_p);
+    RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
+    row_stats_kernel<<<(unsigned)rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
     SD_LAUNCH_CHECK("row_stats_kernel");
     accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, sp->seed,
                                                   nullptr, sp->step, st, B, accepted_len, out_tokens);

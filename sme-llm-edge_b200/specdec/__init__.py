@@ -73,6 +73,7 @@ _SIGS = {
     "specdec_paged_attention_compat_f32": (I, [P, P, P, SZ, P, P, P, P, I, I, I]),
     "specdec_accept_workspace_bytes": (SZ, [I]),
     "specdec_accept_chain": (I, [P, P, P, I, I, I, C.POINTER(Sampling), P, P, P, SZ, P]),
+    "specdec_accept_chain_noalloc": (I, [P, P, P, I, I, I, C.POINTER(Sampling), P, P, P]),
     "specdec_accept_tree": (I, [P, P, P, I, I, I, C.POINTER(Sampling), P, P, P, P, SZ, P]),
     "specdec_sample_rows": (I, [P, I, I, I, C.POINTER(Sampling), P, P, SZ, P]),
     "specdec_compat_verify": (I, [P, P, P, I, I, I, P, P, P]),
