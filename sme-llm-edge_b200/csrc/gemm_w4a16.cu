@@ -9,19 +9,30 @@
 //   deq(w) = fp16((u4 - 8) * scale)   (offset-binary nibbles as written by the
 //            reference packer, server/sve_packing.cpp:8-30)
 //
+// Work decomposition: one output tile = 256 weight rows x MT tokens.  A
+// cluster of S CTAs (1 <= S <= 8) owns one tile and splits its K range; the
+// S partial accumulators are summed on chip through distributed shared memory
+// (each CTA reduces 1/S of the tile's columns from all S CTAs in rank order,
+// so the result is deterministic) and written once.  S is chosen per shape so
+// the grid fills the 148 SMs with little wave quantisation.
+//
 // CTA = 15 warps, warp-specialised:
-//   warp 0      bulk-copy producer of the int4 units (runs 4 k-steps ahead)
-//   warp 14     TMA producer of the activation tiles
+//   warp 0      bulk-copy producer of the int4 units (RS k-steps ahead)
+//   warp 14     TMA producer of the activation tiles (BS half-steps ahead)
 //   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
-//   warps 2-5   epilogue: tcgen05.ld of the accumulators, fp32 store / add
-//   warps 6-13  dequant: int4 -> fp16 in registers, stored in the K-major
-//               128B-swizzled UMMA layout
-// MMA: M = 128 weight rows (two per CTA tile of 256), N = token tile MT,
-// K = 16 per instruction, accumulators fp32 in TMEM (2 x MT columns).
-// Work is split "stream-K" style over (tile, k128) items so every SM gets the
-// same number of k-steps; tiles shared by two CTAs are combined with fp32
-// atomics.  Every mbarrier wait is bounded: on timeout the CTA records
-// SPECDEC_ETIMEOUT in the device status word and unwinds.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulators
+//   warps 6-13  dequant: int4 -> fp16 in registers, written straight into
+//               tensor memory with tcgen05.st (one TMEM lane = one weight row)
+// MMA: M = 128 weight rows (two per tile), N = MT, K = 16 per instruction,
+// A (the dequantised weights) read from TMEM, B (the activations) from shared
+// memory, fp32 accumulators in TMEM.  Keeping A out of shared memory matters:
+// with A staged there, the dequant stores plus the MMA's A reads doubled the
+// shared-memory traffic of a k-step and made it, not the tensor pipe, the
+// limit.  TMEM columns: [0, 2*MT) accumulators, then AS stages of 64 columns
+// (two units x 64 k fp16, two fp16 per 32-bit column).
+// Every mbarrier wait is bounded: on timeout the CTA records SPECDEC_ETIMEOUT
+// in the device status word, skips its output and still meets its cluster
+// barriers.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -29,27 +40,35 @@
 
 namespace specdec {
 
-constexpr int kUnitBytes = 8448;   // 8192 nibble bytes + 128 fp16 scales
+constexpr int kUnitBytes = 8448;  // 8192 nibble bytes + 128 fp16 scales
 constexpr int kRawStageBytes = 2 * kUnitBytes;
 constexpr int kGemmThreads = 480;
-constexpr int kASlotBytes = 32768;  // 256 rows x 64 k fp16
 constexpr int kSmemBudget = 227 * 1024;
+constexpr int kMaxSplit = 8;
+constexpr int kTmemCols = 512;
+constexpr int kAStageCols = 64;  // one half k-step of A: 2 units x 64 k fp16
+constexpr int kMaxTokenTile = 160;
 
-// int4 prefetch depth (k128 items): deeper for small token tiles, whose
-// A/B slots are cheap and whose step is bound by the weight stream.
-__host__ __device__ constexpr int raw_stages_for(int MT) { return MT <= 64 ? 6 : 4; }
-__host__ __device__ constexpr int ab_stages_for(int MT) {
-    return (kSmemBudget - raw_stages_for(MT) * kRawStageBytes - 2048 - 1024) / (kASlotBytes + MT * 128) > 4
-               ? 4
-               : (kSmemBudget - raw_stages_for(MT) * kRawStageBytes - 2048 - 1024) / (kASlotBytes + MT * 128);
+// Ring depths per token tile.  A lives in the TMEM columns the accumulators
+// leave free; raw int4 units and activation tiles share the shared memory.
+__host__ __device__ constexpr int a_stages_for(int MT) {
+    return (kTmemCols - 2 * MT) / kAStageCols > 4 ? 4 : (kTmemCols - 2 * MT) / kAStageCols;
 }
-__host__ __device__ constexpr int tmem_cols_for(int MT) {
-    return 2 * MT <= 32 ? 32 : (2 * MT <= 64 ? 64 : (2 * MT <= 128 ? 128 : (2 * MT <= 256 ? 256 : 512)));
+__host__ __device__ constexpr int raw_stages_for(int MT) { return MT <= 32 ? 8 : (MT <= 64 ? 6 : 4); }
+__host__ __device__ constexpr int b_stages_for(int MT) {
+    return (kSmemBudget - 3072 - raw_stages_for(MT) * kRawStageBytes) / (MT * 128) > 8
+               ? 8
+               : (kSmemBudget - 3072 - raw_stages_for(MT) * kRawStageBytes) / (MT * 128);
 }
 template <int MT>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
-    return 1024 /*align slack*/ + (size_t)ab_stages_for(MT) * (kASlotBytes + MT * 128) +
-           (size_t)raw_stages_for(MT) * kRawStageBytes + 2048;
+    return 1024 /*align slack*/ + (size_t)b_stages_for(MT) * MT * 128 + (size_t)raw_stages_for(MT) * kRawStageBytes +
+           2048;
+}
+// the split-K reduction reuses the B and raw rings for one 128-row half (MT x 128 fp32)
+template <int MT>
+__host__ __device__ constexpr bool reduce_fits() {
+    return (size_t)b_stages_for(MT) * MT * 128 + (size_t)raw_stages_for(MT) * kRawStageBytes >= (size_t)MT * 128 * 4;
 }
 
 // ------------------------------------------------------------ PTX helpers
@@ -122,15 +141,28 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_commit(uint32_t mbar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar) : "memory");
 }
-__device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
+// D (TMEM) (+)= A (TMEM, K-major, lane = row) x B (shared memory descriptor)
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// 32 consecutive columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tc_st_x32(uint32_t taddr, const uint32_t v[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_ld_x16(uint32_t taddr, uint32_t v[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -140,16 +172,34 @@ __device__ __forceinline__ void tc_ld_x16(uint32_t taddr, uint32_t v[16]) {
         : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
 
 // K-major, 128-byte swizzled shared-memory matrix descriptor: rows of 128 B,
 // 8-row core groups 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)1 << 16;               // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;     // stride byte offset between 8-row groups
-    d |= (uint64_t)1 << 46;               // descriptor version for sm_100
-    d |= (uint64_t)2 << 61;               // SWIZZLE_128B
+    d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset between 8-row groups
+    d |= (uint64_t)1 << 46;            // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
     return d;
 }
 // kind::f16 instruction descriptor: D fp32, A = B = fp16, both K-major.
@@ -159,21 +209,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
 
 struct GemmArgs {
     const uint8_t* w;
-    int M, N, KG, m_tiles, n_tiles, total;
+    int M, N, KG, m_tiles, S;
     float* Y;
     int ldy, mode;
-    float* part;   // [grid][2 slots][2 halves][MT][128] partial tiles
-    int* tickets;  // [m_tiles * n_tiles], zero between launches
     DeviceStatus* status;
 };
-
-// CTA whose stream-K item range [c*total/grid, (c+1)*total/grid) holds item i.
-__device__ __forceinline__ int item_owner(long long i, int total, int grid) {
-    int c = (int)((i * grid) / total);
-    while (c + 1 < grid && ((long long)(c + 1) * total) / grid <= i) ++c;
-    while (c > 0 && ((long long)c * total) / grid > i) --c;
-    return c;
-}
 
 __device__ __forceinline__ void record_timeout(DeviceStatus* st, int where) {
     if (st) {
@@ -185,310 +225,188 @@ __device__ __forceinline__ void record_timeout(DeviceStatus* st, int where) {
 template <int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, GemmArgs args) {
-    constexpr int AB = ab_stages_for(MT);
+    constexpr int AS = a_stages_for(MT);
+    constexpr int BS = b_stages_for(MT);
     constexpr int RS = raw_stages_for(MT);
     constexpr int BSLOT = MT * 128;
-    constexpr int TMEM_COLS = tmem_cols_for(MT);
+    constexpr uint32_t A_COL0 = 2 * MT;  // first TMEM column of the A stages
     constexpr uint32_t IDESC = idesc_f16(128, MT);
+    static_assert(AS >= 2 && A_COL0 + AS * kAStageCols <= kTmemCols, "TMEM plan");
 
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    unsigned char* sA = base;                                   // AB x 32 KB
-    unsigned char* sB = sA + AB * kASlotBytes;                  // AB x MT*128
-    unsigned char* sRaw = sB + AB * BSLOT;                      // 4 x 16896
+    unsigned char* sB = base;               // BS x MT*128 (1024-byte aligned slots)
+    unsigned char* sRaw = sB + BS * BSLOT;  // RS x 16896
     uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + RS * kRawStageBytes);
     uint64_t* raw_full = bars;
-    uint64_t* raw_empty = bars + RS;
-    uint64_t* a_full = bars + 2 * RS;
-    uint64_t* b_full = a_full + AB;
-    uint64_t* ab_empty = b_full + AB;
-    uint64_t* acc_full = ab_empty + AB;
-    uint64_t* acc_empty = acc_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    uint64_t* raw_empty = raw_full + RS;
+    uint64_t* a_full = raw_empty + RS;
+    uint64_t* a_empty = a_full + AS;
+    uint64_t* b_full = a_empty + AS;
+    uint64_t* b_empty = b_full + BS;
+    uint64_t* acc_full = b_empty + BS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g0 = (int)(((long long)blockIdx.x * args.total) / gridDim.x);
-    const int g1 = (int)(((long long)(blockIdx.x + 1) * args.total) / gridDim.x);
+    const int S = args.S;
+    const int tile = blockIdx.x / S;
+    const int rank = S > 1 ? (int)cluster_rank() : 0;
+    const int n_tile = tile / args.m_tiles, m_tile = tile % args.m_tiles;
+    const int k0 = (int)(((long long)rank * args.KG) / S);
+    const int k1 = (int)(((long long)(rank + 1) * args.KG) / S);
+    const int n_items = k1 - k0;  // >= 1 (S <= KG)
+    const int n_halves = 2 * n_items;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < RS; ++i) {
             mbar_init(s_addr(&raw_full[i]), 1);
             mbar_init(s_addr(&raw_empty[i]), 8);
         }
-        for (int i = 0; i < AB; ++i) {
+        for (int i = 0; i < AS; ++i) {
             mbar_init(s_addr(&a_full[i]), 8);
+            mbar_init(s_addr(&a_empty[i]), 1);
+        }
+        for (int i = 0; i < BS; ++i) {
             mbar_init(s_addr(&b_full[i]), 1);
-            mbar_init(s_addr(&ab_empty[i]), 1);
+            mbar_init(s_addr(&b_empty[i]), 1);
         }
         mbar_init(s_addr(acc_full), 1);
-        mbar_init(s_addr(acc_empty), 4);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_addr(tmem_slot)),
-                     "r"(TMEM_COLS));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int KG = args.KG;
 
     if (warp == 0) {
-        // ------------------------------------------------ producer
-        if (lane == 0 && g0 < g1) {
-            int r_it = 0, ab_it = 0;
-            // int4 units only: runs up to RS items ahead of the dequant warps
+        // ------------------------------------------------ int4 unit producer
+        if (lane == 0) {
             bool ok = true;
-            for (int g = g0; g < g1 && ok; ++g) {
-                const int tile = g / KG, kg = g % KG;
-                const int n_tile = tile / args.m_tiles;
-                const int rs = r_it % RS;
-                if (r_it >= RS) ok = mbar_wait(s_addr(&raw_empty[rs]), ((r_it / RS) - 1) & 1);
+            int it = 0;
+            for (; it < n_items; ++it) {
+                const int rs = it % RS;
+                if (it >= RS) ok = mbar_wait(s_addr(&raw_empty[rs]), ((it / RS) - 1) & 1);
                 if (!ok || *abort_flag) break;
                 const uint32_t rf = s_addr(&raw_full[rs]);
                 mbar_expect_tx(rf, kRawStageBytes);
                 for (int u = 0; u < 2; ++u) {
-                    const uint8_t* src = args.w + ((size_t)(n_tile * 2 + u) * KG + kg) * kUnitBytes;
+                    const uint8_t* src = args.w + ((size_t)(n_tile * 2 + u) * args.KG + (k0 + it)) * kUnitBytes;
                     bulk_g2s(s_addr(sRaw + rs * kRawStageBytes + u * kUnitBytes), src, kUnitBytes, rf);
                 }
-                ++r_it;
             }
             if (!ok) {
                 *abort_flag = 1;
                 record_timeout(args.status, 1);
             }
-            // drain: every copy issued above completes on its barrier before the CTA exits
-            if (r_it > 0) (void)mbar_wait(s_addr(&raw_full[(r_it - 1) % RS]), ((r_it - 1) / RS) & 1);
+            // drain: the copies issued above complete before the CTA exits
+            if (it > 0) (void)mbar_wait(s_addr(&raw_full[(it - 1) % RS]), ((it - 1) / RS) & 1);
         }
     } else if (warp == 14) {
         // ------------------------------------------------ activation (B operand) producer
-        if (lane == 0 && g0 < g1) {
-            int ab_it = 0;
+        if (lane == 0) {
             bool ok = true;
-            for (int g = g0; g < g1 && ok; ++g) {
-                const int tile = g / KG, kg = g % KG;
-                const int m_tile = tile % args.m_tiles;
-                for (int hk = 0; hk < 2; ++hk) {
-                    const int s = ab_it % AB;
-                    if (ab_it >= AB) ok = mbar_wait(s_addr(&ab_empty[s]), ((ab_it / AB) - 1) & 1);
-                    if (!ok || *abort_flag) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t bf = s_addr(&b_full[s]);
-                    mbar_expect_tx(bf, BSLOT);
-                    tma_load_2d(s_addr(sB + s * BSLOT), &tmap_x, kg * 128 + hk * 64, m_tile * MT, bf);
-                    ++ab_it;
-                }
+            int j = 0;
+            for (; j < n_halves; ++j) {
+                const int s = j % BS;
+                if (j >= BS) ok = mbar_wait(s_addr(&b_empty[s]), ((j / BS) - 1) & 1);
+                if (!ok || *abort_flag) break;
+                const uint32_t bf = s_addr(&b_full[s]);
+                mbar_expect_tx(bf, BSLOT);
+                tma_load_2d(s_addr(sB + s * BSLOT), &tmap_x, (k0 + (j >> 1)) * 128 + (j & 1) * 64, m_tile * MT, bf);
             }
             if (!ok) {
                 *abort_flag = 1;
                 record_timeout(args.status, 5);
             }
-            if (ab_it > 0) (void)mbar_wait(s_addr(&b_full[(ab_it - 1) % AB]), ((ab_it - 1) / AB) & 1);
+            if (j > 0) (void)mbar_wait(s_addr(&b_full[(j - 1) % BS]), ((j - 1) / BS) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0 && g0 < g1) {
-            int ab_it = 0, t_it = 0;
+        if (lane == 0) {
             bool ok = true;
-            for (int g = g0; g < g1 && ok; ++g) {
-                const int kg = g % KG;
-                const bool first = (g == g0) || (kg == 0);
-                const bool last = (g == g1 - 1) || (kg == KG - 1);
-                if (first) {
-                    ok = mbar_wait(s_addr(acc_empty), (t_it & 1) ^ 1);
-                    if (!ok) break;
-                    tc_fence_after();
-                }
-                for (int hk = 0; hk < 2 && ok; ++hk) {
-                    const int s = ab_it % AB;
-                    const uint32_t par = (ab_it / AB) & 1;
-                    ok = mbar_wait(s_addr(&a_full[s]), par) && mbar_wait(s_addr(&b_full[s]), par);
-                    if (!ok || *abort_flag) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a0 = s_addr(sA + s * kASlotBytes);
-                    const uint32_t b0 = s_addr(sB + s * BSLOT);
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        const uint64_t bd = sw128_desc(b0 + ks * 32);
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const uint64_t ad = sw128_desc(a0 + q * 16384 + ks * 32);
-                            const uint32_t acc = (first && hk == 0 && ks == 0) ? 0u : 1u;
-                            tc_mma_f16(tmem + (uint32_t)(q * MT), ad, bd, IDESC, acc);
-                        }
-                    }
-                    tc_commit(s_addr(&ab_empty[s]));
-                    ++ab_it;
-                }
-                if (ok && last) {
-                    tc_commit(s_addr(acc_full));
-                    ++t_it;
-                }
-            }
-            if (!ok) {
-                *abort_flag = 1;
-                record_timeout(args.status, 2);
-            }
-        }
-    } else if (warp < 6) {
-        // ------------------------------------------------ epilogue
-        // A tile whose k-range is split over several CTAs (at stream-K range
-        // boundaries) is finished by the last of them to arrive (atomic
-        // ticket, no waiting): the others park their partial sums in the
-        // workspace, the last one adds all parts in CTA order and writes Y.
-        const int quad = warp & 3;
-        const int et = threadIdx.x - 64;  // 0..127
-        int* s_ticket = reinterpret_cast<int*>(tmem_slot + 2);
-        const size_t slot_floats = (size_t)2 * MT * 128;
-        int t_it = 0;
-        for (int g = g0; g < g1; ++g) {
-            const int kg = g % KG;
-            const bool last = (g == g1 - 1) || (kg == KG - 1);
-            if (!last) continue;
-            const int tile = g / KG;
-            const int n_tile = tile / args.m_tiles, m_tile = tile % args.m_tiles;
-            const int c_lo = item_owner((long long)tile * KG, args.total, gridDim.x);
-            const int c_hi = item_owner((long long)tile * KG + KG - 1, args.total, gridDim.x);
-            const int my_slot = (g0 / KG == tile) ? 0 : 1;
-            if (!mbar_wait(s_addr(acc_full), t_it & 1) || *abort_flag) {
-                *abort_flag = 1;
-                record_timeout(args.status, 3);
-                break;
-            }
-            tc_fence_after();
-            bool finisher = true;
-            if (c_hi > c_lo) {
-                // park this CTA's part, then take a ticket
-                float* mine = args.part + ((size_t)blockIdx.x * 2 + my_slot) * slot_floats;
-#pragma unroll 1
-                for (int q = 0; q < 2; ++q)
-#pragma unroll 1
-                    for (int c = 0; c < MT / 16; ++c) {
-                        uint32_t v[16];
-                        tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
-                        tc_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            __stcg(mine + ((size_t)q * MT + c * 16 + j) * 128 + quad * 32 + lane, __uint_as_float(v[j]));
-                    }
-                __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (et == 0) *s_ticket = atomicAdd(&args.tickets[tile], 1);
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                finisher = (*s_ticket == c_hi - c_lo);
-                if (finisher) __threadfence();
-            }
-            if (finisher) {
-#pragma unroll 1
-                for (int q = 0; q < 2; ++q) {
-                    const int n = n_tile * 256 + q * 128 + quad * 32 + lane;
-#pragma unroll 1
-                    for (int c = 0; c < MT / 16; ++c) {
-                        uint32_t v[16];
-                        tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
-                        tc_wait_ld();
-                        float acc[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-                        // parts in CTA order (deterministic sum); the first part of
-                        // CTA p is its slot 0, a later tile of p its slot 1
-                        const size_t off = ((size_t)q * MT + c * 16) * 128 + quad * 32 + lane;
-                        for (int p = c_lo; p <= c_hi; ++p) {
-                            if (p == (int)blockIdx.x) {
-#pragma unroll
-                                for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(v[j]);
-                            } else {
-                                const int ps = ((((long long)p * args.total) / gridDim.x) / KG == tile) ? 0 : 1;
-                                const float* src = args.part + ((size_t)p * 2 + ps) * slot_floats + off;
-#pragma unroll
-                                for (int j = 0; j < 16; ++j) acc[j] += __ldcg(src + (size_t)j * 128);
-                            }
-                        }
-                        if (n < args.N) {
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                const int m = m_tile * MT + c * 16 + j;
-                                if (m < args.M) {
-                                    float* y = args.Y + (size_t)m * args.ldy + n;
-                                    if (args.mode) *y += acc[j];
-                                    else *y = acc[j];
-                                }
-                            }
-                        }
-                    }
-                }
-                if (c_hi > c_lo && et == 0) args.tickets[tile] = 0;
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_addr(acc_empty));
-            ++t_it;
-        }
-    } else {
-        // ------------------------------------------------ dequant
-        const int dt = threadIdx.x - 192;  // 0..255
-        int r_it = 0, ab_it = 0;
-        bool ok = true;
-        for (int g = g0; g < g1 && ok; ++g) {
-            const int rs = r_it % RS;
-            ok = mbar_wait(s_addr(&raw_full[rs]), (r_it / RS) & 1);
-            if (!ok || *abort_flag) {
-                ok = false;
-                break;
-            }
-            const unsigned char* raw = sRaw + rs * kRawStageBytes;
-            // this thread's row r and its two units' group scales are fixed for the item
-            const int r = dt & 127;
-            const __half2 s2u0 = __half2half2(*reinterpret_cast<const __half*>(raw + 8192 + r * 2));
-            const __half2 s2u1 = __half2half2(*reinterpret_cast<const __half*>(raw + kUnitBytes + 8192 + r * 2));
-            const __half2 bias = __float2half2_rn(1032.0f);
-            for (int hk = 0; hk < 2; ++hk) {
-                const int s = ab_it % AB;
-                if (ab_it >= AB) ok = mbar_wait(s_addr(&ab_empty[s]), ((ab_it / AB) - 1) & 1);
+            for (int j = 0; j < n_halves && ok; ++j) {
+                const int sa = j % AS, sb = j % BS;
+                ok = mbar_wait(s_addr(&a_full[sa]), (j / AS) & 1) && mbar_wait(s_addr(&b_full[sb]), (j / BS) & 1);
                 if (!ok || *abort_flag) {
                     ok = false;
                     break;
                 }
-                unsigned char* a_slot = sA + s * kASlotBytes;
+                tc_fence_after();
+                const uint32_t a0 = tmem + A_COL0 + (uint32_t)(sa * kAStageCols);
+                const uint32_t b0 = s_addr(sB + sb * BSLOT);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t bd = sw128_desc(b0 + ks * 32);
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)  // unit q: A columns q*32 + ks*8 .. +8 (k16 = 8 columns)
+                        tc_mma_f16_ts(tmem + (uint32_t)(q * MT), a0 + (uint32_t)(q * 32 + ks * 8), bd, IDESC,
+                                      (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                tc_commit(s_addr(&a_empty[sa]));
+                tc_commit(s_addr(&b_empty[sb]));
+            }
+            if (ok) tc_commit(s_addr(acc_full));
+            else {
+                *abort_flag = 1;
+                record_timeout(args.status, 2);
+            }
+        }
+    } else if (warp >= 6) {
+        // ------------------------------------------------ dequant
+        // A warp may only touch TMEM lanes 32*(warp%4) .. +31, so warps 6-9
+        // cover the four lane quarters of unit 0 and warps 10-13 those of
+        // unit 1.  Thread = one weight row r of its unit.
+        const int q = (warp - 6) >> 2;
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(q * 32);
+        const __half2 bias = __float2half2_rn(1032.0f);
+        bool ok = true;
+        for (int it = 0; it < n_items && ok; ++it) {
+            const int rs = it % RS;
+            ok = mbar_wait(s_addr(&raw_full[rs]), (it / RS) & 1);
+            // warp-uniform decision: the tcgen05.st below is a .sync.aligned warp instruction
+            ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+            if (!ok) break;
+            const unsigned char* unit = sRaw + rs * kRawStageBytes + q * kUnitBytes;
+            const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(unit + 8192 + r * 2));
+            for (int hk = 0; hk < 2; ++hk) {
+                const int j = 2 * it + hk;
+                const int s = j % AS;
+                if (j >= AS) ok = mbar_wait(s_addr(&a_empty[s]), ((j / AS) - 1) & 1);
+                ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+                if (!ok) break;
                 uint32_t wv[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {  // all loads first: 8 independent shared loads in flight
-                    const int u = i >> 2, kcl = 2 * (i & 3) + (dt >> 7);
-                    wv[i] = *reinterpret_cast<const uint32_t*>(raw + u * kUnitBytes + (((hk * 8 + kcl) * 128 + r) << 2));
-                }
+                for (int i = 0; i < 8; ++i)  // word (kc, r): k = kc*8 .. kc*8+7 of row r; lanes read consecutive words
+                    wv[i] = *reinterpret_cast<const uint32_t*>(unit + (((hk * 8 + i) * 128 + r) << 2));
+                uint32_t outw[32];  // column i*4+jj = fp16 pair (k = 8i+2jj, 8i+2jj+1) of this half
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int u = i >> 2, kcl = 2 * (i & 3) + (dt >> 7);
-                    const __half2 s2 = u ? s2u1 : s2u0;
-                    uint32_t outw[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t t = ((wv[i] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const uint32_t t = ((wv[i] >> (4 * jj)) & 0x000F000Fu) | 0x64006400u;
                         __half2 hv = *reinterpret_cast<const __half2*>(&t);
                         hv = __hmul2(__hsub2(hv, bias), s2);  // exact (u - 8), then one rounding of (u - 8) * s
-                        outw[j] = *reinterpret_cast<uint32_t*>(&hv);
+                        outw[i * 4 + jj] = *reinterpret_cast<uint32_t*>(&hv);
                     }
-                    unsigned char* dst = a_slot + u * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + ((kcl ^ (r & 7)) << 4);
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
                 }
-                fence_async_smem();
+                tc_st_x32(t_row + (uint32_t)(s * kAStageCols), outw);
+                tc_wait_st();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(s_addr(&a_full[s]));
-                ++ab_it;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(s_addr(&raw_empty[rs]));
-            ++r_it;
+            if (ok && lane == 0) mbar_arrive(s_addr(&raw_empty[rs]));
         }
         if (!ok) {
             *abort_flag = 1;
@@ -496,11 +414,100 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     }
 
+    // ---------------------------------------------------- epilogue (all threads)
+    const bool epi_warp = warp >= 2 && warp < 6;
+    const int quad = warp & 3;
+    bool acc_ok = true;
+    if (epi_warp) {
+        acc_ok = mbar_wait(s_addr(acc_full), 0) && !*abort_flag;
+        if (!acc_ok) {
+            *abort_flag = 1;
+            record_timeout(args.status, 3);
+        }
+        tc_fence_after();
+    }
+    if (S == 1) {
+        if (epi_warp && acc_ok) {
+#pragma unroll 1
+            for (int q = 0; q < 2; ++q) {
+                const int n = n_tile * 256 + q * 128 + quad * 32 + lane;
+#pragma unroll 1
+                for (int c = 0; c < MT / 16; ++c) {
+                    uint32_t v[16];
+                    tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
+                    tc_wait_ld();
+                    if (n < args.N) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int m = m_tile * MT + c * 16 + jj;
+                            if (m < args.M) {
+                                float* y = args.Y + (size_t)m * args.ldy + n;
+                                if (args.mode) *y += __uint_as_float(v[jj]);
+                                else *y = __uint_as_float(v[jj]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    } else if constexpr (reduce_fits<MT>()) {
+        // split-K: park this CTA's half-tile in its own shared memory (the A/B
+        // rings are idle once the accumulator is final), then every CTA sums a
+        // column slice over all S CTAs of the cluster through DSMEM.
+        float* red = reinterpret_cast<float*>(base);  // [MT][128]
+        const int cols = 128 / S;                     // S divides 128 (1, 2, 4, 8)
+        const int vec_per_row = cols / 4;
+        for (int q = 0; q < 2; ++q) {
+            if (epi_warp && acc_ok) {
+#pragma unroll 1
+                for (int c = 0; c < MT / 16; ++c) {
+                    uint32_t v[16];
+                    tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) red[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[jj]);
+                }
+            }
+            __syncthreads();
+            cluster_sync_all();
+            const bool cluster_ok = !*abort_flag;
+            if (cluster_ok) {
+                for (int idx = threadIdx.x; idx < MT * vec_per_row; idx += blockDim.x) {
+                    const int mr = idx / vec_per_row;
+                    const int cl = rank * cols + (idx % vec_per_row) * 4;
+                    const uint32_t la = s_addr(red + mr * 128 + cl);
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int p = 0; p < S; ++p) {
+                        const float4 v = ld_dsmem_f4(la, (uint32_t)p);
+                        acc.x += v.x;
+                        acc.y += v.y;
+                        acc.z += v.z;
+                        acc.w += v.w;
+                    }
+                    const int m = m_tile * MT + mr;
+                    const int n = n_tile * 256 + q * 128 + cl;
+                    if (m < args.M) {
+                        float* y = args.Y + (size_t)m * args.ldy + n;
+                        const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (n + e < args.N) {
+                                if (args.mode) y[e] += vals[e];
+                                else y[e] = vals[e];
+                            }
+                        }
+                    }
+                }
+            }
+            cluster_sync_all();  // peers are done reading before the next half overwrites `red`
+        }
+    }
+
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
 
@@ -622,14 +629,16 @@ int make_x_tmap(CUtensorMap* map, const void* X, int M, int K, int ldx, int MT) 
     return SPECDEC_OK;
 }
 
+// Token tile: the smallest that holds M; above 160 tokens, the one of 128 / 160
+// that pads M least (160 on a tie: fewer passes over the weights).
 int pick_mt(int M) {
-    static const int opts[] = {16, 32, 64, 128, 160, 256};
-    if (M <= 256) {
+    static const int opts[] = {16, 32, 64, 128, kMaxTokenTile};
+    if (M <= kMaxTokenTile) {
         for (int o : opts)
             if (o >= M) return o;
     }
-    const int t160 = (M + 159) / 160 * 160, t256 = (M + 255) / 256 * 256;
-    return t160 < t256 ? 160 : 256;
+    const int t160 = (M + 159) / 160 * 160, t128 = (M + 127) / 128 * 128;
+    return t128 < t160 ? 128 : 160;
 }
 
 static int g_num_sms = 0;
@@ -643,79 +652,82 @@ static int num_sms() {
     return g_num_sms;
 }
 
-template <int MT>
-static int launch_tc(const CUtensorMap& map, const GemmArgs& a, int grid, cudaStream_t s) {
-    constexpr size_t smem = gemm_smem_bytes<MT>();
-    static bool attr = false;
-    if (!attr) {
-        SD_CUDA(cudaFuncSetAttribute(w4a16_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
-    }
-    w4a16_tc_kernel<MT><<<grid, kGemmThreads, smem, s>>>(map, a);
-    SD_LAUNCH_CHECK("w4a16_tc_kernel");
-    return SPECDEC_OK;
-}
-
 struct GemmPlan {
-    int MT, m_tiles, n_tiles, KG, total, grid;
-    bool split;  // some tile is shared by several CTAs
+    int MT, m_tiles, n_tiles, KG, S, grid;
 };
 
+// Split factor S (CTAs per tile, a power of two <= 8 and <= KG) minimising
+// waves * (k-steps per CTA + setup), plus a penalty for the on-chip reduction.
 GemmPlan plan_gemm(int M, int N, int K) {
     GemmPlan p;
     p.MT = pick_mt(M);
     p.m_tiles = (M + p.MT - 1) / p.MT;
     p.n_tiles = (N + 255) / 256;
     p.KG = (K + 127) / 128;
-    p.total = p.m_tiles * p.n_tiles * p.KG;
     const int tiles = p.m_tiles * p.n_tiles;
-    p.grid = num_sms();
-    if (p.grid > p.total) p.grid = p.total;
-    p.split = false;
-    for (int c = 0; c < p.grid && !p.split; ++c) {
-        const long long g0 = (long long)c * p.total / p.grid, g1 = (long long)(c + 1) * p.total / p.grid;
-        if (g0 % p.KG || g1 % p.KG) p.split = true;
+    const int sms = num_sms();
+    double best = 1e30;
+    p.S = 1;
+    for (int S = 1; S <= kMaxSplit && S <= p.KG; S *= 2) {
+        const double waves = (double)((tiles * S + sms - 1) / sms);
+        const double items = (double)((p.KG + S - 1) / S);
+        const double cost = waves * (items + 1.0) + (S > 1 ? 1.5 : 0.0);
+        if (cost < best - 1e-9) {
+            best = cost;
+            p.S = S;
+        }
     }
-    (void)tiles;
+    p.grid = tiles * p.S;
     return p;
 }
 
-// Workspace of one launch: per-tile tickets at a fixed offset (the front, so
-// that launches with different token tiles sharing one workspace never
-// overlap each other's tickets), then the parked partial tiles.  The tickets
-// must be zero before the first launch; every launch leaves them zero.
-constexpr size_t kTicketBytes = 1 << 18;  // 65536 tiles
-size_t gemm_workspace_bytes(const GemmPlan& p) {
-    return kTicketBytes + (size_t)p.grid * 2 * 2 * p.MT * 128 * sizeof(float);
-}
-size_t gemm_workspace_bound(int max_m, int max_n, int max_k) {
-    (void)max_m;
-    (void)max_n;
-    (void)max_k;
-    // the partial area depends only on the grid and the token tile (<= 256)
-    return kTicketBytes + (size_t)num_sms() * 2 * 2 * 256 * 128 * sizeof(float);
+template <int MT>
+static int launch_tc(const CUtensorMap& map, const GemmArgs& a, int grid, cudaStream_t s) {
+    constexpr size_t smem = gemm_smem_bytes<MT>();
+    static_assert(smem <= (size_t)kSmemBudget, "shared memory plan exceeds the opt-in limit");
+    static_assert(reduce_fits<MT>(), "split-K reduction buffer does not fit in the rings");
+    // one CTA per SM: every CTA allocates all 512 TMEM columns, so two CTAs of
+    // one cluster must never share an SM
+    static_assert(smem > (size_t)kSmemBudget / 2, "shared memory plan must force one CTA per SM");
+    static bool attr = false;
+    if (!attr) {
+        SD_CUDA(cudaFuncSetAttribute(w4a16_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = (unsigned)a.S;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    SD_CUDA(cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<MT>, map, a));
+    return SPECDEC_OK;
 }
 
-// Launch with a prebuilt tensor map (built for this plan's MT).
+// The kernel needs no global workspace (split tiles are reduced on chip); the
+// workspace arguments of the C ABI are kept and may be NULL / 0.
+size_t gemm_workspace_bytes(const GemmPlan&) { return 0; }
+size_t gemm_workspace_bound(int, int, int) { return 0; }
+
 int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
                 int mode, void* ws, cudaStream_t s) {
+    (void)ws;
     GemmArgs a;
     a.w = reinterpret_cast<const uint8_t*>(w_tiled);
     a.M = M;
     a.N = N;
     a.KG = p.KG;
     a.m_tiles = p.m_tiles;
-    a.n_tiles = p.n_tiles;
-    a.total = p.total;
+    a.S = p.S;
     a.Y = Y;
     a.ldy = ldy;
     a.mode = mode;
-    if ((size_t)p.m_tiles * p.n_tiles * sizeof(int) > kTicketBytes) {
-        set_error("w4a16_gemm: too many output tiles for the ticket area");
-        return SPECDEC_EINVAL;
-    }
-    a.tickets = reinterpret_cast<int*>(ws);
-    a.part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kTicketBytes);
     a.status = device_status_ptr();
     switch (p.MT) {
         case 16: return launch_tc<16>(map, a, p.grid, s);
@@ -723,7 +735,6 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
         case 64: return launch_tc<64>(map, a, p.grid, s);
         case 128: return launch_tc<128>(map, a, p.grid, s);
         case 160: return launch_tc<160>(map, a, p.grid, s);
-        case 256: return launch_tc<256>(map, a, p.grid, s);
         default: break;
     }
     set_error("w4a16_gemm: unsupported token tile");
@@ -770,19 +781,16 @@ extern "C" size_t specdec_w4a16_workspace_bytes(int M, int N, int K) {
 
 extern "C" int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y,
                                   int ldy, int mode, void* workspace, size_t workspace_bytes, void* stream) {
+    (void)workspace;
+    (void)workspace_bytes;
     SD_CHECK(X && w_tiled && Y && M >= 0 && N > 0 && K > 0 && ldx >= K && ldy >= N && (mode == 0 || mode == 1),
              SPECDEC_EINVAL, "w4a16_gemm: bad argument");
     if (M == 0) return SPECDEC_OK;
-    cudaStream_t s = as_stream(stream);
     GemmPlan p = plan_gemm(M, N, K);
-    const size_t need = gemm_workspace_bytes(p);
-    SD_CHECK(workspace && workspace_bytes >= need, SPECDEC_EINVAL, "w4a16_gemm: workspace too small");
     CUtensorMap map;
     int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
     if (rc) return rc;
-    // tickets must start at zero; clear them (the kernel leaves them zero again)
-    SD_CUDA(cudaMemsetAsync(workspace, 0, (size_t)p.m_tiles * p.n_tiles * sizeof(int), s));
-    return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, workspace, s);
+    return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, nullptr, as_stream(stream));
 }
 
 extern "C" int specdec_w4a16_gemm_simt(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y,
