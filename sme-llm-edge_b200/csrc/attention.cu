@@ -13,6 +13,7 @@
 // rust_sve2_flashdecoding_reduce_f32 (lib.rs:1721-1783).
 // GQA head map q_head = kv_head * G + g as in lib.rs:841-842.
 #include "common.cuh"
+#include "internal.h"
 
 namespace specdec {
 

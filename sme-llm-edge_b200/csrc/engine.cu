@@ -18,47 +18,9 @@
 #include <vector>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace specdec {
-// from other translation units
-struct GemmPlan {
-    int MT, m_tiles, n_tiles, KG, total, grid;
-    bool split;
-};
-GemmPlan plan_gemm(int M, int N, int K);
-int make_x_tmap(CUtensorMap* map, const void* X, int M, int K, int ldx, int MT);
-int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
-                int mode, void* ws, cudaStream_t s);
-size_t gemm_workspace_bound(int max_m, int max_n, int max_k);
-size_t w4_tiled_bytes(int N, int K);
-size_t attention_workspace(int B, int R, int Hq, int Hkv, int HD, int max_ctx);
-int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, int Hkv, int HD, const int32_t* tables,
-                     int max_blocks, const int32_t* ctx_len, const uint64_t* mask, int B, int R, int Hq, __half* out,
-                     void* ws, size_t ws_bytes, int max_ctx, cudaStream_t s);
-int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaStream_t s);
-float temp_coeff(float temperature);
-uint64_t top_p_q32(float top_p);
-int launch_accept_chain_dev(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
-                            float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
-                            int32_t* accepted_len, int32_t* out_tokens, void* ws, cudaStream_t s);
-int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, const int32_t* parent, int B, int R, int V,
-                           float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
-                           int32_t* accepted_len, int32_t* path, int32_t* out_tokens, cudaStream_t s);
-int launch_sample_rows_dev(const float* logits, int rows, int k, int V, float temperature, float top_p, uint64_t seed,
-                           const uint32_t* step_dev, int32_t* out, cudaStream_t s);
-struct KVState {
-    int num_blocks, block_size, max_reqs, max_bpr;
-    int32_t* tables;
-    int32_t* nblk;
-    int32_t* len;
-    int32_t* ref;
-    int32_t* ctx;
-    int32_t* scratch;
-    int32_t* status;
-};
-KVState& kv_state(specdec_kv* kv);
-int kv_append_uniform(specdec_kv* kv, int n, int tokens, cudaStream_t s);
-int kv_truncate_dev(specdec_kv* kv, const int32_t* new_len_dev, int n, cudaStream_t s);
 
 // -------------------------------------------------------- synthetic data
 __device__ __forceinline__ float synth_value(uint32_t seed, uint32_t tid, uint64_t e) {

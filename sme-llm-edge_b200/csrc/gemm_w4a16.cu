@@ -16,19 +16,20 @@
 // so the result is deterministic) and written once.  S is chosen per shape so
 // the grid fills the 148 SMs with little wave quantisation.
 //
-// CTA = 15 warps, warp-specialised:
+// CTA = 19 warps, warp-specialised:
 //   warp 0      bulk-copy producer of the int4 units (RS k-steps ahead)
-//   warp 14     TMA producer of the activation tiles (BS half-steps ahead)
+//   warp 18     TMA producer of the activation tiles (ST half-steps ahead)
 //   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
-//   warps 2-5   epilogue: tcgen05.ld of the accumulators
-//   warps 6-13  dequant: int4 -> fp16 in registers, written straight into
-//               tensor memory with tcgen05.st (one TMEM lane = one weight row)
+//   warps 2-17  dequant: int4 -> fp16 in registers, written straight into
+//               tensor memory with tcgen05.st (one TMEM lane = one weight row);
+//               then the epilogue: tcgen05.ld of the accumulators into shared
+//               memory, TMA stores out
 // MMA: M = 128 weight rows (two per tile), N = MT, K = 16 per instruction,
 // A (the dequantised weights) read from TMEM, B (the activations) from shared
 // memory, fp32 accumulators in TMEM.  Keeping A out of shared memory matters:
 // with A staged there, the dequant stores plus the MMA's A reads doubled the
 // shared-memory traffic of a k-step and made it, not the tensor pipe, the
-// limit.  TMEM columns: [0, 2*MT) accumulators, then AS stages of 64 columns
+// limit.  TMEM columns: [0, 2*MT) accumulators, then ST stages of 64 columns
 // (two units x 64 k fp16, two fp16 per 32-bit column).
 // Every mbarrier wait is bounded: on timeout the CTA records SPECDEC_ETIMEOUT
 // in the device status word, skips its output and still meets its cluster
@@ -36,39 +37,42 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include "common.cuh"
+#include "internal.h"
 
 namespace specdec {
 
 constexpr int kUnitBytes = 8448;  // 8192 nibble bytes + 128 fp16 scales
 constexpr int kRawStageBytes = 2 * kUnitBytes;
-constexpr int kGemmThreads = 480;
+constexpr int kGemmThreads = 608;  // 19 warps
+constexpr int kDeqWarps = 16;      // warps 2..17
+constexpr int kBWarp = 18;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kMaxSplit = 8;
 constexpr int kTmemCols = 512;
 constexpr int kAStageCols = 64;  // one half k-step of A: 2 units x 64 k fp16
 constexpr int kMaxTokenTile = 160;
 
-// Ring depths per token tile.  A lives in the TMEM columns the accumulators
-// leave free; raw int4 units and activation tiles share the shared memory.
-__host__ __device__ constexpr int a_stages_for(int MT) {
+constexpr int kRawStages = 8;    // int4 units in flight per CTA: 8 x 16.5 KB
+
+// Ring depth per token tile.  One stage = the A operand of a half k-step in
+// TMEM (64 columns after the 2*MT accumulator columns) plus the matching
+// activation tile in shared memory; both are released by one MMA commit.
+// The raw int4 ring is separate and deeper (it hides HBM latency).
+__host__ __device__ constexpr int stages_for(int MT) {
     return (kTmemCols - 2 * MT) / kAStageCols > 4 ? 4 : (kTmemCols - 2 * MT) / kAStageCols;
-}
-__host__ __device__ constexpr int raw_stages_for(int MT) { return MT <= 32 ? 8 : (MT <= 64 ? 6 : 4); }
-__host__ __device__ constexpr int b_stages_for(int MT) {
-    return (kSmemBudget - 3072 - raw_stages_for(MT) * kRawStageBytes) / (MT * 128) > 8
-               ? 8
-               : (kSmemBudget - 3072 - raw_stages_for(MT) * kRawStageBytes) / (MT * 128);
 }
 template <int MT>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
-    return 1024 /*align slack*/ + (size_t)b_stages_for(MT) * MT * 128 + (size_t)raw_stages_for(MT) * kRawStageBytes +
-           2048;
+    return 1024 /*align slack*/ + (size_t)stages_for(MT) * MT * 128 + (size_t)kRawStages * kRawStageBytes + 2048;
 }
-// the split-K reduction reuses the B and raw rings for one 128-row half (MT x 128 fp32)
+// the epilogue reuses the B and raw rings: two MT x 128 fp32 tiles (both halves,
+// or the parked partial plus the reduced slice of a split tile)
 template <int MT>
 __host__ __device__ constexpr bool reduce_fits() {
-    return (size_t)b_stages_for(MT) * MT * 128 + (size_t)raw_stages_for(MT) * kRawStageBytes >= (size_t)MT * 128 * 4;
+    return (size_t)stages_for(MT) * MT * 128 + (size_t)kRawStages * kRawStageBytes >= (size_t)2 * MT * 128 * 4;
 }
 
 // ------------------------------------------------------------ PTX helpers
@@ -135,6 +139,22 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
         : "memory");
 }
+// shared -> global tile: plain store (mode 0) or element-wise add into Y (mode 1)
+__device__ __forceinline__ void tma_out_2d(const CUtensorMap* map, uint32_t src, int x, int y, int add) {
+    if (add)
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         reinterpret_cast<uint64_t>(map)),
+                     "r"(src), "r"(x), "r"(y)
+                     : "memory");
+    else
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         reinterpret_cast<uint64_t>(map)),
+                     "r"(src), "r"(x), "r"(y)
+                     : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the bulk stores issued so far have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -151,15 +171,13 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, 
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// 32 consecutive columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void tc_st_x32(uint32_t taddr, const uint32_t v[32]) {
+// 16 consecutive columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tc_st_x16(uint32_t taddr, const uint32_t v[16]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -212,6 +230,7 @@ struct GemmArgs {
     int M, N, KG, m_tiles, S;
     float* Y;
     int ldy, mode;
+    int tma_out;  // tmap_y is valid: Y leaves by TMA (box {128 / S, MT})
     DeviceStatus* status;
 };
 
@@ -224,31 +243,34 @@ __device__ __forceinline__ void record_timeout(DeviceStatus* st, int where) {
 
 template <int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, GemmArgs args) {
-    constexpr int AS = a_stages_for(MT);
-    constexpr int BS = b_stages_for(MT);
-    constexpr int RS = raw_stages_for(MT);
+    w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
+                    GemmArgs args) {
+    constexpr int ST = stages_for(MT);
+    constexpr int RS = kRawStages;
     constexpr int BSLOT = MT * 128;
     constexpr uint32_t A_COL0 = 2 * MT;  // first TMEM column of the A stages
     constexpr uint32_t IDESC = idesc_f16(128, MT);
-    static_assert(AS >= 2 && A_COL0 + AS * kAStageCols <= kTmemCols, "TMEM plan");
+    static_assert(ST >= 2 && A_COL0 + ST * kAStageCols <= kTmemCols, "TMEM plan");
 
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    unsigned char* sB = base;               // BS x MT*128 (1024-byte aligned slots)
-    unsigned char* sRaw = sB + BS * BSLOT;  // RS x 16896
+    unsigned char* sB = base;               // ST x MT*128 (1024-byte aligned slots)
+    unsigned char* sRaw = sB + ST * BSLOT;  // RS x 16896
     uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + RS * kRawStageBytes);
     uint64_t* raw_full = bars;
     uint64_t* raw_empty = raw_full + RS;
     uint64_t* a_full = raw_empty + RS;
-    uint64_t* a_empty = a_full + AS;
-    uint64_t* b_full = a_empty + AS;
-    uint64_t* b_empty = b_full + BS;
-    uint64_t* acc_full = b_empty + BS;
+    uint64_t* b_full = a_full + ST;
+    uint64_t* st_empty = b_full + ST;
+    uint64_t* acc_full = st_empty + ST;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // warp index and TMEM base through a shuffle from lane 0: provably
+    // warp-uniform, so the tcgen05 / bulk-copy operands derived from them sit
+    // in uniform registers.  The role loops below run on whole warps for the
+    // same reason; one lane issues.
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
     const int S = args.S;
     const int tile = blockIdx.x / S;
     const int rank = S > 1 ? (int)cluster_rank() : 0;
@@ -261,15 +283,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < RS; ++i) {
             mbar_init(s_addr(&raw_full[i]), 1);
-            mbar_init(s_addr(&raw_empty[i]), 8);
+            mbar_init(s_addr(&raw_empty[i]), kDeqWarps);
         }
-        for (int i = 0; i < AS; ++i) {
-            mbar_init(s_addr(&a_full[i]), 8);
-            mbar_init(s_addr(&a_empty[i]), 1);
-        }
-        for (int i = 0; i < BS; ++i) {
+        for (int i = 0; i < ST; ++i) {
+            mbar_init(s_addr(&a_full[i]), kDeqWarps);
             mbar_init(s_addr(&b_full[i]), 1);
-            mbar_init(s_addr(&b_empty[i]), 1);
+            mbar_init(s_addr(&st_empty[i]), 1);
         }
         mbar_init(s_addr(acc_full), 1);
         *abort_flag = 0;
@@ -284,17 +303,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = __shfl_sync(0xffffffffu, *tmem_slot, 0);
 
     if (warp == 0) {
         // ------------------------------------------------ int4 unit producer
-        if (lane == 0) {
-            bool ok = true;
-            int it = 0;
-            for (; it < n_items; ++it) {
-                const int rs = it % RS;
-                if (it >= RS) ok = mbar_wait(s_addr(&raw_empty[rs]), ((it / RS) - 1) & 1);
-                if (!ok || *abort_flag) break;
+        bool ok = true;
+        int it = 0;
+        for (; it < n_items; ++it) {
+            const int rs = it % RS;
+            if (it >= RS) ok = mbar_wait(s_addr(&raw_empty[rs]), ((it / RS) - 1) & 1);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
+            if (lane == 0) {
                 const uint32_t rf = s_addr(&raw_full[rs]);
                 mbar_expect_tx(rf, kRawStageBytes);
                 for (int u = 0; u < 2; ++u) {
@@ -302,111 +322,151 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     bulk_g2s(s_addr(sRaw + rs * kRawStageBytes + u * kUnitBytes), src, kUnitBytes, rf);
                 }
             }
-            if (!ok) {
-                *abort_flag = 1;
-                record_timeout(args.status, 1);
-            }
-            // drain: the copies issued above complete before the CTA exits
-            if (it > 0) (void)mbar_wait(s_addr(&raw_full[(it - 1) % RS]), ((it - 1) / RS) & 1);
+            __syncwarp();
         }
-    } else if (warp == 14) {
+        if (!ok && lane == 0) {
+            *abort_flag = 1;
+            record_timeout(args.status, 1);
+        }
+        // drain: the copies issued above complete before the CTA exits
+        if (it > 0) (void)mbar_wait(s_addr(&raw_full[(it - 1) % RS]), ((it - 1) / RS) & 1);
+    } else if (warp == kBWarp) {
         // ------------------------------------------------ activation (B operand) producer
-        if (lane == 0) {
-            bool ok = true;
-            int j = 0;
-            for (; j < n_halves; ++j) {
-                const int s = j % BS;
-                if (j >= BS) ok = mbar_wait(s_addr(&b_empty[s]), ((j / BS) - 1) & 1);
-                if (!ok || *abort_flag) break;
-                const uint32_t bf = s_addr(&b_full[s]);
-                mbar_expect_tx(bf, BSLOT);
-                tma_load_2d(s_addr(sB + s * BSLOT), &tmap_x, (k0 + (j >> 1)) * 128 + (j & 1) * 64, m_tile * MT, bf);
+        // Rounds of ST half-steps with the stage index unrolled, so every
+        // shared-memory and TMEM address below is a fixed offset from a
+        // loop-invariant base.
+        bool ok = true, stop = false;
+        int j = 0;
+        for (int j0 = 0; j0 < n_halves && !stop; j0 += ST) {
+#pragma unroll
+            for (int s = 0; s < ST; ++s) {
+                j = j0 + s;
+                if (j >= n_halves) break;
+                if (j0 > 0) ok = mbar_wait(s_addr(&st_empty[s]), ((j0 / ST) - 1) & 1);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                    stop = true;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t bf = s_addr(&b_full[s]);
+                    mbar_expect_tx(bf, BSLOT);
+                    tma_load_2d(s_addr(sB + s * BSLOT), &tmap_x, (k0 + (j >> 1)) * 128 + (j & 1) * 64, m_tile * MT, bf);
+                }
+                __syncwarp();
+                ++j;
             }
-            if (!ok) {
-                *abort_flag = 1;
-                record_timeout(args.status, 5);
-            }
-            if (j > 0) (void)mbar_wait(s_addr(&b_full[(j - 1) % BS]), ((j - 1) / BS) & 1);
         }
+        if (!ok && lane == 0) {
+            *abort_flag = 1;
+            record_timeout(args.status, 5);
+        }
+        // j = half-steps issued; drain the last one
+        if (j > 0) (void)mbar_wait(s_addr(&b_full[(j - 1) % ST]), ((j - 1) / ST) & 1);
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            bool ok = true;
-            for (int j = 0; j < n_halves && ok; ++j) {
-                const int sa = j % AS, sb = j % BS;
-                ok = mbar_wait(s_addr(&a_full[sa]), (j / AS) & 1) && mbar_wait(s_addr(&b_full[sb]), (j / BS) & 1);
-                if (!ok || *abort_flag) {
+        // The descriptors are precomputed offsets of one base: an MMA whose
+        // operands are recomputed in the issue loop costs several times the
+        // tensor-pipe time of the instruction itself.
+        const uint64_t bdesc0 = sw128_desc(s_addr(sB));
+        const uint32_t a_base = tmem + A_COL0;
+        bool ok = true, timed_out = false, stop = false;
+        for (int j0 = 0; j0 < n_halves && !stop; j0 += ST) {
+            const uint32_t par = (uint32_t)(j0 / ST) & 1u;
+#pragma unroll
+            for (int s = 0; s < ST; ++s) {
+                const int j = j0 + s;
+                if (j >= n_halves) break;
+                ok = mbar_wait(s_addr(&a_full[s]), par) && mbar_wait(s_addr(&b_full[s]), par);
+                timed_out = !__all_sync(0xffffffffu, ok);
+                if (timed_out || __any_sync(0xffffffffu, *abort_flag != 0)) {
                     ok = false;
+                    stop = true;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = tmem + A_COL0 + (uint32_t)(sa * kAStageCols);
-                const uint32_t b0 = s_addr(sB + sb * BSLOT);
+                if (lane == 0) {
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t bd = sw128_desc(b0 + ks * 32);
+                    for (int ks = 0; ks < 4; ++ks) {
+                        // B: slot s, k16 slice ks (32 bytes into each 128-byte swizzled row)
+                        const uint64_t bd = bdesc0 + (uint64_t)((s * BSLOT + ks * 32) >> 4);
 #pragma unroll
-                    for (int q = 0; q < 2; ++q)  // unit q: A columns q*32 + ks*8 .. +8 (k16 = 8 columns)
-                        tc_mma_f16_ts(tmem + (uint32_t)(q * MT), a0 + (uint32_t)(q * 32 + ks * 8), bd, IDESC,
-                                      (j > 0 || ks > 0) ? 1u : 0u);
+                        for (int q = 0; q < 2; ++q)  // unit q: A columns q*32 + ks*8 .. +8 (k16 = 8 columns)
+                            tc_mma_f16_ts(tmem + (uint32_t)(q * MT),
+                                          a_base + (uint32_t)(s * kAStageCols + q * 32 + ks * 8), bd, IDESC,
+                                          (j > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    tc_commit(s_addr(&st_empty[s]));
                 }
-                tc_commit(s_addr(&a_empty[sa]));
-                tc_commit(s_addr(&b_empty[sb]));
+                __syncwarp();
             }
+        }
+        if (lane == 0) {
             if (ok) tc_commit(s_addr(acc_full));
             else {
                 *abort_flag = 1;
-                record_timeout(args.status, 2);
+                if (timed_out) record_timeout(args.status, 2);
             }
         }
-    } else if (warp >= 6) {
+    } else if (warp >= 2 && warp < 2 + kDeqWarps) {
         // ------------------------------------------------ dequant
-        // A warp may only touch TMEM lanes 32*(warp%4) .. +31, so warps 6-9
-        // cover the four lane quarters of unit 0 and warps 10-13 those of
-        // unit 1.  Thread = one weight row r of its unit.
-        const int q = (warp - 6) >> 2;
+        // A warp may only touch TMEM lanes 32*(warp%4) .. +31.  The four warps
+        // of one lane quarter split a half-step as (unit q, k-quarter kh): the
+        // thread = weight row r of unit q, 32 k (4 words, 16 TMEM columns).
+        const int dw = warp - 2;
+        const int q = (dw >> 2) & 1;
+        const int kh = dw >> 3;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(q * 32);
+        const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(q * 32 + kh * 16);
         const __half2 bias = __float2half2_rn(1032.0f);
         bool ok = true;
-        for (int it = 0; it < n_items && ok; ++it) {
-            const int rs = it % RS;
-            ok = mbar_wait(s_addr(&raw_full[rs]), (it / RS) & 1);
-            // warp-uniform decision: the tcgen05.st below is a .sync.aligned warp instruction
-            ok = __all_sync(0xffffffffu, ok && !*abort_flag);
-            if (!ok) break;
-            const unsigned char* unit = sRaw + rs * kRawStageBytes + q * kUnitBytes;
-            const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(unit + 8192 + r * 2));
-            for (int hk = 0; hk < 2; ++hk) {
-                const int j = 2 * it + hk;
-                const int s = j % AS;
-                if (j >= AS) ok = mbar_wait(s_addr(&a_empty[s]), ((j / AS) - 1) & 1);
+        // Rounds of ST k-steps = 2*ST half-steps, so the stage of half-step h
+        // of a round is the constant h % ST.
+        for (int it0 = 0; it0 < n_items && ok; it0 += ST) {
+#pragma unroll
+            for (int u = 0; u < ST; ++u) {
+                const int it = it0 + u;
+                if (it >= n_items) break;
+                const int rs = it % RS;
+                ok = mbar_wait(s_addr(&raw_full[rs]), (it / RS) & 1);
+                // warp-uniform decision: the tcgen05.st below is a .sync.aligned warp instruction
                 ok = __all_sync(0xffffffffu, ok && !*abort_flag);
                 if (!ok) break;
-                uint32_t wv[8];
+                const unsigned char* unit = sRaw + rs * kRawStageBytes + q * kUnitBytes;
+                const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(unit + 8192 + r * 2));
 #pragma unroll
-                for (int i = 0; i < 8; ++i)  // word (kc, r): k = kc*8 .. kc*8+7 of row r; lanes read consecutive words
-                    wv[i] = *reinterpret_cast<const uint32_t*>(unit + (((hk * 8 + i) * 128 + r) << 2));
-                uint32_t outw[32];  // column i*4+jj = fp16 pair (k = 8i+2jj, 8i+2jj+1) of this half
+                for (int hk = 0; hk < 2; ++hk) {
+                    const int s = (2 * u + hk) % ST;
+                    const int j = 2 * it + hk;
+                    if (j >= ST) ok = mbar_wait(s_addr(&st_empty[s]), ((j / ST) - 1) & 1);
+                    ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+                    if (!ok) break;
+                    uint32_t wv[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 4; ++i)  // word (kc, r): k = kc*8 .. kc*8+7 of row r; lanes read consecutive words
+                        wv[i] = *reinterpret_cast<const uint32_t*>(unit + (((hk * 8 + kh * 4 + i) * 128 + r) << 2));
+                    uint32_t outw[16];  // column i*4+jj = fp16 pair (k = 8i+2jj, 8i+2jj+1) of this k-quarter
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const uint32_t t = ((wv[i] >> (4 * jj)) & 0x000F000Fu) | 0x64006400u;
-                        __half2 hv = *reinterpret_cast<const __half2*>(&t);
-                        hv = __hmul2(__hsub2(hv, bias), s2);  // exact (u - 8), then one rounding of (u - 8) * s
-                        outw[i * 4 + jj] = *reinterpret_cast<uint32_t*>(&hv);
+                    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const uint32_t t = ((wv[i] >> (4 * jj)) & 0x000F000Fu) | 0x64006400u;
+                            __half2 hv = *reinterpret_cast<const __half2*>(&t);
+                            hv = __hmul2(__hsub2(hv, bias), s2);  // exact (u - 8), then one rounding of (u - 8) * s
+                            outw[i * 4 + jj] = *reinterpret_cast<uint32_t*>(&hv);
+                        }
                     }
+                    tc_st_x16(t_row + (uint32_t)(s * kAStageCols), outw);
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(s_addr(&a_full[s]));
                 }
-                tc_st_x32(t_row + (uint32_t)(s * kAStageCols), outw);
-                tc_wait_st();
-                tc_fence_before();
+                if (!ok) break;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(s_addr(&a_full[s]));
+                if (lane == 0) mbar_arrive(s_addr(&raw_empty[rs]));
             }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(s_addr(&raw_empty[rs]));
         }
         if (!ok) {
             *abort_flag = 1;
@@ -415,66 +475,81 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 
     // ---------------------------------------------------- epilogue (all threads)
-    const bool epi_warp = warp >= 2 && warp < 6;
-    const int quad = warp & 3;
-    bool acc_ok = true;
+    // Warps 2-13 (three per TMEM lane quarter) drain the accumulators into
+    // shared memory as [token][weight row] fp32 (the rings are idle now).  The
+    // tile then leaves by one TMA store per half (a TMA reduce-add for mode 1)
+    // when Y's rows are 16-byte aligned, else by coalesced plain stores.
+    const bool epi_warp = warp >= 2 && warp < 2 + kDeqWarps;
+    const int quad = warp & 3;       // TMEM lane quarter = weight rows quad*32 .. +31
+    const int eg = (warp - 2) >> 2;  // column chunks c = eg, eg + 4, ...
     if (epi_warp) {
-        acc_ok = mbar_wait(s_addr(acc_full), 0) && !*abort_flag;
-        if (!acc_ok) {
+        const bool acc_ok = __all_sync(0xffffffffu, mbar_wait(s_addr(acc_full), 0));
+        if (!acc_ok && lane == 0) {
             *abort_flag = 1;
             record_timeout(args.status, 3);
         }
         tc_fence_after();
     }
-    if (S == 1) {
-        if (epi_warp && acc_ok) {
-#pragma unroll 1
-            for (int q = 0; q < 2; ++q) {
-                const int n = n_tile * 256 + q * 128 + quad * 32 + lane;
-#pragma unroll 1
-                for (int c = 0; c < MT / 16; ++c) {
-                    uint32_t v[16];
-                    tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
-                    tc_wait_ld();
-                    if (n < args.N) {
+    __syncthreads();
+    const bool acc_ok = !*abort_flag;
+    // half q of the accumulator -> dst[token][128]
+    auto drain = [&](int q, float* dst) {
+        for (int c = eg; c < MT / 16; c += kDeqWarps / 4) {
+            uint32_t v[16];
+            tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
+            tc_wait_ld();
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int m = m_tile * MT + c * 16 + jj;
-                            if (m < args.M) {
-                                float* y = args.Y + (size_t)m * args.ldy + n;
-                                if (args.mode) *y += __uint_as_float(v[jj]);
-                                else *y = __uint_as_float(v[jj]);
-                            }
-                        }
+            for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[jj]);
+        }
+    };
+    if (S == 1) {
+        float* stage = reinterpret_cast<float*>(base);  // [2][MT][128]
+        if (epi_warp && acc_ok) {
+            drain(0, stage);
+            drain(1, stage + MT * 128);
+        }
+        fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
+        __syncthreads();
+        if (acc_ok) {
+            if (args.tma_out) {
+                if (threadIdx.x == 0) {
+                    for (int q = 0; q < 2; ++q)  // a half wholly past N has nothing to write
+                        if (n_tile * 256 + q * 128 < args.N)
+                            tma_out_2d(&tmap_y, s_addr(stage + q * MT * 128), n_tile * 256 + q * 128, m_tile * MT,
+                                       args.mode);
+                    bulk_commit();
+                    bulk_wait_read();
+                }
+            } else {
+                for (int idx = threadIdx.x; idx < 2 * MT * 128; idx += blockDim.x) {
+                    const int q = idx / (MT * 128), rem = idx - q * MT * 128;
+                    const int m = m_tile * MT + rem / 128, n = n_tile * 256 + q * 128 + (rem & 127);
+                    if (m < args.M && n < args.N) {
+                        float* y = args.Y + (size_t)m * args.ldy + n;
+                        if (args.mode) *y += stage[idx];
+                        else *y = stage[idx];
                     }
                 }
             }
         }
     } else if constexpr (reduce_fits<MT>()) {
-        // split-K: park this CTA's half-tile in its own shared memory (the A/B
-        // rings are idle once the accumulator is final), then every CTA sums a
-        // column slice over all S CTAs of the cluster through DSMEM.
+        // split-K: park this CTA's half-tile in its own shared memory, then
+        // every CTA sums a column slice over all S CTAs of the cluster through
+        // DSMEM, in rank order, and writes it out.
         float* red = reinterpret_cast<float*>(base);  // [MT][128]
+        float* outs = red + MT * 128;                 // [MT][cols] reduced slice
         const int cols = 128 / S;                     // S divides 128 (1, 2, 4, 8)
         const int vec_per_row = cols / 4;
         for (int q = 0; q < 2; ++q) {
-            if (epi_warp && acc_ok) {
-#pragma unroll 1
-                for (int c = 0; c < MT / 16; ++c) {
-                    uint32_t v[16];
-                    tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) red[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[jj]);
-                }
-            }
+            if (epi_warp && acc_ok) drain(q, red);
             __syncthreads();
             cluster_sync_all();
             const bool cluster_ok = !*abort_flag;
             if (cluster_ok) {
                 for (int idx = threadIdx.x; idx < MT * vec_per_row; idx += blockDim.x) {
                     const int mr = idx / vec_per_row;
-                    const int cl = rank * cols + (idx % vec_per_row) * 4;
+                    const int cv = (idx - mr * vec_per_row) * 4;
+                    const int cl = rank * cols + cv;
                     const uint32_t la = s_addr(red + mr * 128 + cl);
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (int p = 0; p < S; ++p) {
@@ -484,19 +559,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         acc.z += v.z;
                         acc.w += v.w;
                     }
-                    const int m = m_tile * MT + mr;
-                    const int n = n_tile * 256 + q * 128 + cl;
-                    if (m < args.M) {
-                        float* y = args.Y + (size_t)m * args.ldy + n;
-                        const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+                    if (args.tma_out) {
+                        *reinterpret_cast<float4*>(outs + mr * cols + cv) = acc;
+                    } else {
+                        const int m = m_tile * MT + mr;
+                        const int n = n_tile * 256 + q * 128 + cl;
+                        if (m < args.M) {
+                            float* y = args.Y + (size_t)m * args.ldy + n;
+                            const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (n + e < args.N) {
-                                if (args.mode) y[e] += vals[e];
-                                else y[e] = vals[e];
+                            for (int e = 0; e < 4; ++e) {
+                                if (n + e < args.N) {
+                                    if (args.mode) y[e] += vals[e];
+                                    else y[e] = vals[e];
+                                }
                             }
                         }
                     }
+                }
+            }
+            if (args.tma_out) {
+                fence_async_smem();
+                __syncthreads();
+                if (cluster_ok && threadIdx.x == 0 && n_tile * 256 + q * 128 + rank * cols < args.N) {
+                    tma_out_2d(&tmap_y, s_addr(outs), n_tile * 256 + q * 128 + rank * cols, m_tile * MT, args.mode);
+                    bulk_commit();
+                    bulk_wait_read();  // `outs` is rewritten for the next half
                 }
             }
             cluster_sync_all();  // peers are done reading before the next half overwrites `red`
@@ -629,6 +717,21 @@ int make_x_tmap(CUtensorMap* map, const void* X, int M, int K, int ldx, int MT) 
     return SPECDEC_OK;
 }
 
+// Output map: fp32 Y [M][ldy], box {128 / S, MT} (one reduced column slice of a
+// half tile).  Returns 0 when Y cannot be written by TMA.
+static int make_y_tmap(CUtensorMap* map, float* Y, int M, int N, int ldy, int MT, int S) {
+    auto enc = get_encode();
+    if (!enc || (reinterpret_cast<uintptr_t>(Y) & 15) != 0 || (ldy % 4) != 0) return 0;
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)ldy * 4};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / S), (cuuint32_t)MT};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Y, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 1 : 0;
+}
+
 // Token tile: the smallest that holds M; above 160 tokens, the one of 128 / 160
 // that pads M least (160 on a tie: fewer passes over the weights).
 int pick_mt(int M) {
@@ -652,12 +755,72 @@ static int num_sms() {
     return g_num_sms;
 }
 
-struct GemmPlan {
-    int MT, m_tiles, n_tiles, KG, S, grid;
-};
+template <int MT>
+static bool set_smem_attr() {
+    constexpr size_t smem = gemm_smem_bytes<MT>();
+    static_assert(smem <= (size_t)kSmemBudget, "shared memory plan exceeds the opt-in limit");
+    static_assert(reduce_fits<MT>(), "split-K reduction buffer does not fit in the rings");
+    // one CTA per SM: every CTA allocates all 512 TMEM columns, so two CTAs of
+    // one cluster must never share an SM
+    static_assert(smem > (size_t)kSmemBudget / 2, "shared memory plan must force one CTA per SM");
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(w4a16_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        attr = true;
+    }
+    return true;
+}
+
+// How many clusters of S CTAs the device runs at once.  Clusters must fit
+// inside one GPC, so for S = 8 this is fewer than SMs / 8; planning with
+// SMs / S would turn a one-wave grid into two waves.
+template <int MT>
+static int max_active_clusters(int S) {
+    static int cache[4] = {0, 0, 0, 0};
+    const int idx = S == 1 ? 0 : (S == 2 ? 1 : (S == 4 ? 2 : 3));
+    if (!cache[idx]) {
+        int n = 0;
+        if (S == 1) {
+            n = num_sms();
+        } else if (set_smem_attr<MT>()) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)(S * num_sms()));
+            cfg.blockDim = dim3(kGemmThreads);
+            cfg.dynamicSmemBytes = gemm_smem_bytes<MT>();
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = (unsigned)S;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&n, w4a16_tc_kernel<MT>, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+        }
+        cache[idx] = n > 0 ? n : num_sms() / S;
+    }
+    return cache[idx];
+}
+
+static int clusters_for(int MT, int S) {
+    switch (MT) {
+        case 16: return max_active_clusters<16>(S);
+        case 32: return max_active_clusters<32>(S);
+        case 64: return max_active_clusters<64>(S);
+        case 128: return max_active_clusters<128>(S);
+        default: return max_active_clusters<160>(S);
+    }
+}
 
 // Split factor S (CTAs per tile, a power of two <= 8 and <= KG) minimising
 // waves * (k-steps per CTA + setup), plus a penalty for the on-chip reduction.
+// A wave is as many clusters as the device co-schedules.
 GemmPlan plan_gemm(int M, int N, int K) {
     GemmPlan p;
     p.MT = pick_mt(M);
@@ -665,11 +828,11 @@ GemmPlan plan_gemm(int M, int N, int K) {
     p.n_tiles = (N + 255) / 256;
     p.KG = (K + 127) / 128;
     const int tiles = p.m_tiles * p.n_tiles;
-    const int sms = num_sms();
     double best = 1e30;
     p.S = 1;
     for (int S = 1; S <= kMaxSplit && S <= p.KG; S *= 2) {
-        const double waves = (double)((tiles * S + sms - 1) / sms);
+        const int per_wave = clusters_for(p.MT, S);
+        const double waves = (double)((tiles + per_wave - 1) / per_wave);
         const double items = (double)((p.KG + S - 1) / S);
         const double cost = waves * (items + 1.0) + (S > 1 ? 1.5 : 0.0);
         if (cost < best - 1e-9) {
@@ -682,17 +845,11 @@ GemmPlan plan_gemm(int M, int N, int K) {
 }
 
 template <int MT>
-static int launch_tc(const CUtensorMap& map, const GemmArgs& a, int grid, cudaStream_t s) {
+static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_y, const GemmArgs& a, int grid, cudaStream_t s) {
     constexpr size_t smem = gemm_smem_bytes<MT>();
-    static_assert(smem <= (size_t)kSmemBudget, "shared memory plan exceeds the opt-in limit");
-    static_assert(reduce_fits<MT>(), "split-K reduction buffer does not fit in the rings");
-    // one CTA per SM: every CTA allocates all 512 TMEM columns, so two CTAs of
-    // one cluster must never share an SM
-    static_assert(smem > (size_t)kSmemBudget / 2, "shared memory plan must force one CTA per SM");
-    static bool attr = false;
-    if (!attr) {
-        SD_CUDA(cudaFuncSetAttribute(w4a16_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
+    if (!set_smem_attr<MT>()) {
+        set_error("w4a16_gemm: cannot opt in to the shared memory the kernel needs");
+        return SPECDEC_ECUDA;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
@@ -706,7 +863,7 @@ static int launch_tc(const CUtensorMap& map, const GemmArgs& a, int grid, cudaSt
     attrs[0].val.clusterDim.z = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
-    SD_CUDA(cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<MT>, map, a));
+    SD_CUDA(cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<MT>, map, map_y, a));
     return SPECDEC_OK;
 }
 
@@ -729,12 +886,16 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
     a.ldy = ldy;
     a.mode = mode;
     a.status = device_status_ptr();
+    // Y leaves by TMA when its rows are 16-byte aligned; otherwise plain stores.
+    CUtensorMap map_y;
+    a.tma_out = make_y_tmap(&map_y, Y, M, N, ldy, p.MT, p.S);
+    if (!a.tma_out) memset(&map_y, 0, sizeof(map_y));
     switch (p.MT) {
-        case 16: return launch_tc<16>(map, a, p.grid, s);
-        case 32: return launch_tc<32>(map, a, p.grid, s);
-        case 64: return launch_tc<64>(map, a, p.grid, s);
-        case 128: return launch_tc<128>(map, a, p.grid, s);
-        case 160: return launch_tc<160>(map, a, p.grid, s);
+        case 16: return launch_tc<16>(map, map_y, a, p.grid, s);
+        case 32: return launch_tc<32>(map, map_y, a, p.grid, s);
+        case 64: return launch_tc<64>(map, map_y, a, p.grid, s);
+        case 128: return launch_tc<128>(map, map_y, a, p.grid, s);
+        case 160: return launch_tc<160>(map, map_y, a, p.grid, s);
         default: break;
     }
     set_error("w4a16_gemm: unsupported token tile");

@@ -15,19 +15,9 @@
 #include <vector>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace specdec {
-
-struct KVState {
-    int num_blocks, block_size, max_reqs, max_bpr;
-    int32_t* tables;  // [max_reqs, max_bpr], -1 padded
-    int32_t* nblk;    // [max_reqs], -1 = no table
-    int32_t* len;     // [max_reqs]
-    int32_t* ref;     // [num_blocks]
-    int32_t* ctx;     // [max_reqs] length before the last batch append
-    int32_t* scratch; // [max(num_blocks, max_reqs) * 4]
-    int32_t* status;  // [1] ENOMEM flag of the last batch append
-};
 
 constexpr int kKVThreads = 1024;
 

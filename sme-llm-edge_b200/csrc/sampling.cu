@@ -13,6 +13,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace specdec {
 
