@@ -6,9 +6,9 @@
 //
 // The path is HBM-bound, so the kernel is built around keeping enough bytes in
 // flight: warp 0 streams the split's KV blocks (16 tokens; K then V, each as
-// 64-column boxes with 128-byte swizzle) through an ST-deep ring with TMA
-// tensor loads, block numbers read from a copy of the block-table slice in
-// shared memory.  Consumer warps (m-tile mt, key group kg) take blocks
+// 64-column halves with 128-byte swizzle) through an ST-deep ring, one TMA
+// tensor load per block, block numbers read from a copy of the block-table
+// slice in shared memory.  Consumer warps (m-tile mt, key group kg) take blocks
 // j = kg, kg + KG, ...: scores and P.V on the tensor cores (m16n8k16, fp16 in,
 // fp32 accumulate, swizzle-aware ldmatrix) with an online base-2 softmax, then
 // release the stage.  Key groups are merged in shared memory; the S splits of
@@ -156,13 +156,8 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
                 if (phys < 0 || phys >= a.num_blocks) phys = 0;  // a malformed table reads block 0, never out of range
                 const uint32_t fb = s_addr(&full[s]);
                 mbar_expect_tx(fb, BLK);
-                const uint32_t dst = s_addr(ring + (size_t)s * BLK);
-#pragma unroll
-                for (int kv = 0; kv < 2; ++kv)
-#pragma unroll
-                    for (int hb = 0; hb < NBOX; ++hb)
-                        tma_load_2d(dst + (uint32_t)((kv * NBOX + hb) * kBox), &kv_map, hb * 64,
-                                    ((phys * 2 + kv) * a.Hkv + h) * 16, fb);
+                // the whole block (K and V, all column halves) in one request
+                tma_load_5d(s_addr(ring + (size_t)s * BLK), &kv_map, 0, h * 16, 0, 0, phys, fb);
             }
             __syncwarp();
         }
@@ -332,15 +327,28 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
         for (int idx = threadIdx.x; idx < (r1 - r0) * HD; idx += blockDim.x) {
             const int row = r0 + idx / HD, col = idx % HD;
             const uint32_t aM = s_addr(pML + row * 2), aO = s_addr(pO + (size_t)row * HD + col);
+            // every remote load is issued before any is used: one DSMEM round trip
+            float pm[8], pl[8], po[8];
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+                if (p < S) {
+                    pm[p] = ld_dsmem_f32(aM, (uint32_t)p);
+                    pl[p] = ld_dsmem_f32(aM + 4, (uint32_t)p);
+                    po[p] = ld_dsmem_f32(aO, (uint32_t)p);
+                }
             float M = -INFINITY;
-            for (int p = 0; p < S; ++p) M = fmaxf(M, ld_dsmem_f32(aM, (uint32_t)p));
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+                if (p < S) M = fmaxf(M, pm[p]);
             const float Muse = M == -INFINITY ? 0.f : M;
             float acc = 0.f, l = 0.f;
-            for (int p = 0; p < S; ++p) {  // rank order: deterministic
-                const float w = exp2f(ld_dsmem_f32(aM, (uint32_t)p) - Muse);
-                acc += ld_dsmem_f32(aO, (uint32_t)p) * w;
-                l += ld_dsmem_f32(aM + 4, (uint32_t)p) * w;
-            }
+#pragma unroll
+            for (int p = 0; p < 8; ++p)  // rank order: deterministic
+                if (p < S) {
+                    const float w = exp2f(pm[p] - Muse);
+                    acc += po[p] * w;
+                    l += pl[p] * w;
+                }
             const int r = row / a.G, g = row % a.G;
             a.out[(((size_t)(b * a.R + r) * a.Hq) + h * a.G + g) * HD + col] = __float2half_rn(l > 0.f ? acc / l : 0.f);
         }
@@ -445,7 +453,10 @@ static AttnPlan plan_attention(int B, int R, int G, int Hkv, int HD, int max_ctx
         }
     }
     if (p.ST == 0) p.ST = 8;
-    // Split count: minimise waves x blocks per CTA (the cluster merge is cheap).
+    // Split count: minimise waves x (blocks per CTA + a fixed cost per CTA).
+    // The fixed cost (prologue, ring fill, cluster merge, co-scheduling the
+    // cluster) was measured at about 48 blocks' worth of streaming time: with
+    // enough pairs to fill the device, one CTA per pair wins.
     const int pairs = B * Hkv;
     p.S = 1;
     long long best_cost = -1;
@@ -454,7 +465,7 @@ static AttnPlan plan_attention(int B, int R, int G, int Hkv, int HD, int max_ctx
         const size_t sm = attn_smem_bytes(HD, p.MT, p.ST, per);
         const int clusters = attn_clusters(HD, p.threads, sm, S);
         const long long waves = (pairs + clusters - 1) / clusters;
-        const long long cost = waves * (per + 2);
+        const long long cost = waves * (per + 48);
         if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             p.S = S;
@@ -477,17 +488,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 attn_encode() {
     return fn;
 }
 
-// The layer's pool [num_blocks][K|V][Hkv][16][HD] as a 2-D fp16 tensor of
-// rows ((block*2 + kv)*Hkv + head)*16 + token, HD columns; box 16 x 64.
+// The layer's pool [num_blocks][K|V][Hkv][16][HD] as a 5-D fp16 tensor
+// (innermost first): 64 columns, token row h*16 + t (all heads), column half,
+// K|V, block.  One box {64, 16, HD/64, 2, 1} is a whole 16-token block of one
+// head, landing in shared memory as [K|V][half][token][64] with 128-byte
+// swizzle -- the same layout as separate 16 x 64 boxes, in one request.
 static int make_kv_tmap(CUtensorMap* map, const __half* kv, int num_blocks, int Hkv, int HD) {
     auto enc = attn_encode();
     SD_CHECK(enc, SPECDEC_ENOTSUP, "cuTensorMapEncodeTiled unavailable");
     SD_CHECK((reinterpret_cast<uintptr_t>(kv) & 15) == 0, SPECDEC_EINVAL, "attention: KV pool must be 16-byte aligned");
-    cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)num_blocks * 2 * Hkv * 16};
-    cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
-    cuuint32_t box[2] = {64, 16};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(kv), dims, strides, box, estr,
+    const cuuint64_t row = (cuuint64_t)HD * 2, head_block = row * 16 * Hkv;
+    cuuint64_t dims[5] = {64, (cuuint64_t)Hkv * 16, (cuuint64_t)(HD / 64), 2, (cuuint64_t)num_blocks};
+    cuuint64_t strides[4] = {row, 128, head_block, 2 * head_block};
+    cuuint32_t box[5] = {64, 16, (cuuint32_t)(HD / 64), 2, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<__half*>(kv), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     SD_CHECK(r == CUDA_SUCCESS, SPECDEC_EINVAL, "attention: cuTensorMapEncodeTiled failed");

@@ -446,14 +446,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const int cv = (idx - mr * vec_per_row) * 4;
                     const int cl = rank * cols + cv;
                     const uint32_t la = s_addr(red + mr * 128 + cl);
+                    // all S remote loads in flight before the rank-order sum
+                    float4 v[kMaxSplit];
+#pragma unroll
+                    for (int p = 0; p < kMaxSplit; ++p)
+                        if (p < S) v[p] = ld_dsmem_f4(la, (uint32_t)p);
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int p = 0; p < S; ++p) {
-                        const float4 v = ld_dsmem_f4(la, (uint32_t)p);
-                        acc.x += v.x;
-                        acc.y += v.y;
-                        acc.z += v.z;
-                        acc.w += v.w;
-                    }
+#pragma unroll
+                    for (int p = 0; p < kMaxSplit; ++p)
+                        if (p < S) {
+                            acc.x += v[p].x;
+                            acc.y += v[p].y;
+                            acc.z += v[p].z;
+                            acc.w += v[p].w;
+                        }
                     if (args.tma_out) {
                         *reinterpret_cast<float4*>(outs + mr * cols + cv) = acc;
                     } else {
