@@ -11,6 +11,7 @@ the data path).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 8b|tree|14b|tiny]
     python bench.py --impl reference ...   # CPU restatement on the host cores
+    python bench.py --kernel gemm --shape 160,128256,4096   # one hot kernel (profiling)
 """
 from __future__ import annotations
 
@@ -255,10 +256,14 @@ def run_gpu(args, world, rank, local, pg):
     time.sleep(0.3)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if args.nvtx:
+        torch.cuda.nvtx.range_push("specdec_timed_steps")
     ev0.record(stream)
     for _ in range(args.steps):
         eng.step()
     ev1.record(stream)
+    if args.nvtx:
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop()
     barrier(pg, local)
@@ -337,6 +342,64 @@ def run_gpu(args, world, rank, local, pg):
     eng.close()
 
 
+# ------------------------------------------------------------ single-kernel mode
+def run_kernel(args):
+    """One hot kernel on synthetic inputs, for profiler captures: `--kernel gemm
+    --shape M,N,K` (W4A16 GEMM, random int4 weights) or `--kernel attention
+    --shape B,R,Hq,Hkv,hd,ctx` (verify attention over a shuffled paged KV pool).
+    Runs `--steps` timed launches after `--warmup` and prints the mean time;
+    this is a kernel timing, not the benchmark metric."""
+    import ctypes as C
+
+    import torch
+
+    import specdec as S
+
+    L = S.lib()
+    dims = [int(x) for x in args.shape.split(",")]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    if args.kernel == "gemm":
+        M, N, K = dims
+        packed = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
+        scales = (torch.rand((N, (K + 127) // 128), device="cuda", generator=g) * 0.01 + 0.001).half()
+        tiled = torch.empty(L.specdec_w4_tiled_bytes(N, K), dtype=torch.uint8, device="cuda")
+        S.check(L.specdec_w4_tile(ptr(packed), ptr(scales), N, K, ptr(tiled), None))
+        X = torch.randn((M, K), device="cuda", generator=g).half()
+        Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        call = lambda: L.specdec_w4a16_gemm(ptr(X), M, K, ptr(tiled), N, K, ptr(Y), N, 0, None, 0, None)  # noqa: E731
+        algo = {"bytes": N * K // 2 + N * ((K + 127) // 128) * 2, "flops": 2.0 * M * N * K}
+    else:
+        B, R, Hq, Hkv, hd, ctx = dims
+        max_blocks = (ctx + R + 15) // 16 + 1
+        nblk = B * max_blocks
+        pool = (torch.randn((nblk, 2, Hkv, 16, hd), device="cuda", generator=g) * 0.5).half()
+        perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(1)).to("cuda", torch.int32)
+        tables = perm.reshape(B, max_blocks).contiguous()
+        ctxs = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+        mask = torch.tensor([(1 << (r + 1)) - 1 for r in range(R)], dtype=torch.int64, device="cuda")
+        q = torch.randn((B * R, Hq, hd), device="cuda", generator=g).half()
+        out = torch.empty_like(q)
+        call = lambda: L.specdec_attention(ptr(q), ptr(pool), nblk, Hkv, hd, ptr(tables), max_blocks,  # noqa: E731
+                                           ptr(ctxs), ptr(mask), B, R, Hq, ptr(out), None, 0, None)
+        algo = {"bytes": B * Hkv * (ctx + R) * hd * 2 * 2}
+    for _ in range(args.warmup):
+        S.check(call())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / args.steps * 1e3
+    res = {"kernel": args.kernel, "shape": args.shape, "us_per_launch": round(us, 2),
+           "gbs_algorithmic": round(algo["bytes"] / us / 1e3, 1)}
+    if "flops" in algo:
+        res["tflops"] = round(algo["flops"] / us / 1e6, 1)
+    print(json.dumps(res), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -345,8 +408,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--nvtx", action="store_true", help="mark the timed steps with an NVTX range (profiler filter)")
+    ap.add_argument("--kernel", choices=["gemm", "attention"], help="time one hot kernel instead of the step")
+    ap.add_argument("--shape", default="160,128256,4096", help="--kernel shape: M,N,K or B,R,Hq,Hkv,hd,ctx")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.kernel:
+        run_kernel(args)
+        return
     if args.impl == "reference":
         # CPU arm: rank 0 alone measures; other ranks exit without work
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))

@@ -113,67 +113,129 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const __half* _
 }
 
 // out = fp16(x * 1/sqrt(mean(x^2) + eps)) (unit norm weights), lib.rs:21-36.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, int ldx, int H, float eps, __half* __restrict__ out,
-                               int ldo) {
+// One block per row; the row is read from HBM once (float4) into shared
+// memory, summed in a fixed order, and written from there.
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __restrict__ x, int ldx, int H, float eps,
+                                                              __half* __restrict__ out, int ldo) {
+    extern __shared__ float row_s[];  // [H]
     __shared__ float red[32];
     const float* xr = x + (size_t)blockIdx.x * ldx;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-    ss = block_sum<float>(ss, red);
+    const bool vec = (H & 3) == 0 && (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (vec) {
+        for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+            const float4 v = reinterpret_cast<const float4*>(xr)[i];
+            reinterpret_cast<float4*>(row_s)[i] = v;
+            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+        }
+    } else {
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const float v = xr[i];
+            row_s[i] = v;
+            ss = __fadd_rn(ss, __fmul_rn(v, v));
+        }
+    }
+    ss = block_sum<float>(ss, red);  // ends with a barrier: row_s is complete
     const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)H), eps));
     __half* o = out + (size_t)blockIdx.x * ldo;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = __float2half_rn(__fmul_rn(xr[i], r));
+    if (vec && (ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
+        for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+            const float4 v = reinterpret_cast<const float4*>(row_s)[i];
+            __half2 a = __floats2half2_rn(__fmul_rn(v.x, r), __fmul_rn(v.y, r));
+            __half2 b = __floats2half2_rn(__fmul_rn(v.z, r), __fmul_rn(v.w, r));
+            uint2 w;
+            w.x = *reinterpret_cast<uint32_t*>(&a);
+            w.y = *reinterpret_cast<uint32_t*>(&b);
+            reinterpret_cast<uint2*>(o)[i] = w;
+        }
+    } else {
+        for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = __float2half_rn(__fmul_rn(row_s[i], r));
+    }
+}
+static void launch_rmsnorm(const float* x, int ldx, int rows, int H, float eps, __half* out, int ldo, cudaStream_t s) {
+    const size_t smem = (size_t)H * sizeof(float);
+    static size_t opted = 48 * 1024;
+    if (smem > opted) {  // rows wider than 12288 need the opt-in
+        cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        opted = smem;
+    }
+    rmsnorm_kernel<<<rows, kNormThreads, smem, s>>>(x, ldx, H, eps, out, ldo);
 }
 
 // RoPE on q and k (rotate-half pairs d, d + hd/2), K/V into their paged slots,
-// q to fp16.  qkv rows are [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].
+// q to fp16.  qkv rows are [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].  A thread
+// handles two adjacent dims (d, d+1) of a head: float2 loads, half2 stores.
 __global__ void rope_kv_kernel(const float* __restrict__ qkv, int ldq, const int32_t* __restrict__ pos,
                                const int32_t* __restrict__ slot, const int32_t* __restrict__ tables, int max_blocks,
                                int R, const float* __restrict__ cos_t, const float* __restrict__ sin_t, int Hq,
                                int Hkv, int hd, __half* __restrict__ kv_layer, __half* __restrict__ q16) {
     const int m = blockIdx.x;
     const int b = m / R;
-    const int half = hd / 2;
+    const int half = hd / 2, hp = hd / 4;  // pairs of dims per rotated half
     const float* row = qkv + (size_t)m * ldq;
     const float* cs = cos_t + (size_t)pos[m] * half;
     const float* sn = sin_t + (size_t)pos[m] * half;
     const int s = slot[m];
     const int blk = tables[(size_t)b * max_blocks + s / 16];
     const int off = s % 16;
-    const int npairs = (Hq + Hkv) * half;
-    for (int i = threadIdx.x; i < npairs + Hkv * hd; i += blockDim.x) {
-        if (i < npairs) {
-            const int h = i / half, d = i % half;
-            const float a = row[h * hd + d], c = row[h * hd + d + half];
-            const float lo = __fsub_rn(__fmul_rn(a, cs[d]), __fmul_rn(c, sn[d]));
-            const float hi = __fadd_rn(__fmul_rn(c, cs[d]), __fmul_rn(a, sn[d]));
-            if (h < Hq) {
-                q16[(size_t)m * Hq * hd + h * hd + d] = __float2half_rn(lo);
-                q16[(size_t)m * Hq * hd + h * hd + d + half] = __float2half_rn(hi);
-            } else {
-                const int kh = h - Hq;
-                __half* dst = kv_layer + ((((size_t)blk * 2 + 0) * Hkv + kh) * 16 + off) * hd;
-                dst[d] = __float2half_rn(lo);
-                dst[d + half] = __float2half_rn(hi);
-            }
+    const int nrot = (Hq + Hkv) * hp;
+    for (int i = threadIdx.x; i < nrot + Hkv * (hd / 2); i += blockDim.x) {
+        if (i < nrot) {
+            const int h = i / hp, d = (i % hp) * 2;
+            const float2 a = *reinterpret_cast<const float2*>(row + h * hd + d);
+            const float2 c = *reinterpret_cast<const float2*>(row + h * hd + d + half);
+            const float2 cv = *reinterpret_cast<const float2*>(cs + d);
+            const float2 sv = *reinterpret_cast<const float2*>(sn + d);
+            const __half2 lo = __floats2half2_rn(__fsub_rn(__fmul_rn(a.x, cv.x), __fmul_rn(c.x, sv.x)),
+                                                 __fsub_rn(__fmul_rn(a.y, cv.y), __fmul_rn(c.y, sv.y)));
+            const __half2 hi = __floats2half2_rn(__fadd_rn(__fmul_rn(c.x, cv.x), __fmul_rn(a.x, sv.x)),
+                                                 __fadd_rn(__fmul_rn(c.y, cv.y), __fmul_rn(a.y, sv.y)));
+            __half* dst = h < Hq ? q16 + (size_t)m * Hq * hd + h * hd
+                                 : kv_layer + ((((size_t)blk * 2 + 0) * Hkv + (h - Hq)) * 16 + off) * hd;
+            *reinterpret_cast<__half2*>(dst + d) = lo;
+            *reinterpret_cast<__half2*>(dst + d + half) = hi;
         } else {
-            const int j = i - npairs;
+            const int j = (i - nrot) * 2;
             const int vh = j / hd, d = j % hd;
+            const float2 v = *reinterpret_cast<const float2*>(row + (Hq + Hkv) * hd + j);
             __half* dst = kv_layer + ((((size_t)blk * 2 + 1) * Hkv + vh) * 16 + off) * hd;
-            dst[d] = __float2half_rn(row[(Hq + Hkv) * hd + j]);
+            *reinterpret_cast<__half2*>(dst + d) = __floats2half2_rn(v.x, v.y);
         }
     }
 }
 
 // h = fp16(silu(g) * u), gu rows [gate (F) | up (F)] (main.cpp:246-249, 338-340).
+// Grid (ceil(F / 4 / 256), rows): one thread per 4 outputs.
 __global__ void swiglu_kernel(const float* __restrict__ gu, int F, __half* __restrict__ h) {
-    const int m = blockIdx.x;
+    const int m = blockIdx.y;
+    const int i0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i0 >= F) return;
     const float* g = gu + (size_t)m * 2 * F;
-    for (int i = threadIdx.x; i < F; i += blockDim.x) {
-        const float gv = g[i];
+    __half* hr = h + (size_t)m * F;
+    auto one = [](float gv, float uv) {
         const float sv = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
-        h[(size_t)m * F + i] = __float2half_rn(__fmul_rn(sv, g[F + i]));
+        return __fmul_rn(sv, uv);
+    };
+    if ((F & 3) == 0 && i0 + 3 < F) {
+        const float4 gv = *reinterpret_cast<const float4*>(g + i0);
+        const float4 uv = *reinterpret_cast<const float4*>(g + F + i0);
+        __half2 a = __floats2half2_rn(one(gv.x, uv.x), one(gv.y, uv.y));
+        __half2 b = __floats2half2_rn(one(gv.z, uv.z), one(gv.w, uv.w));
+        uint2 w;
+        w.x = *reinterpret_cast<uint32_t*>(&a);
+        w.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(hr + i0) = w;
+    } else {
+        for (int i = i0; i < i0 + 4 && i < F; ++i) hr[i] = __float2half_rn(one(g[i], g[F + i]));
     }
+}
+static void launch_swiglu(const float* gu, int rows, int F, __half* h, cudaStream_t s) {
+    dim3 grid((unsigned)((F + 1023) / 1024), (unsigned)rows);
+    swiglu_kernel<<<grid, 256, 0, s>>>(gu, F, h);
 }
 
 // Chain verify rows: [pending, d_0 .. d_{k-1}] at positions ctx .. ctx + k.
@@ -465,7 +527,7 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
     for (int l = 0; l < c.layers; ++l) {
         const WeightSet& w = e->layers[l];
         __half* kv_l = e->kv + e->layer_stride * l;
-        rmsnorm_kernel<<<M, 256, 0, s>>>(e->x, H, H, c.rms_eps, e->xn, H);
+        launch_rmsnorm(e->x, H, M, H, c.rms_eps, e->xn, H, s);
         ENG_LAUNCH("rmsnorm_kernel");
         ENG_TRY(gemm(e, e->xn, M, H, w.qkv, e->NQKV, e->qkv, e->NQKV, 0));
         rope_kv_kernel<<<M, 256, 0, s>>>(e->qkv, e->NQKV, e->pos, e->slot, kvs.tables, e->max_blocks, Rrows,
@@ -477,15 +539,15 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
                                  e->rc.max_ctx, s));
         prof_mark(e, CAT_ATTENTION);
         ENG_TRY(gemm(e, e->att, M, e->qd, w.o, H, e->x, H, 1));
-        rmsnorm_kernel<<<M, 256, 0, s>>>(e->x, H, H, c.rms_eps, e->xn, H);
+        launch_rmsnorm(e->x, H, M, H, c.rms_eps, e->xn, H, s);
         ENG_LAUNCH("rmsnorm_kernel");
         ENG_TRY(gemm(e, e->xn, M, H, w.gu, 2 * F, e->gu, 2 * F, 0));
-        swiglu_kernel<<<M, 256, 0, s>>>(e->gu, F, e->hmid);
+        launch_swiglu(e->gu, M, F, e->hmid, s);
         ENG_LAUNCH("swiglu_kernel");
         ENG_TRY(gemm(e, e->hmid, M, F, w.down, H, e->x, H, 1));
     }
     if (want_logits) {
-        rmsnorm_kernel<<<M, 256, 0, s>>>(e->x, H, H, c.rms_eps, e->xn, H);
+        launch_rmsnorm(e->x, H, M, H, c.rms_eps, e->xn, H, s);
         ENG_LAUNCH("rmsnorm_kernel");
         ENG_TRY(gemm(e, e->xn, M, H, e->lm, c.vocab, e->logits, c.vocab, 0));
     }
@@ -502,11 +564,11 @@ int draft_hidden_and_logits(specdec_engine* e, int levels) {
         const int head = i < c.n_mtp_heads ? i : c.n_mtp_heads - 1;
         const float* src = i == 0 ? e->h0 : e->dh + (size_t)(i - 1) * H;
         const int lds = i == 0 ? H : levels * H;
-        rmsnorm_kernel<<<B, 256, 0, s>>>(src, lds, H, c.rms_eps, e->dxn, H);
+        launch_rmsnorm(src, lds, B, H, c.rms_eps, e->dxn, H, s);
         ENG_LAUNCH("rmsnorm_kernel");
         ENG_TRY(gemm(e, e->dxn, B, H, e->heads[head], H, e->dh + (size_t)i * H, levels * H, 0));
     }
-    rmsnorm_kernel<<<B * levels, 256, 0, s>>>(e->dh, H, H, c.rms_eps, e->dxn, H);
+    launch_rmsnorm(e->dh, H, B * levels, H, c.rms_eps, e->dxn, H, s);
     ENG_LAUNCH("rmsnorm_kernel");
     ENG_TRY(gemm(e, e->dxn, B * levels, H, e->lm, c.vocab, e->dlogits, c.vocab, 0));
     return SPECDEC_OK;
