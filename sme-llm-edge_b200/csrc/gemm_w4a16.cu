@@ -69,8 +69,7 @@ template <int MT>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
     return 1024 /*align slack*/ + (size_t)stages_for(MT) * MT * 128 + (size_t)kRawStages * kRawStageBytes + 2048;
 }
-// the epilogue reuses the B and raw rings: two MT x 128 fp32 tiles (both halves,
-// or the parked partial plus the reduced slice of a split tile)
+// the epilogue reuses the B and raw rings: two MT x 128 fp32 tiles (both halves)
 template <int MT>
 __host__ __device__ constexpr bool reduce_fits() {
     return (size_t)stages_for(MT) * MT * 128 + (size_t)kRawStages * kRawStageBytes >= (size_t)2 * MT * 128 * 4;
@@ -132,7 +131,7 @@ struct GemmArgs {
     int M, N, KG, m_tiles, S;
     float* Y;
     int ldy, mode;
-    int tma_out;  // tmap_y is valid: Y leaves by TMA (box {128 / S, MT})
+    int tma_out;  // tmap_y is valid: Y leaves by TMA (box {128, MT / S})
     DeviceStatus* status;
 };
 
@@ -397,100 +396,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[jj]);
         }
     };
-    if (S == 1) {
-        float* stage = reinterpret_cast<float*>(base);  // [2][MT][128]
-        if (epi_warp && acc_ok) {
-            drain(0, stage);
-            drain(1, stage + MT * 128);
-        }
-        fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
-        __syncthreads();
-        if (acc_ok) {
-            if (args.tma_out) {
-                if (threadIdx.x == 0) {
-                    for (int q = 0; q < 2; ++q)  // a half wholly past N has nothing to write
-                        if (n_tile * 256 + q * 128 < args.N)
-                            tma_out_2d(&tmap_y, s_addr(stage + q * MT * 128), n_tile * 256 + q * 128, m_tile * MT,
-                                       args.mode);
-                    bulk_commit();
-                    bulk_wait_read();
-                }
-            } else {
-                for (int idx = threadIdx.x; idx < 2 * MT * 128; idx += blockDim.x) {
-                    const int q = idx / (MT * 128), rem = idx - q * MT * 128;
-                    const int m = m_tile * MT + rem / 128, n = n_tile * 256 + q * 128 + (rem & 127);
-                    if (m < args.M && n < args.N) {
-                        float* y = args.Y + (size_t)m * args.ldy + n;
-                        if (args.mode) *y += stage[idx];
-                        else *y = stage[idx];
-                    }
-                }
-            }
-        }
-    } else if constexpr (reduce_fits<MT>()) {
-        // split-K: park this CTA's half-tile in its own shared memory, then
-        // every CTA sums a column slice over all S CTAs of the cluster through
-        // DSMEM, in rank order, and writes it out.
-        float* red = reinterpret_cast<float*>(base);  // [MT][128]
-        float* outs = red + MT * 128;                 // [MT][cols] reduced slice
-        const int cols = 128 / S;                     // S divides 128 (1, 2, 4, 8)
-        const int vec_per_row = cols / 4;
-        for (int q = 0; q < 2; ++q) {
-            if (epi_warp && acc_ok) drain(q, red);
+    // Both halves of this CTA's accumulator are parked in shared memory as
+    // [half][token][128].  The CTA's share of the output is token rows
+    // [r0, r0 + MT/S) of both halves: with S > 1 it sums those rows over the S
+    // CTAs of the cluster through DSMEM, in rank order, in place (each CTA
+    // overwrites only its own rows, which no peer reads), then writes them.
+    float* stage = reinterpret_cast<float*>(base);  // [2][MT][128]
+    const int rows = MT / S, r0 = rank * rows;       // S divides MT (16 | MT, S <= 8)
+    if (epi_warp && acc_ok) {
+        drain(0, stage);
+        drain(1, stage + MT * 128);
+    }
+    if constexpr (reduce_fits<MT>()) {
+        if (S > 1) {
             __syncthreads();
-            cluster_sync_all();
-            const bool cluster_ok = !*abort_flag;
-            if (cluster_ok) {
-                for (int idx = threadIdx.x; idx < MT * vec_per_row; idx += blockDim.x) {
-                    const int mr = idx / vec_per_row;
-                    const int cv = (idx - mr * vec_per_row) * 4;
-                    const int cl = rank * cols + cv;
-                    const uint32_t la = s_addr(red + mr * 128 + cl);
-                    // all S remote loads in flight before the rank-order sum
-                    float4 v[kMaxSplit];
+            cluster_sync_all();  // every CTA's partial tile is parked
+            if (!*abort_flag) {
+                const int nvec = 2 * rows * 32;  // float4 columns of (half, row)
+                for (int idx = threadIdx.x; idx < nvec; idx += blockDim.x) {
+                    const int q = idx / (rows * 32), rem = idx - q * rows * 32;
+                    float* p = stage + (size_t)q * MT * 128 + (r0 + (rem >> 5)) * 128 + (rem & 31) * 4;
+                    const uint32_t la = s_addr(p);
+                    float4 v[kMaxSplit];  // all S remote loads in flight before the sum
 #pragma unroll
-                    for (int p = 0; p < kMaxSplit; ++p)
-                        if (p < S) v[p] = ld_dsmem_f4(la, (uint32_t)p);
+                    for (int pr = 0; pr < kMaxSplit; ++pr)
+                        if (pr < S) v[pr] = ld_dsmem_f4(la, (uint32_t)pr);
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                    for (int p = 0; p < kMaxSplit; ++p)
-                        if (p < S) {
-                            acc.x += v[p].x;
-                            acc.y += v[p].y;
-                            acc.z += v[p].z;
-                            acc.w += v[p].w;
+                    for (int pr = 0; pr < kMaxSplit; ++pr)
+                        if (pr < S) {
+                            acc.x += v[pr].x;
+                            acc.y += v[pr].y;
+                            acc.z += v[pr].z;
+                            acc.w += v[pr].w;
                         }
-                    if (args.tma_out) {
-                        *reinterpret_cast<float4*>(outs + mr * cols + cv) = acc;
-                    } else {
-                        const int m = m_tile * MT + mr;
-                        const int n = n_tile * 256 + q * 128 + cl;
-                        if (m < args.M) {
-                            float* y = args.Y + (size_t)m * args.ldy + n;
-                            const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                if (n + e < args.N) {
-                                    if (args.mode) y[e] += vals[e];
-                                    else y[e] = vals[e];
-                                }
-                            }
-                        }
-                    }
+                    *reinterpret_cast<float4*>(p) = acc;
                 }
             }
-            if (args.tma_out) {
-                fence_async_smem();
-                __syncthreads();
-                if (cluster_ok && threadIdx.x == 0 && n_tile * 256 + q * 128 + rank * cols < args.N) {
-                    tma_out_2d(&tmap_y, s_addr(outs), n_tile * 256 + q * 128 + rank * cols, m_tile * MT, args.mode);
-                    bulk_commit();
-                    bulk_wait_read();  // `outs` is rewritten for the next half
-                }
-            }
-            cluster_sync_all();  // peers are done reading before the next half overwrites `red`
         }
     }
+    fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
+    __syncthreads();
+    if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
+        if (args.tma_out) {
+            if (threadIdx.x == 0) {
+                for (int q = 0; q < 2; ++q)  // a half wholly past N has nothing to write
+                    if (n_tile * 256 + q * 128 < args.N)
+                        tma_out_2d(&tmap_y, s_addr(stage + (size_t)q * MT * 128 + r0 * 128), n_tile * 256 + q * 128,
+                                   m_tile * MT + r0, args.mode);
+                bulk_commit();
+                bulk_wait_read();
+            }
+        } else {
+            for (int idx = threadIdx.x; idx < 2 * rows * 128; idx += blockDim.x) {
+                const int q = idx / (rows * 128), rem = idx - q * rows * 128;
+                const int r = r0 + rem / 128, c = rem & 127;
+                const int m = m_tile * MT + r, n = n_tile * 256 + q * 128 + c;
+                if (m < args.M && n < args.N) {
+                    float* y = args.Y + (size_t)m * args.ldy + n;
+                    const float v = stage[(size_t)q * MT * 128 + r * 128 + c];
+                    if (args.mode) *y += v;
+                    else *y = v;
+                }
+            }
+        }
+    }
+    if (S > 1) cluster_sync_all();  // peers have finished reading this CTA's parked tile
 
     tc_fence_before();
     __syncthreads();
@@ -618,14 +589,14 @@ int make_x_tmap(CUtensorMap* map, const void* X, int M, int K, int ldx, int MT) 
     return SPECDEC_OK;
 }
 
-// Output map: fp32 Y [M][ldy], box {128 / S, MT} (one reduced column slice of a
+// Output map: fp32 Y [M][ldy], box {128, MT / S} (one CTA's token rows of a
 // half tile).  Returns 0 when Y cannot be written by TMA.
 static int make_y_tmap(CUtensorMap* map, float* Y, int M, int N, int ldy, int MT, int S) {
     auto enc = get_encode();
     if (!enc || (reinterpret_cast<uintptr_t>(Y) & 15) != 0 || (ldy % 4) != 0) return 0;
     cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)ldy * 4};
-    cuuint32_t box[2] = {(cuuint32_t)(128 / S), (cuuint32_t)MT};
+    cuuint32_t box[2] = {128, (cuuint32_t)(MT / S)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Y, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
