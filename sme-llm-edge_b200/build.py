@@ -34,7 +34,7 @@ FLAGS = [
 def _compile(src: str) -> str:
     obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
     srcp = os.path.join(CSRC, src)
-    deps = [srcp, os.path.join(CSRC, "common.cuh"), os.path.join(CSRC, "internal.h"), os.path.join(ROOT, "include", "specdec.h")]
+    deps = [srcp, os.path.join(CSRC, "common.cuh"), os.path.join(CSRC, "internal.h"), os.path.join(CSRC, "ptx.cuh"), os.path.join(CSRC, "tcgen05.cuh"), os.path.join(ROOT, "include", "specdec.h")]
     if os.path.exists(obj) and all(os.path.getmtime(obj) >= os.path.getmtime(d) for d in deps):
         return obj
     cmd = [NVCC, *FLAGS, "-c", srcp, "-o", obj]

@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "ptx.cuh"
+#include "tcgen05.cuh"
 
 namespace specdec {
 
@@ -356,6 +357,403 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
     }
 }
 
+// ------------------------------------------------------------ tcgen05 variant
+// For R * G <= 128 query rows (decode / chain verify).  The query tile is the
+// M = 128 side of every MMA, so the scores S = Q.K^T and the output O = P.V
+// accumulate in TMEM and the CUDA cores only run the softmax:
+//   warps 0-3  softmax, one thread per query row (TMEM lane): scale, mask,
+//              row max, P = exp2(s - m) in fp16 into TMEM, running sum.  O is
+//              rescaled only when a row's max grows by more than 2^8, so P
+//              stays below 256 and most groups never touch O.
+//   warp 5     TMA producer: per 16-token block one load for K (per 64-column
+//              half, into a K ring laid out [half][stage][16][64] so that four
+//              consecutive stages are one 64-row K-major operand) and one for V
+//   warp 6     TMEM allocator and MMA issuer: for a group of four blocks,
+//              S[g%2] = Q.K^T (M=128, N=64, K=HD); then O += P.V for the group
+//              before (M=128, N=HD, K=16 per block, P from TMEM, V MN-major)
+//   (warp 4 idles.)  A warp's SM sub-partition is its index mod 4 and TMEM
+//   lane quarter q belongs to sub-partition q, so the producer and the MMA
+//   issuer sit on sub-partitions 1 and 2, away from rows 0-31, the only busy
+//   softmax warp for up to 32 query rows: a single issuing thread slows down
+//   markedly when a busy warp shares its sub-partition.
+// Two CTAs share an SM (one per sequence x KV head leaves most SMs with two),
+// so each allocates only 256 TMEM columns: O [0, HD), S (one 64-column
+// buffer, released by the softmax right after it is read) at 128, P (2 x 32)
+// at 192.  The query tile is an SW128 K-major shared-memory operand.  The MMA
+// issuer polls and issues whichever of the next Q.K^T (its blocks landed and
+// S is free) and the next P.V (its P was written) is ready.
+constexpr int kTcStages = 8;  // two groups of four blocks in flight
+constexpr int kTcTmemCols = 256;
+constexpr int kTcThreads = 224;
+constexpr int kTcLoadWarp = 5, kTcMmaWarp = 6;
+constexpr uint32_t kTmemO = 0, kTmemS = 128, kTmemP = 192;
+
+// 2^x on the special-function unit (2 ulp); the result is rounded to fp16 next.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Bit c = key key0 + c is visible: it exists (c < nkeys, key < L) and is a
+// context key (key < ctx) or a new key whose bit is set in the row's mask.
+__device__ __forceinline__ uint64_t group_visibility(int key0, int ctx, int L, int nkeys, uint64_t rmask) {
+    auto low_bits = [](int k) -> uint64_t {  // bits [0, k), k clamped to [0, 64]
+        return k <= 0 ? 0ull : (k >= 64 ? ~0ull : ((1ull << k) - 1ull));
+    };
+    const int d = key0 - ctx;  // new-key index of bit 0 (negative: the group starts in the context)
+    uint64_t fresh = 0ull;     // bit c = mask bit d + c
+    if (d >= 0) fresh = d < 64 ? (rmask >> d) : 0ull;
+    else fresh = -d < 64 ? (rmask << (-d)) : 0ull;
+    return (low_bits(ctx - key0) | fresh) & low_bits(L - key0) & low_bits(nkeys);
+}
+
+__host__ __device__ constexpr size_t attn_tc_smem_bytes(int HD, int max_per) {
+    return 1024 + (size_t)(HD / 64) * 16384 /* Q */ + (size_t)kTcStages * 2 * (HD / 64) * kBox /* K + V */ +
+           (size_t)((max_per + 3) & ~3) * 4 + (size_t)(2 * kTcStages + 8) * 8 + 16;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+    constexpr int NBOX = HD / 64;
+    constexpr int ST = kTcStages;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sQ = base;                             // [NBOX][128 rows][128 B], swizzled K-major
+    unsigned char* sK = sQ + NBOX * 16384;                // [NBOX][ST][16][128 B]
+    unsigned char* sV = sK + (size_t)NBOX * ST * kBox;    // [ST][NBOX][16][128 B]
+    int* tbl = reinterpret_cast<int*>(sV + (size_t)ST * NBOX * kBox);
+    uint64_t* full = reinterpret_cast<uint64_t*>(tbl + ((a.max_per + 3) & ~3));
+    uint64_t* empty = full + ST;
+    uint64_t* s_full = empty + ST;   // QK of a group landed in S
+    uint64_t* s_free = s_full + 1;   // the softmax read S (4 warps)
+    uint64_t* p_full = s_free + 1;   // [2] softmax wrote P[g%2] (4 warps)
+    uint64_t* pv_done = p_full + 2;  // [2] P.V of a group finished
+    uint64_t* o_final = pv_done + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
+    const int S = a.S;
+    const int split = S > 1 ? (int)cluster_rank() : 0;
+    const int pair = blockIdx.x / S;
+    const int b = pair / a.Hkv, kvh = pair % a.Hkv;
+    const int ctx = a.ctx_len[b];
+    const int L = ctx + a.R;
+    const int nb = min((L + 15) / 16, a.max_blocks);
+    const int per = (nb + S - 1) / S;
+    const int blo = min(nb, split * per), bhi = min(nb, blo + per);
+    const int n = min(bhi - blo, a.max_per);
+    const int ngroups = (n + 3) / 4;
+
+    // ---- Q tile rows qi = r * G + g (zero past QR), written in the 128B-swizzled K-major layout
+    for (int idx = threadIdx.x; idx < 128 * (HD / 8); idx += blockDim.x) {
+        const int qi = idx / (HD / 8), c8 = idx % (HD / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (qi < a.QR) {
+            const int r = qi / a.G, g = qi % a.G;
+            v = *reinterpret_cast<const uint4*>(a.q + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + c8 * 8);
+        }
+        *reinterpret_cast<uint4*>(sQ + (c8 >> 3) * 16384 + qi * 128 + (((c8 & 7) ^ (qi & 7)) << 4)) = v;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) tbl[i] = a.tables[(size_t)b * a.max_blocks + blo + i];
+    fence_async_smem();  // Q is read by the tensor cores (async proxy)
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ST; ++i) {
+            mbar_init(s_addr(&full[i]), 1);
+            mbar_init(s_addr(&empty[i]), 1);
+        }
+        mbar_init(s_addr(s_full), 1);
+        mbar_init(s_addr(s_free), 4);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(s_addr(&p_full[i]), 4);
+            mbar_init(s_addr(&pv_done[i]), 1);
+        }
+        mbar_init(s_addr(o_final), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kTcMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_addr(tmem_slot)),
+                     "r"(kTcTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = __shfl_sync(0xffffffffu, *tmem_slot, 0);
+
+    const int quarter = warp & 3;
+    const int qi = quarter * 32 + lane;                    // softmax warps: this thread's query row
+    const bool soft = warp < 4;
+    const bool rows_here = soft && quarter * 32 < a.QR;  // warp holds at least one real row
+    float m_used = -INFINITY, l_sum = 0.f;
+
+    if (warp == kTcLoadWarp) {
+        // ------------------------------------------------ KV producer
+        bool ok = true;
+        int j = 0;
+        for (; j < n; ++j) {
+            const int s = j % ST;
+            if (j >= ST) ok = mbar_wait(s_addr(&empty[s]), ((j / ST) - 1) & 1);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
+            if (lane == 0) {
+                int phys = tbl[j];
+                if (phys < 0 || phys >= a.num_blocks) phys = 0;  // a malformed table reads block 0, never out of range
+                const uint32_t fb = s_addr(&full[s]);
+                mbar_expect_tx(fb, 2 * NBOX * kBox);
+#pragma unroll
+                for (int hb = 0; hb < NBOX; ++hb)
+                    tma_load_5d(s_addr(sK + ((size_t)hb * ST + s) * kBox), &kmap, 0, kvh * 16, hb, 0, phys, fb);
+                tma_load_5d(s_addr(sV + (size_t)s * NBOX * kBox), &vmap, 0, kvh * 16, 0, 1, phys, fb);
+            }
+            __syncwarp();
+        }
+        if (!ok && lane == 0) {
+            *abort_flag = 1;
+            record_timeout(a.status, 13);
+        }
+        if (j > 0) (void)mbar_wait(s_addr(&full[(j - 1) % ST]), ((j - 1) / ST) & 1);
+    } else if (warp == kTcMmaWarp) {
+        // ------------------------------------------------ MMA issuer
+        // Issues Q.K^T of group gq once its blocks landed and the softmax has
+        // read S for group gq-1, and P.V of group gp once its P is in TMEM,
+        // whichever is ready first.
+        const uint32_t qb = s_addr(sQ), kb = s_addr(sK), vb = s_addr(sV);
+        bool ok = true, timed_out = false;
+        int gq = 0, gp = 0;
+        uint64_t t_idle = 0;
+        while (gp < ngroups) {
+            bool progressed = false;
+            if (gq < ngroups && gq <= gp + 1) {
+                const int nbg = min(4, n - 4 * gq);
+                const int st0 = (4 * gq) % ST;  // ST is a multiple of 4: a group never wraps
+                bool ready = gq == 0 || mbar_try(s_addr(s_free), (gq - 1) & 1);
+                for (int i = 0; i < nbg; ++i) ready = ready && mbar_try(s_addr(&full[st0 + i]), ((4 * gq + i) / ST) & 1);
+                if (__all_sync(0xffffffffu, ready)) {
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t idesc = idesc_f16(128, 16 * nbg);
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; ++kk)
+                            tc_mma_f16_ss(tmem + kTmemS, sw128_desc(qb + (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32)),
+                                          sw128_desc(kb + (uint32_t)(((kk >> 2) * ST + st0) * kBox + (kk & 3) * 32)),
+                                          idesc, kk > 0 ? 1u : 0u);
+                        tc_commit(s_addr(s_full));
+                    }
+                    __syncwarp();
+                    ++gq;
+                    progressed = true;
+                }
+            }
+            if (gp < gq && __all_sync(0xffffffffu, mbar_try(s_addr(&p_full[gp & 1]), (gp >> 1) & 1))) {
+                const int nbg = min(4, n - 4 * gp);
+                tc_fence_after();
+                if (lane == 0) {
+                    for (int i = 0; i < nbg; ++i) {
+                        const int s = (4 * gp + i) % ST;
+                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + (uint32_t)((gp & 1) * 32 + i * 8),
+                                      sw128_mn_desc(vb + (uint32_t)(s * NBOX * kBox), kBox, 1024),
+                                      idesc_f16_bmn(128, HD), (gp > 0 || i > 0) ? 1u : 0u);
+                    }
+                    tc_commit(s_addr(&pv_done[gp & 1]));
+                    for (int i = 0; i < nbg; ++i) tc_commit(s_addr(&empty[(4 * gp + i) % ST]));
+                }
+                __syncwarp();
+                ++gp;
+                progressed = true;
+            }
+            if (progressed) {
+                t_idle = 0;
+            } else {
+                // bounded: give up after ~2 s without progress
+                const uint64_t now = gtimer();
+                if (t_idle == 0) t_idle = now;
+                timed_out = __any_sync(0xffffffffu, now - t_idle > 2000000000ull);
+                if (timed_out || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (lane == 0) {
+            if (ok) tc_commit(s_addr(o_final));
+            else {
+                *abort_flag = 1;
+                if (timed_out) record_timeout(a.status, 14);
+                mbar_arrive(s_addr(o_final));  // release the softmax warps' final wait
+            }
+        }
+    } else if (soft) {
+        // ------------------------------------------------ softmax, one thread per query row
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        const uint64_t rmask = qi < a.QR ? a.mask[qi / a.G] : ~0ull;
+        bool ok = true;
+        for (int g = 0; g < ngroups; ++g) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_addr(s_full), g & 1));
+            if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
+            tc_fence_after();
+            if (!rows_here) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_addr(s_free));
+            } else {
+                uint32_t sv[64];
+                tc_ld_x32(t_lane + kTmemS, sv);
+                tc_ld_x32(t_lane + kTmemS + 32, sv + 32);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_addr(s_free));  // S may be overwritten by the next Q.K^T
+                const int nkeys = 16 * min(4, n - 4 * g);
+                const int key0 = (blo + 4 * g) * 16;
+                // visibility of the group's 64 keys as one word: context keys,
+                // then the new keys this row may see, cut at L and at the group end
+                const uint64_t vis = group_visibility(key0, ctx, L, nkeys, rmask);
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    const float x = ((vis >> c) & 1ull) ? __uint_as_float(sv[c]) * a.scale_log2 : -INFINITY;
+                    sv[c] = __float_as_uint(x);
+                    mx = fmaxf(mx, x);
+                }
+                const bool grow = mx > m_used + 8.0f;  // also when the row had no visible key yet
+                const float m_new = grow ? mx : m_used;
+                const float alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+                const float muse = m_new == -INFINITY ? 0.f : m_new;
+                uint32_t pw[32];
+                float sum = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const __half2 h = __floats2half2_rn(ex2_approx(__uint_as_float(sv[2 * j]) - muse),
+                                                        ex2_approx(__uint_as_float(sv[2 * j + 1]) - muse));
+                    sum += __low2float(h) + __high2float(h);
+                    pw[j] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                // P[g%2] was last read by P.V of group g-2
+                if (g >= 2) ok = mbar_wait(s_addr(&pv_done[g & 1]), ((g - 2) >> 1) & 1);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+                tc_st_x32(t_lane + kTmemP + (uint32_t)((g & 1) * 32), pw);
+                // O holds groups < g; rescale it once P.V of group g-1 has landed
+                if (g > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(s_addr(&pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1));
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int c0 = 0; c0 < HD; c0 += 32) {
+                        uint32_t ov[32];
+                        tc_ld_x32(t_lane + kTmemO + (uint32_t)c0, ov);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                        tc_st_x32(t_lane + kTmemO + (uint32_t)c0, ov);
+                    }
+                }
+                l_sum = l_sum * alpha + sum;
+                m_used = m_new;
+                tc_wait_st();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_addr(&p_full[g & 1]));
+        }
+        if (!ok && lane == 0) {
+            *abort_flag = 1;
+            record_timeout(a.status, 15);
+        }
+        // every MMA has finished (and read its shared-memory operands) after this
+        (void)__all_sync(0xffffffffu, mbar_wait(s_addr(o_final), 0));
+        tc_fence_after();
+    }
+    __syncthreads();  // the Q tile and the rings are free from here on
+
+    // ---- output: this CTA's O rows; one CTA writes, a cluster merges through DSMEM
+    float* pO = reinterpret_cast<float*>(base);  // [128][HD]
+    float* pML = pO + 128 * HD;                  // [128][2] = (m, l)
+    const bool valid = !*abort_flag;
+    if (rows_here && valid) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < HD; c0 += 32) {
+            uint32_t ov[32];
+            tc_ld_x32(tmem + ((uint32_t)(quarter * 32) << 16) + kTmemO + (uint32_t)c0, ov);
+            tc_wait_ld();
+            if (qi < a.QR) {
+                if (S == 1) {
+                    const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
+                    const int r = qi / a.G, g = qi % a.G;
+                    __half* dst = a.out + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + c0;
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8) {
+                        uint4 w;
+                        uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const float x0 = n > 0 ? __uint_as_float(ov[e + 2 * k]) * inv : 0.f;
+                            const float x1 = n > 0 ? __uint_as_float(ov[e + 2 * k + 1]) * inv : 0.f;
+                            const __half2 h = __floats2half2_rn(x0, x1);
+                            wp[k] = *reinterpret_cast<const uint32_t*>(&h);
+                        }
+                        *reinterpret_cast<uint4*>(dst + e) = w;
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) pO[(size_t)qi * HD + c0 + e] = n > 0 ? __uint_as_float(ov[e]) : 0.f;
+                }
+            }
+        }
+        if (S > 1 && qi < a.QR) {
+            pML[qi * 2 + 0] = m_used;
+            pML[qi * 2 + 1] = l_sum;
+        }
+    }
+    if (S > 1) {
+        __syncthreads();
+        cluster_sync_all();
+        const int r0 = split * a.QR / S, r1 = (split + 1) * a.QR / S;
+        if (valid) {
+            for (int idx = threadIdx.x; idx < (r1 - r0) * HD; idx += blockDim.x) {
+                const int row = r0 + idx / HD, col = idx % HD;
+                const uint32_t aM = s_addr(pML + row * 2), aO = s_addr(pO + (size_t)row * HD + col);
+                float pm[8], pl[8], po[8];
+#pragma unroll
+                for (int p = 0; p < 8; ++p)
+                    if (p < S) {
+                        pm[p] = ld_dsmem_f32(aM, (uint32_t)p);
+                        pl[p] = ld_dsmem_f32(aM + 4, (uint32_t)p);
+                        po[p] = ld_dsmem_f32(aO, (uint32_t)p);
+                    }
+                float M = -INFINITY;
+#pragma unroll
+                for (int p = 0; p < 8; ++p)
+                    if (p < S) M = fmaxf(M, pm[p]);
+                const float Muse = M == -INFINITY ? 0.f : M;
+                float acc = 0.f, l = 0.f;
+#pragma unroll
+                for (int p = 0; p < 8; ++p)  // rank order: deterministic
+                    if (p < S) {
+                        const float w = exp2f(pm[p] - Muse);
+                        acc += po[p] * w;
+                        l += pl[p] * w;
+                    }
+                const int r = row / a.G, g = row % a.G;
+                a.out[(((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + col] =
+                    __float2half_rn(l > 0.f ? acc / l : 0.f);
+            }
+        }
+        cluster_sync_all();  // peers keep their partials until every rank has read them
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kTcMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
+    }
+}
+
 // ------------------------------------------------------------ host side
 struct AttnPlan {
     int MT, KG, QRP, threads, S, ST, max_per;
@@ -493,14 +891,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 attn_encode() {
 // K|V, block.  One box {64, 16, HD/64, 2, 1} is a whole 16-token block of one
 // head, landing in shared memory as [K|V][half][token][64] with 128-byte
 // swizzle -- the same layout as separate 16 x 64 boxes, in one request.
-static int make_kv_tmap(CUtensorMap* map, const __half* kv, int num_blocks, int Hkv, int HD) {
+// `halves` / `kvs` = how many column halves / K|V planes one box spans.
+static int make_kv_tmap(CUtensorMap* map, const __half* kv, int num_blocks, int Hkv, int HD, int halves = -1,
+                        int kvs = 2) {
+    if (halves < 0) halves = HD / 64;
     auto enc = attn_encode();
     SD_CHECK(enc, SPECDEC_ENOTSUP, "cuTensorMapEncodeTiled unavailable");
     SD_CHECK((reinterpret_cast<uintptr_t>(kv) & 15) == 0, SPECDEC_EINVAL, "attention: KV pool must be 16-byte aligned");
     const cuuint64_t row = (cuuint64_t)HD * 2, head_block = row * 16 * Hkv;
     cuuint64_t dims[5] = {64, (cuuint64_t)Hkv * 16, (cuuint64_t)(HD / 64), 2, (cuuint64_t)num_blocks};
     cuuint64_t strides[4] = {row, 128, head_block, 2 * head_block};
-    cuuint32_t box[5] = {64, 16, (cuuint32_t)(HD / 64), 2, 1};
+    cuuint32_t box[5] = {64, 16, (cuuint32_t)halves, (cuuint32_t)kvs, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<__half*>(kv), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -512,6 +913,74 @@ static int make_kv_tmap(CUtensorMap* map, const __half* kv, int num_blocks, int 
 // The kernel needs no global workspace (splits are merged on chip).
 size_t attention_workspace(int, int, int, int, int, int) { return 0; }
 
+static const void* attn_tc_fn(int HD) {
+    return HD == 128 ? reinterpret_cast<const void*>(attn_tc_kernel<128>) : reinterpret_cast<const void*>(attn_tc_kernel<64>);
+}
+
+// tcgen05 variant: split count from the same cost model as the legacy kernel.
+static AttnPlan plan_attention_tc(int B, int R, int Hkv, int HD, int max_ctx) {
+    AttnPlan p;
+    p.MT = 8;
+    p.KG = 1;
+    p.QRP = 128;
+    p.threads = kTcThreads;
+    p.ST = kTcStages;
+    const int nb_max = (max_ctx + R + 15) / 16;
+    const int pairs = B * Hkv;
+    static bool opted[2] = {false, false};
+    if (!opted[HD == 128]) {
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaFuncSetAttribute(attn_tc_fn(HD), cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        opted[HD == 128] = true;
+    }
+    p.S = 1;
+    long long best_cost = -1;
+    for (int S = 1; S <= 8 && S <= nb_max; ++S) {
+        const int per = (nb_max + S - 1) / S;
+        const size_t sm = attn_tc_smem_bytes(HD, per);
+        int clusters = 0;
+        {
+            static std::mutex mu;
+            static std::map<std::tuple<int, size_t, int>, int> cache;
+            std::lock_guard<std::mutex> lk(mu);
+            auto key = std::make_tuple(HD, sm, S);
+            auto it = cache.find(key);
+            if (it != cache.end()) {
+                clusters = it->second;
+            } else {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3((unsigned)(S * 148));
+                cfg.blockDim = dim3(kTcThreads);
+                cfg.dynamicSmemBytes = sm;
+                cudaLaunchAttribute at[1];
+                at[0].id = cudaLaunchAttributeClusterDimension;
+                at[0].val.clusterDim.x = (unsigned)S;
+                at[0].val.clusterDim.y = 1;
+                at[0].val.clusterDim.z = 1;
+                cfg.attrs = at;
+                cfg.numAttrs = 1;
+                if (cudaOccupancyMaxActiveClusters(&clusters, attn_tc_fn(HD), &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    clusters = 0;
+                }
+                if (clusters <= 0) clusters = 148 / S > 0 ? 148 / S : 1;
+                cache[key] = clusters;
+            }
+        }
+        const long long waves = (pairs + clusters - 1) / clusters;
+        const long long cost = waves * (per + 48);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            p.S = S;
+        }
+    }
+    p.max_per = (nb_max + p.S - 1) / p.S;
+    p.smem = attn_tc_smem_bytes(HD, p.max_per);
+    return p;
+}
+
 int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, int Hkv, int HD, const int32_t* tables,
                      int max_blocks, const int32_t* ctx_len, const uint64_t* mask, int B, int R, int Hq, __half* out,
                      void* ws, size_t ws_bytes, int max_ctx, cudaStream_t s) {
@@ -520,6 +989,50 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
     SD_CHECK(HD == 64 || HD == 128, SPECDEC_EINVAL, "attention: head_dim must be 64 or 128");
     SD_CHECK(Hkv > 0 && Hq % Hkv == 0 && R >= 1 && R <= 64, SPECDEC_EINVAL, "attention: bad head / row counts");
     SD_CHECK(num_blocks > 0 && max_blocks > 0, SPECDEC_EINVAL, "attention: empty block pool or table");
+    if (R * (Hq / Hkv) <= 128) {
+        // up to 128 query rows: the tcgen05 kernel
+        AttnPlan p = plan_attention_tc(B, R, Hkv, HD, max_ctx);
+        CUtensorMap kmap, vmap;
+        int rc = make_kv_tmap(&kmap, kv_layer, num_blocks, Hkv, HD, 1, 1);
+        if (!rc) rc = make_kv_tmap(&vmap, kv_layer, num_blocks, Hkv, HD, HD / 64, 1);
+        if (rc) return rc;
+        AttnArgs a = {};
+        a.q = q;
+        a.Hkv = Hkv;
+        a.Hq = Hq;
+        a.G = Hq / Hkv;
+        a.num_blocks = num_blocks;
+        a.tables = tables;
+        a.max_blocks = max_blocks;
+        a.ctx_len = ctx_len;
+        a.mask = mask;
+        a.B = B;
+        a.R = R;
+        a.QR = R * a.G;
+        a.MT = p.MT;
+        a.KG = p.KG;
+        a.S = p.S;
+        a.ST = p.ST;
+        a.max_per = p.max_per;
+        a.out = out;
+        a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)HD));
+        a.status = device_status_ptr();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(B * Hkv * p.S));
+        cfg.blockDim = dim3((unsigned)p.threads);
+        cfg.dynamicSmemBytes = p.smem;
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)p.S;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (HD == 128) SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<128>, kmap, vmap, a));
+        else SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<64>, kmap, vmap, a));
+        return SPECDEC_OK;
+    }
     AttnPlan p = plan_attention(B, R, Hq / Hkv, Hkv, HD, max_ctx);
     SD_CHECK(p.MT <= 16, SPECDEC_EINVAL, "attention: R * G must be <= 256");
     SD_CHECK(attn_merge_fits(HD, p.MT, p.KG, p.ST), SPECDEC_EINVAL, "attention: merge area does not fit");
