@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
     uint64_t* empty = full + ST;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + ST);
 
+    pdl_trigger();  // a following GEMM may start streaming its weights
     const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
     const int S = a.S;
     const int split = S > 1 ? (int)cluster_rank() : 0;
@@ -435,6 +436,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+    pdl_trigger();  // a following GEMM may start streaming its weights
     const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
     const int S = a.S;
     const int split = S > 1 ? (int)cluster_rank() : 0;

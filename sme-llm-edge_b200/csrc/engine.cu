@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace specdec {
 
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
                                                               __half* __restrict__ out, int ldo) {
     extern __shared__ float row_s[];  // [H]
     __shared__ float red[32];
+    pdl_trigger();  // a following GEMM may start streaming its weights
     const float* xr = x + (size_t)blockIdx.x * ldx;
     float ss = 0.f;
     const bool vec = (H & 3) == 0 && (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
@@ -211,6 +213,7 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int ldq, const int
 // h = fp16(silu(g) * u), gu rows [gate (F) | up (F)] (main.cpp:246-249, 338-340).
 // Grid (ceil(F / 4 / 256), rows): one thread per 4 outputs.
 __global__ void swiglu_kernel(const float* __restrict__ gu, int F, __half* __restrict__ h) {
+    pdl_trigger();  // a following GEMM may start streaming its weights
     const int m = blockIdx.y;
     const int i0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i0 >= F) return;
@@ -496,7 +499,7 @@ int gemm(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int
     int rc = make_x_tmap(&map, X, M, K, K, p.MT);
     if (rc) return rc;
     ++e->kernels_per_step;
-    rc = gemm_launch(map, p, w, M, N, Y, ldy, mode, e->gemm_ws, e->stream);
+    rc = gemm_launch(map, p, w, M, N, Y, ldy, mode, e->gemm_ws, e->stream, /*pdl=*/true);
     prof_mark(e, e->gemm_cat);
     return rc;
 }

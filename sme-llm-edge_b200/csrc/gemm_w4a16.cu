@@ -82,6 +82,7 @@ struct GemmArgs {
     float* Y;
     int ldy, mode;
     int tma_out;  // tmap_y is valid: Y leaves by TMA (box {128, MT / S})
+    int pdl;      // launched as a programmatic dependent: only the weights may be read before pdl_wait()
     DeviceStatus* status;
 };
 
@@ -149,8 +150,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = __shfl_sync(0xffffffffu, *tmem_slot, 0);
 
+    pdl_trigger();  // the next kernel may start its prologue
     if (warp == 0) {
         // ------------------------------------------------ int4 unit producer
+        // (weights: read before pdl_wait -- they are written once, before any step)
         bool ok = true;
         int it = 0;
         for (; it < n_items; ++it) {
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (it > 0) (void)mbar_wait(s_addr(&raw_full[(it - 1) % RS]), ((it - 1) / RS) & 1);
     } else if (warp == kBWarp) {
         // ------------------------------------------------ activation (B operand) producer
+        if (args.pdl) pdl_wait();  // X is written by the kernel before this one
         // Rounds of ST half-steps with the stage index unrolled, so every
         // shared-memory and TMEM address below is a fixed offset from a
         // loop-invariant base.
@@ -386,6 +390,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     }
     fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
+    if (args.pdl) pdl_wait();  // Y may still be read or written by earlier kernels
     __syncthreads();
     if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
         if (args.tma_out) {
@@ -678,13 +683,15 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_y, const Gem
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attrs[1];
+    cudaLaunchAttribute attrs[2];
     attrs[0].id = cudaLaunchAttributeClusterDimension;
     attrs[0].val.clusterDim.x = (unsigned)a.S;
     attrs[0].val.clusterDim.y = 1;
     attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = a.pdl ? 2 : 1;
     SD_CUDA(cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<MT>, map, map_y, a));
     return SPECDEC_OK;
 }
@@ -695,7 +702,7 @@ size_t gemm_workspace_bytes(const GemmPlan&) { return 0; }
 size_t gemm_workspace_bound(int, int, int) { return 0; }
 
 int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
-                int mode, void* ws, cudaStream_t s) {
+                int mode, void* ws, cudaStream_t s, bool pdl) {
     (void)ws;
     GemmArgs a;
     a.w = reinterpret_cast<const uint8_t*>(w_tiled);
@@ -707,6 +714,7 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
     a.Y = Y;
     a.ldy = ldy;
     a.mode = mode;
+    a.pdl = pdl ? 1 : 0;
     a.status = device_status_ptr();
     // Y leaves by TMA when its rows are 16-byte aligned; otherwise plain stores.
     CUtensorMap map_y;
@@ -773,7 +781,7 @@ extern "C" int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void*
     CUtensorMap map;
     int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
     if (rc) return rc;
-    return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, nullptr, as_stream(stream));
+    return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, nullptr, as_stream(stream), false);
 }
 
 extern "C" int specdec_w4a16_gemm_simt(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y,

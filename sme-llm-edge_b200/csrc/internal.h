@@ -26,8 +26,11 @@ struct GemmPlan {
 };
 GemmPlan plan_gemm(int M, int N, int K);
 int make_x_tmap(CUtensorMap* map, const void* X, int M, int K, int ldx, int MT);
+// pdl: launch as a programmatic dependent of the previous kernel in the stream
+// (its weight stream starts before that kernel has finished; only for weights
+// that no kernel in flight writes).
 int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
-                int mode, void* ws, cudaStream_t s);
+                int mode, void* ws, cudaStream_t s, bool pdl = false);
 size_t gemm_workspace_bound(int max_m, int max_n, int max_k);
 size_t w4_tiled_bytes(int N, int K);
 

@@ -122,6 +122,11 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
     return v;
 }
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue now / wait until the kernels this one depends on have completed and
+// their memory is visible.  Both are no-ops outside such a launch.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // marks the device status word SPECDEC_ETIMEOUT; `where` names the wait that gave up (last reporter)
 __device__ __forceinline__ void record_timeout(DeviceStatus* st, int where) {
     if (st) {
