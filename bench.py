@@ -116,23 +116,15 @@ def dist_setup():
 
 
 def reduce_max(pg, x: float, local: int) -> float:
-    if pg is None:
-        return x
-    import torch
+    from specdec.dist import reduce_max as rmax
 
-    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-    pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    return float(t.item())
+    return rmax(pg, x, f"cuda:{local}")
 
 
 def reduce_sum(pg, x: float, local: int) -> float:
-    if pg is None:
-        return x
-    import torch
+    from specdec.dist import reduce_sum as rsum
 
-    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-    pg.all_reduce(t, op=pg.ReduceOp.SUM)
-    return float(t.item())
+    return rsum(pg, x, f"cuda:{local}")
 
 
 def barrier(pg, local):
@@ -143,13 +135,20 @@ def barrier(pg, local):
         torch.cuda.synchronize()
 
 
-def ctx_lengths(cfg, rank):
+def ctx_lengths(cfg, rank, world=1):
+    """Context lengths of this rank's sequences: the global batch (batch per
+    GPU x world) is drawn once and sharded by request."""
+    from specdec.dist import shard_range
+
     B = cfg["batch"]
     if cfg.get("ragged"):
         lo, hi = cfg["ragged"]
-        rng = np.random.default_rng(cfg["seed"] * 1000 + rank)
-        return rng.integers(lo, hi + 1, B).astype(np.int32)
-    return np.full(B, cfg["ctx"], np.int32)
+        rng = np.random.default_rng(cfg["seed"] * 1000)
+        glob = rng.integers(lo, hi + 1, B * world).astype(np.int32)
+    else:
+        glob = np.full(B * world, cfg["ctx"], np.int32)
+    a, b = shard_range(B * world, world, rank)
+    return glob[a:b]
 
 
 def workload_bytes_flops(shape, ctx, rows, weight_bytes):
@@ -238,7 +237,7 @@ def run_gpu(args, world, rank, local, pg):
     torch.cuda.set_device(local)
     cfg = dict(CONFIGS[args.config])
     shape = S.MODEL_SHAPES[cfg["shape"]]
-    ctx = ctx_lengths(cfg, rank)
+    ctx = ctx_lengths(cfg, rank, world)
     extra = (args.warmup + 2 * args.steps + 8) * 65
     eng = S.Engine(shape, batch=cfg["batch"], draft_len=cfg["draft_len"] or 4, max_ctx=int(ctx.max()) + extra,
                    temperature=cfg["temperature"], top_p=1.0, seed=cfg["seed"] + 1000 * rank,
