@@ -382,7 +382,8 @@ def run_kernel(args):
         perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(1)).to("cuda", torch.int32)
         tables = perm.reshape(B, max_blocks).contiguous()
         ctxs = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
-        mask = torch.tensor([(1 << (r + 1)) - 1 for r in range(R)], dtype=torch.int64, device="cuda")
+        causal = np.array([(1 << (r + 1)) - 1 for r in range(R)], dtype=np.uint64)  # row r sees new keys 0..r
+        mask = torch.from_numpy(causal.view(np.int64)).to("cuda")
         q = torch.randn((B * R, Hq, hd), device="cuda", generator=g).half()
         out = torch.empty_like(q)
         call = lambda: L.specdec_attention(ptr(q), ptr(pool), nblk, Hkv, hd, ptr(tables), max_blocks,  # noqa: E731

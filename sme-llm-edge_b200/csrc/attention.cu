@@ -440,8 +440,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
     const int S = a.S;
     const int split = S > 1 ? (int)cluster_rank() : 0;
-    const int pair = blockIdx.x / S;
+    // cluster = (pair, 128-row tile of the query rows); a.MT = number of row tiles
+    const int pair = (blockIdx.x / S) / a.MT, mtile = (blockIdx.x / S) % a.MT;
     const int b = pair / a.Hkv, kvh = pair % a.Hkv;
+    const int row0 = mtile * 128;                      // first query row of this tile
+    const int QR = min(128, a.QR - row0);              // rows of this tile
     const int ctx = a.ctx_len[b];
     const int L = ctx + a.R;
     const int nb = min((L + 15) / 16, a.max_blocks);
@@ -450,12 +453,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int n = min(bhi - blo, a.max_per);
     const int ngroups = (n + 3) / 4;
 
-    // ---- Q tile rows qi = r * G + g (zero past QR), written in the 128B-swizzled K-major layout
+    // ---- Q tile rows row0 + qi = r * G + g (zero past QR), written in the 128B-swizzled K-major layout
     for (int idx = threadIdx.x; idx < 128 * (HD / 8); idx += blockDim.x) {
         const int qi = idx / (HD / 8), c8 = idx % (HD / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (qi < a.QR) {
-            const int r = qi / a.G, g = qi % a.G;
+        if (qi < QR) {
+            const int r = (row0 + qi) / a.G, g = (row0 + qi) % a.G;
             v = *reinterpret_cast<const uint4*>(a.q + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + c8 * 8);
         }
         *reinterpret_cast<uint4*>(sQ + (c8 >> 3) * 16384 + qi * 128 + (((c8 & 7) ^ (qi & 7)) << 4)) = v;
@@ -490,7 +493,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int quarter = warp & 3;
     const int qi = quarter * 32 + lane;                    // softmax warps: this thread's query row
     const bool soft = warp < 4;
-    const bool rows_here = soft && quarter * 32 < a.QR;  // warp holds at least one real row
+    const bool rows_here = soft && quarter * 32 < QR;  // warp holds at least one real row
     float m_used = -INFINITY, l_sum = 0.f;
 
     if (warp == kTcLoadWarp) {
@@ -592,7 +595,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     } else if (soft) {
         // ------------------------------------------------ softmax, one thread per query row
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-        const uint64_t rmask = qi < a.QR ? a.mask[qi / a.G] : ~0ull;
+        const uint64_t rmask = qi < QR ? a.mask[(row0 + qi) / a.G] : ~0ull;
         bool ok = true;
         for (int g = 0; g < ngroups; ++g) {
             ok = __all_sync(0xffffffffu, mbar_wait(s_addr(s_full), g & 1));
@@ -683,10 +686,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             uint32_t ov[32];
             tc_ld_x32(tmem + ((uint32_t)(quarter * 32) << 16) + kTmemO + (uint32_t)c0, ov);
             tc_wait_ld();
-            if (qi < a.QR) {
+            if (qi < QR) {
                 if (S == 1) {
                     const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
-                    const int r = qi / a.G, g = qi % a.G;
+                    const int r = (row0 + qi) / a.G, g = (row0 + qi) % a.G;
                     __half* dst = a.out + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + c0;
 #pragma unroll
                     for (int e = 0; e < 32; e += 8) {
@@ -707,7 +710,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 }
             }
         }
-        if (S > 1 && qi < a.QR) {
+        if (S > 1 && qi < QR) {
             pML[qi * 2 + 0] = m_used;
             pML[qi * 2 + 1] = l_sum;
         }
@@ -715,7 +718,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     if (S > 1) {
         __syncthreads();
         cluster_sync_all();
-        const int r0 = split * a.QR / S, r1 = (split + 1) * a.QR / S;
+        const int r0 = split * QR / S, r1 = (split + 1) * QR / S;
         if (valid) {
             for (int idx = threadIdx.x; idx < (r1 - r0) * HD; idx += blockDim.x) {
                 const int row = r0 + idx / HD, col = idx % HD;
@@ -741,7 +744,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                         acc += po[p] * w;
                         l += pl[p] * w;
                     }
-                const int r = row / a.G, g = row % a.G;
+                const int r = (row0 + row) / a.G, g = (row0 + row) % a.G;
                 a.out[(((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + col] =
                     __float2half_rn(l > 0.f ? acc / l : 0.f);
             }
@@ -991,9 +994,10 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
     SD_CHECK(HD == 64 || HD == 128, SPECDEC_EINVAL, "attention: head_dim must be 64 or 128");
     SD_CHECK(Hkv > 0 && Hq % Hkv == 0 && R >= 1 && R <= 64, SPECDEC_EINVAL, "attention: bad head / row counts");
     SD_CHECK(num_blocks > 0 && max_blocks > 0, SPECDEC_EINVAL, "attention: empty block pool or table");
-    if (R * (Hq / Hkv) <= 128) {
-        // up to 128 query rows: the tcgen05 kernel
-        AttnPlan p = plan_attention_tc(B, R, Hkv, HD, max_ctx);
+    if (R * (Hq / Hkv) <= 256) {
+        // the tcgen05 kernel, one CTA (cluster) per 128 query rows
+        const int mtiles = (R * (Hq / Hkv) + 127) / 128;
+        AttnPlan p = plan_attention_tc(B * mtiles, R, Hkv, HD, max_ctx);
         CUtensorMap kmap, vmap;
         int rc = make_kv_tmap(&kmap, kv_layer, num_blocks, Hkv, HD, 1, 1);
         if (!rc) rc = make_kv_tmap(&vmap, kv_layer, num_blocks, Hkv, HD, HD / 64, 1);
@@ -1011,7 +1015,7 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
         a.B = B;
         a.R = R;
         a.QR = R * a.G;
-        a.MT = p.MT;
+        a.MT = mtiles;
         a.KG = p.KG;
         a.S = p.S;
         a.ST = p.ST;
@@ -1020,7 +1024,7 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
         a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)HD));
         a.status = device_status_ptr();
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(B * Hkv * p.S));
+        cfg.gridDim = dim3((unsigned)(B * Hkv * mtiles * p.S));
         cfg.blockDim = dim3((unsigned)p.threads);
         cfg.dynamicSmemBytes = p.smem;
         cfg.stream = s;
