@@ -308,15 +308,15 @@ def run_gpu(args, world, rank, local, pg):
                 "achieved": round(gemm_tflops, 1), "peak": peaks.get("bf16_tflops_sustained", 1400.0),
                 "unit": "TFLOP/s", "peak_source": f"{peak_src} bf16 sustained"}
     else:
-        roof = {"kernel": "attn_kernel (verify attention)", "bound": "hbm", "achieved": round(attn_gbs, 1),
+        roof = {"kernel": "attn_tc_kernel (verify attention)", "bound": "hbm", "achieved": round(attn_gbs, 1),
                 "peak": peaks.get("hbm_gbs", 6650.0), "unit": "GB/s", "peak_source": f"{peak_src} hbm copy"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
     # DRAM bytes (read + write) of one launch from the committed ncu captures
     # (profiles/), with that launch's algorithmic bytes beside them
     if roof["bound"] == "tensor":
-        roof.update(traffic=333.4e6, traffic_launch="lm_head M=160 N=128256 K=4096", traffic_algorithmic=271.3e6)
+        roof.update(traffic=332.4e6, traffic_launch="lm_head M=160 N=128256 K=4096", traffic_algorithmic=271.3e6)
     else:
-        roof.update(traffic=276.6e6, traffic_launch="attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048",
+        roof.update(traffic=276.2e6, traffic_launch="attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048",
                     traffic_algorithmic=269.1e6)
     verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_bytes": vbytes,
               "verify_hbm_frac_of_measured": round(vbytes / (verify_ms * 1e-3) / 1e9 / peaks.get("hbm_gbs", 6650.0), 4),
