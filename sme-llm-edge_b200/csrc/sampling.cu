@@ -38,6 +38,7 @@ struct RowSmem {
     DevRowStats st;
     int result;
     u128 big;
+    u128 total;
 };
 
 __device__ __forceinline__ uint32_t mass_of(float z, float m, float c) {
@@ -56,12 +57,24 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2)
 __device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, float* out_max, int* out_idx) {
     float bv = -INFINITY;
     int bi = -1;
-    for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        float v = z[j];
+    // each thread visits its indices in increasing order: strict > keeps the first of equal values
+    auto upd = [&](float v, int j) {
         if (v > bv || (bi < 0 && v == bv)) {
             bv = v;
             bi = j;
         }
+    };
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+        const float4* z4 = reinterpret_cast<const float4*>(z);
+        for (int q = threadIdx.x; q < V / 4; q += blockDim.x) {
+            const float4 v = z4[q];
+            upd(v.x, 4 * q);
+            upd(v.y, 4 * q + 1);
+            upd(v.z, 4 * q + 2);
+            upd(v.w, 4 * q + 3);
+        }
+    } else {
+        for (int j = threadIdx.x; j < V; j += blockDim.x) upd(z[j], j);
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -170,13 +183,21 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
         uint64_t s = 0;
         const int lane = threadIdx.x & 31;
         const int warp_base = (threadIdx.x >> 5) * 32, stride = blockDim.x;
-        for (int base = warp_base; base < V; base += stride) {
-            const int j = base + lane;
-            const bool valid = j < V;
-            const float zj = valid ? z[j] : 0.0f;
-            const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
-            s += e;
-            if (nucleus) warp_hist_add(sm.hist, logit_key(zj) >> 24, e, valid);
+        if (!nucleus && (V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+            const float4* z4 = reinterpret_cast<const float4*>(z);
+            for (int q = threadIdx.x; q < V / 4; q += blockDim.x) {
+                const float4 v = z4[q];
+                s += (uint64_t)mass_of(v.x, m, c) + mass_of(v.y, m, c) + mass_of(v.z, m, c) + mass_of(v.w, m, c);
+            }
+        } else {
+            for (int base = warp_base; base < V; base += stride) {
+                const int j = base + lane;
+                const bool valid = j < V;
+                const float zj = valid ? z[j] : 0.0f;
+                const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
+                s += e;
+                if (nucleus) warp_hist_add(sm.hist, logit_key(zj) >> 24, e, valid);
+            }
         }
         s = block_sum<uint64_t>(s, sm.red64);
         r.sum = s;
@@ -247,48 +268,96 @@ __device__ u128 block_incl_scan_u128(u128 v, RowSmem& sm, u128* total) {
     return v + before;
 }
 
-// Smallest j (index order) whose running mass exceeds `target`.
-template <class MassFn>
-__device__ int cta_inverse_cdf(int V, u128 target, MassFn mass, RowSmem& sm) {
-    u128 running = 0;
-    if (threadIdx.x == 0) sm.result = -1;
-    const int per_tile = blockDim.x * 4;
-    for (int tile = 0; tile < V; tile += per_tile) {
-        const int j0 = tile + threadIdx.x * 4;
-        u128 mv[4];
-        u128 local = 0;
+__device__ __forceinline__ u128 shfl_u128(u128 v, int src) {
+    const uint64_t lo = __shfl_sync(0xffffffffu, (uint64_t)v, src);
+    const uint64_t hi = __shfl_sync(0xffffffffu, (uint64_t)(v >> 64), src);
+    return ((u128)hi << 64) | lo;
+}
+__device__ __forceinline__ u128 warp_incl_scan_u128(u128 v) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int j = j0 + q;
-            mv[q] = j < V ? mass(j) : (u128)0;
-            local += mv[q];
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t lo = __shfl_up_sync(0xffffffffu, (uint64_t)v, o);
+        const uint64_t hi = __shfl_up_sync(0xffffffffu, (uint64_t)(v >> 64), o);
+        if (lane >= o) v += ((u128)hi << 64) | lo;
+    }
+    return v;
+}
+
+// Smallest j (index order) whose running mass exceeds target_of(total), where
+// total = sum of all masses; returns -1 when the total is zero (or does not
+// exceed the target).  *total_out receives the total.
+// Warp w owns the contiguous index range [w*C, (w+1)*C): one coalesced pass
+// gives the warp totals; the warp holding the target then splits its range
+// into 32 contiguous sub-ranges (one per lane), finds the sub-range, and walks
+// it 32 indices at a time.  About one pass over the row instead of a
+// block-wide scan per tile.
+template <class MassFn, class TargetFn>
+__device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, RowSmem& sm, u128* total_out) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int C = (((V + nw - 1) / nw) + 31) & ~31;  // per-warp range, a multiple of 32
+    const int lo = wid * C, hi = min(V, lo + C);
+    u128 t = 0;
+    for (int j = lo + lane; j < hi; j += 32) t += mass(j);
+    t = warp_sum_u128(t);
+    __syncthreads();  // sm.scan may still be read by a previous caller
+    if (lane == 0) sm.scan[wid] = t;
+    __syncthreads();
+    if (wid == 0) {
+        const u128 v = lane < nw ? sm.scan[lane] : (u128)0;
+        const u128 incl = warp_incl_scan_u128(v);
+        const u128 total = shfl_u128(incl, 31);
+        const u128 target = target_of(total);
+        const bool hit = lane < nw && incl - v <= target && target < incl;
+        const unsigned b = __ballot_sync(0xffffffffu, hit);
+        if (hit && lane == __ffs(b) - 1) sm.big = target - (incl - v);
+        if (lane == 0) {
+            sm.redi[0] = b ? __ffs(b) - 1 : -1;
+            sm.total = total;
+            sm.result = -1;
         }
-        u128 total;
-        const u128 incl = block_incl_scan_u128(local, sm, &total);
-        if (running + total > target) {
-            u128 before = running + incl - local;
-            if (before <= target && target < running + incl) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    before += mv[q];
-                    if (before > target) {
-                        sm.result = j0 + q;
-                        break;
-                    }
+    }
+    __syncthreads();
+    const int W = sm.redi[0];
+    *total_out = sm.total;
+    if (W >= 0 && wid == W) {
+        const u128 tgt = sm.big;
+        const int sub = C / 32;  // lane l: sub-range [lo + l*sub, lo + (l+1)*sub)
+        const int slo = min(hi, lo + lane * sub), shi = min(hi, slo + sub);
+        u128 st = 0;
+        for (int j = slo; j < shi; ++j) st += mass(j);
+        const u128 si = warp_incl_scan_u128(st);
+        const bool h = si - st <= tgt && tgt < si;
+        const unsigned hb = __ballot_sync(0xffffffffu, h);
+        if (hb) {
+            const int L = __ffs(hb) - 1;
+            const u128 rem = tgt - shfl_u128(si - st, L);
+            const int clo = min(hi, lo + L * sub), chi = min(hi, clo + sub);
+            u128 run = 0;
+            for (int j0 = clo; j0 < chi; j0 += 32) {
+                const int j = j0 + lane;
+                const u128 m = j < chi ? mass(j) : (u128)0;
+                const u128 inc = warp_incl_scan_u128(m);
+                const unsigned fb = __ballot_sync(0xffffffffu, j < chi && run + inc > rem);
+                if (fb) {
+                    if (lane == 0) sm.result = j0 + __ffs(fb) - 1;
+                    break;
                 }
+                run += shfl_u128(inc, 31);
             }
-            __syncthreads();
-            const int r = sm.result;
-            __syncthreads();
-            return r;
         }
-        running += total;
-        __syncthreads();
     }
     __syncthreads();
     const int r = sm.result;
     __syncthreads();
     return r;
+}
+
+// Smallest j (index order) whose running mass exceeds `target`.
+template <class MassFn>
+__device__ int cta_inverse_cdf(int V, u128 target, MassFn mass, RowSmem& sm) {
+    u128 total;
+    return cta_inverse_cdf_total(V, mass, [target](u128) { return target; }, sm, &total);
 }
 
 __device__ int cta_sample_nucleus(const float* z, int V, float c, const DevRowStats& st, uint64_t u64, RowSmem& sm) {
@@ -371,23 +440,16 @@ __global__ void __launch_bounds__(kRowThreads) accept_chain_kernel(const float* 
                 const u128 y = (u128)nucleus_mass(zq, stq, c, j) * stp.nuc;
                 return x > y ? x - y : (u128)0;
             };
-            // total residual mass
-            u128 part = 0;
-            for (int j = threadIdx.x; j < V; j += blockDim.x) part += resid(j);
+            // draw from the residual: target = U * R / 2^64 with R the total residual mass
             u128 R = 0;
-            {
-                u128 tot;
-                (void)block_incl_scan_u128(part, sm, &tot);
-                R = tot;
-            }
-            __syncthreads();
-            if (R == 0) {
-                tok = cta_sample_nucleus(zp, V, c, stp, u64, sm);
-            } else {
-                const uint64_t rh = (uint64_t)(R >> 64), rl = (uint64_t)R;
-                const u128 tgt = (u128)u64 * rh + (u128)mulhi64(u64, rl);
-                tok = cta_inverse_cdf(V, tgt, resid, sm);
-            }
+            tok = cta_inverse_cdf_total(
+                V, resid,
+                [u64](u128 tot) {
+                    const uint64_t rh = (uint64_t)(tot >> 64), rl = (uint64_t)tot;
+                    return (u128)u64 * rh + (u128)mulhi64(u64, rl);
+                },
+                sm, &R);
+            if (R == 0) tok = cta_sample_nucleus(zp, V, c, stp, u64, sm);
         }
     }
     if (threadIdx.x == 0) {
