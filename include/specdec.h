@@ -166,6 +166,14 @@ int specdec_w4_untile(const void* tiled, int N, int K, uint8_t* packed, uint16_t
 size_t specdec_w4a16_workspace_bytes(int M, int N, int K);
 int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
                        int mode, void* workspace, size_t workspace_bytes, void* stream);
+/* Gate/up projection fused with SwiGLU (server/main.cpp:246-249, 338-340):
+ * h[m, f] = fp16(silu(g) * u), g = X . gate[f], u = X . up[f], for f < F,
+ * h fp16 [M, F] with row stride ldh.  w_gu_tiled holds 256 * ceil(F / 128)
+ * rows in the tiled layout: rows 256t .. 256t+127 are gate rows 128t ..
+ * 128t+127 and the next 128 the up rows of the same features (rows past F
+ * zero: nibbles 8, scale 0).  One launch; g and u never leave the chip. */
+int specdec_w4a16_gemm_swiglu(const uint16_t* X, int M, int ldx, const void* w_gu_tiled, int F, int K, uint16_t* h,
+                              int ldh, void* stream);
 /* Same contraction on the CUDA cores (used to cross-check the tensor path). */
 int specdec_w4a16_gemm_simt(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
                             int mode, void* stream);

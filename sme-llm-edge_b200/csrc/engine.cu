@@ -36,10 +36,14 @@ __device__ __forceinline__ float synth_value(uint32_t seed, uint32_t tid, uint64
 
 // Row segments of a fused weight matrix: rows [end[i-1], end[i]) come from
 // tensor tid[i] (row index relative to the segment start), e.g. QKV = [q|k|v].
+// inter > 0 instead interleaves two tensors of inter rows in 128-row blocks
+// (row n: tensor tid[(n / 128) % 2], row (n / 256) * 128 + n % 128; zero rows
+// past inter), the gate/up layout of the fused SwiGLU GEMM.
 struct RowSegs {
     int n;
     int end[3];
     uint32_t tid[3];
+    int inter;
 };
 
 // One thread per (row n, group g): same quantiser as the oracle generator
@@ -58,10 +62,22 @@ __global__ void synth_w4_tiled_kernel(uint32_t seed, RowSegs segs, int N, int K,
         *reinterpret_cast<uint16_t*>(unit + 8192 + r * 2) = 0;
         return;
     }
-    int si = 0;
-    while (si + 1 < segs.n && n >= segs.end[si]) ++si;
-    const uint32_t tid = segs.tid[si];
-    const int row = n - (si ? segs.end[si - 1] : 0);
+    uint32_t tid;
+    int row;
+    if (segs.inter > 0) {
+        tid = segs.tid[(n >> 7) & 1];
+        row = (n >> 8) * 128 + (n & 127);
+        if (row >= segs.inter) {
+            for (int kc = 0; kc < 16; ++kc) *reinterpret_cast<uint32_t*>(unit + ((kc * 128 + r) << 2)) = 0x88888888u;
+            *reinterpret_cast<uint16_t*>(unit + 8192 + r * 2) = 0;
+            return;
+        }
+    } else {
+        int si = 0;
+        while (si + 1 < segs.n && n >= segs.end[si]) ++si;
+        tid = segs.tid[si];
+        row = n - (si ? segs.end[si - 1] : 0);
+    }
     float amax = 0.f;
     for (int t = 0; t < gl; ++t)
         amax = fmaxf(amax, fabsf(synth_value(seed, tid, (uint64_t)row * K + (uint64_t)g * 128 + t)));
@@ -208,37 +224,6 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int ldq, const int
             *reinterpret_cast<__half2*>(dst + d) = __floats2half2_rn(v.x, v.y);
         }
     }
-}
-
-// h = fp16(silu(g) * u), gu rows [gate (F) | up (F)] (main.cpp:246-249, 338-340).
-// Grid (ceil(F / 4 / 256), rows): one thread per 4 outputs.
-__global__ void swiglu_kernel(const float* __restrict__ gu, int F, __half* __restrict__ h) {
-    pdl_trigger();  // a following GEMM may start streaming its weights
-    const int m = blockIdx.y;
-    const int i0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (i0 >= F) return;
-    const float* g = gu + (size_t)m * 2 * F;
-    __half* hr = h + (size_t)m * F;
-    auto one = [](float gv, float uv) {
-        const float sv = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
-        return __fmul_rn(sv, uv);
-    };
-    if ((F & 3) == 0 && i0 + 3 < F) {
-        const float4 gv = *reinterpret_cast<const float4*>(g + i0);
-        const float4 uv = *reinterpret_cast<const float4*>(g + F + i0);
-        __half2 a = __floats2half2_rn(one(gv.x, uv.x), one(gv.y, uv.y));
-        __half2 b = __floats2half2_rn(one(gv.z, uv.z), one(gv.w, uv.w));
-        uint2 w;
-        w.x = *reinterpret_cast<uint32_t*>(&a);
-        w.y = *reinterpret_cast<uint32_t*>(&b);
-        *reinterpret_cast<uint2*>(hr + i0) = w;
-    } else {
-        for (int i = i0; i < i0 + 4 && i < F; ++i) hr[i] = __float2half_rn(one(g[i], g[F + i]));
-    }
-}
-static void launch_swiglu(const float* gu, int rows, int F, __half* h, cudaStream_t s) {
-    dim3 grid((unsigned)((F + 1023) / 1024), (unsigned)rows);
-    swiglu_kernel<<<grid, 256, 0, s>>>(gu, F, h);
 }
 
 // Chain verify rows: [pending, d_0 .. d_{k-1}] at positions ctx .. ctx + k.
@@ -417,7 +402,6 @@ struct specdec_engine {
     float* qkv = nullptr;
     __half* q16 = nullptr;
     __half* att = nullptr;
-    float* gu = nullptr;
     __half* hmid = nullptr;
     float* logits = nullptr;
     float* dlogits = nullptr;
@@ -504,6 +488,18 @@ int gemm(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int
     return rc;
 }
 
+// gate/up projection + SwiGLU in one launch: h fp16 [M, F]
+int gemm_swiglu(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w_gu, int F, __half* h) {
+    GemmPlan p = plan_gemm_swiglu(M, F, K);
+    CUtensorMap map;
+    int rc = make_x_tmap(&map, X, M, K, K, p.MT);
+    if (rc) return rc;
+    ++e->kernels_per_step;
+    rc = gemm_launch_swiglu(map, p, w_gu, M, F, h, F, e->stream, /*pdl=*/true);
+    prof_mark(e, e->gemm_cat);
+    return rc;
+}
+
 #define ENG_TRY(x)              \
     do {                        \
         int _rc = (x);          \
@@ -544,9 +540,7 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
         ENG_TRY(gemm(e, e->att, M, e->qd, w.o, H, e->x, H, 1));
         launch_rmsnorm(e->x, H, M, H, c.rms_eps, e->xn, H, s);
         ENG_LAUNCH("rmsnorm_kernel");
-        ENG_TRY(gemm(e, e->xn, M, H, w.gu, 2 * F, e->gu, 2 * F, 0));
-        launch_swiglu(e->gu, M, F, e->hmid, s);
-        ENG_LAUNCH("swiglu_kernel");
+        ENG_TRY(gemm_swiglu(e, e->xn, M, H, w.gu, F, e->hmid));
         ENG_TRY(gemm(e, e->hmid, M, F, w.down, H, e->x, H, 1));
     }
     if (want_logits) {
@@ -729,7 +723,7 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
     // weights
     e->sz_qkv = w4_tiled_bytes(e->NQKV, H);
     e->sz_o = w4_tiled_bytes(H, e->qd);
-    e->sz_gu = w4_tiled_bytes(2 * F, H);
+    e->sz_gu = w4_tiled_bytes(128 * swiglu_units(F), H);
     e->sz_down = w4_tiled_bytes(H, F);
     e->sz_lm = w4_tiled_bytes(V, H);
     e->sz_head = w4_tiled_bytes(H, H);
@@ -772,7 +766,7 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
     const int Mx = e->Mmax;
     if ((rcode = dalloc(e, &e->x, (size_t)Mx * H)) || (rcode = dalloc(e, &e->xn, (size_t)Mx * H)) ||
         (rcode = dalloc(e, &e->qkv, (size_t)Mx * e->NQKV)) || (rcode = dalloc(e, &e->q16, (size_t)Mx * e->qd)) ||
-        (rcode = dalloc(e, &e->att, (size_t)Mx * e->qd)) || (rcode = dalloc(e, &e->gu, (size_t)Mx * 2 * F)) ||
+        (rcode = dalloc(e, &e->att, (size_t)Mx * e->qd)) ||
         (rcode = dalloc(e, &e->hmid, (size_t)Mx * F)) || (rcode = dalloc(e, &e->logits, (size_t)e->M * V)) ||
         (rcode = dalloc(e, &e->dlogits, (size_t)e->Mdraft * V)) || (rcode = dalloc(e, &e->dh, (size_t)e->Mdraft * H)) ||
         (rcode = dalloc(e, &e->dxn, (size_t)std::max(e->Mdraft, e->B) * H)) ||
@@ -795,7 +789,7 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
         cudaMemcpy(e->active, on.data(), 4 * e->B, cudaMemcpyHostToDevice);
     }
     // workspaces
-    const int maxN = std::max(std::max(V, 2 * F), std::max(e->NQKV, H));
+    const int maxN = std::max(std::max(V, 128 * swiglu_units(F)), std::max(e->NQKV, H));
     e->gemm_ws_bytes = gemm_workspace_bound(Mx, maxN, std::max(H, F));
     if ((rcode = dalloc(e, reinterpret_cast<char**>(&e->gemm_ws), e->gemm_ws_bytes))) return fail(rcode);
     cudaMemset(e->gemm_ws, 0, e->gemm_ws_bytes);
@@ -827,6 +821,7 @@ extern "C" int specdec_engine_init_weights(specdec_engine* e, uint32_t seed) {
     auto one = [](uint32_t tid, int N) {
         RowSegs r;
         r.n = 1;
+        r.inter = 0;
         r.end[0] = N;
         r.tid[0] = tid;
         return r;
@@ -838,6 +833,7 @@ extern "C" int specdec_engine_init_weights(specdec_engine* e, uint32_t seed) {
         const uint32_t base = (uint32_t)l * 16u;
         RowSegs qkv;
         qkv.n = 3;
+        qkv.inter = 0;
         qkv.end[0] = qd;
         qkv.end[1] = qd + kd;
         qkv.end[2] = qd + 2 * kd;
@@ -846,13 +842,14 @@ extern "C" int specdec_engine_init_weights(specdec_engine* e, uint32_t seed) {
         qkv.tid[2] = base + 2;
         RowSegs gu;
         gu.n = 2;
-        gu.end[0] = F;
-        gu.end[1] = 2 * F;
+        gu.end[0] = 0;
+        gu.end[1] = 0;
+        gu.inter = F;
         gu.tid[0] = base + 4;
         gu.tid[1] = base + 5;
         if ((rc = synth(qkv, e->NQKV, H, e->layers[l].qkv))) return rc;
         if ((rc = synth(one(base + 3, H), H, qd, e->layers[l].o))) return rc;
-        if ((rc = synth(gu, 2 * F, H, e->layers[l].gu))) return rc;
+        if ((rc = synth(gu, 128 * swiglu_units(F), H, e->layers[l].gu))) return rc;
         if ((rc = synth(one(base + 6, H), H, F, e->layers[l].down))) return rc;
     }
     if ((rc = synth(one(0x10001u, V), V, H, e->lm))) return rc;

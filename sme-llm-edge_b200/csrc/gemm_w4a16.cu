@@ -80,8 +80,10 @@ struct GemmArgs {
     const uint8_t* w;
     int M, N, KG, m_tiles, S;
     float* Y;
-    int ldy, mode;
-    int tma_out;  // tmap_y is valid: Y leaves by TMA (box {128, MT / S})
+    int ldy, mode;  // mode 0 store, 1 add, 2 SwiGLU (h = silu(gate) * up into H, below)
+    __half* H;      // mode 2: fp16 [M, F] with row stride ldy; weight tile t = [gate rows 128t.. | up rows 128t..]
+    int F;          // mode 2: columns of H
+    int tma_out;  // tmap_y is valid: the output leaves by TMA (box {128, MT / S}; fp16 over H in mode 2)
     int pdl;      // launched as a programmatic dependent: only the weights may be read before pdl_wait()
     DeviceStatus* status;
 };
@@ -389,10 +391,67 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
     }
+    // Mode 2 (SwiGLU): half 0 holds gate rows 128 * n_tile .. +127 and half 1
+    // the up rows of the same features, so this CTA's token rows give
+    // h[m][128 * n_tile + c] = fp16(silu(g) * u) (main.cpp:246-249, 338-340).
+    // Every thread keeps its results in registers until all have read the
+    // fp32 rows, then the CTA overwrites the start of its own half-0 rows
+    // (no peer reads them) with a dense fp16 [rows][128] box.
+    __half* hbox = reinterpret_cast<__half*>(stage + r0 * 128);
+    if (args.mode == 2) {
+        constexpr int kItems = (MT * 16 + kGemmThreads - 1) / kGemmThreads;  // (row, 8 features) per thread
+        const int nitems = rows * 16;
+        uint4 hv[kItems];
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+            const int idx = threadIdx.x + it * kGemmThreads;
+            if (idx < nitems) {
+                const float* gp = stage + (r0 + (idx >> 4)) * 128 + (idx & 15) * 8;
+                const float* up = gp + MT * 128;
+                float g[8], u[8];
+                *reinterpret_cast<float4*>(g) = *reinterpret_cast<const float4*>(gp);
+                *reinterpret_cast<float4*>(g + 4) = *reinterpret_cast<const float4*>(gp + 4);
+                *reinterpret_cast<float4*>(u) = *reinterpret_cast<const float4*>(up);
+                *reinterpret_cast<float4*>(u + 4) = *reinterpret_cast<const float4*>(up + 4);
+                uint32_t w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float a = __fmul_rn(__fdiv_rn(g[2 * j], __fadd_rn(1.0f, expf(-g[2 * j]))), u[2 * j]);
+                    const float b =
+                        __fmul_rn(__fdiv_rn(g[2 * j + 1], __fadd_rn(1.0f, expf(-g[2 * j + 1]))), u[2 * j + 1]);
+                    __half2 h2 = __floats2half2_rn(a, b);
+                    w[j] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                hv[it] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+            const int idx = threadIdx.x + it * kGemmThreads;
+            if (idx < nitems) *reinterpret_cast<uint4*>(hbox + (idx >> 4) * 128 + (idx & 15) * 8) = hv[it];
+        }
+    }
     fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
     if (args.pdl) pdl_wait();  // Y may still be read or written by earlier kernels
     __syncthreads();
-    if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
+    if (args.mode == 2) {
+        if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
+            if (args.tma_out) {
+                if (threadIdx.x == 0) {
+                    tma_out_2d(&tmap_y, s_addr(hbox), n_tile * 128, m_tile * MT + r0, 0);
+                    bulk_commit();
+                    bulk_wait_read();
+                }
+            } else {
+                for (int idx = threadIdx.x; idx < rows * 128; idx += blockDim.x) {
+                    const int m = m_tile * MT + r0 + (idx >> 7), f = n_tile * 128 + (idx & 127);
+                    if (m < args.M && f < args.F) args.H[(size_t)m * args.ldy + f] = hbox[idx];
+                }
+            }
+        }
+    } else if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
         if (args.tma_out) {
             if (threadIdx.x == 0) {
                 for (int q = 0; q < 2; ++q)  // a half wholly past N has nothing to write
@@ -559,6 +618,20 @@ static int make_y_tmap(CUtensorMap* map, float* Y, int M, int N, int ldy, int MT
     return r == CUDA_SUCCESS ? 1 : 0;
 }
 
+// fp16 h [M, F] of the SwiGLU epilogue (box {128 features, MT / S tokens}).
+static int make_h_tmap(CUtensorMap* map, __half* h, int M, int F, int ldh, int MT, int S) {
+    auto enc = get_encode();
+    if (!enc || (reinterpret_cast<uintptr_t>(h) & 15) != 0 || (ldh % 8) != 0) return 0;
+    cuuint64_t dims[2] = {(cuuint64_t)F, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)ldh * 2};
+    cuuint32_t box[2] = {128, (cuuint32_t)(MT / S)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, h, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 1 : 0;
+}
+
 // Token tile: the smallest that holds M; above 160 tokens, the one of 128 / 160
 // that pads M least (160 on a tie: fewer passes over the weights).
 int pick_mt(int M) {
@@ -701,25 +774,8 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_y, const Gem
 size_t gemm_workspace_bytes(const GemmPlan&) { return 0; }
 size_t gemm_workspace_bound(int, int, int) { return 0; }
 
-int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
-                int mode, void* ws, cudaStream_t s, bool pdl) {
-    (void)ws;
-    GemmArgs a;
-    a.w = reinterpret_cast<const uint8_t*>(w_tiled);
-    a.M = M;
-    a.N = N;
-    a.KG = p.KG;
-    a.m_tiles = p.m_tiles;
-    a.S = p.S;
-    a.Y = Y;
-    a.ldy = ldy;
-    a.mode = mode;
-    a.pdl = pdl ? 1 : 0;
-    a.status = device_status_ptr();
-    // Y leaves by TMA when its rows are 16-byte aligned; otherwise plain stores.
-    CUtensorMap map_y;
-    a.tma_out = make_y_tmap(&map_y, Y, M, N, ldy, p.MT, p.S);
-    if (!a.tma_out) memset(&map_y, 0, sizeof(map_y));
+static int launch_mt(const CUtensorMap& map, const CUtensorMap& map_y, const GemmArgs& a, const GemmPlan& p,
+                     cudaStream_t s) {
     switch (p.MT) {
         case 16: return launch_tc<16>(map, map_y, a, p.grid, s);
         case 32: return launch_tc<32>(map, map_y, a, p.grid, s);
@@ -730,6 +786,52 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
     }
     set_error("w4a16_gemm: unsupported token tile");
     return SPECDEC_EINVAL;
+}
+
+static GemmArgs gemm_args(const GemmPlan& p, const void* w_tiled, int M, int N, int ldy, int mode, bool pdl) {
+    GemmArgs a;
+    a.w = reinterpret_cast<const uint8_t*>(w_tiled);
+    a.M = M;
+    a.N = N;
+    a.KG = p.KG;
+    a.m_tiles = p.m_tiles;
+    a.S = p.S;
+    a.Y = nullptr;
+    a.ldy = ldy;
+    a.mode = mode;
+    a.H = nullptr;
+    a.F = 0;
+    a.tma_out = 0;
+    a.pdl = pdl ? 1 : 0;
+    a.status = device_status_ptr();
+    return a;
+}
+
+int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
+                int mode, void* ws, cudaStream_t s, bool pdl) {
+    (void)ws;
+    GemmArgs a = gemm_args(p, w_tiled, M, N, ldy, mode, pdl);
+    a.Y = Y;
+    // Y leaves by TMA when its rows are 16-byte aligned; otherwise plain stores.
+    CUtensorMap map_y;
+    a.tma_out = make_y_tmap(&map_y, Y, M, N, ldy, p.MT, p.S);
+    if (!a.tma_out) memset(&map_y, 0, sizeof(map_y));
+    return launch_mt(map, map_y, a, p, s);
+}
+
+int swiglu_units(int F) { return 2 * ((F + 127) / 128); }
+
+GemmPlan plan_gemm_swiglu(int M, int F, int K) { return plan_gemm(M, 128 * swiglu_units(F), K); }
+
+int gemm_launch_swiglu(const CUtensorMap& map, const GemmPlan& p, const void* w_gu, int M, int F, __half* h, int ldh,
+                       cudaStream_t s, bool pdl) {
+    GemmArgs a = gemm_args(p, w_gu, M, 128 * swiglu_units(F), ldh, 2, pdl);
+    a.H = h;
+    a.F = F;
+    CUtensorMap map_h;
+    a.tma_out = make_h_tmap(&map_h, h, M, F, ldh, p.MT, p.S);
+    if (!a.tma_out) memset(&map_h, 0, sizeof(map_h));
+    return launch_mt(map, map_h, a, p, s);
 }
 
 size_t w4_tiled_bytes(int N, int K) {
@@ -782,6 +884,18 @@ extern "C" int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void*
     int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
     if (rc) return rc;
     return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, nullptr, as_stream(stream), false);
+}
+
+extern "C" int specdec_w4a16_gemm_swiglu(const uint16_t* X, int M, int ldx, const void* w_gu_tiled, int F, int K,
+                                         uint16_t* h, int ldh, void* stream) {
+    SD_CHECK(X && w_gu_tiled && h && M >= 0 && F > 0 && K > 0 && ldx >= K && ldh >= F, SPECDEC_EINVAL,
+             "w4a16_gemm_swiglu: bad argument");
+    if (M == 0) return SPECDEC_OK;
+    GemmPlan p = plan_gemm_swiglu(M, F, K);
+    CUtensorMap map;
+    int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
+    if (rc) return rc;
+    return gemm_launch_swiglu(map, p, w_gu_tiled, M, F, reinterpret_cast<__half*>(h), ldh, as_stream(stream), false);
 }
 
 extern "C" int specdec_w4a16_gemm_simt(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y,

@@ -31,6 +31,14 @@ int make_x_tmap(CUtensorMap* map, const void* X, int M, int K, int ldx, int MT);
 // that no kernel in flight writes).
 int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, int M, int N, float* Y, int ldy,
                 int mode, void* ws, cudaStream_t s, bool pdl = false);
+// Fused gate/up GEMM with the SwiGLU epilogue: h[m, f] = fp16(silu(g) * u)
+// for f < F, from weights whose 256-row tile t holds gate rows 128t .. 128t+127
+// then the up rows of the same features (zero rows past F): swiglu_units(F)
+// 128-row units.
+int swiglu_units(int F);
+GemmPlan plan_gemm_swiglu(int M, int F, int K);
+int gemm_launch_swiglu(const CUtensorMap& map, const GemmPlan& p, const void* w_gu, int M, int F, __half* h, int ldh,
+                       cudaStream_t s, bool pdl = false);
 size_t gemm_workspace_bound(int max_m, int max_n, int max_k);
 size_t w4_tiled_bytes(int N, int K);
 

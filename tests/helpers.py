@@ -68,6 +68,23 @@ def tile_w4(packed: np.ndarray, scales: np.ndarray, N: int, K: int) -> np.ndarra
     return out.reshape(-1)
 
 
+def interleave_gu(gate, up, F: int):
+    """Gate/up rows of the fused SwiGLU weight: 128-row blocks alternate
+    gate rows 128t.. and up rows 128t.., zero rows (nibbles 8, scale 0) past
+    F.  gate/up = (packed [F, K/2], scales [F, G]); returns (packed, scales, N)."""
+    units = 2 * ((F + 127) // 128)
+    N = 128 * units
+    packed = np.full((N, gate[0].shape[1]), 0x88, np.uint8)
+    scales = np.zeros((N, gate[1].shape[1]), gate[1].dtype)
+    for t in range(units // 2):
+        lo, hi = 128 * t, min(F, 128 * t + 128)
+        for part, (p, s) in enumerate((gate, up)):
+            r0 = 256 * t + 128 * part
+            packed[r0:r0 + hi - lo] = p[lo:hi]
+            scales[r0:r0 + hi - lo] = s[lo:hi]
+    return packed, scales, N
+
+
 def margin_ok(z: np.ndarray, thr: float = 1e-2) -> bool:
     top = np.sort(z)[-2:]
     return float(top[1] - top[0]) >= thr

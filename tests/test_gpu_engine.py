@@ -15,7 +15,7 @@ import pytest
 
 import oracle as O
 import specdec as S
-from helpers import margin_ok, tile_w4
+from helpers import interleave_gu, margin_ok, tile_w4
 
 pytestmark = pytest.mark.gpu
 
@@ -42,10 +42,10 @@ def test_engine_weights_bit_identical_to_oracle(cuda_device):
     qkv = eng.read("w_qkv0", np.uint8, (S.lib().specdec_w4_tiled_bytes(qd + 2 * kd, H),))
     np.testing.assert_array_equal(
         qkv, tile_w4(np.vstack([p[0] for p in parts]), np.vstack([p[1] for p in parts]), qd + 2 * kd, H))
-    gu_parts = [O.synth_w4(0, O.layer_tensor(0, w), F, H) for w in (O.T_GATE, O.T_UP)]
-    gu = eng.read("w_gu0", np.uint8, (S.lib().specdec_w4_tiled_bytes(2 * F, H),))
-    np.testing.assert_array_equal(
-        gu, tile_w4(np.vstack([p[0] for p in gu_parts]), np.vstack([p[1] for p in gu_parts]), 2 * F, H))
+    gu_packed, gu_scales, NGU = interleave_gu(*[O.synth_w4(0, O.layer_tensor(0, w), F, H) for w in (O.T_GATE, O.T_UP)],
+                                              F)
+    gu = eng.read("w_gu0", np.uint8, (S.lib().specdec_w4_tiled_bytes(NGU, H),))
+    np.testing.assert_array_equal(gu, tile_w4(gu_packed, gu_scales, NGU, H))
     down = eng.read("w_down0", np.uint8, (S.lib().specdec_w4_tiled_bytes(H, F),))
     np.testing.assert_array_equal(down, tile_w4(*O.synth_w4(0, O.layer_tensor(0, O.T_DOWN), H, F), H, F))
     head = eng.read("w_head0", np.uint8, (S.lib().specdec_w4_tiled_bytes(H, H),))

@@ -7,7 +7,7 @@ import pytest
 
 import oracle as O
 import specdec as S
-from helpers import dev, empty, margin_ok, ptr, stream_ptr, sync, tile_w4, zeros
+from helpers import dev, empty, interleave_gu, margin_ok, ptr, stream_ptr, sync, tile_w4, zeros
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "ref_golden.npz")
@@ -247,6 +247,44 @@ def test_w4a16_simt_matches_tcgen05(cuda_device):
     S.check(S.lib().specdec_w4a16_gemm_simt(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y2), N, 0, stream_ptr()))
     sync()
     np.testing.assert_allclose(Y1.cpu().numpy(), Y2.cpu().numpy(), rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("M,F,K,pad", [(1, 256, 512, 0), (5, 1376, 512, 0), (160, 1376, 1024, 8), (33, 384, 640, 0),
+                                       (300, 512, 256, 0), (7, 1001, 384, 0), (64, 1792, 4096, 0)])
+def test_w4a16_gemm_swiglu_matches_unfused(cuda_device, M, F, K, pad):
+    """The fused gate/up GEMM + SwiGLU epilogue equals the plain GEMM over the
+    same interleaved weights followed by fp16(silu(g) * u), up to the one ulp
+    that expf and numpy's exp may differ by; g and u match the oracle's
+    contraction of the separate gate / up weights."""
+    import torch
+
+    gate, up = O.synth_w4(5, 21, F, K), O.synth_w4(5, 22, F, K)
+    packed, scales, N = interleave_gu(gate, up, F)
+    assert N == 128 * 2 * ((F + 127) // 128)
+    d_tiled = dev(tile_w4(packed, scales, N, K))
+    rng = np.random.default_rng(M + F)
+    X16 = O.f16_bits(rng.standard_normal((M, K)) * 0.5)
+    dX = dev(X16)
+    ldh = F + pad
+    h = zeros((M, ldh), torch.float16)
+    S.check(S.lib().specdec_w4a16_gemm_swiglu(ptr(dX), M, K, ptr(d_tiled), F, K, ptr(h), ldh, stream_ptr()))
+    Y = zeros((M, N), torch.float32)
+    ws_b = S.lib().specdec_w4a16_workspace_bytes(M, N, K)
+    ws = zeros(max(ws_b, 1), torch.uint8)
+    S.check(S.lib().specdec_w4a16_gemm(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y), N, 0, ptr(ws), ws_b, stream_ptr()))
+    sync()
+    y = Y.cpu().numpy().reshape(M, N // 256, 2, 128)
+    g = y[:, :, 0, :].reshape(M, -1)[:, :F]
+    u = y[:, :, 1, :].reshape(M, -1)[:, :F]
+    np.testing.assert_allclose(g, O.w4a16_gemm(X16, *gate), rtol=2e-3, atol=2e-3)
+    np.testing.assert_allclose(u, O.w4a16_gemm(X16, *up), rtol=2e-3, atol=2e-3)
+    with np.errstate(over="ignore"):
+        ref = (g / (np.float32(1) + np.exp(-g)) * u).astype(np.float16)
+    hh = h.cpu().numpy()
+    got = hh[:, :F]
+    err = np.abs(got.astype(np.float32) - ref.astype(np.float32))
+    assert np.all(err <= np.spacing(np.abs(ref)).astype(np.float32)), float(err.max())
+    assert np.all(hh[:, F:] == 0)  # the row padding is not written
 
 
 # ---------------------------------------------------------------- attention
