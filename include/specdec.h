@@ -166,6 +166,18 @@ int specdec_w4_untile(const void* tiled, int N, int K, uint8_t* packed, uint16_t
 size_t specdec_w4a16_workspace_bytes(int M, int N, int K);
 int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
                        int mode, void* workspace, size_t workspace_bytes, void* stream);
+/* The launch plan for a shape: out[0] token tile, out[1] 128-row weight
+ * units per CTA (1 or 2), out[2] CTAs splitting the k range of a tile (1, 2,
+ * 4, 8), out[3] CTAs launched.  units = 0: the plan specdec_w4a16_gemm picks;
+ * 1 or 2: the best plan with that many units per CTA (2 is the plan of
+ * specdec_w4a16_gemm_swiglu). */
+int specdec_w4a16_plan(int M, int N, int K, int units, int32_t* out);
+/* specdec_w4a16_gemm with the units per CTA (qn 1 / 2) and the k split
+ * (1, 2, 4, 8; <= ceil(K / 128)) fixed by the caller instead of the planner:
+ * for validating and timing every path.  Same result up to the order of the
+ * k-range sums. */
+int specdec_w4a16_gemm_with_plan(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y,
+                                 int ldy, int mode, int qn, int split, void* stream);
 /* Gate/up projection fused with SwiGLU (server/main.cpp:246-249, 338-340):
  * h[m, f] = fp16(silu(g) * u), g = X . gate[f], u = X . up[f], for f < F,
  * h fp16 [M, F] with row stride ldh.  w_gu_tiled holds 256 * ceil(F / 128)

@@ -9,28 +9,29 @@
 //   deq(w) = fp16((u4 - 8) * scale)   (offset-binary nibbles as written by the
 //            reference packer, server/sve_packing.cpp:8-30)
 //
-// Work decomposition: one output tile = 256 weight rows x MT tokens.  A
-// cluster of S CTAs (1 <= S <= 8) owns one tile and splits its K range; the
-// S partial accumulators are summed on chip through distributed shared memory
-// (each CTA reduces 1/S of the tile's columns from all S CTAs in rank order,
-// so the result is deterministic) and written once.  S is chosen per shape so
-// the grid fills the 148 SMs with little wave quantisation.
+// Work decomposition: one output tile = QN x 128 weight rows x MT tokens
+// (QN = 2, or QN = 1 for weight matrices with too few 256-row tiles to fill
+// the SMs).  A cluster of S CTAs (1 <= S <= 8) owns one tile and splits its K
+// range; the S partial accumulators are summed on chip through distributed
+// shared memory (each CTA reduces 1/S of the tile's token rows from all S CTAs
+// in rank order, so the result is deterministic) and written once.  QN and S
+// are chosen per shape from a cost model of waves, k-steps and reduction.
 //
 // CTA = 19 warps, warp-specialised:
 //   warp 0      bulk-copy producer of the int4 units (RS k-steps ahead)
-//   warp 18     TMA producer of the activation tiles (ST half-steps ahead)
+//   warp 18     TMA producer of the activation tiles (SB half-steps ahead)
 //   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
 //   warps 2-17  dequant: int4 -> fp16 in registers, written straight into
 //               tensor memory with tcgen05.st (one TMEM lane = one weight row);
 //               then the epilogue: tcgen05.ld of the accumulators into shared
 //               memory, TMA stores out
-// MMA: M = 128 weight rows (two per tile), N = MT, K = 16 per instruction,
+// MMA: M = 128 weight rows (QN per tile), N = MT, K = 16 per instruction,
 // A (the dequantised weights) read from TMEM, B (the activations) from shared
 // memory, fp32 accumulators in TMEM.  Keeping A out of shared memory matters:
 // with A staged there, the dequant stores plus the MMA's A reads doubled the
 // shared-memory traffic of a k-step and made it, not the tensor pipe, the
-// limit.  TMEM columns: [0, 2*MT) accumulators, then ST stages of 64 columns
-// (two units x 64 k fp16, two fp16 per 32-bit column).
+// limit.  TMEM columns: [0, QN*MT) accumulators, then ST stages of 64 columns
+// (QN units x 128/QN k fp16, two fp16 per 32-bit column).
 // Every mbarrier wait is bounded: on timeout the CTA records SPECDEC_ETIMEOUT
 // in the device status word, skips its output and still meets its cluster
 // barriers.
@@ -47,33 +48,54 @@
 namespace specdec {
 
 constexpr int kUnitBytes = 8448;  // 8192 nibble bytes + 128 fp16 scales
-constexpr int kRawStageBytes = 2 * kUnitBytes;
 constexpr int kGemmThreads = 608;  // 19 warps
 constexpr int kDeqWarps = 16;      // warps 2..17
 constexpr int kBWarp = 18;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kMaxSplit = 8;
 constexpr int kTmemCols = 512;
-constexpr int kAStageCols = 64;  // one half k-step of A: 2 units x 64 k fp16
+constexpr int kAStageCols = 64;  // one A stage: QN units x 128/QN k fp16
 constexpr int kMaxTokenTile = 160;
 
-constexpr int kRawStages = 8;    // int4 units in flight per CTA: 8 x 16.5 KB
-
-// Ring depth per token tile.  One stage = the A operand of a half k-step in
-// TMEM (64 columns after the 2*MT accumulator columns) plus the matching
-// activation tile in shared memory; both are released by one MMA commit.
-// The raw int4 ring is separate and deeper (it hides HBM latency).
-__host__ __device__ constexpr int stages_for(int MT) {
-    return (kTmemCols - 2 * MT) / kAStageCols > 4 ? 4 : (kTmemCols - 2 * MT) / kAStageCols;
+// A CTA owns QN 128-row weight units (QN = 2: 256-row tiles; QN = 1: 128-row
+// tiles, twice as many, for weight matrices too small to fill the SMs
+// otherwise).  One pipeline stage covers KS = 128 / QN k of every unit: 64
+// TMEM columns of A and an MT x KS activation tile.  Ring depths, in stages
+// unless noted:
+//   ST  A stages in TMEM (after the QN*MT accumulator columns)
+//   SB  activation tiles in shared memory, a multiple of ST: a tile comes from
+//       L2 with about twice the latency of one stage's MMAs, so its ring runs
+//       further ahead than the TMEM one where shared memory allows
+//   RS  raw int4 k-steps (QN 8448-byte units each) in shared memory; deep
+//       enough to hide HBM latency, and what the smem budget leaves
+__host__ __device__ constexpr int stages_for(int MT, int QN) {
+    return (kTmemCols - QN * MT) / kAStageCols > 4 ? 4 : (kTmemCols - QN * MT) / kAStageCols;
 }
-template <int MT>
+__host__ __device__ constexpr int bslot_bytes(int MT, int QN) { return MT * 256 / QN; }
+__host__ __device__ constexpr int bstages_for(int MT, int QN) {
+    return (QN == 1 && MT > 64) ? stages_for(MT, QN) : 2 * stages_for(MT, QN);
+}
+__host__ __device__ constexpr int rstages_for(int MT, int QN) {
+    return QN == 1 ? (MT > 128 ? 6 : 8) : (MT > 128 ? 6 : (MT > 64 ? 5 : 8));
+}
+constexpr int kEarlyRaw = 2;  // <= every rstages_for
+template <int MT, int QN>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
-    return 1024 /*align slack*/ + (size_t)stages_for(MT) * MT * 128 + (size_t)kRawStages * kRawStageBytes + 2048;
+    return 1024 /*align slack*/ + (size_t)bstages_for(MT, QN) * bslot_bytes(MT, QN) +
+           (size_t)rstages_for(MT, QN) * QN * kUnitBytes + 2048;
 }
-// the epilogue reuses the B and raw rings: two MT x 128 fp32 tiles (both halves)
-template <int MT>
+// Requested at launch: at least half the opt-in budget, so that two CTAs
+// never share an SM (each allocates all 512 TMEM columns).
+template <int MT, int QN>
+__host__ __device__ constexpr size_t gemm_launch_smem() {
+    return gemm_smem_bytes<MT, QN>() > (size_t)kSmemBudget / 2 + 1024 ? gemm_smem_bytes<MT, QN>()
+                                                                       : (size_t)kSmemBudget / 2 + 1024;
+}
+// the epilogue reuses the B and raw rings: QN MT x 128 fp32 tiles
+template <int MT, int QN>
 __host__ __device__ constexpr bool reduce_fits() {
-    return (size_t)stages_for(MT) * MT * 128 + (size_t)kRawStages * kRawStageBytes >= (size_t)2 * MT * 128 * 4;
+    return (size_t)bstages_for(MT, QN) * bslot_bytes(MT, QN) + (size_t)rstages_for(MT, QN) * QN * kUnitBytes >=
+           (size_t)QN * MT * 128 * 4;
 }
 
 struct GemmArgs {
@@ -88,28 +110,36 @@ struct GemmArgs {
     DeviceStatus* status;
 };
 
-template <int MT>
+template <int MT, int QN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
                     GemmArgs args) {
-    constexpr int ST = stages_for(MT);
-    constexpr int RS = kRawStages;
-    constexpr int BSLOT = MT * 128;
-    constexpr uint32_t A_COL0 = 2 * MT;  // first TMEM column of the A stages
+    static_assert(QN == 1 || QN == 2, "one or two 128-row units per CTA");
+    constexpr int ST = stages_for(MT, QN);
+    constexpr int SB = bstages_for(MT, QN);
+    constexpr int RS = rstages_for(MT, QN);
+    constexpr int KS = 128 / QN;               // k per stage and unit
+    constexpr int BSLOT = bslot_bytes(MT, QN);  // KS / 64 swizzled panels of MT x 64 fp16
+    constexpr int PANEL = MT * 128;
+    constexpr int RAWB = QN * kUnitBytes;      // one raw k-step
+    constexpr uint32_t A_COL0 = QN * MT;       // first TMEM column of the A stages
     constexpr uint32_t IDESC = idesc_f16(128, MT);
     static_assert(ST >= 2 && A_COL0 + ST * kAStageCols <= kTmemCols, "TMEM plan");
+    static_assert(SB % ST == 0, "B ring rounds cover whole A rings");
+    static_assert(2 * (RS + ST + SB) + 1 <= 240, "barrier area");
 
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-    unsigned char* sB = base;               // ST x MT*128 (1024-byte aligned slots)
-    unsigned char* sRaw = sB + ST * BSLOT;  // RS x 16896
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + RS * kRawStageBytes);
+    unsigned char* sB = base;               // SB x BSLOT (1024-byte aligned slots)
+    unsigned char* sRaw = sB + SB * BSLOT;  // RS x RAWB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + RS * RAWB);
     uint64_t* raw_full = bars;
     uint64_t* raw_empty = raw_full + RS;
-    uint64_t* a_full = raw_empty + RS;
-    uint64_t* b_full = a_full + ST;
-    uint64_t* st_empty = b_full + ST;
-    uint64_t* acc_full = st_empty + ST;
+    uint64_t* a_full = raw_empty + RS;  // ST: the 16 dequant warps' columns are in TMEM
+    uint64_t* a_empty = a_full + ST;    // ST: MMA commit, the stage's MMAs have read them
+    uint64_t* b_full = a_empty + ST;    // SB: activation tile landed (TMA bytes)
+    uint64_t* b_empty = b_full + SB;    // SB: MMA commit
+    uint64_t* acc_full = b_empty + SB;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -125,7 +155,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int k0 = (int)(((long long)rank * args.KG) / S);
     const int k1 = (int)(((long long)(rank + 1) * args.KG) / S);
     const int n_items = k1 - k0;  // >= 1 (S <= KG)
-    const int n_halves = 2 * n_items;
+    const int n_stages = QN * n_items;
+    // int4 k-step it (the QN 128-row units of the tile) -> raw ring slot it % RS
+    auto issue_raw = [&](int it) {
+        const uint32_t rf = s_addr(&raw_full[it % RS]);
+        mbar_expect_tx(rf, RAWB);
+        for (int u = 0; u < QN; ++u) {
+            const uint8_t* src = args.w + ((size_t)(n_tile * QN + u) * args.KG + (k0 + it)) * kUnitBytes;
+            bulk_g2s(s_addr(sRaw + (it % RS) * RAWB + u * kUnitBytes), src, kUnitBytes, rf);
+        }
+    };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < RS; ++i) {
@@ -134,13 +173,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int i = 0; i < ST; ++i) {
             mbar_init(s_addr(&a_full[i]), kDeqWarps);
+            mbar_init(s_addr(&a_empty[i]), 1);
+        }
+        for (int i = 0; i < SB; ++i) {
             mbar_init(s_addr(&b_full[i]), 1);
-            mbar_init(s_addr(&st_empty[i]), 1);
+            mbar_init(s_addr(&b_empty[i]), 1);
         }
         mbar_init(s_addr(acc_full), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
+        // the first kEarlyRaw int4 k-steps start streaming now, ahead of the
+        // TMEM allocation and the block-wide barrier (issuing more here delays
+        // that barrier by more than it gains)
+        for (int it = 0; it < kEarlyRaw && it < n_items; ++it) issue_raw(it);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_addr(tmem_slot)),
@@ -156,21 +202,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------ int4 unit producer
         // (weights: read before pdl_wait -- they are written once, before any step)
+        // k-steps 0 .. kEarlyRaw-1 were issued before the block-wide barrier
         bool ok = true;
-        int it = 0;
+        int it = kEarlyRaw < n_items ? kEarlyRaw : n_items;
         for (; it < n_items; ++it) {
-            const int rs = it % RS;
-            if (it >= RS) ok = mbar_wait(s_addr(&raw_empty[rs]), ((it / RS) - 1) & 1);
+            if (it >= RS) ok = mbar_wait(s_addr(&raw_empty[it % RS]), ((it / RS) - 1) & 1);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
-            if (lane == 0) {
-                const uint32_t rf = s_addr(&raw_full[rs]);
-                mbar_expect_tx(rf, kRawStageBytes);
-                for (int u = 0; u < 2; ++u) {
-                    const uint8_t* src = args.w + ((size_t)(n_tile * 2 + u) * args.KG + (k0 + it)) * kUnitBytes;
-                    bulk_g2s(s_addr(sRaw + rs * kRawStageBytes + u * kUnitBytes), src, kUnitBytes, rf);
-                }
-            }
+            if (lane == 0) issue_raw(it);
             __syncwarp();
         }
         if (!ok && lane == 0) {
@@ -182,26 +221,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp == kBWarp) {
         // ------------------------------------------------ activation (B operand) producer
         if (args.pdl) pdl_wait();  // X is written by the kernel before this one
-        // Rounds of ST half-steps with the stage index unrolled, so every
-        // shared-memory and TMEM address below is a fixed offset from a
-        // loop-invariant base.
+        // Rounds of SB stages with the slot index unrolled, so every
+        // shared-memory address below is a fixed offset from a loop-invariant
+        // base.
         bool ok = true, stop = false;
         int j = 0;
-        for (int j0 = 0; j0 < n_halves && !stop; j0 += ST) {
+        for (int j0 = 0; j0 < n_stages && !stop; j0 += SB) {
 #pragma unroll
-            for (int s = 0; s < ST; ++s) {
-                j = j0 + s;
-                if (j >= n_halves) break;
-                if (j0 > 0) ok = mbar_wait(s_addr(&st_empty[s]), ((j0 / ST) - 1) & 1);
+            for (int sb = 0; sb < SB; ++sb) {
+                j = j0 + sb;
+                if (j >= n_stages) break;
+                if (j0 > 0) ok = mbar_wait(s_addr(&b_empty[sb]), ((j0 / SB) - 1) & 1);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) {
                     stop = true;
                     break;
                 }
                 if (lane == 0) {
-                    const uint32_t bf = s_addr(&b_full[s]);
+                    const uint32_t bf = s_addr(&b_full[sb]);
                     mbar_expect_tx(bf, BSLOT);
-                    tma_load_2d(s_addr(sB + s * BSLOT), &tmap_x, (k0 + (j >> 1)) * 128 + (j & 1) * 64, m_tile * MT, bf);
+#pragma unroll
+                    for (int pn = 0; pn < KS / 64; ++pn)
+                        tma_load_2d(s_addr(sB + sb * BSLOT + pn * PANEL), &tmap_x, k0 * 128 + j * KS + pn * 64,
+                                    m_tile * MT, bf);
                 }
                 __syncwarp();
                 ++j;
@@ -211,68 +253,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             *abort_flag = 1;
             record_timeout(args.status, 5);
         }
-        // j = half-steps issued; drain the last one
-        if (j > 0) (void)mbar_wait(s_addr(&b_full[(j - 1) % ST]), ((j - 1) / ST) & 1);
+        // j = stages issued; drain the last one
+        if (j > 0) (void)mbar_wait(s_addr(&b_full[(j - 1) % SB]), ((j - 1) / SB) & 1);
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        // The descriptors are precomputed offsets of one base: an MMA whose
+        // One thread runs the loop: a stage's 8 MMAs are queued behind the
+        // previous stage's, so the time from one commit to the next stage's
+        // first MMA is idle tensor pipe and is kept to one barrier probe.  The
+        // descriptors are precomputed offsets of one base: an MMA whose
         // operands are recomputed in the issue loop costs several times the
         // tensor-pipe time of the instruction itself.
-        const uint64_t bdesc0 = sw128_desc(s_addr(sB));
-        const uint32_t a_base = tmem + A_COL0;
-        bool ok = true, timed_out = false, stop = false;
-        for (int j0 = 0; j0 < n_halves && !stop; j0 += ST) {
-            const uint32_t par = (uint32_t)(j0 / ST) & 1u;
+        if (lane == 0) {
+            const uint64_t bdesc0 = sw128_desc(s_addr(sB));
+            const uint32_t a_base = tmem + A_COL0;
+            bool ok = true;
+            // rounds of SB stages: B slot u, A stage u % ST (both constants)
+            for (int j0 = 0; j0 < n_stages && ok; j0 += SB) {
+                const uint32_t bpar = (uint32_t)(j0 / SB) & 1u;
+                const int a_uses = j0 / ST;  // uses of every A stage before this round
 #pragma unroll
-            for (int s = 0; s < ST; ++s) {
-                const int j = j0 + s;
-                if (j >= n_halves) break;
-                ok = mbar_wait(s_addr(&a_full[s]), par) && mbar_wait(s_addr(&b_full[s]), par);
-                timed_out = !__all_sync(0xffffffffu, ok);
-                if (timed_out || __any_sync(0xffffffffu, *abort_flag != 0)) {
-                    ok = false;
-                    stop = true;
-                    break;
-                }
-                tc_fence_after();
-                if (lane == 0) {
+                for (int u = 0; u < SB; ++u) {
+                    const int j = j0 + u;
+                    if (j >= n_stages) break;
+                    const int s = u % ST;
+                    if (!mbar_wait(s_addr(&a_full[s]), (uint32_t)(a_uses + u / ST) & 1u) ||
+                        !mbar_wait(s_addr(&b_full[u]), bpar)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        // B: slot s, k16 slice ks (32 bytes into each 128-byte swizzled row)
-                        const uint64_t bd = bdesc0 + (uint64_t)((s * BSLOT + ks * 32) >> 4);
+                    for (int ks = 0; ks < KS / 16; ++ks) {
+                        // B: slot u, panel ks / 4, k16 slice ks % 4 (32 bytes into each 128-byte swizzled row)
+                        const uint64_t bd = bdesc0 + (uint64_t)((u * BSLOT + (ks >> 2) * PANEL + (ks & 3) * 32) >> 4);
 #pragma unroll
-                        for (int q = 0; q < 2; ++q)  // unit q: A columns q*32 + ks*8 .. +8 (k16 = 8 columns)
+                        for (int q = 0; q < QN; ++q)  // unit q: A columns q*KS/2 + ks*8 .. +8 (k16 = 8 columns)
                             tc_mma_f16_ts(tmem + (uint32_t)(q * MT),
-                                          a_base + (uint32_t)(s * kAStageCols + q * 32 + ks * 8), bd, IDESC,
+                                          a_base + (uint32_t)(s * kAStageCols + q * (KS / 2) + ks * 8), bd, IDESC,
                                           (j > 0 || ks > 0) ? 1u : 0u);
                     }
-                    tc_commit(s_addr(&st_empty[s]));
+                    tc_commit(s_addr(&a_empty[s]));
+                    tc_commit(s_addr(&b_empty[u]));
                 }
-                __syncwarp();
             }
-        }
-        if (lane == 0) {
             if (ok) tc_commit(s_addr(acc_full));
-            else {
+            else {  // a stage never filled: a producer failed (and flagged it) or timed out
                 *abort_flag = 1;
-                if (timed_out) record_timeout(args.status, 2);
+                record_timeout(args.status, 2);
             }
         }
+        __syncwarp();
     } else if (warp >= 2 && warp < 2 + kDeqWarps) {
         // ------------------------------------------------ dequant
         // A warp may only touch TMEM lanes 32*(warp%4) .. +31.  The four warps
-        // of one lane quarter split a half-step as (unit q, k-quarter kh): the
+        // of one lane quarter split a stage as (unit q, 32-k slice kh): the
         // thread = weight row r of unit q, 32 k (4 words, 16 TMEM columns).
         const int dw = warp - 2;
-        const int q = (dw >> 2) & 1;
-        const int kh = dw >> 3;
+        const int q = (dw >> 2) % QN;
+        const int kh = (dw >> 2) / QN;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(q * 32 + kh * 16);
+        const uint32_t t_row =
+            tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(q * (KS / 2) + kh * 16);
         const __half2 bias = __float2half2_rn(1032.0f);
         bool ok = true;
-        // Rounds of ST k-steps = 2*ST half-steps, so the stage of half-step h
-        // of a round is the constant h % ST.
+        // Rounds of ST k-steps = QN*ST stages, so the stage of the round's
+        // stage h is the constant h % ST.
         for (int it0 = 0; it0 < n_items && ok; it0 += ST) {
 #pragma unroll
             for (int u = 0; u < ST; ++u) {
@@ -283,19 +329,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // warp-uniform decision: the tcgen05.st below is a .sync.aligned warp instruction
                 ok = __all_sync(0xffffffffu, ok && !*abort_flag);
                 if (!ok) break;
-                const unsigned char* unit = sRaw + rs * kRawStageBytes + q * kUnitBytes;
+                const unsigned char* unit = sRaw + rs * RAWB + q * kUnitBytes;
                 const __half2 s2 = __half2half2(*reinterpret_cast<const __half*>(unit + 8192 + r * 2));
 #pragma unroll
-                for (int hk = 0; hk < 2; ++hk) {
-                    const int s = (2 * u + hk) % ST;
-                    const int j = 2 * it + hk;
-                    if (j >= ST) ok = mbar_wait(s_addr(&st_empty[s]), ((j / ST) - 1) & 1);
+                for (int hk = 0; hk < QN; ++hk) {
+                    const int s = (QN * u + hk) % ST;
+                    const int j = QN * it + hk;
+                    if (j >= ST) ok = mbar_wait(s_addr(&a_empty[s]), ((j / ST) - 1) & 1);
                     ok = __all_sync(0xffffffffu, ok && !*abort_flag);
                     if (!ok) break;
                     uint32_t wv[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i)  // word (kc, r): k = kc*8 .. kc*8+7 of row r; lanes read consecutive words
-                        wv[i] = *reinterpret_cast<const uint32_t*>(unit + (((hk * 8 + kh * 4 + i) * 128 + r) << 2));
+                        wv[i] = *reinterpret_cast<const uint32_t*>(
+                            unit + (((hk * (KS / 8) + kh * 4 + i) * 128 + r) << 2));
                     uint32_t outw[16];  // column i*4+jj = fp16 pair (k = 8i+2jj, 8i+2jj+1) of this k-quarter
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -325,9 +372,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 
     // ---------------------------------------------------- epilogue (all threads)
-    // Warps 2-13 (three per TMEM lane quarter) drain the accumulators into
+    // Warps 2-17 (four per TMEM lane quarter) drain the accumulators into
     // shared memory as [token][weight row] fp32 (the rings are idle now).  The
-    // tile then leaves by one TMA store per half (a TMA reduce-add for mode 1)
+    // tile then leaves by one TMA store per unit (a TMA reduce-add for mode 1)
     // when Y's rows are 16-byte aligned, else by coalesced plain stores.
     const bool epi_warp = warp >= 2 && warp < 2 + kDeqWarps;
     const int quad = warp & 3;       // TMEM lane quarter = weight rows quad*32 .. +31
@@ -352,23 +399,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[jj]);
         }
     };
-    // Both halves of this CTA's accumulator are parked in shared memory as
-    // [half][token][128].  The CTA's share of the output is token rows
-    // [r0, r0 + MT/S) of both halves: with S > 1 it sums those rows over the S
+    // The QN units of this CTA's accumulator are parked in shared memory as
+    // [unit][token][128].  The CTA's share of the output is token rows
+    // [r0, r0 + MT/S) of every unit: with S > 1 it sums those rows over the S
     // CTAs of the cluster through DSMEM, in rank order, in place (each CTA
     // overwrites only its own rows, which no peer reads), then writes them.
-    float* stage = reinterpret_cast<float*>(base);  // [2][MT][128]
+    float* stage = reinterpret_cast<float*>(base);  // [QN][MT][128]
     const int rows = MT / S, r0 = rank * rows;       // S divides MT (16 | MT, S <= 8)
     if (epi_warp && acc_ok) {
-        drain(0, stage);
-        drain(1, stage + MT * 128);
+#pragma unroll
+        for (int q = 0; q < QN; ++q) drain(q, stage + q * MT * 128);
     }
-    if constexpr (reduce_fits<MT>()) {
+    if constexpr (reduce_fits<MT, QN>()) {
         if (S > 1) {
             __syncthreads();
             cluster_sync_all();  // every CTA's partial tile is parked
             if (!*abort_flag) {
-                const int nvec = 2 * rows * 32;  // float4 columns of (half, row)
+                const int nvec = QN * rows * 32;  // float4 columns of (unit, row)
                 for (int idx = threadIdx.x; idx < nvec; idx += blockDim.x) {
                     const int q = idx / (rows * 32), rem = idx - q * rows * 32;
                     float* p = stage + (size_t)q * MT * 128 + (r0 + (rem >> 5)) * 128 + (rem & 31) * 4;
@@ -398,7 +445,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // fp32 rows, then the CTA overwrites the start of its own half-0 rows
     // (no peer reads them) with a dense fp16 [rows][128] box.
     __half* hbox = reinterpret_cast<__half*>(stage + r0 * 128);
-    if (args.mode == 2) {
+    if (QN == 2 && args.mode == 2) {
         constexpr int kItems = (MT * 16 + kGemmThreads - 1) / kGemmThreads;  // (row, 8 features) per thread
         const int nitems = rows * 16;
         uint4 hv[kItems];
@@ -436,7 +483,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
     if (args.pdl) pdl_wait();  // Y may still be read or written by earlier kernels
     __syncthreads();
-    if (args.mode == 2) {
+    if (QN == 2 && args.mode == 2) {
         if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
             if (args.tma_out) {
                 if (threadIdx.x == 0) {
@@ -454,18 +501,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
         if (args.tma_out) {
             if (threadIdx.x == 0) {
-                for (int q = 0; q < 2; ++q)  // a half wholly past N has nothing to write
-                    if (n_tile * 256 + q * 128 < args.N)
-                        tma_out_2d(&tmap_y, s_addr(stage + (size_t)q * MT * 128 + r0 * 128), n_tile * 256 + q * 128,
+                for (int q = 0; q < QN; ++q)  // a unit wholly past N has nothing to write
+                    if ((n_tile * QN + q) * 128 < args.N)
+                        tma_out_2d(&tmap_y, s_addr(stage + (size_t)q * MT * 128 + r0 * 128), (n_tile * QN + q) * 128,
                                    m_tile * MT + r0, args.mode);
                 bulk_commit();
                 bulk_wait_read();
             }
         } else {
-            for (int idx = threadIdx.x; idx < 2 * rows * 128; idx += blockDim.x) {
+            for (int idx = threadIdx.x; idx < QN * rows * 128; idx += blockDim.x) {
                 const int q = idx / (rows * 128), rem = idx - q * rows * 128;
                 const int r = r0 + rem / 128, c = rem & 127;
-                const int m = m_tile * MT + r, n = n_tile * 256 + q * 128 + c;
+                const int m = m_tile * MT + r, n = (n_tile * QN + q) * 128 + c;
                 if (m < args.M && n < args.N) {
                     float* y = args.Y + (size_t)m * args.ldy + n;
                     const float v = stage[(size_t)q * MT * 128 + r * 128 + c];
@@ -655,17 +702,17 @@ static int num_sms() {
     return g_num_sms;
 }
 
-template <int MT>
+template <int MT, int QN>
 static bool set_smem_attr() {
-    constexpr size_t smem = gemm_smem_bytes<MT>();
+    constexpr size_t smem = gemm_launch_smem<MT, QN>();
     static_assert(smem <= (size_t)kSmemBudget, "shared memory plan exceeds the opt-in limit");
-    static_assert(reduce_fits<MT>(), "split-K reduction buffer does not fit in the rings");
+    static_assert(reduce_fits<MT, QN>(), "split-K reduction buffer does not fit in the rings");
     // one CTA per SM: every CTA allocates all 512 TMEM columns, so two CTAs of
     // one cluster must never share an SM
     static_assert(smem > (size_t)kSmemBudget / 2, "shared memory plan must force one CTA per SM");
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(w4a16_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        if (cudaFuncSetAttribute(w4a16_tc_kernel<MT, QN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess) {
             cudaGetLastError();
             return false;
@@ -678,7 +725,7 @@ static bool set_smem_attr() {
 // How many clusters of S CTAs the device runs at once.  Clusters must fit
 // inside one GPC, so for S = 8 this is fewer than SMs / 8; planning with
 // SMs / S would turn a one-wave grid into two waves.
-template <int MT>
+template <int MT, int QN>
 static int max_active_clusters(int S) {
     static int cache[4] = {0, 0, 0, 0};
     const int idx = S == 1 ? 0 : (S == 2 ? 1 : (S == 4 ? 2 : 3));
@@ -686,11 +733,11 @@ static int max_active_clusters(int S) {
         int n = 0;
         if (S == 1) {
             n = num_sms();
-        } else if (set_smem_attr<MT>()) {
+        } else if (set_smem_attr<MT, QN>()) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3((unsigned)(S * num_sms()));
             cfg.blockDim = dim3(kGemmThreads);
-            cfg.dynamicSmemBytes = gemm_smem_bytes<MT>();
+            cfg.dynamicSmemBytes = gemm_launch_smem<MT, QN>();
             cudaLaunchAttribute at[1];
             at[0].id = cudaLaunchAttributeClusterDimension;
             at[0].val.clusterDim.x = (unsigned)S;
@@ -698,7 +745,7 @@ static int max_active_clusters(int S) {
             at[0].val.clusterDim.z = 1;
             cfg.attrs = at;
             cfg.numAttrs = 1;
-            if (cudaOccupancyMaxActiveClusters(&n, w4a16_tc_kernel<MT>, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&n, w4a16_tc_kernel<MT, QN>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
                 n = 0;
             }
@@ -708,46 +755,77 @@ static int max_active_clusters(int S) {
     return cache[idx];
 }
 
-static int clusters_for(int MT, int S) {
+template <int QN>
+static int clusters_for_qn(int MT, int S) {
     switch (MT) {
-        case 16: return max_active_clusters<16>(S);
-        case 32: return max_active_clusters<32>(S);
-        case 64: return max_active_clusters<64>(S);
-        case 128: return max_active_clusters<128>(S);
-        default: return max_active_clusters<160>(S);
+        case 16: return max_active_clusters<16, QN>(S);
+        case 32: return max_active_clusters<32, QN>(S);
+        case 64: return max_active_clusters<64, QN>(S);
+        case 128: return max_active_clusters<128, QN>(S);
+        default: return max_active_clusters<160, QN>(S);
     }
 }
+static int clusters_for(int MT, int QN, int S) { return QN == 1 ? clusters_for_qn<1>(MT, S) : clusters_for_qn<2>(MT, S); }
 
-// Split factor S (CTAs per tile, a power of two <= 8 and <= KG) minimising
-// waves * (k-steps per CTA + setup), plus a penalty for the on-chip reduction.
-// A wave is as many clusters as the device co-schedules.
-GemmPlan plan_gemm(int M, int N, int K) {
+// Estimated time (us) of one plan: waves of co-scheduled clusters, each CTA
+// running ceil(KG / S) k-steps of QN units (8 MMAs of N = MT per unit and
+// k-step, at the power-capped tensor rate) plus its fixed setup and epilogue,
+// and the DSMEM reduction of split tiles (its data grows with QN).  Fitted to
+// timelines measured on B200.
+static double plan_cost(int MT, int QN, int S, int tiles, int KG) {
+    const int per_wave = clusters_for(MT, QN, S);
+    const double waves = (double)((tiles + per_wave - 1) / per_wave);
+    const double t8 = 0.28 + 0.0018 * MT;  // us per 8 MMAs (one unit, one k-step)
+    const double main = (double)((KG + S - 1) / S) * QN * t8;
+    return waves * (main + 5.0) + (S > 1 ? 0.8 + 2.1 * QN : 0.0);
+}
+
+// Units per CTA QN (from qn_mask: bit 0 allows 1, bit 1 allows 2) and split
+// factor S (CTAs per tile, a power of two <= 8 and <= KG) of least cost.
+static GemmPlan plan_gemm_qn(int M, int N, int K, int qn_mask) {
     GemmPlan p;
     p.MT = pick_mt(M);
     p.m_tiles = (M + p.MT - 1) / p.MT;
-    p.n_tiles = (N + 255) / 256;
     p.KG = (K + 127) / 128;
-    const int tiles = p.m_tiles * p.n_tiles;
     double best = 1e30;
+    p.QN = 2;
     p.S = 1;
-    for (int S = 1; S <= kMaxSplit && S <= p.KG; S *= 2) {
-        const int per_wave = clusters_for(p.MT, S);
-        const double waves = (double)((tiles + per_wave - 1) / per_wave);
-        const double items = (double)((p.KG + S - 1) / S);
-        const double cost = waves * (items + 1.0) + (S > 1 ? 1.5 : 0.0);
-        if (cost < best - 1e-9) {
-            best = cost;
-            p.S = S;
+    for (int QN = 2; QN >= 1; --QN) {
+        if (!(qn_mask & QN)) continue;
+        const int tiles = p.m_tiles * ((N + 128 * QN - 1) / (128 * QN));
+        for (int S = 1; S <= kMaxSplit && S <= p.KG; S *= 2) {
+            const double cost = plan_cost(p.MT, QN, S, tiles, p.KG);
+            if (cost < best - 1e-9) {
+                best = cost;
+                p.QN = QN;
+                p.S = S;
+            }
         }
     }
-    p.grid = tiles * p.S;
+    p.n_tiles = (N + 128 * p.QN - 1) / (128 * p.QN);
+    p.grid = p.m_tiles * p.n_tiles * p.S;
     return p;
 }
 
-template <int MT>
+GemmPlan plan_gemm(int M, int N, int K) { return plan_gemm_qn(M, N, K, 3); }
+
+// A plan with QN and S fixed by the caller (validation of every path).
+static GemmPlan plan_fixed(int M, int N, int K, int QN, int S) {
+    GemmPlan p;
+    p.MT = pick_mt(M);
+    p.m_tiles = (M + p.MT - 1) / p.MT;
+    p.KG = (K + 127) / 128;
+    p.QN = QN;
+    p.S = S;
+    p.n_tiles = (N + 128 * QN - 1) / (128 * QN);
+    p.grid = p.m_tiles * p.n_tiles * S;
+    return p;
+}
+
+template <int MT, int QN>
 static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_y, const GemmArgs& a, int grid, cudaStream_t s) {
-    constexpr size_t smem = gemm_smem_bytes<MT>();
-    if (!set_smem_attr<MT>()) {
+    constexpr size_t smem = gemm_launch_smem<MT, QN>();
+    if (!set_smem_attr<MT, QN>()) {
         set_error("w4a16_gemm: cannot opt in to the shared memory the kernel needs");
         return SPECDEC_ECUDA;
     }
@@ -765,7 +843,7 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_y, const Gem
     attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = a.pdl ? 2 : 1;
-    SD_CUDA(cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<MT>, map, map_y, a));
+    SD_CUDA(cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<MT, QN>, map, map_y, a));
     return SPECDEC_OK;
 }
 
@@ -774,16 +852,25 @@ static int launch_tc(const CUtensorMap& map, const CUtensorMap& map_y, const Gem
 size_t gemm_workspace_bytes(const GemmPlan&) { return 0; }
 size_t gemm_workspace_bound(int, int, int) { return 0; }
 
-static int launch_mt(const CUtensorMap& map, const CUtensorMap& map_y, const GemmArgs& a, const GemmPlan& p,
-                     cudaStream_t s) {
+template <int QN>
+static int launch_mt_qn(const CUtensorMap& map, const CUtensorMap& map_y, const GemmArgs& a, const GemmPlan& p,
+                        cudaStream_t s) {
     switch (p.MT) {
-        case 16: return launch_tc<16>(map, map_y, a, p.grid, s);
-        case 32: return launch_tc<32>(map, map_y, a, p.grid, s);
-        case 64: return launch_tc<64>(map, map_y, a, p.grid, s);
-        case 128: return launch_tc<128>(map, map_y, a, p.grid, s);
-        case 160: return launch_tc<160>(map, map_y, a, p.grid, s);
+        case 16: return launch_tc<16, QN>(map, map_y, a, p.grid, s);
+        case 32: return launch_tc<32, QN>(map, map_y, a, p.grid, s);
+        case 64: return launch_tc<64, QN>(map, map_y, a, p.grid, s);
+        case 128: return launch_tc<128, QN>(map, map_y, a, p.grid, s);
+        case 160: return launch_tc<160, QN>(map, map_y, a, p.grid, s);
         default: break;
     }
+    set_error("w4a16_gemm: unsupported token tile");
+    return SPECDEC_EINVAL;
+}
+
+static int launch_mt(const CUtensorMap& map, const CUtensorMap& map_y, const GemmArgs& a, const GemmPlan& p,
+                     cudaStream_t s) {
+    if (p.QN == 1) return launch_mt_qn<1>(map, map_y, a, p, s);
+    if (p.QN == 2) return launch_mt_qn<2>(map, map_y, a, p, s);
     set_error("w4a16_gemm: unsupported token tile");
     return SPECDEC_EINVAL;
 }
@@ -821,10 +908,15 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
 
 int swiglu_units(int F) { return 2 * ((F + 127) / 128); }
 
-GemmPlan plan_gemm_swiglu(int M, int F, int K) { return plan_gemm(M, 128 * swiglu_units(F), K); }
+// the SwiGLU epilogue pairs gate and up units: two units per CTA
+GemmPlan plan_gemm_swiglu(int M, int F, int K) { return plan_gemm_qn(M, 128 * swiglu_units(F), K, 2); }
 
 int gemm_launch_swiglu(const CUtensorMap& map, const GemmPlan& p, const void* w_gu, int M, int F, __half* h, int ldh,
                        cudaStream_t s, bool pdl) {
+    if (p.QN != 2) {
+        set_error("w4a16_gemm_swiglu: the plan must pair gate and up units");
+        return SPECDEC_EINVAL;
+    }
     GemmArgs a = gemm_args(p, w_gu, M, 128 * swiglu_units(F), ldh, 2, pdl);
     a.H = h;
     a.F = F;
@@ -880,6 +972,30 @@ extern "C" int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void*
              SPECDEC_EINVAL, "w4a16_gemm: bad argument");
     if (M == 0) return SPECDEC_OK;
     GemmPlan p = plan_gemm(M, N, K);
+    CUtensorMap map;
+    int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
+    if (rc) return rc;
+    return gemm_launch(map, p, w_tiled, M, N, Y, ldy, mode, nullptr, as_stream(stream), false);
+}
+
+extern "C" int specdec_w4a16_plan(int M, int N, int K, int units, int32_t* out) {
+    SD_CHECK(out && M > 0 && N > 0 && K > 0 && units >= 0 && units <= 2, SPECDEC_EINVAL, "w4a16_plan: bad argument");
+    const GemmPlan p = plan_gemm_qn(M, N, K, units == 0 ? 3 : units);
+    out[0] = p.MT;
+    out[1] = p.QN;
+    out[2] = p.S;
+    out[3] = p.grid;
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_w4a16_gemm_with_plan(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K,
+                                            float* Y, int ldy, int mode, int qn, int split, void* stream) {
+    SD_CHECK(X && w_tiled && Y && M >= 0 && N > 0 && K > 0 && ldx >= K && ldy >= N && (mode == 0 || mode == 1) &&
+                 (qn == 1 || qn == 2) && (split == 1 || split == 2 || split == 4 || split == 8) &&
+                 split <= (K + 127) / 128,
+             SPECDEC_EINVAL, "w4a16_gemm_with_plan: bad argument");
+    if (M == 0) return SPECDEC_OK;
+    const GemmPlan p = plan_fixed(M, N, K, qn, split);
     CUtensorMap map;
     int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);
     if (rc) return rc;

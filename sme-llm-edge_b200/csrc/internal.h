@@ -19,7 +19,8 @@ namespace specdec {
 struct GemmPlan {
     int MT;       // token tile
     int m_tiles;  // token tiles
-    int n_tiles;  // 256-row weight tiles
+    int QN;       // 128-row weight units per CTA (1 or 2)
+    int n_tiles;  // weight tiles of 128 * QN rows
     int KG;       // 128-wide k steps
     int S;        // CTAs per tile (cluster size, split of the k range)
     int grid;     // CTAs launched

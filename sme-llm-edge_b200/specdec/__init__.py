@@ -83,6 +83,8 @@ _SIGS = {
     "specdec_w4a16_workspace_bytes": (SZ, [I, I, I]),
     "specdec_w4a16_gemm": (I, [P, I, I, P, I, I, P, I, I, P, SZ, P]),
     "specdec_w4a16_gemm_swiglu": (I, [P, I, I, P, I, I, P, I, P]),
+    "specdec_w4a16_plan": (I, [I, I, I, I, P]),
+    "specdec_w4a16_gemm_with_plan": (I, [P, I, I, P, I, I, P, I, I, I, I, P]),
     "specdec_w4a16_gemm_simt": (I, [P, I, I, P, I, I, P, I, I, P]),
     "specdec_attention_workspace_bytes": (SZ, [I, I, I, I, I, I]),
     "specdec_attention": (I, [P, P, I, I, I, P, I, P, P, I, I, I, P, P, SZ, P]),

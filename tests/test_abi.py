@@ -47,3 +47,26 @@ def test_invalid_arguments_fail_loudly_without_gpu():
     assert rc == specdec.EINVAL and "bad argument" in specdec.last_error()
     h = C.c_void_p()
     assert specdec.lib().specdec_kv_create(0, 16, 1, 1, C.byref(h)) == specdec.EINVAL
+
+
+def test_gemm_plan_is_consistent():
+    """The planner's choice (host logic only): a valid token tile, units per
+    CTA and split, and a grid of tiles x split; small weight matrices get
+    one-unit tiles so the grid covers more SMs."""
+    import ctypes as C
+
+    import specdec
+
+    out = (C.c_int32 * 4)()
+    for M, N, K in [(1, 4096, 4096), (16, 4096, 4096), (160, 4096, 4096), (160, 4096, 14336), (160, 6144, 4096),
+                    (160, 28672, 4096), (160, 128256, 4096), (300, 512, 256), (7, 100, 200)]:
+        assert specdec.lib().specdec_w4a16_plan(M, N, K, 0, out) == 0
+        MT, QN, S, grid = list(out)
+        assert MT in (16, 32, 64, 128, 160) and (M <= MT or MT in (128, 160))
+        assert QN in (1, 2) and S in (1, 2, 4, 8) and S <= (K + 127) // 128 and MT % S == 0
+        m_tiles = (M + MT - 1) // MT
+        n_tiles = (N + 128 * QN - 1) // (128 * QN)
+        assert grid == m_tiles * n_tiles * S
+    assert specdec.lib().specdec_w4a16_plan(160, 4096, 14336, 0, out) == 0 and out[1] == 1
+    assert specdec.lib().specdec_w4a16_plan(160, 4096, 14336, 2, out) == 0 and out[1] == 2
+    assert specdec.lib().specdec_w4a16_plan(0, 4096, 4096, 0, out) != 0

@@ -234,6 +234,33 @@ def test_w4a16_gemm_tcgen05_matches_oracle(cuda_device, M, N, K):
     np.testing.assert_allclose(Y.cpu().numpy(), 2 * y, rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("M,N,K", [(160, 4096, 1024), (16, 1024, 2048), (100, 768, 1024), (300, 640, 512),
+                                   (32, 384, 384)])
+def test_w4a16_gemm_every_plan_matches_oracle(cuda_device, M, N, K):
+    """Every (units per CTA, k split) path the planner may pick, on one shape:
+    each within the GEMM tolerance of the oracle, and add mode exact."""
+    import torch
+
+    packed, scales, X16, d_tiled = _gemm_case(M, N, K, seed=7)
+    ref = O.w4a16_gemm(X16, packed, scales)
+    dX = dev(X16)
+    KG = (K + 127) // 128
+    for qn in (1, 2):
+        for split in (1, 2, 4, 8):
+            if split > KG:
+                continue
+            Y = zeros((M, N), torch.float32)
+            S.check(S.lib().specdec_w4a16_gemm_with_plan(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y), N, 0, qn, split,
+                                                         stream_ptr()))
+            sync()
+            y = Y.cpu().numpy()
+            np.testing.assert_allclose(y, ref, rtol=2e-3, atol=2e-3, err_msg=f"qn={qn} split={split}")
+            S.check(S.lib().specdec_w4a16_gemm_with_plan(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y), N, 1, qn, split,
+                                                         stream_ptr()))
+            sync()
+            np.testing.assert_allclose(Y.cpu().numpy(), 2 * y, rtol=1e-6, atol=1e-6, err_msg=f"qn={qn} split={split}")
+
+
 def test_w4a16_simt_matches_tcgen05(cuda_device):
     import torch
 
@@ -268,10 +295,12 @@ def test_w4a16_gemm_swiglu_matches_unfused(cuda_device, M, F, K, pad):
     ldh = F + pad
     h = zeros((M, ldh), torch.float16)
     S.check(S.lib().specdec_w4a16_gemm_swiglu(ptr(dX), M, K, ptr(d_tiled), F, K, ptr(h), ldh, stream_ptr()))
+    # the unfused GEMM on the fused call's plan: the same k-range sums, so the same g and u
+    plan = (C.c_int32 * 4)()
+    S.check(S.lib().specdec_w4a16_plan(M, N, K, 2, plan))
     Y = zeros((M, N), torch.float32)
-    ws_b = S.lib().specdec_w4a16_workspace_bytes(M, N, K)
-    ws = zeros(max(ws_b, 1), torch.uint8)
-    S.check(S.lib().specdec_w4a16_gemm(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y), N, 0, ptr(ws), ws_b, stream_ptr()))
+    S.check(S.lib().specdec_w4a16_gemm_with_plan(ptr(dX), M, K, ptr(d_tiled), N, K, ptr(Y), N, 0, 2, plan[2],
+                                                 stream_ptr()))
     sync()
     y = Y.cpu().numpy().reshape(M, N // 256, 2, 128)
     g = y[:, :, 0, :].reshape(M, -1)[:, :F]
