@@ -359,34 +359,42 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
 }
 
 // ------------------------------------------------------------ tcgen05 variant
-// For R * G <= 128 query rows (decode / chain verify).  The query tile is the
-// M = 128 side of every MMA, so the scores S = Q.K^T and the output O = P.V
-// accumulate in TMEM and the CUDA cores only run the softmax:
-//   warps 0-3  softmax, one thread per query row (TMEM lane): scale, mask,
-//              row max, P = exp2(s - m) in fp16 into TMEM, running sum.  O is
-//              rescaled only when a row's max grows by more than 2^8, so P
-//              stays below 256 and most groups never touch O.
-//   warp 5     TMA producer: per 16-token block one load for K (per 64-column
-//              half, into a K ring laid out [half][stage][16][64] so that four
-//              consecutive stages are one 64-row K-major operand) and one for V
-//   warp 6     TMEM allocator and MMA issuer: for a group of four blocks,
-//              S[g%2] = Q.K^T (M=128, N=64, K=HD); then O += P.V for the group
-//              before (M=128, N=HD, K=16 per block, P from TMEM, V MN-major)
-//   (warp 4 idles.)  A warp's SM sub-partition is its index mod 4 and TMEM
-//   lane quarter q belongs to sub-partition q, so the producer and the MMA
-//   issuer sit on sub-partitions 1 and 2, away from rows 0-31, the only busy
-//   softmax warp for up to 32 query rows: a single issuing thread slows down
-//   markedly when a busy warp shares its sub-partition.
+// For up to 128 query rows per CTA (decode / chain verify; a cluster of CTAs
+// per 128-row tile beyond).  The query tile is the M = 128 side of every MMA,
+// so the scores S = Q.K^T and the output O = P.V accumulate in TMEM and the
+// CUDA cores only run the softmax.  A group = four 16-token blocks = 64 keys.
+//   warps 0-7  softmax: warp w serves the query rows of TMEM lane quarter
+//              w % 4 and keys [32 * (w / 4), +32) of every group, one thread
+//              per row: scale, mask, row max (the two halves of a row swap
+//              theirs through shared memory), P = exp2(s - m) in fp16 into
+//              TMEM, running sum.  O is rescaled only when a row's max grows
+//              by more than 2^8, so P stays below 256 and most groups never
+//              touch O.
+//   warp 8     V producer, warp 9 K producer: one TMA load per block and
+//              64-column half into a ring of two groups each (K laid out
+//              [half][slot * 4 + block][16][64] so that a group is one 64-row
+//              K-major operand per half; V [slot * 4 + block][half][16][64]).
+//              A K slot is released by its group's Q.K^T and a V slot by its
+//              P.V, so the next K loads start while the softmax still runs.
+//   warp 10    TMEM allocator and MMA issuer: polls and issues whichever of
+//              the next Q.K^T (its K landed and S is free) and the next P.V
+//              (its P was written and its V landed) is ready.
+// A warp's SM sub-partition is its index mod 4 and TMEM lane quarter q belongs
+// to sub-partition q; up to 32 query rows (chain verify) only warps 0 and 4
+// compute, and the K producer and the MMA issuer sit on sub-partitions 1 and
+// 2, away from them: a single issuing thread slows down markedly when a busy
+// warp shares its sub-partition.
 // Two CTAs share an SM (one per sequence x KV head leaves most SMs with two),
 // so each allocates only 256 TMEM columns: O [0, HD), S (one 64-column
 // buffer, released by the softmax right after it is read) at 128, P (2 x 32)
-// at 192.  The query tile is an SW128 K-major shared-memory operand.  The MMA
-// issuer polls and issues whichever of the next Q.K^T (its blocks landed and
-// S is free) and the next P.V (its P was written) is ready.
-constexpr int kTcStages = 8;  // two groups of four blocks in flight
+// at 192.  The K / V streams start before the CTA loads its query tile and
+// allocates TMEM.
+constexpr int kTcGroupSlots = 2;                 // groups of four blocks in flight per ring
+constexpr int kTcStages = 4 * kTcGroupSlots;     // blocks per ring
 constexpr int kTcTmemCols = 256;
-constexpr int kTcThreads = 224;
-constexpr int kTcLoadWarp = 5, kTcMmaWarp = 6;
+constexpr int kTcSoftWarps = 8;
+constexpr int kTcVLoadWarp = 8, kTcKLoadWarp = 9, kTcMmaWarp = 10;
+constexpr int kTcThreads = 32 * (kTcMmaWarp + 1);
 constexpr uint32_t kTmemO = 0, kTmemS = 128, kTmemP = 192;
 
 // 2^x on the special-function unit (2 ulp); the result is rounded to fp16 next.
@@ -411,7 +419,8 @@ __device__ __forceinline__ uint64_t group_visibility(int key0, int ctx, int L, i
 
 __host__ __device__ constexpr size_t attn_tc_smem_bytes(int HD, int max_per) {
     return 1024 + (size_t)(HD / 64) * 16384 /* Q */ + (size_t)kTcStages * 2 * (HD / 64) * kBox /* K + V */ +
-           (size_t)((max_per + 3) & ~3) * 4 + (size_t)(2 * kTcStages + 8) * 8 + 16;
+           (size_t)((max_per + 3) & ~3) * 4 + 2 * 2 * 128 * 4 /* row max / sum exchange */ +
+           (size_t)(4 * kTcGroupSlots + 12) * 8 + 16;
 }
 
 template <int HD>
@@ -419,6 +428,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
     constexpr int NBOX = HD / 64;
     constexpr int ST = kTcStages;
+    constexpr int GS = kTcGroupSlots;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -426,14 +436,18 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     unsigned char* sK = sQ + NBOX * 16384;                // [NBOX][ST][16][128 B]
     unsigned char* sV = sK + (size_t)NBOX * ST * kBox;    // [ST][NBOX][16][128 B]
     int* tbl = reinterpret_cast<int*>(sV + (size_t)ST * NBOX * kBox);
-    uint64_t* full = reinterpret_cast<uint64_t*>(tbl + ((a.max_per + 3) & ~3));
-    uint64_t* empty = full + ST;
-    uint64_t* s_full = empty + ST;   // QK of a group landed in S
-    uint64_t* s_free = s_full + 1;   // the softmax read S (4 warps)
-    uint64_t* p_full = s_free + 1;   // [2] softmax wrote P[g%2] (4 warps)
-    uint64_t* pv_done = p_full + 2;  // [2] P.V of a group finished
+    float* xch = reinterpret_cast<float*>(tbl + ((a.max_per + 3) & ~3));  // [2 phases][2 halves][128 lanes]
+    uint64_t* k_full = reinterpret_cast<uint64_t*>(xch + 2 * 2 * 128);
+    uint64_t* k_empty = k_full + GS;
+    uint64_t* v_full = k_empty + GS;
+    uint64_t* v_empty = v_full + GS;
+    uint64_t* s_full = v_empty + GS;  // Q.K^T of a group landed in S
+    uint64_t* s_free = s_full + 1;    // the softmax read S (8 warps)
+    uint64_t* p_full = s_free + 1;    // [2] softmax wrote P[g%2] (8 warps)
+    uint64_t* pv_done = p_full + 2;   // [2] P.V of a group finished
     uint64_t* o_final = pv_done + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+    uint64_t* xbar = o_final + 1;     // [4] the two softmax warps of a lane quarter posted their values
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     pdl_trigger();  // a following GEMM may start streaming its weights
@@ -453,67 +467,79 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int n = min(bhi - blo, a.max_per);
     const int ngroups = (n + 3) / 4;
 
-    // ---- Q tile rows row0 + qi = r * G + g (zero past QR), written in the 128B-swizzled K-major layout
-    for (int idx = threadIdx.x; idx < 128 * (HD / 8); idx += blockDim.x) {
-        const int qi = idx / (HD / 8), c8 = idx % (HD / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (qi < QR) {
-            const int r = (row0 + qi) / a.G, g = (row0 + qi) % a.G;
-            v = *reinterpret_cast<const uint4*>(a.q + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD + c8 * 8);
-        }
-        *reinterpret_cast<uint4*>(sQ + (c8 >> 3) * 16384 + qi * 128 + (((c8 & 7) ^ (qi & 7)) << 4)) = v;
-    }
+    // block table slice and barriers first: the producers start streaming K and
+    // V right after the first block-wide barrier
     for (int i = threadIdx.x; i < n; i += blockDim.x) tbl[i] = a.tables[(size_t)b * a.max_blocks + blo + i];
-    fence_async_smem();  // Q is read by the tensor cores (async proxy)
     if (threadIdx.x == 0) {
-        for (int i = 0; i < ST; ++i) {
-            mbar_init(s_addr(&full[i]), 1);
-            mbar_init(s_addr(&empty[i]), 1);
+        for (int i = 0; i < GS; ++i) {
+            mbar_init(s_addr(&k_full[i]), 1);
+            mbar_init(s_addr(&k_empty[i]), 1);
+            mbar_init(s_addr(&v_full[i]), 1);
+            mbar_init(s_addr(&v_empty[i]), 1);
         }
         mbar_init(s_addr(s_full), 1);
-        mbar_init(s_addr(s_free), 4);
+        mbar_init(s_addr(s_free), kTcSoftWarps);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(s_addr(&p_full[i]), 4);
+            mbar_init(s_addr(&p_full[i]), kTcSoftWarps);
             mbar_init(s_addr(&pv_done[i]), 1);
         }
         mbar_init(s_addr(o_final), 1);
+        for (int i = 0; i < 4; ++i) mbar_init(s_addr(&xbar[i]), 2);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kTcMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_addr(tmem_slot)),
-                     "r"(kTcTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = __shfl_sync(0xffffffffu, *tmem_slot, 0);
 
     const int quarter = warp & 3;
-    const int qi = quarter * 32 + lane;                    // softmax warps: this thread's query row
-    const bool soft = warp < 4;
+    const int half = (warp >> 2) & 1;                  // softmax warps: key half of every group
+    const int qi = quarter * 32 + lane;                // softmax warps: this thread's query row (TMEM lane)
+    const bool soft = warp < kTcSoftWarps;
     const bool rows_here = soft && quarter * 32 < QR;  // warp holds at least one real row
-    float m_used = -INFINITY, l_sum = 0.f;
+    float m_used = -INFINITY, l_sum = 0.f;             // l_sum: this half's keys
+    uint32_t tmem = 0;
+    // Exchange k of a value with the other key half of the row (same lane, the
+    // quarter's other softmax warp): each posts into buffer k % 2 and arrives;
+    // the barrier's phase k completes when both have.  A buffer is rewritten
+    // two exchanges later, after the partner's arrival for the exchange in
+    // between, i.e. after it has read.  Bounded: false on timeout.
+    auto exchange = [&](int k, float& v) -> bool {
+        float* xb = xch + (k & 1) * 256;
+        xb[half * 128 + qi] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_addr(&xbar[quarter]));
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(s_addr(&xbar[quarter]), (uint32_t)k & 1u));
+        if (ok) v = xb[(half ^ 1) * 128 + qi];
+        return ok;
+    };
 
-    if (warp == kTcLoadWarp) {
-        // ------------------------------------------------ KV producer
+    if (warp == kTcKLoadWarp || warp == kTcVLoadWarp) {
+        // ------------------------------------------------ K / V producer, one group per wait
+        const bool is_k = warp == kTcKLoadWarp;
+        uint64_t* fullb = is_k ? k_full : v_full;
+        uint64_t* emptyb = is_k ? k_empty : v_empty;
         bool ok = true;
-        int j = 0;
-        for (; j < n; ++j) {
-            const int s = j % ST;
-            if (j >= ST) ok = mbar_wait(s_addr(&empty[s]), ((j / ST) - 1) & 1);
+        int g = 0;
+        for (; g < ngroups; ++g) {
+            const int slot = g % GS;
+            if (g >= GS) ok = mbar_wait(s_addr(&emptyb[slot]), ((g / GS) - 1) & 1);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
             if (lane == 0) {
-                int phys = tbl[j];
-                if (phys < 0 || phys >= a.num_blocks) phys = 0;  // a malformed table reads block 0, never out of range
-                const uint32_t fb = s_addr(&full[s]);
-                mbar_expect_tx(fb, 2 * NBOX * kBox);
+                const int nbg = min(4, n - 4 * g);
+                const uint32_t fb = s_addr(&fullb[slot]);
+                mbar_expect_tx(fb, (uint32_t)(nbg * NBOX * kBox));
+                for (int i = 0; i < nbg; ++i) {
+                    int phys = tbl[4 * g + i];
+                    if (phys < 0 || phys >= a.num_blocks) phys = 0;  // a malformed table reads block 0, never out of range
+                    const int s = slot * 4 + i;
+                    if (is_k) {
 #pragma unroll
-                for (int hb = 0; hb < NBOX; ++hb)
-                    tma_load_5d(s_addr(sK + ((size_t)hb * ST + s) * kBox), &kmap, 0, kvh * 16, hb, 0, phys, fb);
-                tma_load_5d(s_addr(sV + (size_t)s * NBOX * kBox), &vmap, 0, kvh * 16, 0, 1, phys, fb);
+                        for (int hb = 0; hb < NBOX; ++hb)
+                            tma_load_5d(s_addr(sK + ((size_t)hb * ST + s) * kBox), &kmap, 0, kvh * 16, hb, 0, phys, fb);
+                    } else {
+                        tma_load_5d(s_addr(sV + (size_t)s * NBOX * kBox), &vmap, 0, kvh * 16, 0, 1, phys, fb);
+                    }
+                }
             }
             __syncwarp();
         }
@@ -521,168 +547,212 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             *abort_flag = 1;
             record_timeout(a.status, 13);
         }
-        if (j > 0) (void)mbar_wait(s_addr(&full[(j - 1) % ST]), ((j - 1) / ST) & 1);
-    } else if (warp == kTcMmaWarp) {
-        // ------------------------------------------------ MMA issuer
-        // Issues Q.K^T of group gq once its blocks landed and the softmax has
-        // read S for group gq-1, and P.V of group gp once its P is in TMEM,
-        // whichever is ready first.
-        const uint32_t qb = s_addr(sQ), kb = s_addr(sK), vb = s_addr(sV);
-        bool ok = true, timed_out = false;
-        int gq = 0, gp = 0;
-        uint64_t t_idle = 0;
-        while (gp < ngroups) {
-            bool progressed = false;
-            if (gq < ngroups && gq <= gp + 1) {
-                const int nbg = min(4, n - 4 * gq);
-                const int st0 = (4 * gq) % ST;  // ST is a multiple of 4: a group never wraps
-                bool ready = gq == 0 || mbar_try(s_addr(s_free), (gq - 1) & 1);
-                for (int i = 0; i < nbg; ++i) ready = ready && mbar_try(s_addr(&full[st0 + i]), ((4 * gq + i) / ST) & 1);
-                if (__all_sync(0xffffffffu, ready)) {
-                    tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t idesc = idesc_f16(128, 16 * nbg);
+        // the loads issued above land before the CTA exits
+        if (g > 0) (void)mbar_wait(s_addr(&fullb[(g - 1) % GS]), ((g - 1) / GS) & 1);
+    } else {
+        // ------------------------------------------------ query tile and TMEM (warps 0-7 and 10)
+        if (soft) {
+            // rows row0 + qi = r * G + g (zero past QR), in the 128B-swizzled K-major layout
+            for (int idx = threadIdx.x; idx < 128 * (HD / 8); idx += 32 * kTcSoftWarps) {
+                const int r_i = idx / (HD / 8), c8 = idx % (HD / 8);
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (r_i < QR) {
+                    const int r = (row0 + r_i) / a.G, g = (row0 + r_i) % a.G;
+                    v = *reinterpret_cast<const uint4*>(a.q + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD +
+                                                        c8 * 8);
+                }
+                *reinterpret_cast<uint4*>(sQ + (c8 >> 3) * 16384 + r_i * 128 + (((c8 & 7) ^ (r_i & 7)) << 4)) = v;
+            }
+            fence_async_smem();  // Q is read by the tensor cores (async proxy)
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_addr(tmem_slot)),
+                         "r"(kTcTmemCols));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
+        tc_fence_before();
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * (kTcSoftWarps + 1)) : "memory");  // warps 0-7 and 10
+        tc_fence_after();
+        tmem = __shfl_sync(0xffffffffu, *tmem_slot, 0);
+
+        if (warp == kTcMmaWarp) {
+            // ------------------------------------------------ MMA issuer
+            const uint32_t qb = s_addr(sQ), kb = s_addr(sK), vb = s_addr(sV);
+            bool ok = true, timed_out = false;
+            int gq = 0, gp = 0;
+            uint64_t t_idle = 0;
+            while (gp < ngroups) {
+                bool progressed = false;
+                if (gq < ngroups && gq <= gp + 1) {
+                    const bool ready = mbar_try(s_addr(&k_full[gq % GS]), (gq / GS) & 1) &&
+                                       (gq == 0 || mbar_try(s_addr(s_free), (gq - 1) & 1));
+                    if (__all_sync(0xffffffffu, ready)) {
+                        tc_fence_after();
+                        if (lane == 0) {
+                            const int nbg = min(4, n - 4 * gq);
+                            const int st0 = (gq % GS) * 4;
+                            const uint32_t idesc = idesc_f16(128, 16 * nbg);
 #pragma unroll
-                        for (int kk = 0; kk < HD / 16; ++kk)
-                            tc_mma_f16_ss(tmem + kTmemS, sw128_desc(qb + (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32)),
-                                          sw128_desc(kb + (uint32_t)(((kk >> 2) * ST + st0) * kBox + (kk & 3) * 32)),
-                                          idesc, kk > 0 ? 1u : 0u);
-                        tc_commit(s_addr(s_full));
+                            for (int kk = 0; kk < HD / 16; ++kk)
+                                tc_mma_f16_ss(tmem + kTmemS,
+                                              sw128_desc(qb + (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32)),
+                                              sw128_desc(kb + (uint32_t)(((kk >> 2) * ST + st0) * kBox + (kk & 3) * 32)),
+                                              idesc, kk > 0 ? 1u : 0u);
+                            tc_commit(s_addr(s_full));
+                            tc_commit(s_addr(&k_empty[gq % GS]));
+                        }
+                        __syncwarp();
+                        ++gq;
+                        progressed = true;
                     }
+                }
+                if (gp < gq) {
+                    const bool ready = mbar_try(s_addr(&p_full[gp & 1]), (gp >> 1) & 1) &&
+                                       mbar_try(s_addr(&v_full[gp % GS]), (gp / GS) & 1);
+                    if (__all_sync(0xffffffffu, ready)) {
+                        tc_fence_after();
+                        if (lane == 0) {
+                            const int nbg = min(4, n - 4 * gp);
+                            for (int i = 0; i < nbg; ++i) {
+                                const int s = (gp % GS) * 4 + i;
+                                tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + (uint32_t)((gp & 1) * 32 + i * 8),
+                                              sw128_mn_desc(vb + (uint32_t)(s * NBOX * kBox), kBox, 1024),
+                                              idesc_f16_bmn(128, HD), (gp > 0 || i > 0) ? 1u : 0u);
+                            }
+                            tc_commit(s_addr(&pv_done[gp & 1]));
+                            tc_commit(s_addr(&v_empty[gp % GS]));
+                        }
+                        __syncwarp();
+                        ++gp;
+                        progressed = true;
+                    }
+                }
+                if (progressed) {
+                    t_idle = 0;
+                } else {
+                    // bounded: give up after ~2 s without progress
+                    const uint64_t now = gtimer();
+                    if (t_idle == 0) t_idle = now;
+                    timed_out = __any_sync(0xffffffffu, now - t_idle > 2000000000ull);
+                    if (timed_out || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            if (lane == 0) {
+                if (ok) tc_commit(s_addr(o_final));
+                else {
+                    *abort_flag = 1;
+                    if (timed_out) record_timeout(a.status, 14);
+                    mbar_arrive(s_addr(o_final));  // release the softmax warps' final wait
+                }
+            }
+        } else {
+            // ------------------------------------------------ softmax, one thread per (query row, key half)
+            const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+            const uint64_t rmask = qi < QR ? a.mask[(row0 + qi) / a.G] : ~0ull;
+            bool ok = true;
+            for (int g = 0; g < ngroups; ++g) {
+                ok = __all_sync(0xffffffffu, mbar_wait(s_addr(s_full), g & 1));
+                if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
+                tc_fence_after();
+                if (!rows_here) {
                     __syncwarp();
-                    ++gq;
-                    progressed = true;
-                }
-            }
-            if (gp < gq && __all_sync(0xffffffffu, mbar_try(s_addr(&p_full[gp & 1]), (gp >> 1) & 1))) {
-                const int nbg = min(4, n - 4 * gp);
-                tc_fence_after();
-                if (lane == 0) {
-                    for (int i = 0; i < nbg; ++i) {
-                        const int s = (4 * gp + i) % ST;
-                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + (uint32_t)((gp & 1) * 32 + i * 8),
-                                      sw128_mn_desc(vb + (uint32_t)(s * NBOX * kBox), kBox, 1024),
-                                      idesc_f16_bmn(128, HD), (gp > 0 || i > 0) ? 1u : 0u);
+                    if (lane == 0) mbar_arrive(s_addr(s_free));
+                } else {
+                    uint32_t sv[32];
+                    tc_ld_x32(t_lane + kTmemS + (uint32_t)(half * 32), sv);
+                    tc_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(s_addr(s_free));  // S may be overwritten by the next Q.K^T
+                    const int nkeys = 16 * min(4, n - 4 * g);
+                    const int key0 = (blo + 4 * g) * 16;
+                    // visibility of the group's 64 keys as one word: context keys,
+                    // then the new keys this row may see, cut at L and at the group end
+                    const uint32_t vis = (uint32_t)(group_visibility(key0, ctx, L, nkeys, rmask) >> (32 * half));
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const float x = ((vis >> c) & 1u) ? __uint_as_float(sv[c]) * a.scale_log2 : -INFINITY;
+                        sv[c] = __float_as_uint(x);
+                        mx = fmaxf(mx, x);
                     }
-                    tc_commit(s_addr(&pv_done[gp & 1]));
-                    for (int i = 0; i < nbg; ++i) tc_commit(s_addr(&empty[(4 * gp + i) % ST]));
-                }
-                __syncwarp();
-                ++gp;
-                progressed = true;
-            }
-            if (progressed) {
-                t_idle = 0;
-            } else {
-                // bounded: give up after ~2 s without progress
-                const uint64_t now = gtimer();
-                if (t_idle == 0) t_idle = now;
-                timed_out = __any_sync(0xffffffffu, now - t_idle > 2000000000ull);
-                if (timed_out || __any_sync(0xffffffffu, *abort_flag != 0)) {
-                    ok = false;
-                    break;
-                }
-            }
-        }
-        if (lane == 0) {
-            if (ok) tc_commit(s_addr(o_final));
-            else {
-                *abort_flag = 1;
-                if (timed_out) record_timeout(a.status, 14);
-                mbar_arrive(s_addr(o_final));  // release the softmax warps' final wait
-            }
-        }
-    } else if (soft) {
-        // ------------------------------------------------ softmax, one thread per query row
-        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-        const uint64_t rmask = qi < QR ? a.mask[(row0 + qi) / a.G] : ~0ull;
-        bool ok = true;
-        for (int g = 0; g < ngroups; ++g) {
-            ok = __all_sync(0xffffffffu, mbar_wait(s_addr(s_full), g & 1));
-            if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
-            tc_fence_after();
-            if (!rows_here) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(s_addr(s_free));
-            } else {
-                uint32_t sv[64];
-                tc_ld_x32(t_lane + kTmemS, sv);
-                tc_ld_x32(t_lane + kTmemS + 32, sv + 32);
-                tc_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(s_addr(s_free));  // S may be overwritten by the next Q.K^T
-                const int nkeys = 16 * min(4, n - 4 * g);
-                const int key0 = (blo + 4 * g) * 16;
-                // visibility of the group's 64 keys as one word: context keys,
-                // then the new keys this row may see, cut at L and at the group end
-                const uint64_t vis = group_visibility(key0, ctx, L, nkeys, rmask);
-                float mx = -INFINITY;
+                    // the row max over both key halves
+                    float mo = mx;
+                    ok = exchange(g, mo);
+                    if (!ok) break;
+                    mx = fmaxf(mx, mo);
+                    const bool grow = mx > m_used + 8.0f;  // also when the row had no visible key yet
+                    const float m_new = grow ? mx : m_used;
+                    const float alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+                    const float muse = m_new == -INFINITY ? 0.f : m_new;
+                    uint32_t pw[16];
+                    float sum = 0.f;
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const float x = ((vis >> c) & 1ull) ? __uint_as_float(sv[c]) * a.scale_log2 : -INFINITY;
-                    sv[c] = __float_as_uint(x);
-                    mx = fmaxf(mx, x);
-                }
-                const bool grow = mx > m_used + 8.0f;  // also when the row had no visible key yet
-                const float m_new = grow ? mx : m_used;
-                const float alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
-                const float muse = m_new == -INFINITY ? 0.f : m_new;
-                uint32_t pw[32];
-                float sum = 0.f;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const __half2 h = __floats2half2_rn(ex2_approx(__uint_as_float(sv[2 * j]) - muse),
-                                                        ex2_approx(__uint_as_float(sv[2 * j + 1]) - muse));
-                    sum += __low2float(h) + __high2float(h);
-                    pw[j] = *reinterpret_cast<const uint32_t*>(&h);
-                }
-                // P[g%2] was last read by P.V of group g-2
-                if (g >= 2) ok = mbar_wait(s_addr(&pv_done[g & 1]), ((g - 2) >> 1) & 1);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                tc_fence_after();
-                tc_st_x32(t_lane + kTmemP + (uint32_t)((g & 1) * 32), pw);
-                // O holds groups < g; rescale it once P.V of group g-1 has landed
-                if (g > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(s_addr(&pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1));
+                    for (int j = 0; j < 16; ++j) {
+                        const __half2 h = __floats2half2_rn(ex2_approx(__uint_as_float(sv[2 * j]) - muse),
+                                                            ex2_approx(__uint_as_float(sv[2 * j + 1]) - muse));
+                        sum += __low2float(h) + __high2float(h);
+                        pw[j] = *reinterpret_cast<const uint32_t*>(&h);
+                    }
+                    // P[g%2] was last read by P.V of group g-2
+                    if (g >= 2) ok = mbar_wait(s_addr(&pv_done[g & 1]), ((g - 2) >> 1) & 1);
+                    ok = __all_sync(0xffffffffu, ok);
                     if (!ok) break;
                     tc_fence_after();
+                    tc_st_x16(t_lane + kTmemP + (uint32_t)((g & 1) * 32 + half * 16), pw);
+                    // O holds groups < g; rescale this half's O columns once P.V of group g-1 has landed
+                    if (g > 0 && __any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
+                        ok = __all_sync(0xffffffffu, mbar_wait(s_addr(&pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1));
+                        if (!ok) break;
+                        tc_fence_after();
 #pragma unroll
-                    for (int c0 = 0; c0 < HD; c0 += 32) {
-                        uint32_t ov[32];
-                        tc_ld_x32(t_lane + kTmemO + (uint32_t)c0, ov);
-                        tc_wait_ld();
+                        for (int c0 = half * (HD / 2); c0 < (half + 1) * (HD / 2); c0 += 32) {
+                            uint32_t ov[32];
+                            tc_ld_x32(t_lane + kTmemO + (uint32_t)c0, ov);
+                            tc_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-                        tc_st_x32(t_lane + kTmemO + (uint32_t)c0, ov);
+                            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                            tc_st_x32(t_lane + kTmemO + (uint32_t)c0, ov);
+                        }
                     }
+                    l_sum = l_sum * alpha + sum;
+                    m_used = m_new;
+                    tc_wait_st();
                 }
-                l_sum = l_sum * alpha + sum;
-                m_used = m_new;
-                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_addr(&p_full[g & 1]));
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_addr(&p_full[g & 1]));
+            if (!ok && lane == 0) {
+                *abort_flag = 1;
+                record_timeout(a.status, 15);
+            }
+            // every MMA has finished (and read its shared-memory operands) after this
+            (void)__all_sync(0xffffffffu, mbar_wait(s_addr(o_final), 0));
+            tc_fence_after();
+            // the row's sum over both key halves
+            if (rows_here && ok) {
+                float lo = l_sum;
+                if (exchange(ngroups, lo)) l_sum += lo;
+                else if (lane == 0) {
+                    *abort_flag = 1;
+                    record_timeout(a.status, 16);
+                }
+            }
         }
-        if (!ok && lane == 0) {
-            *abort_flag = 1;
-            record_timeout(a.status, 15);
-        }
-        // every MMA has finished (and read its shared-memory operands) after this
-        (void)__all_sync(0xffffffffu, mbar_wait(s_addr(o_final), 0));
-        tc_fence_after();
     }
     __syncthreads();  // the Q tile and the rings are free from here on
 
-    // ---- output: this CTA's O rows; one CTA writes, a cluster merges through DSMEM
+    // ---- output: this CTA's O rows (each softmax warp half of the columns);
+    // one CTA writes, a cluster merges through DSMEM
     float* pO = reinterpret_cast<float*>(base);  // [128][HD]
     float* pML = pO + 128 * HD;                  // [128][2] = (m, l)
     const bool valid = !*abort_flag;
     if (rows_here && valid) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < HD; c0 += 32) {
+        for (int c0 = half * (HD / 2); c0 < (half + 1) * (HD / 2); c0 += 32) {
             uint32_t ov[32];
             tc_ld_x32(tmem + ((uint32_t)(quarter * 32) << 16) + kTmemO + (uint32_t)c0, ov);
             tc_wait_ld();
@@ -710,7 +780,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 }
             }
         }
-        if (S > 1 && qi < QR) {
+        if (S > 1 && half == 0 && qi < QR) {
             pML[qi * 2 + 0] = m_used;
             pML[qi * 2 + 1] = l_sum;
         }
