@@ -576,6 +576,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
         if (warp == kTcMmaWarp) {
             // ------------------------------------------------ MMA issuer
+            // Polls with test_wait: a try_wait on a barrier that is not ready
+            // may suspend the thread while the other operation is ready.
             const uint32_t qb = s_addr(sQ), kb = s_addr(sK), vb = s_addr(sV);
             bool ok = true, timed_out = false;
             int gq = 0, gp = 0;
@@ -583,8 +585,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             while (gp < ngroups) {
                 bool progressed = false;
                 if (gq < ngroups && gq <= gp + 1) {
-                    const bool ready = mbar_try(s_addr(&k_full[gq % GS]), (gq / GS) & 1) &&
-                                       (gq == 0 || mbar_try(s_addr(s_free), (gq - 1) & 1));
+                    const bool ready = mbar_test(s_addr(&k_full[gq % GS]), (gq / GS) & 1) &&
+                                       (gq == 0 || mbar_test(s_addr(s_free), (gq - 1) & 1));
                     if (__all_sync(0xffffffffu, ready)) {
                         tc_fence_after();
                         if (lane == 0) {
@@ -606,8 +608,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     }
                 }
                 if (gp < gq) {
-                    const bool ready = mbar_try(s_addr(&p_full[gp & 1]), (gp >> 1) & 1) &&
-                                       mbar_try(s_addr(&v_full[gp % GS]), (gp / GS) & 1);
+                    const bool ready = mbar_test(s_addr(&p_full[gp & 1]), (gp >> 1) & 1) &&
+                                       mbar_test(s_addr(&v_full[gp % GS]), (gp / GS) & 1);
                     if (__all_sync(0xffffffffu, ready)) {
                         tc_fence_after();
                         if (lane == 0) {

@@ -32,6 +32,19 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking probe (test_wait): for loops that poll several barriers, where
+// try_wait could suspend the thread on one that is not ready while another is.
+__device__ __forceinline__ bool mbar_test(uint32_t a, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // try_wait that lets the thread sleep (up to hint_ns) until the phase completes,
 // so waiting warps do not take issue slots from the working ones.
 __device__ __forceinline__ bool mbar_try_sleep(uint32_t a, uint32_t parity, uint32_t hint_ns) {
