@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
 //              by more than 2^8, so P stays below 256 and most groups never
 //              touch O.
 //   warp 8     V producer, warp 9 K producer: one TMA load per block and
-//              64-column half into a ring of two groups each (K laid out
+//              64-column half into a ring of GS groups each (K laid out
 //              [half][slot * 4 + block][16][64] so that a group is one 64-row
 //              K-major operand per half; V [slot * 4 + block][half][16][64]).
 //              A K slot is released by its group's Q.K^T and a V slot by its
@@ -389,8 +389,13 @@ __global__ void __launch_bounds__(MAXW * 32, MAXW == kAttnSmallWarps ? 3 : 1)
 // buffer, released by the softmax right after it is read) at 128, P (2 x 32)
 // at 192.  The K / V streams start before the CTA loads its query tile and
 // allocates TMEM.
-constexpr int kTcGroupSlots = 2;                 // groups of four blocks in flight per ring
-constexpr int kTcStages = 4 * kTcGroupSlots;     // blocks per ring
+// The query tile holds QROWS rows in shared memory: 128, or 32 when the tile
+// has at most 32 rows (chain verify).  The M = 128 MMAs then read rows 32-127
+// from the memory after the tile (the rings): those rows' S, P and O lanes are
+// never read, and the 24 KB saved (HD = 128) deepen both rings to three
+// groups, which the V stream needs: a V slot refills only after the P.V of the
+// group before last, and its HBM latency under load exceeds two groups.
+__host__ __device__ constexpr int tc_group_slots(int QROWS) { return QROWS == 32 ? 3 : 2; }
 constexpr int kTcTmemCols = 256;
 constexpr int kTcSoftWarps = 8;
 constexpr int kTcVLoadWarp = 8, kTcKLoadWarp = 9, kTcMmaWarp = 10;
@@ -417,23 +422,27 @@ __device__ __forceinline__ uint64_t group_visibility(int key0, int ctx, int L, i
     return (low_bits(ctx - key0) | fresh) & low_bits(L - key0) & low_bits(nkeys);
 }
 
-__host__ __device__ constexpr size_t attn_tc_smem_bytes(int HD, int max_per) {
-    return 1024 + (size_t)(HD / 64) * 16384 /* Q */ + (size_t)kTcStages * 2 * (HD / 64) * kBox /* K + V */ +
-           (size_t)((max_per + 3) & ~3) * 4 + 2 * 2 * 128 * 4 /* row max / sum exchange */ +
-           (size_t)(4 * kTcGroupSlots + 12) * 8 + 16;
+__host__ __device__ constexpr size_t attn_tc_smem_bytes(int HD, int QROWS, int max_per) {
+    return 1024 + (size_t)(HD / 64) * QROWS * 128 /* Q */ +
+           (size_t)4 * tc_group_slots(QROWS) * 2 * (HD / 64) * kBox /* K + V */ + (size_t)((max_per + 3) & ~3) * 4 +
+           2 * 2 * 128 * 4 /* row max / sum exchange */ + (size_t)(4 * tc_group_slots(QROWS) + 12) * 8 + 16;
 }
 
-template <int HD>
+template <int HD, int QROWS>
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
     constexpr int NBOX = HD / 64;
-    constexpr int ST = kTcStages;
-    constexpr int GS = kTcGroupSlots;
+    constexpr int GS = tc_group_slots(QROWS);  // groups of four blocks in flight per ring
+    constexpr int ST = 4 * GS;                 // blocks per ring
+    constexpr int QPANEL = QROWS * 128;        // one 64-column half of the query tile
+    // the MMAs read 128 query rows: the rows past a 32-row tile lie in the rings
+    static_assert(QROWS == 128 || (HD / 64) * QPANEL + (size_t)2 * ST * (HD / 64) * kBox >= (HD / 64) * 16384,
+                  "rows past the query tile stay inside the CTA's shared memory");
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* sQ = base;                             // [NBOX][128 rows][128 B], swizzled K-major
-    unsigned char* sK = sQ + NBOX * 16384;                // [NBOX][ST][16][128 B]
+    unsigned char* sQ = base;                             // [NBOX][QROWS][128 B], swizzled K-major
+    unsigned char* sK = sQ + NBOX * QPANEL;               // [NBOX][ST][16][128 B]
     unsigned char* sV = sK + (size_t)NBOX * ST * kBox;    // [ST][NBOX][16][128 B]
     int* tbl = reinterpret_cast<int*>(sV + (size_t)ST * NBOX * kBox);
     float* xch = reinterpret_cast<float*>(tbl + ((a.max_per + 3) & ~3));  // [2 phases][2 halves][128 lanes]
@@ -553,7 +562,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         // ------------------------------------------------ query tile and TMEM (warps 0-7 and 10)
         if (soft) {
             // rows row0 + qi = r * G + g (zero past QR), in the 128B-swizzled K-major layout
-            for (int idx = threadIdx.x; idx < 128 * (HD / 8); idx += 32 * kTcSoftWarps) {
+            for (int idx = threadIdx.x; idx < QROWS * (HD / 8); idx += 32 * kTcSoftWarps) {
                 const int r_i = idx / (HD / 8), c8 = idx % (HD / 8);
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if (r_i < QR) {
@@ -561,7 +570,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     v = *reinterpret_cast<const uint4*>(a.q + (((size_t)(b * a.R + r) * a.Hq) + kvh * a.G + g) * HD +
                                                         c8 * 8);
                 }
-                *reinterpret_cast<uint4*>(sQ + (c8 >> 3) * 16384 + r_i * 128 + (((c8 & 7) ^ (r_i & 7)) << 4)) = v;
+                *reinterpret_cast<uint4*>(sQ + (c8 >> 3) * QPANEL + r_i * 128 + (((c8 & 7) ^ (r_i & 7)) << 4)) = v;
             }
             fence_async_smem();  // Q is read by the tensor cores (async proxy)
         } else {
@@ -596,7 +605,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
                             for (int kk = 0; kk < HD / 16; ++kk)
                                 tc_mma_f16_ss(tmem + kTmemS,
-                                              sw128_desc(qb + (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32)),
+                                              sw128_desc(qb + (uint32_t)((kk >> 2) * QPANEL + (kk & 3) * 32)),
                                               sw128_desc(kb + (uint32_t)(((kk >> 2) * ST + st0) * kBox + (kk & 3) * 32)),
                                               idesc, kk > 0 ? 1u : 0u);
                             tc_commit(s_addr(s_full));
@@ -990,39 +999,44 @@ static int make_kv_tmap(CUtensorMap* map, const __half* kv, int num_blocks, int 
 // The kernel needs no global workspace (splits are merged on chip).
 size_t attention_workspace(int, int, int, int, int, int) { return 0; }
 
-static const void* attn_tc_fn(int HD) {
-    return HD == 128 ? reinterpret_cast<const void*>(attn_tc_kernel<128>) : reinterpret_cast<const void*>(attn_tc_kernel<64>);
+static const void* attn_tc_fn(int HD, int QROWS) {
+    if (HD == 128)
+        return QROWS == 32 ? reinterpret_cast<const void*>(attn_tc_kernel<128, 32>)
+                           : reinterpret_cast<const void*>(attn_tc_kernel<128, 128>);
+    return QROWS == 32 ? reinterpret_cast<const void*>(attn_tc_kernel<64, 32>)
+                       : reinterpret_cast<const void*>(attn_tc_kernel<64, 128>);
 }
 
 // tcgen05 variant: split count from the same cost model as the legacy kernel.
-static AttnPlan plan_attention_tc(int B, int R, int Hkv, int HD, int max_ctx) {
+static AttnPlan plan_attention_tc(int B, int R, int Hkv, int HD, int max_ctx, int QROWS) {
     AttnPlan p;
     p.MT = 8;
     p.KG = 1;
-    p.QRP = 128;
+    p.QRP = QROWS;
     p.threads = kTcThreads;
-    p.ST = kTcStages;
+    p.ST = 4 * tc_group_slots(QROWS);
     const int nb_max = (max_ctx + R + 15) / 16;
     const int pairs = B * Hkv;
-    static bool opted[2] = {false, false};
-    if (!opted[HD == 128]) {
+    static bool opted[4] = {false, false, false, false};
+    const int vi = (HD == 128 ? 2 : 0) + (QROWS == 32 ? 1 : 0);
+    if (!opted[vi]) {
         int dev = 0, optin = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaFuncSetAttribute(attn_tc_fn(HD), cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
-        opted[HD == 128] = true;
+        cudaFuncSetAttribute(attn_tc_fn(HD, QROWS), cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        opted[vi] = true;
     }
     p.S = 1;
     long long best_cost = -1;
     for (int S = 1; S <= 8 && S <= nb_max; ++S) {
         const int per = (nb_max + S - 1) / S;
-        const size_t sm = attn_tc_smem_bytes(HD, per);
+        const size_t sm = attn_tc_smem_bytes(HD, QROWS, per);
         int clusters = 0;
         {
             static std::mutex mu;
             static std::map<std::tuple<int, size_t, int>, int> cache;
             std::lock_guard<std::mutex> lk(mu);
-            auto key = std::make_tuple(HD, sm, S);
+            auto key = std::make_tuple(HD * 1000 + QROWS, sm, S);
             auto it = cache.find(key);
             if (it != cache.end()) {
                 clusters = it->second;
@@ -1038,7 +1052,7 @@ static AttnPlan plan_attention_tc(int B, int R, int Hkv, int HD, int max_ctx) {
                 at[0].val.clusterDim.z = 1;
                 cfg.attrs = at;
                 cfg.numAttrs = 1;
-                if (cudaOccupancyMaxActiveClusters(&clusters, attn_tc_fn(HD), &cfg) != cudaSuccess) {
+                if (cudaOccupancyMaxActiveClusters(&clusters, attn_tc_fn(HD, QROWS), &cfg) != cudaSuccess) {
                     cudaGetLastError();
                     clusters = 0;
                 }
@@ -1054,7 +1068,7 @@ static AttnPlan plan_attention_tc(int B, int R, int Hkv, int HD, int max_ctx) {
         }
     }
     p.max_per = (nb_max + p.S - 1) / p.S;
-    p.smem = attn_tc_smem_bytes(HD, p.max_per);
+    p.smem = attn_tc_smem_bytes(HD, QROWS, p.max_per);
     return p;
 }
 
@@ -1069,7 +1083,8 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
     if (R * (Hq / Hkv) <= 256) {
         // the tcgen05 kernel, one CTA (cluster) per 128 query rows
         const int mtiles = (R * (Hq / Hkv) + 127) / 128;
-        AttnPlan p = plan_attention_tc(B * mtiles, R, Hkv, HD, max_ctx);
+        const int qrows = R * (Hq / Hkv) <= 32 ? 32 : 128;  // query rows the tile stores
+        AttnPlan p = plan_attention_tc(B * mtiles, R, Hkv, HD, max_ctx, qrows);
         CUtensorMap kmap, vmap;
         int rc = make_kv_tmap(&kmap, kv_layer, num_blocks, Hkv, HD, 1, 1);
         if (!rc) rc = make_kv_tmap(&vmap, kv_layer, num_blocks, Hkv, HD, HD / 64, 1);
@@ -1107,8 +1122,10 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
         at[0].val.clusterDim.z = 1;
         cfg.attrs = at;
         cfg.numAttrs = 1;
-        if (HD == 128) SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<128>, kmap, vmap, a));
-        else SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<64>, kmap, vmap, a));
+        if (HD == 128 && qrows == 32) SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<128, 32>, kmap, vmap, a));
+        else if (HD == 128) SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<128, 128>, kmap, vmap, a));
+        else if (qrows == 32) SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<64, 32>, kmap, vmap, a));
+        else SD_CUDA(cudaLaunchKernelEx(&cfg, attn_tc_kernel<64, 128>, kmap, vmap, a));
         return SPECDEC_OK;
     }
     AttnPlan p = plan_attention(B, R, Hq / Hkv, Hkv, HD, max_ctx);
