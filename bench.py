@@ -314,9 +314,9 @@ def run_gpu(args, world, rank, local, pg):
     # DRAM bytes (read + write) of one launch from the committed ncu captures
     # (profiles/), with that launch's algorithmic bytes beside them
     if roof["bound"] == "tensor":
-        roof.update(traffic=332.4e6, traffic_launch="lm_head M=160 N=128256 K=4096", traffic_algorithmic=271.3e6)
+        roof.update(traffic=334.4e6, traffic_launch="lm_head M=160 N=128256 K=4096", traffic_algorithmic=271.3e6)
     else:
-        roof.update(traffic=276.2e6, traffic_launch="attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048",
+        roof.update(traffic=277.6e6, traffic_launch="attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048",
                     traffic_algorithmic=269.1e6)
     verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_bytes": vbytes,
               "verify_hbm_frac_of_measured": round(vbytes / (verify_ms * 1e-3) / 1e9 / peaks.get("hbm_gbs", 6650.0), 4),
