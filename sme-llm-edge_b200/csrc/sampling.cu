@@ -29,9 +29,14 @@ static_assert(sizeof(DevRowStats) == 32, "row stats layout");
 
 constexpr int kRowThreads = 1024;
 
+constexpr int kCdfChunk = 256;      // inverse CDF: elements per recorded chunk total (8 per lane)
+constexpr int kCdfChunksPerWarp = 32;  // so V <= 32 warps x 32 chunks x 256 = 262144
+constexpr int kMaxVocab = (kRowThreads / 32) * kCdfChunksPerWarp * kCdfChunk;
+
 struct RowSmem {
     uint64_t hist[256];
     u128 scan[32];
+    u128 chunk[32][kCdfChunksPerWarp];  // inverse CDF: mass of every 256-element chunk of a warp's range
     uint64_t red64[32];
     float redf[32];
     int redi[32];
@@ -65,8 +70,24 @@ __device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, floa
         }
     };
     if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+        // four float4 loads in flight per thread; indices still visited in increasing order
         const float4* z4 = reinterpret_cast<const float4*>(z);
-        for (int q = threadIdx.x; q < V / 4; q += blockDim.x) {
+        const int n4 = V / 4, bd = blockDim.x;
+        int q = threadIdx.x;
+        for (; q + 3 * bd < n4; q += 4 * bd) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = 4 * (q + u * bd);
+                upd(v[u].x, j);
+                upd(v[u].y, j + 1);
+                upd(v[u].z, j + 2);
+                upd(v[u].w, j + 3);
+            }
+        }
+        for (; q < n4; q += bd) {
             const float4 v = z4[q];
             upd(v.x, 4 * q);
             upd(v.y, 4 * q + 1);
@@ -185,7 +206,18 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
         const int warp_base = (threadIdx.x >> 5) * 32, stride = blockDim.x;
         if (!nucleus && (V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
             const float4* z4 = reinterpret_cast<const float4*>(z);
-            for (int q = threadIdx.x; q < V / 4; q += blockDim.x) {
+            const int n4 = V / 4, bd = blockDim.x;
+            int q = threadIdx.x;
+            for (; q + 3 * bd < n4; q += 4 * bd) {  // four float4 loads in flight per thread
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    s += (uint64_t)mass_of(v[u].x, m, c) + mass_of(v[u].y, m, c) + mass_of(v[u].z, m, c) +
+                         mass_of(v[u].w, m, c);
+            }
+            for (; q < n4; q += bd) {
                 const float4 v = z4[q];
                 s += (uint64_t)mass_of(v.x, m, c) + mass_of(v.y, m, c) + mass_of(v.z, m, c) + mass_of(v.w, m, c);
             }
@@ -287,20 +319,30 @@ __device__ __forceinline__ u128 warp_incl_scan_u128(u128 v) {
 // Smallest j (index order) whose running mass exceeds target_of(total), where
 // total = sum of all masses; returns -1 when the total is zero (or does not
 // exceed the target).  *total_out receives the total.
-// Warp w owns the contiguous index range [w*C, (w+1)*C): one coalesced pass
-// gives the warp totals; the warp holding the target then splits its range
-// into 32 contiguous sub-ranges (one per lane), finds the sub-range, and walks
-// it 32 indices at a time.  About one pass over the row instead of a
-// block-wide scan per tile.
+// Warp w owns the contiguous index range [w*C, (w+1)*C), C a multiple of 256,
+// and walks it in 256-element chunks (lane l: 8 contiguous elements), keeping
+// every chunk's mass in shared memory.  The warp whose range holds the target
+// then finds the chunk from those totals and re-reads only that chunk.  One
+// pass over the row plus 256 elements; every sum is an integer sum, so the
+// result does not depend on the order.
 template <class MassFn, class TargetFn>
 __device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, RowSmem& sm, u128* total_out) {
+    constexpr int E = kCdfChunk / 32;  // elements per lane and chunk
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int C = (((V + nw - 1) / nw) + 31) & ~31;  // per-warp range, a multiple of 32
+    const int C = ((V + nw - 1) / nw + kCdfChunk - 1) / kCdfChunk * kCdfChunk;
+    const int nch = C / kCdfChunk;  // <= kCdfChunksPerWarp (V <= 262144, checked by the launchers)
     const int lo = wid * C, hi = min(V, lo + C);
     u128 t = 0;
-    for (int j = lo + lane; j < hi; j += 32) t += mass(j);
-    t = warp_sum_u128(t);
-    __syncthreads();  // sm.scan may still be read by a previous caller
+    __syncthreads();  // sm.scan / sm.chunk may still be read by a previous caller
+    for (int ch = 0; ch < nch; ++ch) {
+        const int base = lo + ch * kCdfChunk + lane * E;
+        u128 sc = 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) sc += base + e < hi ? mass(base + e) : (u128)0;  // unrolled: loads in flight together
+        sc = warp_sum_u128(sc);
+        if (lane == 0) sm.chunk[wid][ch] = sc;
+        t += sc;
+    }
     if (lane == 0) sm.scan[wid] = t;
     __syncthreads();
     if (wid == 0) {
@@ -322,28 +364,32 @@ __device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, Row
     *total_out = sm.total;
     if (W >= 0 && wid == W) {
         const u128 tgt = sm.big;
-        const int sub = C / 32;  // lane l: sub-range [lo + l*sub, lo + (l+1)*sub)
-        const int slo = min(hi, lo + lane * sub), shi = min(hi, slo + sub);
-        u128 st = 0;
-        for (int j = slo; j < shi; ++j) st += mass(j);
-        const u128 si = warp_incl_scan_u128(st);
-        const bool h = si - st <= tgt && tgt < si;
-        const unsigned hb = __ballot_sync(0xffffffffu, h);
+        // the chunk holding the target
+        const u128 v = lane < nch ? sm.chunk[W][lane] : (u128)0;
+        const u128 incl = warp_incl_scan_u128(v);
+        const bool hit = lane < nch && incl - v <= tgt && tgt < incl;
+        const unsigned hb = __ballot_sync(0xffffffffu, hit);
         if (hb) {
-            const int L = __ffs(hb) - 1;
-            const u128 rem = tgt - shfl_u128(si - st, L);
-            const int clo = min(hi, lo + L * sub), chi = min(hi, clo + sub);
-            u128 run = 0;
-            for (int j0 = clo; j0 < chi; j0 += 32) {
-                const int j = j0 + lane;
-                const u128 m = j < chi ? mass(j) : (u128)0;
-                const u128 inc = warp_incl_scan_u128(m);
-                const unsigned fb = __ballot_sync(0xffffffffu, j < chi && run + inc > rem);
-                if (fb) {
-                    if (lane == 0) sm.result = j0 + __ffs(fb) - 1;
-                    break;
+            const int ch = __ffs(hb) - 1;
+            const u128 rem = tgt - shfl_u128(incl - v, ch);
+            // its 256 elements: lane sums, a warp scan, then the lane's 8 in order
+            const int base = lo + ch * kCdfChunk + lane * E;
+            u128 sl = 0;
+#pragma unroll
+            for (int e = 0; e < E; ++e) sl += base + e < hi ? mass(base + e) : (u128)0;
+            const u128 li = warp_incl_scan_u128(sl);
+            const bool h2 = li - sl <= rem && rem < li;
+            const unsigned b2 = __ballot_sync(0xffffffffu, h2);
+            if (h2 && lane == __ffs(b2) - 1) {  // the lane's 8 elements in order (recomputed)
+                u128 run = li - sl;
+                for (int e = 0; e < E; ++e) {
+                    const u128 me = base + e < hi ? mass(base + e) : (u128)0;
+                    if (run + me > rem) {
+                        sm.result = base + e;
+                        break;
+                    }
+                    run += me;
                 }
-                run += shfl_u128(inc, 31);
             }
         }
     }
@@ -731,6 +777,7 @@ int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaS
 int launch_accept_chain_dev(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
                             float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
                             int32_t* accepted_len, int32_t* out_tokens, void* ws, cudaStream_t s) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_accept_chain_dev: vocabulary above 262144");
     const bool greedy = !(temperature > 0.0f);
     const float c = greedy ? 0.0f : temp_coeff(temperature);
     const uint64_t tp = top_p_q32(top_p);
@@ -748,6 +795,7 @@ int launch_accept_chain_dev(const float* target, const float* draft, const int32
 int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, const int32_t* parent, int B, int R, int V,
                            float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
                            int32_t* accepted_len, int32_t* path, int32_t* out_tokens, cudaStream_t s) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_accept_tree_dev: vocabulary above 262144");
     const bool greedy = !(temperature > 0.0f);
     accept_tree_kernel<<<B, kRowThreads, 0, s>>>(target, node_tokens, parent, R, V, greedy ? 0.0f : temp_coeff(temperature),
                                                  top_p_q32(top_p), greedy, seed, step_dev, 0u, accepted_len, path,
@@ -758,6 +806,7 @@ int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, cons
 
 int launch_sample_rows_dev(const float* logits, int rows, int k, int V, float temperature, float top_p, uint64_t seed,
                            const uint32_t* step_dev, int32_t* out, cudaStream_t s) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_sample_rows_dev: vocabulary above 262144");
     const bool greedy = !(temperature > 0.0f);
     sample_rows_kernel<<<rows, kRowThreads, 0, s>>>(logits, k, V, greedy ? 0.0f : temp_coeff(temperature),
                                                     top_p_q32(top_p), greedy, seed, step_dev, 0u, out);
@@ -774,6 +823,7 @@ extern "C" size_t specdec_accept_workspace_bytes(int rows) { return (size_t)(row
 extern "C" int specdec_accept_chain(const float* target, const float* draft, const int32_t* drafts, int B, int k,
                                     int V, const specdec_sampling* sp, int32_t* accepted_len, int32_t* out_tokens,
                                     void* workspace, size_t workspace_bytes, void* stream) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "specdec_accept_chain: vocabulary above 262144");
     SD_CHECK(sp && target && drafts && accepted_len && out_tokens, SPECDEC_EINVAL, "accept_chain: null argument");
     SD_CHECK(B >= 0 && k >= 0 && V > 0, SPECDEC_EINVAL, "accept_chain: bad shape");
     if (B == 0) return SPECDEC_OK;
@@ -839,6 +889,7 @@ static int static_accept_rows(DevRowStats** out) {
 extern "C" int specdec_accept_chain_noalloc(const float* target, const float* draft, const int32_t* drafts, int B,
                                             int k, int V, const specdec_sampling* sp, int32_t* accepted_len,
                                             int32_t* out_tokens, void* stream) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "specdec_accept_chain_noalloc: vocabulary above 262144");
     SD_CHECK(sp && target && drafts && accepted_len && out_tokens, SPECDEC_EINVAL,
              "accept_chain_noalloc: null argument");
     SD_CHECK(B >= 0 && k >= 0 && V > 0, SPECDEC_EINVAL, "accept_chain_noalloc: bad shape");
@@ -871,6 +922,7 @@ extern "C" int specdec_accept_tree(const float* target, const int32_t* node_toke
                                    int R, int V, const specdec_sampling* sp, int32_t* accepted_len,
                                    int32_t* path_nodes, int32_t* out_tokens, void* workspace, size_t workspace_bytes,
                                    void* stream) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "specdec_accept_tree: vocabulary above 262144");
     (void)workspace;
     (void)workspace_bytes;
     SD_CHECK(sp && target && node_tokens && parent && accepted_len && path_nodes && out_tokens, SPECDEC_EINVAL,
@@ -888,6 +940,7 @@ extern "C" int specdec_accept_tree(const float* target, const int32_t* node_toke
 
 extern "C" int specdec_sample_rows(const float* logits, int rows, int k, int V, const specdec_sampling* sp,
                                    int32_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "specdec_sample_rows: vocabulary above 262144");
     (void)workspace;
     (void)workspace_bytes;
     SD_CHECK(sp && logits && out && rows >= 0 && k >= 1 && V > 0, SPECDEC_EINVAL, "sample_rows: bad argument");
