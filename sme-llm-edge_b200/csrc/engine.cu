@@ -184,8 +184,10 @@ static void launch_rmsnorm(const float* x, int ldx, int rows, int H, float eps, 
     rmsnorm_kernel<<<rows, kNormThreads, smem, s>>>(x, ldx, H, eps, out, ldo);
 }
 
-// RoPE on q and k (rotate-half pairs d, d + hd/2), K/V into their paged slots,
-// q to fp16.  qkv rows are [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].  A thread
+// RoPE on q and k (rotate-half pairs d, d + hd/2, as rust_sme_rope_f32,
+// src/sme_kernel/rust_sme/src/lib.rs:621-666), K/V into their paged slots,
+// q to fp16 (head dims that do not divide 128; otherwise the QKV GEMM's
+// epilogue does this).  qkv rows are [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)].  A thread
 // handles two adjacent dims (d, d+1) of a head: float2 loads, half2 stores.
 __global__ void rope_kv_kernel(const float* __restrict__ qkv, int ldq, const int32_t* __restrict__ pos,
                                const int32_t* __restrict__ slot, const int32_t* __restrict__ tables, int max_blocks,
@@ -488,6 +490,18 @@ int gemm(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int
     return rc;
 }
 
+// QKV projection + RoPE + K/V into their paged slots in one launch
+int gemm_qkv_rope(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int N, const RopeArgs& ra) {
+    GemmPlan p = plan_gemm_qkv(M, N, K);
+    CUtensorMap map;
+    int rc = make_x_tmap(&map, X, M, K, K, p.MT);
+    if (rc) return rc;
+    ++e->kernels_per_step;
+    rc = gemm_launch_qkv_rope(map, p, w, M, N, ra, e->stream, /*pdl=*/true);
+    prof_mark(e, e->gemm_cat);
+    return rc;
+}
+
 // gate/up projection + SwiGLU in one launch: h fp16 [M, F]
 int gemm_swiglu(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w_gu, int F, __half* h) {
     GemmPlan p = plan_gemm_swiglu(M, F, K);
@@ -528,10 +542,27 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
         __half* kv_l = e->kv + e->layer_stride * l;
         launch_rmsnorm(e->x, H, M, H, c.rms_eps, e->xn, H, s);
         ENG_LAUNCH("rmsnorm_kernel");
-        ENG_TRY(gemm(e, e->xn, M, H, w.qkv, e->NQKV, e->qkv, e->NQKV, 0));
-        rope_kv_kernel<<<M, 256, 0, s>>>(e->qkv, e->NQKV, e->pos, e->slot, kvs.tables, e->max_blocks, Rrows,
-                                         e->rope_cos, e->rope_sin, c.n_q_heads, c.n_kv_heads, hd, kv_l, e->q16);
-        ENG_LAUNCH("rope_kv_kernel");
+        if (128 % hd == 0) {  // whole heads per 128-row unit: RoPE and the KV write in the GEMM epilogue
+            RopeArgs ra;
+            ra.pos = e->pos;
+            ra.slot = e->slot;
+            ra.tables = kvs.tables;
+            ra.max_blocks = e->max_blocks;
+            ra.R = Rrows;
+            ra.cos_t = e->rope_cos;
+            ra.sin_t = e->rope_sin;
+            ra.Hq = c.n_q_heads;
+            ra.Hkv = c.n_kv_heads;
+            ra.hd = hd;
+            ra.kv_layer = kv_l;
+            ra.q16 = e->q16;
+            ENG_TRY(gemm_qkv_rope(e, e->xn, M, H, w.qkv, e->NQKV, ra));
+        } else {
+            ENG_TRY(gemm(e, e->xn, M, H, w.qkv, e->NQKV, e->qkv, e->NQKV, 0));
+            rope_kv_kernel<<<M, 256, 0, s>>>(e->qkv, e->NQKV, e->pos, e->slot, kvs.tables, e->max_blocks, Rrows,
+                                             e->rope_cos, e->rope_sin, c.n_q_heads, c.n_kv_heads, hd, kv_l, e->q16);
+            ENG_LAUNCH("rope_kv_kernel");
+        }
         ++e->kernels_per_step;
         ENG_TRY(launch_attention(e->q16, kv_l, e->num_blocks, c.n_kv_heads, hd, kvs.tables, e->max_blocks, kvs.ctx,
                                  e->mask, B, Rrows, c.n_q_heads, e->att, e->attn_ws, e->attn_ws_bytes,

@@ -102,12 +102,13 @@ struct GemmArgs {
     const uint8_t* w;
     int M, N, KG, m_tiles, S;
     float* Y;
-    int ldy, mode;  // mode 0 store, 1 add, 2 SwiGLU (h = silu(gate) * up into H, below)
+    int ldy, mode;  // mode 0 store, 1 add, 2 SwiGLU (h = silu(gate) * up into H, below), 3 QKV + RoPE (rope)
     __half* H;      // mode 2: fp16 [M, F] with row stride ldy; weight tile t = [gate rows 128t.. | up rows 128t..]
     int F;          // mode 2: columns of H
     int tma_out;  // tmap_y is valid: the output leaves by TMA (box {128, MT / S}; fp16 over H in mode 2)
     int pdl;      // launched as a programmatic dependent: only the weights may be read before pdl_wait()
     DeviceStatus* status;
+    RopeArgs rope;  // mode 3
 };
 
 template <int MT, int QN>
@@ -483,7 +484,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_async_smem();  // the generic-proxy writes above, before the TMA reads them
     if (args.pdl) pdl_wait();  // Y may still be read or written by earlier kernels
     __syncthreads();
-    if (QN == 2 && args.mode == 2) {
+    if (QN == 1 && args.mode == 3) {
+        // Mode 3 (QKV + RoPE + KV write; rotate-half RoPE as rust_sme_rope_f32,
+        // src/sme_kernel/rust_sme/src/lib.rs:621-666): this
+        // CTA's token rows of the tile's 128 / hd heads.  An item = dims
+        // (d, d+1) and (d + hd/2, d + hd/2 + 1) of one head of one token, the
+        // same arithmetic as the standalone RoPE pass.
+        const RopeArgs& ra = args.rope;
+        const int hd = ra.hd, halfd = hd / 2;
+        const int per_head = halfd / 2, per_tok = 128 / hd * per_head;  // = 32
+        if (acc_ok && !*abort_flag) {
+            for (int idx = threadIdx.x; idx < rows * per_tok; idx += blockDim.x) {
+                const int rr = idx / per_tok, w = idx - rr * per_tok;
+                const int m = m_tile * MT + r0 + rr;
+                if (m >= args.M) continue;
+                const int hu = w / per_head, d = (w - hu * per_head) * 2;
+                const int h = n_tile * (128 / hd) + hu;  // head in [q | k | v]
+                if (h >= ra.Hq + 2 * ra.Hkv) continue;
+                const float* row = stage + (size_t)(r0 + rr) * 128 + hu * hd;
+                const float2 a = *reinterpret_cast<const float2*>(row + d);
+                const float2 c = *reinterpret_cast<const float2*>(row + d + halfd);
+                __half* dst;
+                if (h < ra.Hq) {
+                    dst = ra.q16 + (size_t)m * ra.Hq * hd + (size_t)h * hd;
+                } else {
+                    const int b = m / ra.R, sl = ra.slot[m];
+                    const int blk = ra.tables[(size_t)b * ra.max_blocks + sl / 16];
+                    const int kvsel = h < ra.Hq + ra.Hkv ? 0 : 1, kh = h - ra.Hq - kvsel * ra.Hkv;
+                    dst = ra.kv_layer + ((((size_t)blk * 2 + kvsel) * ra.Hkv + kh) * 16 + sl % 16) * hd;
+                }
+                if (h < ra.Hq + ra.Hkv) {
+                    const float* cs = ra.cos_t + (size_t)ra.pos[m] * halfd;
+                    const float* sn = ra.sin_t + (size_t)ra.pos[m] * halfd;
+                    const float2 cv = *reinterpret_cast<const float2*>(cs + d);
+                    const float2 sv = *reinterpret_cast<const float2*>(sn + d);
+                    *reinterpret_cast<__half2*>(dst + d) =
+                        __floats2half2_rn(__fsub_rn(__fmul_rn(a.x, cv.x), __fmul_rn(c.x, sv.x)),
+                                          __fsub_rn(__fmul_rn(a.y, cv.y), __fmul_rn(c.y, sv.y)));
+                    *reinterpret_cast<__half2*>(dst + d + halfd) =
+                        __floats2half2_rn(__fadd_rn(__fmul_rn(c.x, cv.x), __fmul_rn(a.x, sv.x)),
+                                          __fadd_rn(__fmul_rn(c.y, cv.y), __fmul_rn(a.y, sv.y)));
+                } else {
+                    *reinterpret_cast<__half2*>(dst + d) = __floats2half2_rn(a.x, a.y);
+                    *reinterpret_cast<__half2*>(dst + d + halfd) = __floats2half2_rn(c.x, c.y);
+                }
+            }
+        }
+    } else if (QN == 2 && args.mode == 2) {
         if (acc_ok && !*abort_flag && m_tile * MT + r0 < args.M) {
             if (args.tma_out) {
                 if (threadIdx.x == 0) {
@@ -891,6 +938,7 @@ static GemmArgs gemm_args(const GemmPlan& p, const void* w_tiled, int M, int N, 
     a.tma_out = 0;
     a.pdl = pdl ? 1 : 0;
     a.status = device_status_ptr();
+    memset(&a.rope, 0, sizeof(a.rope));
     return a;
 }
 
@@ -907,6 +955,22 @@ int gemm_launch(const CUtensorMap& map, const GemmPlan& p, const void* w_tiled, 
 }
 
 int swiglu_units(int F) { return 2 * ((F + 127) / 128); }
+
+// the QKV + RoPE epilogue keeps whole heads in one-unit tiles
+GemmPlan plan_gemm_qkv(int M, int N, int K) { return plan_gemm_qn(M, N, K, 1); }
+
+int gemm_launch_qkv_rope(const CUtensorMap& map, const GemmPlan& p, const void* w_qkv, int M, int N, const RopeArgs& ra,
+                         cudaStream_t s, bool pdl) {
+    if (p.QN != 1 || ra.hd <= 0 || 128 % ra.hd != 0 || ra.hd % 4 != 0 || N != (ra.Hq + 2 * ra.Hkv) * ra.hd) {
+        set_error("w4a16_gemm_qkv_rope: the plan must use one-unit tiles of whole heads");
+        return SPECDEC_EINVAL;
+    }
+    GemmArgs a = gemm_args(p, w_qkv, M, N, 0, 3, pdl);
+    a.rope = ra;
+    CUtensorMap unused;
+    memset(&unused, 0, sizeof(unused));
+    return launch_mt(map, unused, a, p, s);
+}
 
 // the SwiGLU epilogue pairs gate and up units: two units per CTA
 GemmPlan plan_gemm_swiglu(int M, int F, int K) { return plan_gemm_qn(M, 128 * swiglu_units(F), K, 2); }

@@ -40,6 +40,25 @@ int swiglu_units(int F);
 GemmPlan plan_gemm_swiglu(int M, int F, int K);
 int gemm_launch_swiglu(const CUtensorMap& map, const GemmPlan& p, const void* w_gu, int M, int F, __half* h, int ldh,
                        cudaStream_t s, bool pdl = false);
+// Fused QKV projection + RoPE + KV-cache write: the epilogue of the one-unit
+// tiles (each tile = 128 / hd whole heads of [q | k | v]) applies rotate-half
+// RoPE (pairs d, d + hd/2, cos/sin tables [pos][hd/2]) to q and k, writes q as
+// fp16 [M, Hq*hd] and k / v as fp16 into the paged slots of kv_layer
+// ([num_blocks][2][Hkv][16][hd]); no fp32 output.  hd must divide 128.
+struct RopeArgs {
+    const int32_t* pos;     // [M] positions
+    const int32_t* slot;    // [M] KV slot (token index within the sequence)
+    const int32_t* tables;  // [B, max_blocks]
+    int max_blocks, R;      // R = rows per sequence
+    const float* cos_t;     // [max_pos][hd/2]
+    const float* sin_t;
+    int Hq, Hkv, hd;
+    __half* kv_layer;
+    __half* q16;
+};
+GemmPlan plan_gemm_qkv(int M, int N, int K);
+int gemm_launch_qkv_rope(const CUtensorMap& map, const GemmPlan& p, const void* w_qkv, int M, int N, const RopeArgs& ra,
+                         cudaStream_t s, bool pdl = false);
 size_t gemm_workspace_bound(int max_m, int max_n, int max_k);
 size_t w4_tiled_bytes(int N, int K);
 

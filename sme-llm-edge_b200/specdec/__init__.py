@@ -20,7 +20,9 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libspecdec_sm100.so")
+# SPECDEC_LIB selects another build of the library (e.g. to compare two builds
+# on one machine); the in-tree build otherwise.
+LIB_PATH = os.environ.get("SPECDEC_LIB") or os.path.join(_HERE, "libspecdec_sm100.so")
 
 OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, ENOTSUP = range(6)
 
