@@ -614,8 +614,9 @@ int record_step(specdec_engine* e) {
         const int k = e->k;
         ENG_TRY(draft_hidden_and_logits(e, k));
         ++e->kernels_per_step;
+        // the draft rows' statistics go where the acceptance reads them: after the B*(k+1) target rows
         ENG_TRY(launch_sample_rows_dev(e->dlogits, B * k, k, V, sp.temperature, sp.top_p, sp.seed, e->step, e->drafts,
-                                       s));
+                                       static_cast<char*>(e->acc_ws) + (size_t)B * (k + 1) * kAcceptStatsBytes, s));
         prof_mark(e, CAT_ACCEPT);
         ++e->kernels_per_step;
         ENG_TRY(kv_append_uniform(e->kvm, B, R, s));
@@ -626,7 +627,7 @@ int record_step(specdec_engine* e) {
         ENG_TRY(forward(e, R, true));
         e->kernels_per_step += 2;
         ENG_TRY(launch_accept_chain_dev(e->logits, e->dlogits, e->drafts, B, k, V, sp.temperature, sp.top_p, sp.seed,
-                                        e->step, e->acc, e->out_tokens, e->acc_ws, s));
+                                        e->step, e->acc, e->out_tokens, e->acc_ws, true, s));
         prof_mark(e, CAT_ACCEPT);
         commit_chain_kernel<<<B, 256, 0, s>>>(e->acc, e->out_tokens, R, kvs.ctx, e->active, e->x, c.hidden, e->new_len,
                                               e->pending, e->h0, e->emitted, e->step);
@@ -828,7 +829,7 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
                                 attention_workspace(e->B, 64, mc->n_q_heads, Hkv, hd, rc->max_ctx));
     if ((rcode = dalloc(e, reinterpret_cast<char**>(&e->attn_ws), e->attn_ws_bytes))) return fail(rcode);
     cudaMemset(e->attn_ws, 0, e->attn_ws_bytes);
-    if ((rcode = dalloc(e, reinterpret_cast<char**>(&e->acc_ws), (size_t)e->B * (2 * e->R + 1) * 32))) return fail(rcode);
+    if ((rcode = dalloc(e, reinterpret_cast<char**>(&e->acc_ws), (size_t)e->B * (2 * e->R + 1) * kAcceptStatsBytes))) return fail(rcode);
     if (cudaMallocHost(&e->h_ctrl, sizeof(int32_t) * (e->B + 8)) != cudaSuccess) return fail(SPECDEC_ENOMEM);
     for (int b = 0; b < e->B; ++b) e->h_ctrl[b] = 1;  // every sequence starts active
     if (cudaMallocHost(&e->h_out, sizeof(int32_t) * (e->B * (e->R + 1) + 8)) != cudaSuccess) return fail(SPECDEC_ENOMEM);

@@ -390,14 +390,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncthreads();
     const bool acc_ok = !*abort_flag;
-    // half q of the accumulator -> dst[token][128]
+    // half q of the accumulator -> dst[token][128]: a warp's 16-column
+    // chunks c = eg, eg + 4, ... are all loaded before one wait
     auto drain = [&](int q, float* dst) {
-        for (int c = eg; c < MT / 16; c += kDeqWarps / 4) {
-            uint32_t v[16];
-            tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v);
-            tc_wait_ld();
+        constexpr int kChunks = MT / 16, kGroups = kDeqWarps / 4, kPer = (kChunks + kGroups - 1) / kGroups;
+        uint32_t v[kPer][16];
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[jj]);
+        for (int i = 0; i < kPer; ++i) {
+            const int c = eg + i * kGroups;
+            if (c < kChunks) tc_ld_x16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(q * MT + c * 16), v[i]);
+        }
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int c = eg + i * kGroups;
+            if (c < kChunks) {
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * 128 + quad * 32 + lane] = __uint_as_float(v[i][jj]);
+            }
         }
     };
     // The QN units of this CTA's accumulator are parked in shared memory as
@@ -465,9 +475,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 uint32_t w[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float a = __fmul_rn(__fdiv_rn(g[2 * j], __fadd_rn(1.0f, expf(-g[2 * j]))), u[2 * j]);
-                    const float b =
-                        __fmul_rn(__fdiv_rn(g[2 * j + 1], __fadd_rn(1.0f, expf(-g[2 * j + 1]))), u[2 * j + 1]);
+                    // fast exp and divide (one MUFU op each): within a few fp32 ulp,
+                    // well inside the fp16 rounding of h
+                    const float a = __fmul_rn(__fdividef(g[2 * j], __fadd_rn(1.0f, __expf(-g[2 * j]))), u[2 * j]);
+                    const float b = __fmul_rn(__fdividef(g[2 * j + 1], __fadd_rn(1.0f, __expf(-g[2 * j + 1]))),
+                                              u[2 * j + 1]);
                     __half2 h2 = __floats2half2_rn(a, b);
                     w[j] = *reinterpret_cast<uint32_t*>(&h2);
                 }

@@ -69,17 +69,19 @@ int launch_attention(const __half* q, const __half* kv_layer, int num_blocks, in
                      void* ws, size_t ws_bytes, int max_ctx, cudaStream_t s);
 
 // ---------------------------------------------------------------- sampling / acceptance
+constexpr size_t kAcceptStatsBytes = 32;  // one logits row's statistics in the acceptance scratch
 int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaStream_t s);
 float temp_coeff(float temperature);
 uint64_t top_p_q32(float top_p);
 int launch_accept_chain_dev(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
                             float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
-                            int32_t* accepted_len, int32_t* out_tokens, void* ws, cudaStream_t s);
+                            int32_t* accepted_len, int32_t* out_tokens, void* ws, bool draft_stats_ready,
+                            cudaStream_t s);
 int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, const int32_t* parent, int B, int R, int V,
                            float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
                            int32_t* accepted_len, int32_t* path, int32_t* out_tokens, cudaStream_t s);
 int launch_sample_rows_dev(const float* logits, int rows, int k, int V, float temperature, float top_p, uint64_t seed,
-                           const uint32_t* step_dev, int32_t* out, cudaStream_t s);
+                           const uint32_t* step_dev, int32_t* out, void* stats, cudaStream_t s);
 
 // ---------------------------------------------------------------- paged KV block manager
 struct KVState {

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace specdec {
 
@@ -25,7 +26,7 @@ struct DevRowStats {
     int32_t argmax;
     int32_t pad;
 };
-static_assert(sizeof(DevRowStats) == 32, "row stats layout");
+static_assert(sizeof(DevRowStats) == kAcceptStatsBytes, "row stats layout");
 
 constexpr int kRowThreads = 1024;
 
@@ -184,6 +185,33 @@ __device__ void select_digit(RowSmem& sm, uint64_t thr, uint64_t* G, uint32_t* d
     __syncthreads();
 }
 
+// Integer mass sum over z[0, n) (no nucleus): four float4 loads in flight per
+// thread when z is 16-byte aligned and n a multiple of 4.
+__device__ uint64_t cta_mass_sum(const float* __restrict__ z, int n, float m, float c, RowSmem& sm) {
+    uint64_t s = 0;
+    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+        const float4* z4 = reinterpret_cast<const float4*>(z);
+        const int n4 = n / 4, bd = blockDim.x;
+        int q = threadIdx.x;
+        for (; q + 3 * bd < n4; q += 4 * bd) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                s += (uint64_t)mass_of(v[u].x, m, c) + mass_of(v[u].y, m, c) + mass_of(v[u].z, m, c) +
+                     mass_of(v[u].w, m, c);
+        }
+        for (; q < n4; q += bd) {
+            const float4 v = z4[q];
+            s += (uint64_t)mass_of(v.x, m, c) + mass_of(v.y, m, c) + mass_of(v.z, m, c) + mass_of(v.w, m, c);
+        }
+    } else {
+        for (int j = threadIdx.x; j < n; j += blockDim.x) s += mass_of(z[j], m, c);
+    }
+    return block_sum<uint64_t>(s, sm.red64);
+}
+
 // Full row statistics (max, argmax, mass sum, top-p threshold, nucleus mass).
 __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint64_t tp, bool need_mass, RowSmem& sm,
                               DevRowStats* st) {
@@ -204,23 +232,8 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
         uint64_t s = 0;
         const int lane = threadIdx.x & 31;
         const int warp_base = (threadIdx.x >> 5) * 32, stride = blockDim.x;
-        if (!nucleus && (V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
-            const float4* z4 = reinterpret_cast<const float4*>(z);
-            const int n4 = V / 4, bd = blockDim.x;
-            int q = threadIdx.x;
-            for (; q + 3 * bd < n4; q += 4 * bd) {  // four float4 loads in flight per thread
-                float4 v[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    s += (uint64_t)mass_of(v[u].x, m, c) + mass_of(v[u].y, m, c) + mass_of(v[u].z, m, c) +
-                         mass_of(v[u].w, m, c);
-            }
-            for (; q < n4; q += bd) {
-                const float4 v = z4[q];
-                s += (uint64_t)mass_of(v.x, m, c) + mass_of(v.y, m, c) + mass_of(v.z, m, c) + mass_of(v.w, m, c);
-            }
+        if (!nucleus) {
+            s = cta_mass_sum(z, V, m, c, sm);
         } else {
             for (int base = warp_base; base < V; base += stride) {
                 const int j = base + lane;
@@ -228,10 +241,10 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
                 const float zj = valid ? z[j] : 0.0f;
                 const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
                 s += e;
-                if (nucleus) warp_hist_add(sm.hist, logit_key(zj) >> 24, e, valid);
+                warp_hist_add(sm.hist, logit_key(zj) >> 24, e, valid);
             }
+            s = block_sum<uint64_t>(s, sm.red64);
         }
-        s = block_sum<uint64_t>(s, sm.red64);
         r.sum = s;
         r.nuc = s;
         if (nucleus) {
@@ -316,24 +329,26 @@ __device__ __forceinline__ u128 warp_incl_scan_u128(u128 v) {
     return v;
 }
 
-// Smallest j (index order) whose running mass exceeds target_of(total), where
-// total = sum of all masses; returns -1 when the total is zero (or does not
-// exceed the target).  *total_out receives the total.
-// Warp w owns the contiguous index range [w*C, (w+1)*C), C a multiple of 256,
-// and walks it in 256-element chunks (lane l: 8 contiguous elements), keeping
-// every chunk's mass in shared memory.  The warp whose range holds the target
-// then finds the chunk from those totals and re-reads only that chunk.  One
-// pass over the row plus 256 elements; every sum is an integer sum, so the
-// result does not depend on the order.
-template <class MassFn, class TargetFn>
-__device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, RowSmem& sm, u128* total_out) {
+// Inverse CDF over the index range [L, H), in two phases so that a cluster
+// can exchange range totals in between.
+// Phase 1 (cta_cdf_chunks): warp w owns the contiguous range
+// [L + w*C, L + (w+1)*C), C a multiple of 256, and walks it in 256-element
+// chunks (lane l: 8 contiguous elements), keeping every chunk's mass in
+// shared memory and every warp's total in sm.scan; returns the range total.
+// Phase 2 (cta_cdf_find): the smallest j in [L, H) whose running mass from L
+// exceeds `target` -- the warp whose range holds the target finds the chunk
+// from the recorded totals and re-reads only that chunk; -1 when the target
+// is not below the total.  One pass over the range plus 256 elements; every
+// sum is an integer sum, so the result does not depend on the order.
+template <class MassFn>
+__device__ u128 cta_cdf_chunks(int L, int H, MassFn mass, RowSmem& sm) {
     constexpr int E = kCdfChunk / 32;  // elements per lane and chunk
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int C = ((V + nw - 1) / nw + kCdfChunk - 1) / kCdfChunk * kCdfChunk;
-    const int nch = C / kCdfChunk;  // <= kCdfChunksPerWarp (V <= 262144, checked by the launchers)
-    const int lo = wid * C, hi = min(V, lo + C);
+    const int C = ((H - L + nw - 1) / nw + kCdfChunk - 1) / kCdfChunk * kCdfChunk;
+    const int nch = C / kCdfChunk;  // <= kCdfChunksPerWarp (H - L <= 262144, checked by the launchers)
+    const int lo = L + wid * C, hi = min(H, lo + C);
     u128 t = 0;
-    __syncthreads();  // sm.scan / sm.chunk may still be read by a previous caller
+    __syncthreads();  // sm.scan / sm.chunk / sm.total may still be read by a previous caller
     for (int ch = 0; ch < nch; ++ch) {
         const int base = lo + ch * kCdfChunk + lane * E;
         u128 sc = 0;
@@ -346,23 +361,34 @@ __device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, Row
     if (lane == 0) sm.scan[wid] = t;
     __syncthreads();
     if (wid == 0) {
+        const u128 tot = warp_sum_u128(lane < nw ? sm.scan[lane] : (u128)0);
+        if (lane == 0) sm.total = tot;
+    }
+    __syncthreads();
+    return sm.total;
+}
+
+template <class MassFn>
+__device__ int cta_cdf_find(int L, int H, MassFn mass, u128 target, RowSmem& sm) {
+    constexpr int E = kCdfChunk / 32;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int C = ((H - L + nw - 1) / nw + kCdfChunk - 1) / kCdfChunk * kCdfChunk;
+    const int nch = C / kCdfChunk;
+    if (wid == 0) {
         const u128 v = lane < nw ? sm.scan[lane] : (u128)0;
         const u128 incl = warp_incl_scan_u128(v);
-        const u128 total = shfl_u128(incl, 31);
-        const u128 target = target_of(total);
         const bool hit = lane < nw && incl - v <= target && target < incl;
         const unsigned b = __ballot_sync(0xffffffffu, hit);
         if (hit && lane == __ffs(b) - 1) sm.big = target - (incl - v);
         if (lane == 0) {
             sm.redi[0] = b ? __ffs(b) - 1 : -1;
-            sm.total = total;
             sm.result = -1;
         }
     }
     __syncthreads();
     const int W = sm.redi[0];
-    *total_out = sm.total;
     if (W >= 0 && wid == W) {
+        const int lo = L + W * C, hi = min(H, lo + C);
         const u128 tgt = sm.big;
         // the chunk holding the target
         const u128 v = lane < nch ? sm.chunk[W][lane] : (u128)0;
@@ -397,6 +423,16 @@ __device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, Row
     const int r = sm.result;
     __syncthreads();
     return r;
+}
+
+// Smallest j (index order) whose running mass exceeds target_of(total), where
+// total = sum of all masses; returns -1 when the total is zero (or does not
+// exceed the target).  *total_out receives the total.
+template <class MassFn, class TargetFn>
+__device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, RowSmem& sm, u128* total_out) {
+    const u128 total = cta_cdf_chunks(0, V, mass, sm);
+    *total_out = total;
+    return cta_cdf_find(0, V, mass, target_of(total), sm);
 }
 
 // Smallest j (index order) whose running mass exceeds `target`.
@@ -507,6 +543,205 @@ __global__ void __launch_bounds__(kRowThreads) accept_chain_kernel(const float* 
     }
 }
 
+// ------------------------------------------- chain acceptance, one cluster per sequence
+// For greedy acceptance and for sampling without a nucleus (top_p = 1): the
+// S CTAs of a cluster split every logits row of their sequence into S
+// contiguous vocabulary slices (CTA r: [r*Vs, (r+1)*Vs), Vs a multiple of 4).
+// Row arg-max and mass sums are per-slice partials merged in rank order
+// through distributed shared memory; the final draw exchanges the slices'
+// mass totals and the CTA whose slice holds the target searches it.  All
+// masses are integers, so every total, and with it every decision, is the one
+// the single-CTA kernels above take.
+constexpr int kAcceptClusterMaxK = 16;
+constexpr int kAcceptClusterRows = 2 * kAcceptClusterMaxK + 1;
+constexpr int kAcceptClusterMax = 8;
+
+struct AcceptXchg {
+    float pmax[kAcceptClusterRows];      // this CTA's slice partials, read by its peers
+    int parg[kAcceptClusterRows];
+    uint64_t psum[kAcceptClusterRows];
+    uint64_t ptot[2][2];                 // slice total of a draw (low, high words); two draws at most
+    DevRowStats st[kAcceptClusterRows];  // merged statistics (identical in every CTA)
+    u128 local;                          // the draw's target, relative to the owner's slice
+    u128 total_scratch;
+    int owner;
+    int a;
+    int tok;                             // the owner's result, read by rank 0
+};
+
+// Publishes this CTA's slice total t in slot `slot`; every CTA then reads the
+// S totals in rank order, forms target_of(total) and finds the slice holding
+// it.  Returns the cluster total; xs.owner (-1 if none) and xs.local are set.
+template <class TargetFn>
+__device__ u128 cluster_draw_owner(AcceptXchg& xs, int slot, u128 t, int S, TargetFn target_of) {
+    if (threadIdx.x == 0) {
+        xs.ptot[slot][0] = (uint64_t)t;
+        xs.ptot[slot][1] = (uint64_t)(t >> 64);
+    }
+    cluster_sync_all();
+    if (threadIdx.x == 0) {
+        const uint32_t a0 = s_addr(&xs.ptot[slot][0]), a1 = s_addr(&xs.ptot[slot][1]);
+        u128 total = 0;
+        for (int r = 0; r < S; ++r)
+            total += ((u128)ld_dsmem_u64(a1, (uint32_t)r) << 64) | ld_dsmem_u64(a0, (uint32_t)r);
+        const u128 target = target_of(total);
+        int owner = -1;
+        u128 pre = 0, local = 0;
+        for (int r = 0; r < S && owner < 0; ++r) {
+            const u128 tr = ((u128)ld_dsmem_u64(a1, (uint32_t)r) << 64) | ld_dsmem_u64(a0, (uint32_t)r);
+            if (pre <= target && target < pre + tr) {
+                owner = r;
+                local = target - pre;
+            }
+            pre += tr;
+        }
+        xs.owner = owner;
+        xs.local = local;
+        xs.total_scratch = total;
+    }
+    __syncthreads();
+    return xs.total_scratch;
+}
+
+__global__ void __launch_bounds__(kRowThreads) accept_chain_cluster_kernel(
+    const float* __restrict__ target, const float* __restrict__ draft, const int32_t* __restrict__ drafts, int k,
+    int V, float c, bool greedy, uint64_t seed, const uint32_t* step_dev, uint32_t step_host,
+    const DevRowStats* __restrict__ qstats, int S, int32_t* __restrict__ accepted_len,
+    int32_t* __restrict__ out_tokens) {
+    __shared__ RowSmem sm;
+    __shared__ AcceptXchg xs;
+    const uint32_t step = step_dev ? *step_dev : step_host;
+    const int rank = (int)cluster_rank();
+    const int b = blockIdx.x / S;
+    const int Vs = ((V + S - 1) / S + 3) & ~3;
+    const int L = min(V, rank * Vs), H = min(V, L + Vs);
+    const float* P = target + (size_t)b * (k + 1) * V;
+    const float* Q = draft + (size_t)b * k * V;
+    const int32_t* D = drafts + (size_t)b * k;
+    // rows 0..k: the target rows; k+1..2k: the draft rows, when their statistics are not given
+    const bool own_q = !greedy && qstats == nullptr;
+    const int nrows = (k + 1) + (own_q ? k : 0);
+    auto row = [&](int i) { return i <= k ? P + (size_t)i * V : Q + (size_t)(i - k - 1) * V; };
+
+    for (int i = 0; i < nrows; ++i) {
+        float m;
+        int am;
+        cta_argmax(row(i) + L, H - L, sm, &m, &am);
+        if (threadIdx.x == 0) {
+            xs.pmax[i] = m;
+            xs.parg[i] = am < 0 ? -1 : am + L;
+        }
+    }
+    cluster_sync_all();
+    if (threadIdx.x < nrows) {
+        const int i = threadIdx.x;
+        float v = -INFINITY;
+        int idx = -1;
+        for (int r = 0; r < S; ++r)
+            argmax_merge(v, idx, ld_dsmem_f32(s_addr(&xs.pmax[i]), (uint32_t)r),
+                         (int)ld_dsmem_u32(s_addr(&xs.parg[i]), (uint32_t)r));
+        DevRowStats st;
+        st.max = v;
+        st.argmax = idx;
+        st.tau = 0;
+        st.sum = 0;
+        st.nuc = 0;
+        st.pad = 0;
+        xs.st[i] = st;
+    }
+    __syncthreads();
+    if (!greedy) {
+        for (int i = 0; i < nrows; ++i) {
+            const uint64_t part = cta_mass_sum(row(i) + L, H - L, xs.st[i].max, c, sm);
+            if (threadIdx.x == 0) xs.psum[i] = part;
+        }
+        cluster_sync_all();
+        if (threadIdx.x < nrows) {
+            uint64_t t = 0;
+            for (int r = 0; r < S; ++r) t += ld_dsmem_u64(s_addr(&xs.psum[threadIdx.x]), (uint32_t)r);
+            xs.st[threadIdx.x].sum = t;
+            xs.st[threadIdx.x].nuc = t;
+        }
+        __syncthreads();
+    }
+    // the sequential min(1, p/q) tests (as accept_chain_kernel), taken identically in every CTA
+    if (threadIdx.x == 0) {
+        int a = 0;
+        if (greedy) {
+            while (a < k && xs.st[a].argmax == D[a]) ++a;
+        } else {
+            while (a < k) {
+                const int x = D[a];
+                const DevRowStats sp = xs.st[a];
+                const DevRowStats sq = own_q ? xs.st[k + 1 + a] : qstats[(size_t)b * k + a];
+                uint64_t ep = 0, eq = 0;
+                if (x >= 0 && x < V) {
+                    ep = mass_of(P[(size_t)a * V + x], sp.max, c);
+                    eq = mass_of(Q[(size_t)a * V + x], sq.max, c);
+                }
+                const uint32_t u = uniform_u32(seed, step, (uint32_t)b, (uint32_t)a, U_ACCEPT);
+                const u128 lhs = (u128)u * eq * sp.nuc;
+                const u128 rhs = ((u128)ep * sq.nuc) << 32;
+                if (!(lhs < rhs)) break;
+                ++a;
+            }
+        }
+        xs.a = a;
+        xs.tok = -1;
+    }
+    __syncthreads();
+    const int a = xs.a;
+    if (greedy) {
+        if (threadIdx.x == 0) xs.tok = xs.st[a].argmax;
+    } else {
+        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)a, U_RESAMPLE);
+        const float* zp = P + (size_t)a * V;
+        const DevRowStats stp = xs.st[a];
+        bool bonus = a == k;
+        int slot = 0;
+        if (!bonus) {
+            // the residual max(0, p - q) on the first rejected position
+            const float* zq = Q + (size_t)a * V;
+            const DevRowStats stq = own_q ? xs.st[k + 1 + a] : qstats[(size_t)b * k + a];
+            auto resid = [&](int j) -> u128 {
+                const u128 x = (u128)mass_of(zp[j], stp.max, c) * stq.nuc;
+                const u128 y = (u128)mass_of(zq[j], stq.max, c) * stp.nuc;
+                return x > y ? x - y : (u128)0;
+            };
+            const u128 R = cluster_draw_owner(xs, slot++, cta_cdf_chunks(L, H, resid, sm), S, [u64](u128 tot) {
+                const uint64_t rh = (uint64_t)(tot >> 64), rl = (uint64_t)tot;
+                return (u128)u64 * rh + (u128)mulhi64(u64, rl);
+            });
+            if (R == 0) {
+                bonus = true;  // p and q agree: draw from p
+            } else if (rank == xs.owner) {
+                const int t = cta_cdf_find(L, H, resid, xs.local, sm);
+                if (threadIdx.x == 0) xs.tok = t;
+            }
+        }
+        if (bonus) {
+            auto pmass = [&](int j) -> u128 { return (u128)mass_of(zp[j], stp.max, c); };
+            (void)cluster_draw_owner(xs, slot, cta_cdf_chunks(L, H, pmass, sm), S,
+                                     [u64](u128 tot) { return (u128)mulhi64(u64, (uint64_t)tot); });
+            if (rank == xs.owner) {
+                const int t = cta_cdf_find(L, H, pmass, xs.local, sm);
+                if (threadIdx.x == 0) xs.tok = t;
+            }
+        }
+    }
+    cluster_sync_all();  // the owner's token is in its shared memory
+    if (rank == 0 && threadIdx.x == 0) {
+        const int owner = greedy ? 0 : xs.owner;
+        const int tok = owner < 0 ? -1 : (int)ld_dsmem_u32(s_addr(&xs.tok), (uint32_t)owner);
+        int32_t* out = out_tokens + (size_t)b * (k + 1);
+        for (int i = 0; i < a; ++i) out[i] = D[i];
+        out[a] = tok;
+        for (int i = a + 1; i <= k; ++i) out[i] = -1;
+        accepted_len[b] = a;
+    }
+    cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
+}
+
 // Tree acceptance, one CTA per sequence; statistics of the visited rows are
 // computed on demand (a path visits at most depth+1 of the R rows).
 __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* __restrict__ target,
@@ -606,22 +841,41 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
     }
 }
 
-// Draft sampling: one CTA per row.
+// Draft sampling: one CTA per row.  Without a nucleus the row's mass total
+// comes out of the inverse-CDF pass itself (the draw's target is a fraction
+// of that total), so a row is read twice: arg-max, then masses.  When
+// `stats` is given, the row's statistics are kept there for the acceptance.
 __global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* __restrict__ logits, int k, int V,
                                                                   float c, uint64_t tp, bool greedy, uint64_t seed,
                                                                   const uint32_t* step_dev, uint32_t step_host,
-                                                                  int32_t* __restrict__ out) {
+                                                                  int32_t* __restrict__ out,
+                                                                  DevRowStats* __restrict__ stats) {
     __shared__ RowSmem sm;
     const uint32_t step = step_dev ? *step_dev : step_host;
     const int r = blockIdx.x;
     const float* z = logits + (size_t)r * V;
     DevRowStats st;
-    cta_row_stats(z, V, c, tp, !greedy, sm, &st);
-    int tok = st.argmax;
-    if (!greedy)
-        tok = cta_sample_nucleus(z, V, c, st,
-                                 uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k), U_DRAFT), sm);
-    if (threadIdx.x == 0) out[r] = tok;
+    int tok;
+    if (!greedy && tp >= (1ull << 32)) {
+        cta_row_stats(z, V, c, tp, false, sm, &st);  // max and arg-max only
+        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k), U_DRAFT);
+        const float m = st.max;
+        u128 total = 0;
+        tok = cta_inverse_cdf_total(
+            V, [&](int j) -> u128 { return (u128)mass_of(z[j], m, c); },
+            [u64](u128 tot) { return (u128)mulhi64(u64, (uint64_t)tot); }, sm, &total);
+        st.sum = st.nuc = (uint64_t)total;  // <= V * 2^31 < 2^64
+    } else {
+        cta_row_stats(z, V, c, tp, !greedy, sm, &st);
+        tok = st.argmax;
+        if (!greedy)
+            tok = cta_sample_nucleus(z, V, c, st,
+                                     uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k), U_DRAFT), sm);
+    }
+    if (threadIdx.x == 0) {
+        out[r] = tok;
+        if (stats) stats[r] = st;
+    }
 }
 
 // Top-k (descending value, ascending index) per row: k rounds of arg-max with
@@ -774,22 +1028,66 @@ int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaS
     return SPECDEC_OK;
 }
 
-int launch_accept_chain_dev(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
-                            float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
-                            int32_t* accepted_len, int32_t* out_tokens, void* ws, cudaStream_t s) {
-    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_accept_chain_dev: vocabulary above 262144");
+// Cluster size of the sliced chain acceptance: the largest power of two
+// <= 8 whose B * S CTAs fit one wave on the device's SMs.
+static int accept_cluster_size(int B) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) (void)cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int S = kAcceptClusterMax;
+    while (S > 1 && (long long)B * S > sms) S >>= 1;
+    return S;
+}
+
+// Chain acceptance: the sliced cluster kernel for greedy decisions and
+// sampling without a nucleus (k <= 16), else row statistics into `st`
+// (B*(k+1) target rows, then B*k draft rows) and one CTA per sequence.
+// With draft_stats_ready the draft rows' statistics are already in st (the
+// draft sampler wrote them), and are not recomputed.
+static int launch_accept_chain_impl(const float* target, const float* draft, const int32_t* drafts, int B, int k,
+                                    int V, float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
+                                    uint32_t step_host, DevRowStats* st, bool draft_stats_ready,
+                                    int32_t* accepted_len, int32_t* out_tokens, cudaStream_t s) {
     const bool greedy = !(temperature > 0.0f);
     const float c = greedy ? 0.0f : temp_coeff(temperature);
     const uint64_t tp = top_p_q32(top_p);
+    const float* dq = greedy ? target : draft;
+    if ((greedy || tp >= (1ull << 32)) && k <= kAcceptClusterMaxK) {
+        const int S = accept_cluster_size(B);
+        const DevRowStats* qstats = (!greedy && draft_stats_ready) ? st + (size_t)B * (k + 1) : nullptr;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(B * S));
+        cfg.blockDim = dim3(kRowThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)S;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        SD_CUDA(cudaLaunchKernelEx(&cfg, accept_chain_cluster_kernel, target, dq, drafts, k, V, c, greedy, seed,
+                                   step_dev, step_host, qstats, S, accepted_len, out_tokens));
+        return SPECDEC_OK;
+    }
+    SD_CHECK(st, SPECDEC_EINVAL, "accept_chain: row statistics scratch required");
     const int rows = B * (k + 1) + (greedy ? 0 : B * k);
-    RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
-    DevRowStats* st = reinterpret_cast<DevRowStats*>(ws);
-    row_stats_kernel<<<rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
+    RowSet a{target, B * (k + 1)}, bq{dq, greedy ? 0 : B * k};
+    row_stats_kernel<<<(unsigned)rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
     SD_LAUNCH_CHECK("row_stats_kernel");
-    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, seed,
-                                                  step_dev, 0u, st, B, accepted_len, out_tokens);
+    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, dq, drafts, k, V, c, greedy, seed, step_dev, step_host, st,
+                                                  B, accepted_len, out_tokens);
     SD_LAUNCH_CHECK("accept_chain_kernel");
     return SPECDEC_OK;
+}
+
+int launch_accept_chain_dev(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
+                            float temperature, float top_p, uint64_t seed, const uint32_t* step_dev,
+                            int32_t* accepted_len, int32_t* out_tokens, void* ws, bool draft_stats_ready,
+                            cudaStream_t s) {
+    SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_accept_chain_dev: vocabulary above 262144");
+    return launch_accept_chain_impl(target, draft, drafts, B, k, V, temperature, top_p, seed, step_dev, 0u,
+                                    reinterpret_cast<DevRowStats*>(ws), draft_stats_ready, accepted_len, out_tokens, s);
 }
 
 int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, const int32_t* parent, int B, int R, int V,
@@ -805,11 +1103,12 @@ int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, cons
 }
 
 int launch_sample_rows_dev(const float* logits, int rows, int k, int V, float temperature, float top_p, uint64_t seed,
-                           const uint32_t* step_dev, int32_t* out, cudaStream_t s) {
+                           const uint32_t* step_dev, int32_t* out, void* stats, cudaStream_t s) {
     SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_sample_rows_dev: vocabulary above 262144");
     const bool greedy = !(temperature > 0.0f);
     sample_rows_kernel<<<rows, kRowThreads, 0, s>>>(logits, k, V, greedy ? 0.0f : temp_coeff(temperature),
-                                                    top_p_q32(top_p), greedy, seed, step_dev, 0u, out);
+                                                    top_p_q32(top_p), greedy, seed, step_dev, 0u, out,
+                                                    reinterpret_cast<DevRowStats*>(stats));
     SD_LAUNCH_CHECK("sample_rows_kernel");
     return SPECDEC_OK;
 }
@@ -829,20 +1128,11 @@ extern "C" int specdec_accept_chain(const float* target, const float* draft, con
     if (B == 0) return SPECDEC_OK;
     const bool greedy = !(sp->temperature > 0.0f);
     SD_CHECK(greedy || draft, SPECDEC_EINVAL, "accept_chain: draft logits required when sampling");
-    const int rows = B * (k + 1) + (greedy ? 0 : B * k);
     SD_CHECK(workspace && workspace_bytes >= specdec_accept_workspace_bytes(B * (2 * k + 1)), SPECDEC_EINVAL,
              "accept_chain: workspace too small");
-    cudaStream_t s = as_stream(stream);
-    const float c = greedy ? 0.0f : temp_coeff(sp->temperature);
-    const uint64_t tp = top_p_q32(sp->top_p);
-    RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
-    DevRowStats* st = reinterpret_cast<DevRowStats*>(workspace);
-    row_stats_kernel<<<rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
-    SD_LAUNCH_CHECK("row_stats_kernel");
-    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, sp->seed,
-                                                  nullptr, sp->step, st, B, accepted_len, out_tokens);
-    SD_LAUNCH_CHECK("accept_chain_kernel");
-    return SPECDEC_OK;
+    return launch_accept_chain_impl(target, draft, drafts, B, k, V, sp->temperature, sp->top_p, sp->seed, nullptr,
+                                    sp->step, reinterpret_cast<DevRowStats*>(workspace), false, accepted_len,
+                                    out_tokens, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -906,16 +1196,8 @@ extern "C" int specdec_accept_chain_noalloc(const float* target, const float* dr
     DevRowStats* st = nullptr;
     int rc = static_accept_rows(&st);
     if (rc) return rc;
-    cudaStream_t s = as_stream(stream);
-    const float c = greedy ? 0.0f : temp_coeff(sp->temperature);
-    const uint64_t tp = top_p_q32(sp->top_p);
-    RowSet a{target, B * (k + 1)}, bq{greedy ? target : draft, greedy ? 0 : B * k};
-    row_stats_kernel<<<(unsigned)rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
-    SD_LAUNCH_CHECK("row_stats_kernel");
-    accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, greedy ? target : draft, drafts, k, V, c, greedy, sp->seed,
-                                                  nullptr, sp->step, st, B, accepted_len, out_tokens);
-    SD_LAUNCH_CHECK("accept_chain_kernel");
-    return SPECDEC_OK;
+    return launch_accept_chain_impl(target, draft, drafts, B, k, V, sp->temperature, sp->top_p, sp->seed, nullptr,
+                                    sp->step, st, false, accepted_len, out_tokens, as_stream(stream));
 }
 
 extern "C" int specdec_accept_tree(const float* target, const int32_t* node_tokens, const int32_t* parent, int B,
@@ -948,7 +1230,7 @@ extern "C" int specdec_sample_rows(const float* logits, int rows, int k, int V, 
     const bool greedy = !(sp->temperature > 0.0f);
     sample_rows_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(
         logits, k, V, greedy ? 0.0f : temp_coeff(sp->temperature), top_p_q32(sp->top_p), greedy, sp->seed, nullptr, sp->step,
-        out);
+        out, nullptr);
     SD_LAUNCH_CHECK("sample_rows_kernel");
     return SPECDEC_OK;
 }

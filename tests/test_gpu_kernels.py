@@ -21,8 +21,12 @@ def _i32(shape):
 
 # ---------------------------------------------------------------- acceptance
 @pytest.mark.parametrize("B,k,V,T,tp", [(5, 4, 1000, 0.0, 1.0), (6, 4, 3000, 0.8, 1.0), (7, 8, 5000, 0.7, 0.9),
-                                         (3, 3, 32000, 1.0, 1.0), (4, 8, 128256, 0.7, 0.9)])
+                                         (3, 3, 32000, 1.0, 1.0), (4, 8, 128256, 0.7, 0.9), (32, 4, 128256, 0.8, 1.0),
+                                         (9, 2, 4099, 1.0, 1.0), (9, 2, 4099, 0.0, 1.0), (1, 16, 777, 1.3, 1.0)])
 def test_accept_chain_bit_exact(cuda_device, B, k, V, T, tp):
+    """Greedy and top_p = 1 take the sliced cluster kernel (cluster sizes 8, 4
+    and, at B = 32, 4 CTAs per sequence; V = 4099 and 777 leave ragged,
+    unaligned slices), top_p < 1 the one-CTA kernel."""
     rng = np.random.default_rng(B * 1000 + V)
     tgt = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
     dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.5).astype(np.float32)
@@ -39,6 +43,40 @@ def test_accept_chain_bit_exact(cuda_device, B, k, V, T, tp):
     ws_b = S.lib().specdec_accept_workspace_bytes(B * (2 * k + 1))
     ws = empty(ws_b, torch.uint8)
     sp = S.sampling(T, tp, 1234, 7)
+    S.check(S.lib().specdec_accept_chain(ptr(d_t), ptr(d_d), ptr(d_dr), B, k, V, C.byref(sp), ptr(acc), ptr(out),
+                                         ptr(ws), ws_b, stream_ptr()))
+    sync()
+    assert acc.cpu().numpy().tolist() == acc_o.tolist()
+    assert out.cpu().numpy().tolist() == out_o.tolist()
+
+
+@pytest.mark.parametrize("k", [0, 3])
+def test_accept_chain_zero_residual_and_bonus_only(cuda_device, k):
+    """q == p with out-of-range draft tokens: the forced rejection leaves a
+    zero residual, so the token is drawn from p (the fallback draw); k = 0
+    draws the bonus token only."""
+    B, V = 4, 2000
+    rng = np.random.default_rng(5)
+    tgt = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    dr = np.ascontiguousarray(tgt[:, :k])
+    if k:
+        drafts = O.sample_rows(dr.reshape(B * k, V), k, 1.0, 1.0, 9, 0).reshape(B, k)
+        drafts[:, 1] = -1
+        drafts[2, 0] = V + 5
+    else:
+        drafts = np.zeros((B, 0), np.int32)
+    acc_o, out_o = O.accept_chain(tgt, dr, drafts, 1.0, 1.0, 1234, 7)
+    if k:
+        assert acc_o.tolist() == [1, 1, 0, 1]
+    import torch
+
+    d_t = dev(tgt)
+    d_d = dev(dr) if k else dev(np.zeros(1, np.float32))
+    d_dr = dev(drafts) if k else dev(np.zeros(1, np.int32))
+    acc, out = _i32(B), _i32((B, k + 1))
+    ws_b = S.lib().specdec_accept_workspace_bytes(B * (2 * k + 1))
+    ws = empty(ws_b, torch.uint8)
+    sp = S.sampling(1.0, 1.0, 1234, 7)
     S.check(S.lib().specdec_accept_chain(ptr(d_t), ptr(d_d), ptr(d_dr), B, k, V, C.byref(sp), ptr(acc), ptr(out),
                                          ptr(ws), ws_b, stream_ptr()))
     sync()
@@ -280,9 +318,9 @@ def test_w4a16_simt_matches_tcgen05(cuda_device):
                                        (300, 512, 256, 0), (7, 1001, 384, 0), (64, 1792, 4096, 0)])
 def test_w4a16_gemm_swiglu_matches_unfused(cuda_device, M, F, K, pad):
     """The fused gate/up GEMM + SwiGLU epilogue equals the plain GEMM over the
-    same interleaved weights followed by fp16(silu(g) * u), up to the one ulp
-    that expf and numpy's exp may differ by; g and u match the oracle's
-    contraction of the separate gate / up weights."""
+    same interleaved weights followed by fp16(silu(g) * u), up to one fp16 ulp
+    (the epilogue's fast exp and divide are within a few fp32 ulp); g and u
+    match the oracle's contraction of the separate gate / up weights."""
     import torch
 
     gate, up = O.synth_w4(5, 21, F, K), O.synth_w4(5, 22, F, K)
