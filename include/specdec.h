@@ -160,9 +160,10 @@ int specdec_w4_untile(const void* tiled, int N, int K, uint8_t* packed, uint16_t
 /* Y[m, n] = sum_k X[m, k] * W[n, k] (mode 0 store, 1 add).  X fp16 [M, K]
  * (row stride ldx elements, 16-byte aligned), Y fp32 with row stride ldy.
  * The int4 weights are dequantised in registers and multiplied on the tcgen05
- * tensor cores with TMEM accumulators.  The workspace (size from
- * specdec_w4a16_workspace_bytes) holds partial tiles of k-ranges split across
- * CTAs; the result is deterministic (parts are summed in a fixed order). */
+ * tensor cores with TMEM accumulators.  Partial tiles of k-ranges split
+ * across the CTAs of a cluster are summed on chip in a fixed order, so the
+ * result is deterministic; the workspace (specdec_w4a16_workspace_bytes, 0)
+ * is kept for the interface and may be NULL. */
 size_t specdec_w4a16_workspace_bytes(int M, int N, int K);
 int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
                        int mode, void* workspace, size_t workspace_bytes, void* stream);
