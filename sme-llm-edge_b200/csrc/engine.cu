@@ -174,7 +174,80 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
         for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = __float2half_rn(__fmul_rn(row_s[i], r));
     }
 }
+// The same RMSNorm with each thread's float4s of the row held in registers and
+// no shared memory beyond the 16-byte reduction, so its CTAs fit beside a
+// running GEMM CTA (which leaves ~12K registers and a few KB of shared memory
+// on its SM).  Launched as a programmatic dependent, its CTAs become resident
+// while the kernel that writes x is still running and wait on
+// griddepcontrol.wait, so no launch latency sits between the two.
+constexpr int kNormRowThreads = 128;
+template <int VPT>  // float4s per thread: H <= 4 * kNormRowThreads * VPT
+__global__ void __launch_bounds__(kNormRowThreads) rmsnorm_reg_kernel(const float* __restrict__ x, int ldx, int H,
+                                                                      float eps, __half* __restrict__ out, int ldo) {
+    __shared__ float red[kNormRowThreads / 32];
+    pdl_trigger();  // a following GEMM may start streaming its weights
+    pdl_wait();     // x is written by the kernel before this one
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * ldx);
+    const int n4 = H / 4;
+    float4 v[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int j = threadIdx.x + i * kNormRowThreads;
+        v[i] = j < n4 ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        ss = __fadd_rn(ss, __fmul_rn(v[i].x, v[i].x));
+        ss = __fadd_rn(ss, __fmul_rn(v[i].y, v[i].y));
+        ss = __fadd_rn(ss, __fmul_rn(v[i].z, v[i].z));
+        ss = __fadd_rn(ss, __fmul_rn(v[i].w, v[i].w));
+    }
+    ss = block_sum<float>(ss, red);
+    const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)H), eps));
+    uint2* o = reinterpret_cast<uint2*>(out + (size_t)blockIdx.x * ldo);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int j = threadIdx.x + i * kNormRowThreads;
+        if (j < n4) {
+            __half2 a = __floats2half2_rn(__fmul_rn(v[i].x, r), __fmul_rn(v[i].y, r));
+            __half2 b = __floats2half2_rn(__fmul_rn(v[i].z, r), __fmul_rn(v[i].w, r));
+            uint2 w;
+            w.x = *reinterpret_cast<uint32_t*>(&a);
+            w.y = *reinterpret_cast<uint32_t*>(&b);
+            o[j] = w;
+        }
+    }
+}
+
+template <int VPT>
+static cudaError_t launch_rmsnorm_reg(const float* x, int ldx, int rows, int H, float eps, __half* out, int ldo,
+                                      cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)rows);
+    cfg.blockDim = dim3(kNormRowThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rmsnorm_reg_kernel<VPT>, x, ldx, H, eps, out, ldo);
+}
+
 static void launch_rmsnorm(const float* x, int ldx, int rows, int H, float eps, __half* out, int ldo, cudaStream_t s) {
+    const bool vec = (H & 3) == 0 && (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldo & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 7) == 0;
+    const int per = 4 * kNormRowThreads;  // row elements per float4 per thread
+    if (vec && H <= 16 * per) {
+        // a launch error is reported by the caller's launch check
+        if (H <= 4 * per) (void)launch_rmsnorm_reg<4>(x, ldx, rows, H, eps, out, ldo, s);
+        else if (H <= 8 * per) (void)launch_rmsnorm_reg<8>(x, ldx, rows, H, eps, out, ldo, s);
+        else if (H <= 12 * per) (void)launch_rmsnorm_reg<12>(x, ldx, rows, H, eps, out, ldo, s);
+        else (void)launch_rmsnorm_reg<16>(x, ldx, rows, H, eps, out, ldo, s);
+        return;
+    }
     const size_t smem = (size_t)H * sizeof(float);
     static size_t opted = 48 * 1024;
     if (smem > opted) {  // rows wider than 12288 need the opt-in
