@@ -343,7 +343,8 @@ def run_gpu(args, world, rank, local, pg):
     e_ms = reduce_max(pg, t0.elapsed_time(t1), local)
     e_tok = reduce_sum(pg, int(eng.read("emitted", np.int64, (1,))[0]) - e0, local)
     e2e = {"value": e_tok / (e_ms / 1e3), "unit": "accepted tokens/s", "h2d_bytes_per_step": 4 * B,
-           "d2h_bytes_per_step": 4 * B + 4 * B * R}
+           "d2h_bytes_per_step": 4 * B + 4 * B * R, "ms_per_step": round(e_ms / args.steps, 4),
+           "tokens_per_step": round(e_tok / args.steps / max(1, world), 2)}
 
     # per-kernel device time (eager steps with an event after every launch)
     prof = eng.profile(3)
