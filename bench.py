@@ -47,18 +47,46 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML polled every ~2 ms from a thread (the timed steps are tens of
+    ms), the device matched by PCI bus id; nvidia-smi -lms 200 as a fallback.
+    Read-only: no clock or power setting is touched."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.lines = []
+        self.nv = None
+        self.samples = []
+        self.stop_flag = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
+        try:
+            self.nv, self.h = self._nvml_handle()
+            self.max_mhz = float(self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nv = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
@@ -68,11 +96,30 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def _poll(self):
+        nv, h = self.nv, self.h
+        while not self.stop_flag.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((mhz, bits))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        self.stop_flag.set()
+        if self.nv is not None:
+            self.t.join(timeout=5)
+            sm = [m for m, _ in self.samples]
+            reasons = sorted({n for _, bits in self.samples for n, bit in self.REASONS if bits & bit})
+            return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "sm_min_mhz": min(sm) if sm else None, "reasons": reasons, "samples": len(sm),
+                    "source": "nvml, every ~2 ms during the timed steps"}
         if self.proc:
             self.proc.terminate()
             try:
@@ -94,7 +141,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi -lms 200"}
 
 
 def dist_setup():
@@ -304,10 +351,9 @@ def run_gpu(args, world, rank, local, pg):
     emitted0 = int(eng.read("emitted", np.int64, (1,))[0])
     clocks = ClockSampler(local)
     barrier(pg, local)
-    clocks.start()
-    time.sleep(0.3)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    clocks.start()
     if args.nvtx:
         torch.cuda.nvtx.range_push("specdec_timed_steps")
     ev0.record(stream)
