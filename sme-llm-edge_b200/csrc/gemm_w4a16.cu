@@ -417,9 +417,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // overwrites only its own rows, which no peer reads), then writes them.
     float* stage = reinterpret_cast<float*>(base);  // [QN][MT][128]
     const int rows = MT / S, r0 = rank * rows;       // S divides MT (16 | MT, S <= 8)
+    // Mode 2 without a k split: the gate and up rows of a feature share a
+    // TMEM lane (unit 0 at columns 0.., unit 1 at MT..), so each thread forms
+    // h = fp16(silu(g) * u) from its two loads and writes the fp16 [MT][128]
+    // box directly -- no fp32 staging of g and u in shared memory.
+    const bool swiglu_direct = QN == 2 && args.mode == 2 && S == 1;
     if (epi_warp && acc_ok) {
+        if (swiglu_direct) {
+            constexpr int kChunks = MT / 16, kGroups = kDeqWarps / 4;
+            __half* h = reinterpret_cast<__half*>(stage);
+            const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+            for (int c = eg; c < kChunks; c += kGroups) {
+                uint32_t g[16], u[16];
+                tc_ld_x16(trow + (uint32_t)(c * 16), g);
+                tc_ld_x16(trow + (uint32_t)(MT + c * 16), u);
+                tc_wait_ld();
 #pragma unroll
-        for (int q = 0; q < QN; ++q) drain(q, stage + q * MT * 128);
+                for (int jj = 0; jj < 16; ++jj) {
+                    // fast exp and divide (one MUFU op each): within a few fp32 ulp,
+                    // well inside the fp16 rounding of h
+                    const float gv = __uint_as_float(g[jj]);
+                    const float hv = __fmul_rn(__fdividef(gv, __fadd_rn(1.0f, __expf(-gv))), __uint_as_float(u[jj]));
+                    h[(c * 16 + jj) * 128 + quad * 32 + lane] = __float2half_rn(hv);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < QN; ++q) drain(q, stage + q * MT * 128);
+        }
     }
     if constexpr (reduce_fits<MT, QN>()) {
         if (S > 1) {
@@ -456,7 +481,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // fp32 rows, then the CTA overwrites the start of its own half-0 rows
     // (no peer reads them) with a dense fp16 [rows][128] box.
     __half* hbox = reinterpret_cast<__half*>(stage + r0 * 128);
-    if (QN == 2 && args.mode == 2) {
+    if (QN == 2 && args.mode == 2 && !swiglu_direct) {
         constexpr int kItems = (MT * 16 + kGemmThreads - 1) / kGemmThreads;  // (row, 8 features) per thread
         const int nitems = rows * 16;
         uint4 hv[kItems];

@@ -314,7 +314,7 @@ def test_w4a16_simt_matches_tcgen05(cuda_device):
     np.testing.assert_allclose(Y1.cpu().numpy(), Y2.cpu().numpy(), rtol=2e-3, atol=2e-3)
 
 
-@pytest.mark.parametrize("M,F,K,pad", [(1, 256, 512, 0), (5, 1376, 512, 0), (160, 1376, 1024, 8), (33, 384, 640, 0),
+@pytest.mark.parametrize("M,F,K,pad", [(160, 14336, 512, 0), (1, 256, 512, 0), (5, 1376, 512, 0), (160, 1376, 1024, 8), (33, 384, 640, 0),
                                        (300, 512, 256, 0), (7, 1001, 384, 0), (64, 1792, 4096, 0)])
 def test_w4a16_gemm_swiglu_matches_unfused(cuda_device, M, F, K, pad):
     """The fused gate/up GEMM + SwiGLU epilogue equals the plain GEMM over the
