@@ -450,8 +450,10 @@ def run_gpu(args, world, rank, local, pg):
 # ------------------------------------------------------------ single-kernel mode
 def run_kernel(args):
     """One hot kernel on synthetic inputs, for profiler captures: `--kernel gemm
-    --shape M,N,K` (W4A16 GEMM, random int4 weights) or `--kernel attention
-    --shape B,R,Hq,Hkv,hd,ctx` (verify attention over a shuffled paged KV pool).
+    --shape M,N,K` (W4A16 GEMM, random int4 weights), `--kernel attention
+    --shape B,R,Hq,Hkv,hd,ctx` (verify attention over a shuffled paged KV pool)
+    or `--kernel accept --shape B,k,V,T,top_p` (chain acceptance on fp32 logits;
+    default the acceptance micro-benchmark 256,7,128256,0.7,0.9).
     Runs `--steps` timed launches after `--warmup` and prints the mean time;
     this is a kernel timing, not the benchmark metric."""
     import ctypes as C
@@ -461,9 +463,28 @@ def run_kernel(args):
     import specdec as S
 
     L = S.lib()
-    dims = [int(x) for x in args.shape.split(",")]
     g = torch.Generator(device="cuda").manual_seed(0)
     ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    if args.kernel == "accept":
+        # chain acceptance on fp32 logits: target N(0, 3) [B, k+1, V], draft =
+        # target + N(0, 0.5) [B, k, V], drafts = the draft rows' arg-max
+        parts = (args.shape if args.shape.count(",") == 4 else "256,7,128256,0.7,0.9").split(",")
+        B, k, V = (int(x) for x in parts[:3])
+        T, tp = float(parts[3]), float(parts[4])
+        ga = torch.Generator(device="cuda").manual_seed(4)
+        tgt = torch.randn((B, k + 1, V), device="cuda", generator=ga) * 3
+        dr = tgt[:, :k] + torch.randn((B, k, V), device="cuda", generator=ga) * 0.5
+        drafts = dr.argmax(-1).to(torch.int32).contiguous()
+        acc = torch.empty(B, dtype=torch.int32, device="cuda")
+        out = torch.empty((B, k + 1), dtype=torch.int32, device="cuda")
+        ws_b = L.specdec_accept_workspace_bytes(B * (2 * k + 1))
+        ws = torch.empty(ws_b, dtype=torch.uint8, device="cuda")
+        sp = S.sampling(T, tp, 4, 0)
+        call = lambda: L.specdec_accept_chain(ptr(tgt), ptr(dr), ptr(drafts), B, k, V, C.byref(sp),  # noqa: E731
+                                              ptr(acc), ptr(out), ptr(ws), ws_b, None)
+        algo = {"bytes": (2 * k + 1) * B * V * 4}
+        args.shape = f"{B},{k},{V},{T},{tp}"
+    dims = [int(x) for x in args.shape.split(",")] if args.kernel != "accept" else []
     if args.kernel == "gemm":
         M, N, K = dims
         packed = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
@@ -474,7 +495,7 @@ def run_kernel(args):
         Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
         call = lambda: L.specdec_w4a16_gemm(ptr(X), M, K, ptr(tiled), N, K, ptr(Y), N, 0, None, 0, None)  # noqa: E731
         algo = {"bytes": N * K // 2 + N * ((K + 127) // 128) * 2, "flops": 2.0 * M * N * K}
-    else:
+    elif args.kernel == "attention":
         B, R, Hq, Hkv, hd, ctx = dims
         max_blocks = (ctx + R + 15) // 16 + 1
         nblk = B * max_blocks
@@ -503,6 +524,12 @@ def run_kernel(args):
            "gbs_algorithmic": round(algo["bytes"] / us / 1e3, 1)}
     if "flops" in algo:
         res["tflops"] = round(algo["flops"] / us / 1e6, 1)
+    peaks, src = load_peaks()
+    res["hbm_frac"] = round(algo["bytes"] / us / 1e3 / peaks["hbm_gbs"], 3)
+    res["hbm_peak_gbs"] = peaks["hbm_gbs"]
+    res["peak_source"] = src
+    if args.kernel == "accept":
+        res["mean_accepted"] = round(float(acc.float().mean()), 3)
     print(json.dumps(res), flush=True)
 
 
@@ -515,8 +542,9 @@ def main():
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--nvtx", action="store_true", help="mark the timed steps with an NVTX range (profiler filter)")
-    ap.add_argument("--kernel", choices=["gemm", "attention"], help="time one hot kernel instead of the step")
-    ap.add_argument("--shape", default="160,128256,4096", help="--kernel shape: M,N,K or B,R,Hq,Hkv,hd,ctx")
+    ap.add_argument("--kernel", choices=["gemm", "attention", "accept"], help="time one hot kernel instead of the step")
+    ap.add_argument("--shape", default="160,128256,4096",
+                    help="--kernel shape: M,N,K (gemm), B,R,Hq,Hkv,hd,ctx (attention) or B,k,V,T,top_p (accept)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.kernel:

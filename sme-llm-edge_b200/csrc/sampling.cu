@@ -131,19 +131,31 @@ __device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, floa
     __syncthreads();
 }
 
-// Adds e into H[bin] for every valid lane; whole warp must call together.
-__device__ __forceinline__ void warp_hist_add(uint64_t* H, uint32_t bin, uint32_t e, bool valid) {
-    const int lane = threadIdx.x & 31;
-    unsigned active = __ballot_sync(0xffffffffu, valid && e != 0);
-    while (active) {
-        const int leader = __ffs(active) - 1;
-        const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
-        const unsigned grp = __ballot_sync(0xffffffffu, valid && e != 0 && bin == lb);
-        uint64_t v = ((grp >> lane) & 1u) ? (uint64_t)e : 0ull;
-        v = warp_sum(v);
-        if (lane == leader) atomicAdd((unsigned long long*)&H[lb], (unsigned long long)v);
-        active &= ~grp;
+// Per-warp mass histograms for the top-p radix select: warp w owns
+// whist[w][0][256] (the low 16 bits of each mass) and whist[w][1][256] (the
+// high bits), updated by 32-bit shared-memory atomics from every lane (only
+// lanes of the same warp contend).  A warp sees at most 8192 elements of a row
+// (V <= 262144 over 32 warps), so the halves stay below 2^29 and 2^28 and the
+// merge recombines them exactly.
+__device__ __forceinline__ void hist_add_lane(uint32_t* Hw, uint32_t bin, uint32_t e) {
+    if (e) {
+        atomicAdd(&Hw[bin], e & 0xFFFFu);
+        atomicAdd(&Hw[256 + bin], e >> 16);
     }
+}
+
+// The per-warp histograms summed into sm.hist, then cleared for the next pass.
+__device__ __forceinline__ void merge_warp_hists(uint32_t* whist, RowSmem& sm) {
+    const int nw = blockDim.x >> 5;
+    __syncthreads();
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+        uint64_t t = 0;
+        for (int w = 0; w < nw; ++w) t += ((uint64_t)whist[w * 512 + 256 + b] << 16) + whist[w * 512 + b];
+        sm.hist[b] = t;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nw * 512; i += blockDim.x) whist[i] = 0;
+    __syncthreads();
 }
 
 // Warp 0 picks the highest digit whose cumulative mass (from the top) reaches thr.
@@ -213,8 +225,12 @@ __device__ uint64_t cta_mass_sum(const float* __restrict__ z, int n, float m, fl
 }
 
 // Full row statistics (max, argmax, mass sum, top-p threshold, nucleus mass).
+// The top-p threshold is a radix select on the logit key, 8 bits per pass,
+// over mass-weighted histograms: whist ([warps][256] u64, zeroed, only needed
+// when tp < 2^32) holds one private histogram per warp.
+constexpr size_t kWarpHistBytes = (size_t)(kRowThreads / 32) * 512 * sizeof(uint32_t);
 __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint64_t tp, bool need_mass, RowSmem& sm,
-                              DevRowStats* st) {
+                              DevRowStats* st, uint32_t* whist = nullptr) {
     float m;
     int am;
     cta_argmax(z, V, sm, &m, &am);
@@ -227,21 +243,22 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
     r.nuc = 0;
     if (need_mass) {
         const bool nucleus = tp < (1ull << 32);
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
-        __syncthreads();
         uint64_t s = 0;
         const int lane = threadIdx.x & 31;
         const int warp_base = (threadIdx.x >> 5) * 32, stride = blockDim.x;
+        uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
         if (!nucleus) {
             s = cta_mass_sum(z, V, m, c, sm);
         } else {
+            for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist[i] = 0;
+            __syncthreads();
             for (int base = warp_base; base < V; base += stride) {
                 const int j = base + lane;
                 const bool valid = j < V;
                 const float zj = valid ? z[j] : 0.0f;
                 const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
                 s += e;
-                warp_hist_add(sm.hist, logit_key(zj) >> 24, e, valid);
+                hist_add_lane(Hw, logit_key(zj) >> 24, e);
             }
             s = block_sum<uint64_t>(s, sm.red64);
         }
@@ -250,25 +267,22 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
         if (nucleus) {
             uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
             if (thr < 1) thr = 1;
-            __syncthreads();
+            merge_warp_hists(whist, sm);
             uint64_t G = 0, last = 0;
             uint32_t prefix = 0, dg = 0;
             select_digit(sm, thr, &G, &dg, &last);
             prefix = dg << 24;
             for (int d = 2; d >= 0; --d) {
                 const int shift = 8 * d;
-                for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
-                __syncthreads();
                 for (int base = warp_base; base < V; base += stride) {
                     const int j = base + lane;
                     bool valid = j < V;
                     const float zj = valid ? z[j] : 0.0f;
                     const uint32_t key = logit_key(zj);
                     valid = valid && ((key >> (shift + 8)) == (prefix >> (shift + 8)));
-                    const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
-                    warp_hist_add(sm.hist, (key >> shift) & 255u, e, valid);
+                    if (valid) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
                 }
-                __syncthreads();
+                merge_warp_hists(whist, sm);
                 select_digit(sm, thr, &G, &dg, &last);
                 prefix |= dg << shift;
             }
@@ -457,11 +471,12 @@ __global__ void __launch_bounds__(kRowThreads) row_stats_kernel(RowSet a, RowSet
                                                                 bool need_mass_a, bool need_mass_b,
                                                                 DevRowStats* out) {
     __shared__ RowSmem sm;
+    extern __shared__ uint32_t whist_dyn[];  // kWarpHistBytes when tp < 2^32
     const int r = blockIdx.x;
     const bool in_a = r < a.rows;
     const float* z = in_a ? a.base + (size_t)r * V : b.base + (size_t)(r - a.rows) * V;
     DevRowStats st;
-    cta_row_stats(z, V, c, tp, in_a ? need_mass_a : need_mass_b, sm, &st);
+    cta_row_stats(z, V, c, tp, in_a ? need_mass_a : need_mass_b, sm, &st, whist_dyn);
     if (threadIdx.x == 0) out[r] = st;
 }
 
@@ -753,6 +768,7 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
                                                                   int32_t* __restrict__ path_nodes,
                                                                   int32_t* __restrict__ out_tokens) {
     __shared__ RowSmem sm;
+    extern __shared__ uint32_t whist_dyn[];  // kWarpHistBytes when tp < 2^32
     __shared__ int s_removed[64];
     __shared__ int s_nremoved, s_next, s_emit_mode;
     __shared__ uint64_t s_remaining;
@@ -770,7 +786,7 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
     for (;;) {
         const float* z = P + (size_t)cur * V;
         DevRowStats st;
-        cta_row_stats(z, V, c, tp, !greedy, sm, &st);
+        cta_row_stats(z, V, c, tp, !greedy, sm, &st, whist_dyn);
         if (threadIdx.x == 0) {
             int next = -1;
             s_nremoved = 0;
@@ -851,6 +867,7 @@ __global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* _
                                                                   int32_t* __restrict__ out,
                                                                   DevRowStats* __restrict__ stats) {
     __shared__ RowSmem sm;
+    extern __shared__ uint32_t whist_dyn[];  // kWarpHistBytes when tp < 2^32
     const uint32_t step = step_dev ? *step_dev : step_host;
     const int r = blockIdx.x;
     const float* z = logits + (size_t)r * V;
@@ -866,7 +883,7 @@ __global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* _
             [u64](u128 tot) { return (u128)mulhi64(u64, (uint64_t)tot); }, sm, &total);
         st.sum = st.nuc = (uint64_t)total;  // <= V * 2^31 < 2^64
     } else {
-        cta_row_stats(z, V, c, tp, !greedy, sm, &st);
+        cta_row_stats(z, V, c, tp, !greedy, sm, &st, whist_dyn);
         tok = st.argmax;
         if (!greedy)
             tok = cta_sample_nucleus(z, V, c, st,
@@ -1028,6 +1045,26 @@ int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaS
     return SPECDEC_OK;
 }
 
+// Dynamic shared memory of the row-statistics kernels: the per-warp top-p
+// histograms, needed only when the rows need mass sums and a nucleus.  They
+// exceed the 48 KB default, so the kernels opt in once per device.
+static int hist_smem(bool need_mass, uint64_t tp, size_t* bytes) {
+    *bytes = 0;
+    if (!need_mass || tp >= (1ull << 32)) return SPECDEC_OK;
+    static bool done[64] = {};
+    int dev = 0;
+    SD_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !done[dev]) {
+        const int sz = (int)kWarpHistBytes;
+        SD_CUDA(cudaFuncSetAttribute(row_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sz));
+        SD_CUDA(cudaFuncSetAttribute(accept_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sz));
+        SD_CUDA(cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sz));
+        if (dev >= 0 && dev < 64) done[dev] = true;
+    }
+    *bytes = kWarpHistBytes;
+    return SPECDEC_OK;
+}
+
 // Cluster size of the sliced chain acceptance: the largest power of two
 // <= 8 whose B * S CTAs fit one wave on the device's SMs.
 static int accept_cluster_size(int B) {
@@ -1073,7 +1110,10 @@ static int launch_accept_chain_impl(const float* target, const float* draft, con
     SD_CHECK(st, SPECDEC_EINVAL, "accept_chain: row statistics scratch required");
     const int rows = B * (k + 1) + (greedy ? 0 : B * k);
     RowSet a{target, B * (k + 1)}, bq{dq, greedy ? 0 : B * k};
-    row_stats_kernel<<<(unsigned)rows, kRowThreads, 0, s>>>(a, bq, V, c, tp, !greedy, true, st);
+    size_t hs = 0;
+    int rc = hist_smem(!greedy, tp, &hs);
+    if (rc) return rc;
+    row_stats_kernel<<<(unsigned)rows, kRowThreads, hs, s>>>(a, bq, V, c, tp, !greedy, true, st);
     SD_LAUNCH_CHECK("row_stats_kernel");
     accept_chain_kernel<<<B, kRowThreads, 0, s>>>(target, dq, drafts, k, V, c, greedy, seed, step_dev, step_host, st,
                                                   B, accepted_len, out_tokens);
@@ -1095,7 +1135,10 @@ int launch_accept_tree_dev(const float* target, const int32_t* node_tokens, cons
                            int32_t* accepted_len, int32_t* path, int32_t* out_tokens, cudaStream_t s) {
     SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_accept_tree_dev: vocabulary above 262144");
     const bool greedy = !(temperature > 0.0f);
-    accept_tree_kernel<<<B, kRowThreads, 0, s>>>(target, node_tokens, parent, R, V, greedy ? 0.0f : temp_coeff(temperature),
+    size_t hs = 0;
+    int rc = hist_smem(!greedy, top_p_q32(top_p), &hs);
+    if (rc) return rc;
+    accept_tree_kernel<<<B, kRowThreads, hs, s>>>(target, node_tokens, parent, R, V, greedy ? 0.0f : temp_coeff(temperature),
                                                  top_p_q32(top_p), greedy, seed, step_dev, 0u, accepted_len, path,
                                                  out_tokens);
     SD_LAUNCH_CHECK("accept_tree_kernel");
@@ -1106,7 +1149,10 @@ int launch_sample_rows_dev(const float* logits, int rows, int k, int V, float te
                            const uint32_t* step_dev, int32_t* out, void* stats, cudaStream_t s) {
     SD_CHECK(V <= kMaxVocab, SPECDEC_EINVAL, "launch_sample_rows_dev: vocabulary above 262144");
     const bool greedy = !(temperature > 0.0f);
-    sample_rows_kernel<<<rows, kRowThreads, 0, s>>>(logits, k, V, greedy ? 0.0f : temp_coeff(temperature),
+    size_t hs = 0;
+    int rc = hist_smem(!greedy, top_p_q32(top_p), &hs);
+    if (rc) return rc;
+    sample_rows_kernel<<<rows, kRowThreads, hs, s>>>(logits, k, V, greedy ? 0.0f : temp_coeff(temperature),
                                                     top_p_q32(top_p), greedy, seed, step_dev, 0u, out,
                                                     reinterpret_cast<DevRowStats*>(stats));
     SD_LAUNCH_CHECK("sample_rows_kernel");
@@ -1213,7 +1259,10 @@ extern "C" int specdec_accept_tree(const float* target, const int32_t* node_toke
     if (B == 0) return SPECDEC_OK;
     const bool greedy = !(sp->temperature > 0.0f);
     const float c = greedy ? 0.0f : temp_coeff(sp->temperature);
-    accept_tree_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(target, node_tokens, parent, R, V, c,
+    size_t hs = 0;
+    int rc = hist_smem(!greedy, top_p_q32(sp->top_p), &hs);
+    if (rc) return rc;
+    accept_tree_kernel<<<B, kRowThreads, hs, as_stream(stream)>>>(target, node_tokens, parent, R, V, c,
                                                                  top_p_q32(sp->top_p), greedy, sp->seed, nullptr,
                                                                  sp->step, accepted_len, path_nodes, out_tokens);
     SD_LAUNCH_CHECK("accept_tree_kernel");
@@ -1228,7 +1277,10 @@ extern "C" int specdec_sample_rows(const float* logits, int rows, int k, int V, 
     SD_CHECK(sp && logits && out && rows >= 0 && k >= 1 && V > 0, SPECDEC_EINVAL, "sample_rows: bad argument");
     if (rows == 0) return SPECDEC_OK;
     const bool greedy = !(sp->temperature > 0.0f);
-    sample_rows_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(
+    size_t hs = 0;
+    int rc = hist_smem(!greedy, top_p_q32(sp->top_p), &hs);
+    if (rc) return rc;
+    sample_rows_kernel<<<rows, kRowThreads, hs, as_stream(stream)>>>(
         logits, k, V, greedy ? 0.0f : temp_coeff(sp->temperature), top_p_q32(sp->top_p), greedy, sp->seed, nullptr, sp->step,
         out, nullptr);
     SD_LAUNCH_CHECK("sample_rows_kernel");
