@@ -131,6 +131,39 @@ __device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, floa
     __syncthreads();
 }
 
+// Calls f(z_j) for every element of the row z[0, V) once, in no particular
+// order: four float4 loads in flight per thread when z is 16-byte aligned and
+// V a multiple of 4, else one element per thread and iteration.
+template <class F>
+__device__ __forceinline__ void for_each_row_value(const float* __restrict__ z, int V, F f) {
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+        const float4* z4 = reinterpret_cast<const float4*>(z);
+        const int n4 = V / 4, bd = blockDim.x;
+        int q = threadIdx.x;
+        for (; q + 3 * bd < n4; q += 4 * bd) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                f(v[u].x);
+                f(v[u].y);
+                f(v[u].z);
+                f(v[u].w);
+            }
+        }
+        for (; q < n4; q += bd) {
+            const float4 v = z4[q];
+            f(v.x);
+            f(v.y);
+            f(v.z);
+            f(v.w);
+        }
+    } else {
+        for (int j = threadIdx.x; j < V; j += blockDim.x) f(z[j]);
+    }
+}
+
 // Per-warp mass histograms for the top-p radix select: warp w owns
 // whist[w][0][256] (the low 16 bits of each mass) and whist[w][1][256] (the
 // high bits), updated by 32-bit shared-memory atomics from every lane (only
@@ -244,22 +277,17 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
     if (need_mass) {
         const bool nucleus = tp < (1ull << 32);
         uint64_t s = 0;
-        const int lane = threadIdx.x & 31;
-        const int warp_base = (threadIdx.x >> 5) * 32, stride = blockDim.x;
         uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
         if (!nucleus) {
             s = cta_mass_sum(z, V, m, c, sm);
         } else {
             for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist[i] = 0;
             __syncthreads();
-            for (int base = warp_base; base < V; base += stride) {
-                const int j = base + lane;
-                const bool valid = j < V;
-                const float zj = valid ? z[j] : 0.0f;
-                const uint32_t e = valid ? mass_of(zj, m, c) : 0u;
+            for_each_row_value(z, V, [&](float zj) {
+                const uint32_t e = mass_of(zj, m, c);
                 s += e;
                 hist_add_lane(Hw, logit_key(zj) >> 24, e);
-            }
+            });
             s = block_sum<uint64_t>(s, sm.red64);
         }
         r.sum = s;
@@ -274,14 +302,11 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
             prefix = dg << 24;
             for (int d = 2; d >= 0; --d) {
                 const int shift = 8 * d;
-                for (int base = warp_base; base < V; base += stride) {
-                    const int j = base + lane;
-                    bool valid = j < V;
-                    const float zj = valid ? z[j] : 0.0f;
+                const uint32_t want = prefix >> (shift + 8);
+                for_each_row_value(z, V, [&](float zj) {
                     const uint32_t key = logit_key(zj);
-                    valid = valid && ((key >> (shift + 8)) == (prefix >> (shift + 8)));
-                    if (valid) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
-                }
+                    if ((key >> (shift + 8)) == want) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
+                });
                 merge_warp_hists(whist, sm);
                 select_digit(sm, thr, &G, &dg, &last);
                 prefix |= dg << shift;
@@ -770,7 +795,7 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
     __shared__ RowSmem sm;
     extern __shared__ uint32_t whist_dyn[];  // kWarpHistBytes when tp < 2^32
     __shared__ int s_removed[64];
-    __shared__ int s_nremoved, s_next, s_emit_mode;
+    __shared__ int s_nremoved, s_next;
     __shared__ uint64_t s_remaining;
     const uint32_t step = step_dev ? *step_dev : step_host;
     const int b = blockIdx.x;
@@ -790,7 +815,6 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
         if (threadIdx.x == 0) {
             int next = -1;
             s_nremoved = 0;
-            s_emit_mode = 0;
             if (greedy) {
                 for (int ch = cur + 1; ch < R; ++ch)
                     if (parent[ch] == cur && tok[ch] == st.argmax) {
