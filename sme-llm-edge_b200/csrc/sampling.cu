@@ -171,10 +171,8 @@ __device__ __forceinline__ void for_each_row_value(const float* __restrict__ z, 
 // (V <= 262144 over 32 warps), so the halves stay below 2^29 and 2^28 and the
 // merge recombines them exactly.
 __device__ __forceinline__ void hist_add_lane(uint32_t* Hw, uint32_t bin, uint32_t e) {
-    if (e) {
-        atomicAdd(&Hw[bin], e & 0xFFFFu);
-        atomicAdd(&Hw[256 + bin], e >> 16);
-    }
+    if (e & 0xFFFFu) atomicAdd(&Hw[bin], e & 0xFFFFu);
+    if (e >> 16) atomicAdd(&Hw[256 + bin], e >> 16);
 }
 
 // The per-warp histograms summed into sm.hist, then cleared for the next pass.
@@ -259,9 +257,14 @@ __device__ uint64_t cta_mass_sum(const float* __restrict__ z, int n, float m, fl
 
 // Full row statistics (max, argmax, mass sum, top-p threshold, nucleus mass).
 // The top-p threshold is a radix select on the logit key, 8 bits per pass,
-// over mass-weighted histograms: whist ([warps][256] u64, zeroed, only needed
-// when tp < 2^32) holds one private histogram per warp.
-constexpr size_t kWarpHistBytes = (size_t)(kRowThreads / 32) * 512 * sizeof(uint32_t);
+// over mass-weighted histograms.  whist (only needed when tp < 2^32) holds one
+// private histogram per warp ([warps][2][256] u32) and then a list of up to
+// kNucleusList (key, mass) pairs: the second pass records the elements whose
+// top digit was selected, and the last two passes read only that list (or the
+// row again, when it overflowed).
+constexpr int kNucleusList = 8192;
+constexpr size_t kWarpHistWords = (size_t)(kRowThreads / 32) * 512;
+constexpr size_t kWarpHistBytes = kWarpHistWords * sizeof(uint32_t) + (size_t)kNucleusList * sizeof(uint2) + 16;
 __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint64_t tp, bool need_mass, RowSmem& sm,
                               DevRowStats* st, uint32_t* whist = nullptr) {
     float m;
@@ -278,10 +281,13 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
         const bool nucleus = tp < (1ull << 32);
         uint64_t s = 0;
         uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
+        uint2* list = reinterpret_cast<uint2*>(whist + kWarpHistWords);
+        int* list_n = reinterpret_cast<int*>(list + kNucleusList);
         if (!nucleus) {
             s = cta_mass_sum(z, V, m, c, sm);
         } else {
             for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist[i] = 0;
+            if (threadIdx.x == 0) *list_n = 0;
             __syncthreads();
             for_each_row_value(z, V, [&](float zj) {
                 const uint32_t e = mass_of(zj, m, c);
@@ -303,10 +309,28 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
             for (int d = 2; d >= 0; --d) {
                 const int shift = 8 * d;
                 const uint32_t want = prefix >> (shift + 8);
-                for_each_row_value(z, V, [&](float zj) {
-                    const uint32_t key = logit_key(zj);
-                    if ((key >> (shift + 8)) == want) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
-                });
+                if (d == 2) {
+                    for_each_row_value(z, V, [&](float zj) {
+                        const uint32_t key = logit_key(zj);
+                        if ((key >> (shift + 8)) == want) {
+                            const uint32_t e = mass_of(zj, m, c);
+                            hist_add_lane(Hw, (key >> shift) & 255u, e);
+                            const int at = atomicAdd(list_n, 1);
+                            if (at < kNucleusList) list[at] = make_uint2(key, e);
+                        }
+                    });
+                } else if (*list_n <= kNucleusList) {
+                    const int n = *list_n;
+                    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                        const uint2 en = list[i];
+                        if ((en.x >> (shift + 8)) == want) hist_add_lane(Hw, (en.x >> shift) & 255u, en.y);
+                    }
+                } else {
+                    for_each_row_value(z, V, [&](float zj) {
+                        const uint32_t key = logit_key(zj);
+                        if ((key >> (shift + 8)) == want) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
+                    });
+                }
                 merge_warp_hists(whist, sm);
                 select_digit(sm, thr, &G, &dg, &last);
                 prefix |= dg << shift;
