@@ -533,6 +533,56 @@ def run_kernel(args):
     print(json.dumps(res), flush=True)
 
 
+def run_accept_sharded(args):
+    """The acceptance micro-benchmark with the vocabulary split across the
+    ranks of a torchrun job (one GPU each, NCCL): rank r holds columns
+    [v0, v0 + Vs) of every logits row and the ranks exchange per-row
+    statistics only (specdec.dist.accept_chain_vocab_sharded).  Times the
+    whole sharded acceptance, collectives included, as the slowest rank's
+    device time."""
+    import torch
+
+    import specdec as S
+    from specdec.dist import TorchComm, accept_chain_vocab_sharded, vocab_shard
+
+    world, rank, local, pg = dist_setup()
+    try:
+        torch.cuda.set_device(local)
+        parts = (args.shape if args.shape.count(",") == 4 else "256,7,128256,0.7,0.9").split(",")
+        B, k, V = (int(x) for x in parts[:3])
+        T, tp = float(parts[3]), float(parts[4])
+        v0, vs = vocab_shard(V, world, rank)
+        g = torch.Generator(device="cuda").manual_seed(4 + 1000 * rank)
+        tgt = torch.randn((B, k + 1, vs), device="cuda", generator=g) * 3
+        dr = tgt[:, :k] + torch.randn((B, k, vs), device="cuda", generator=g) * 0.5
+        drafts = torch.randint(0, V, (B, k), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5),
+                               dtype=torch.int32)
+        comm = TorchComm(torch.distributed)
+        sp = S.sampling(T, tp, 4, 0)
+        for _ in range(args.warmup):
+            accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm)
+        torch.cuda.synchronize()
+        barrier(pg, local)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            acc, _ = accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm)
+        e1.record()
+        torch.cuda.synchronize()
+        us = reduce_max(pg, e0.elapsed_time(e1) / args.steps * 1e3, local)
+        if rank == 0:
+            peaks, src = load_peaks()
+            total = (2 * k + 1) * B * V * 4
+            print(json.dumps({"kernel": "accept (vocabulary-sharded)", "shape": f"{B},{k},{V},{T},{tp}",
+                              "n_gpus": world, "us_per_launch": round(us, 2),
+                              "gbs_algorithmic_per_gpu": round(total / world / us / 1e3, 1),
+                              "hbm_frac_per_gpu": round(total / world / us / 1e3 / peaks["hbm_gbs"], 3),
+                              "mean_accepted": round(float(acc.float().mean()), 3)}), flush=True)
+    finally:
+        if pg is not None:
+            pg.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -547,6 +597,9 @@ def main():
                     help="--kernel shape: M,N,K (gemm), B,R,Hq,Hkv,hd,ctx (attention) or B,k,V,T,top_p (accept)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.kernel == "accept" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_accept_sharded(args)
+        return
     if args.kernel:
         run_kernel(args)
         return

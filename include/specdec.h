@@ -144,6 +144,52 @@ int specdec_accept_tree(const float* target, const int32_t* node_tokens, const i
 int specdec_sample_rows(const float* logits, int rows, int k, int V, const specdec_sampling* sp, int32_t* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Vocabulary-sharded chain acceptance (the 8-way variant of the acceptance
+ * micro-benchmark; replaces verify_drafts_sve2, speculative_decoder.cpp:53-77,
+ * when the lm_head is split by vocabulary across GPUs).  Rank w of W holds
+ * vocabulary columns [v0, v0 + Vs) of every logits row, ranks in vocabulary
+ * order: target shard [B][k+1][Vs], draft shard [B][k][Vs] (row-major, fp32).
+ * The caller runs the steps in order and combines across ranks between them
+ * (NCCL or any collective); every decision then equals specdec_accept_chain's
+ * on the whole rows.  rows_p = B*(k+1) target rows, rows_q = B*k draft rows.
+ *  1. specdec_shard_row_max on both shards; all-gather max/arg [W][rows];
+ *     specdec_shard_merge_max -> per-row max and arg-max (global index).
+ *     Greedy (temperature 0): go to 5 with parg only.
+ *  2. specdec_shard_row_mass -> per-row integer mass sums; all-reduce (sum).
+ *  3. top_p < 1: for digit 3, 2, 1, 0: specdec_shard_digit_hist (rows x 256
+ *     u64); all-reduce (sum); specdec_shard_select_digit -> prefix, G, last.
+ *     Then tau = prefix and nuc = G + last; with top_p = 1: tau = 0, nuc = sum.
+ *  4. specdec_shard_point_mass -> ep, eq [B*k]; all-reduce (sum).
+ *  5. specdec_shard_accept_test -> accepted [B] (identical on every rank).
+ *     Greedy: the emitted token is parg[b*(k+1) + accepted[b]].
+ *  6. specdec_shard_draw_totals -> [B][4] u64; all-gather [W][B][4].
+ *  7. specdec_shard_draw -> token or -1 per sequence; all-reduce (max).
+ * Unsigned 64-bit values may travel as signed 64-bit: every sum stays below
+ * 2^63.  Shard widths up to 262144; k >= 1. */
+int specdec_shard_row_max(const float* z, int rows, int Vs, int v0, float* out_max, int32_t* out_arg, void* stream);
+int specdec_shard_merge_max(const float* gmax, const int32_t* garg, int W, int rows, float* out_max, int32_t* out_arg,
+                            void* stream);
+int specdec_shard_row_mass(const float* z, int rows, int Vs, const float* gmax, float temperature, uint64_t* out_sum,
+                           void* stream);
+int specdec_shard_digit_hist(const float* z, int rows, int Vs, const float* gmax, float temperature,
+                             const uint32_t* prefix, int digit, uint64_t* out_hist, void* stream);
+int specdec_shard_select_digit(const uint64_t* hist, int rows, int digit, const uint64_t* gsum, float top_p,
+                               uint32_t* prefix, uint64_t* G, uint64_t* last, void* stream);
+int specdec_shard_point_mass(const float* target, const float* draft, const int32_t* drafts, int B, int k, int Vs,
+                             int v0, float temperature, const float* pmax, const uint32_t* ptau, const float* qmax,
+                             const uint32_t* qtau, uint64_t* ep, uint64_t* eq, void* stream);
+int specdec_shard_accept_test(const int32_t* drafts, int B, int k, const specdec_sampling* sp, const int32_t* parg,
+                              const uint64_t* pnuc, const uint64_t* qnuc, const uint64_t* ep, const uint64_t* eq,
+                              int32_t* accepted, void* stream);
+int specdec_shard_draw_totals(const float* target, const float* draft, int B, int k, int Vs, float temperature,
+                              const int32_t* accepted, const float* pmax, const uint32_t* ptau, const float* qmax,
+                              const uint32_t* qtau, const uint64_t* pnuc, const uint64_t* qnuc, uint64_t* out_tot,
+                              void* stream);
+int specdec_shard_draw(const float* target, const float* draft, int B, int k, int Vs, int v0,
+                       const specdec_sampling* sp, const int32_t* accepted, const float* pmax, const uint32_t* ptau,
+                       const float* qmax, const uint32_t* qtau, const uint64_t* pnuc, const uint64_t* qnuc,
+                       const uint64_t* gtot, int W, int rank, int32_t* tok_out, void* stream);
+
 /* Reference-semantics greedy verify on device pointers (see
  * sve2_speculative_verify_f32 above). */
 int specdec_compat_verify(const float* logits, const int32_t* drafts, const int32_t* lens, int V, int max_draft,

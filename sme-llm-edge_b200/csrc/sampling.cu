@@ -1078,6 +1078,288 @@ __global__ void compat_count_kernel(const int32_t* __restrict__ best, const int3
     replacement[b] = mism ? best[(size_t)b * max_draft + cnt] : -1;
 }
 
+// -------------------------------------- vocabulary-sharded chain acceptance
+// Each rank holds columns [v0, v0 + Vs) of every logits row: target shard
+// [B][k+1][Vs], draft shard [B][k][Vs].  The kernels below compute shard
+// partials; the caller sums or gathers them across ranks between the steps
+// (maxima and arg-maxima merged in rank order, integer mass sums and
+// histograms summed, residual totals gathered), so every decision is the one
+// the single-GPU acceptance takes on the whole rows.
+
+// (1) row max / arg-max of the shard (global index, -1 for a row of NaN)
+__global__ void __launch_bounds__(kRowThreads) shard_row_max_kernel(const float* __restrict__ z, int Vs, int v0,
+                                                                    float* __restrict__ out_max,
+                                                                    int32_t* __restrict__ out_arg) {
+    __shared__ RowSmem sm;
+    float m;
+    int am;
+    cta_argmax(z + (size_t)blockIdx.x * Vs, Vs, sm, &m, &am);
+    if (threadIdx.x == 0) {
+        out_max[blockIdx.x] = m;
+        out_arg[blockIdx.x] = am < 0 ? -1 : am + v0;
+    }
+}
+
+// (2) the W ranks' partials ([W][rows]) merged in rank order
+__global__ void shard_merge_max_kernel(const float* __restrict__ gmax, const int32_t* __restrict__ garg, int W,
+                                       int rows, float* __restrict__ out_max, int32_t* __restrict__ out_arg) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    float v = -INFINITY;
+    int idx = -1;
+    for (int w = 0; w < W; ++w) argmax_merge(v, idx, gmax[(size_t)w * rows + r], garg[(size_t)w * rows + r]);
+    out_max[r] = v;
+    out_arg[r] = idx;
+}
+
+// (3) integer mass sum of the shard row at the global row max
+__global__ void __launch_bounds__(kRowThreads) shard_row_mass_kernel(const float* __restrict__ z, int Vs,
+                                                                     const float* __restrict__ gmax, float c,
+                                                                     unsigned long long* __restrict__ out_sum) {
+    __shared__ RowSmem sm;
+    const uint64_t s = cta_mass_sum(z + (size_t)blockIdx.x * Vs, Vs, gmax[blockIdx.x], c, sm);
+    if (threadIdx.x == 0) out_sum[blockIdx.x] = s;
+}
+
+// (4) mass-weighted histogram of key digit d (3 = top byte) over the shard
+// elements whose higher digits equal prefix's
+__global__ void __launch_bounds__(kRowThreads) shard_digit_hist_kernel(const float* __restrict__ z, int Vs,
+                                                                       const float* __restrict__ gmax, float c,
+                                                                       const uint32_t* __restrict__ prefix, int d,
+                                                                       unsigned long long* __restrict__ out_hist) {
+    __shared__ RowSmem sm;
+    extern __shared__ uint32_t whist_dyn[];  // kWarpHistWords words
+    const float* zr = z + (size_t)blockIdx.x * Vs;
+    const float m = gmax[blockIdx.x];
+    uint32_t* Hw = whist_dyn + (threadIdx.x >> 5) * 512;
+    for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist_dyn[i] = 0;
+    __syncthreads();
+    const int shift = 8 * d;
+    const uint32_t want = d == 3 ? 0u : prefix[blockIdx.x] >> (shift + 8);
+    for_each_row_value(zr, Vs, [&](float zj) {
+        const uint32_t key = logit_key(zj);
+        if (d == 3 || (key >> (shift + 8)) == want) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
+    });
+    merge_warp_hists(whist_dyn, sm);
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) out_hist[(size_t)blockIdx.x * 256 + b] = sm.hist[b];
+}
+
+// (5) per row (one warp): the digit of the summed histogram where the mass
+// from the top reaches thr = max(1, floor(sum * tp / 2^32)), as select_digit;
+// G carries the mass above, last the chosen bin's, prefix the digits so far
+__global__ void shard_select_digit_kernel(const unsigned long long* __restrict__ hist, int rows, int d,
+                                          const unsigned long long* __restrict__ gsum, uint64_t tp,
+                                          uint32_t* __restrict__ prefix, unsigned long long* __restrict__ G,
+                                          unsigned long long* __restrict__ last) {
+    const int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;  // whole warps
+    uint64_t thr = (uint64_t)(((u128)gsum[r] * tp) >> 32);
+    if (thr < 1) thr = 1;
+    const unsigned long long* h = hist + (size_t)r * 256;
+    uint64_t local = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) local += h[255 - 8 * lane - i];
+    uint64_t incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint64_t g0 = d == 3 ? 0ull : G[r];
+    const unsigned hit = __ballot_sync(0xffffffffu, g0 + incl >= thr);
+    const int f = hit ? (__ffs(hit) - 1) : 31;
+    if (lane == f) {
+        uint64_t cum = g0 + incl - local;
+        int chosen = 255 - 8 * f - 7;
+        for (int i = 0; i < 8; ++i) {
+            const int bin = 255 - 8 * f - i;
+            if (cum + h[bin] >= thr) {
+                chosen = bin;
+                break;
+            }
+            cum += h[bin];
+        }
+        G[r] = cum;
+        last[r] = h[chosen];
+        prefix[r] = (d == 3 ? 0u : prefix[r]) | ((uint32_t)chosen << (8 * d));
+    }
+}
+
+// (6) the nucleus masses of the drafted tokens in the shard that owns them (0 elsewhere)
+__global__ void shard_point_mass_kernel(const float* __restrict__ target, const float* __restrict__ draft,
+                                        const int32_t* __restrict__ drafts, int B, int k, int Vs, int v0, float c,
+                                        const float* __restrict__ pmax, const uint32_t* __restrict__ ptau,
+                                        const float* __restrict__ qmax, const uint32_t* __restrict__ qtau,
+                                        unsigned long long* __restrict__ ep, unsigned long long* __restrict__ eq) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= B * k) return;
+    const int b = t / k, i = t - b * k, x = drafts[t];
+    uint64_t a = 0, q = 0;
+    if (x >= v0 && x < v0 + Vs) {
+        const int prow = b * (k + 1) + i, qrow = t;
+        const float zp = target[(size_t)prow * Vs + (x - v0)], zq = draft[(size_t)qrow * Vs + (x - v0)];
+        a = logit_key(zp) < ptau[prow] ? 0u : mass_of(zp, pmax[prow], c);
+        q = logit_key(zq) < qtau[qrow] ? 0u : mass_of(zq, qmax[qrow], c);
+    }
+    ep[t] = a;
+    eq[t] = q;
+}
+
+// (7) the sequential min(1, p/q) tests (as accept_chain_kernel), one thread per sequence
+__global__ void shard_accept_test_kernel(const int32_t* __restrict__ drafts, int B, int k, bool greedy, uint64_t seed,
+                                         uint32_t step, const int32_t* __restrict__ parg,
+                                         const unsigned long long* __restrict__ pnuc,
+                                         const unsigned long long* __restrict__ qnuc,
+                                         const unsigned long long* __restrict__ ep,
+                                         const unsigned long long* __restrict__ eq, int32_t* __restrict__ a_out) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int32_t* D = drafts + (size_t)b * k;
+    int a = 0;
+    if (greedy) {
+        while (a < k && parg[b * (k + 1) + a] == D[a]) ++a;
+    } else {
+        while (a < k) {
+            const uint32_t u = uniform_u32(seed, step, (uint32_t)b, (uint32_t)a, U_ACCEPT);
+            const u128 lhs = (u128)u * eq[b * k + a] * pnuc[b * (k + 1) + a];
+            const u128 rhs = ((u128)ep[b * k + a] * qnuc[b * k + a]) << 32;
+            if (!(lhs < rhs)) break;
+            ++a;
+        }
+    }
+    a_out[b] = a;
+}
+
+struct ShardRows {
+    const float* target;
+    const float* draft;
+    int k, Vs, v0;
+    float c;
+    const float* pmax;
+    const uint32_t* ptau;
+    const float* qmax;
+    const uint32_t* qtau;
+    const unsigned long long* pnuc;
+    const unsigned long long* qnuc;
+};
+
+// (8) per sequence b with a = a_in[b]: the shard's residual total (a < k) and
+// nucleus total of target row a, as u128 halves out[b] = {R lo, R hi, P lo, P hi}
+__global__ void __launch_bounds__(kRowThreads) shard_draw_totals_kernel(ShardRows sr, const int32_t* __restrict__ a_in,
+                                                                        unsigned long long* __restrict__ out) {
+    __shared__ RowSmem sm;
+    const int b = blockIdx.x, a = a_in[b], k = sr.k;
+    const int prow = b * (k + 1) + a;
+    const float* zp = sr.target + (size_t)prow * sr.Vs;
+    const float pm = sr.pmax[prow];
+    const uint32_t pt = sr.ptau[prow];
+    const float c = sr.c;
+    auto pmass = [&](int j) -> u128 {
+        const float v = zp[j];
+        return logit_key(v) < pt ? (u128)0 : (u128)mass_of(v, pm, c);
+    };
+    u128 R = 0;
+    if (a < k) {
+        const int qrow = b * k + a;
+        const float* zq = sr.draft + (size_t)qrow * sr.Vs;
+        const float qm = sr.qmax[qrow];
+        const uint32_t qt = sr.qtau[qrow];
+        const uint64_t Np = sr.pnuc[prow], Nq = sr.qnuc[qrow];
+        auto resid = [&](int j) -> u128 {
+            const float w = zq[j];
+            const u128 x = pmass(j) * Nq;
+            const u128 y = (logit_key(w) < qt ? (u128)0 : (u128)mass_of(w, qm, c)) * Np;
+            return x > y ? x - y : (u128)0;
+        };
+        R = cta_cdf_chunks(0, sr.Vs, resid, sm);
+    }
+    const u128 P = cta_cdf_chunks(0, sr.Vs, pmass, sm);
+    if (threadIdx.x == 0) {
+        out[(size_t)b * 4 + 0] = (uint64_t)R;
+        out[(size_t)b * 4 + 1] = (uint64_t)(R >> 64);
+        out[(size_t)b * 4 + 2] = (uint64_t)P;
+        out[(size_t)b * 4 + 3] = (uint64_t)(P >> 64);
+    }
+}
+
+// (9) per sequence: the draw from the gathered totals ([W][B][4]).  The
+// residual when a < k and its total is nonzero, else target row a's nucleus;
+// the rank whose shard holds the target (ranks in vocabulary order) searches
+// it, the others write -1.
+__global__ void __launch_bounds__(kRowThreads) shard_draw_kernel(ShardRows sr, const int32_t* __restrict__ a_in,
+                                                                 const unsigned long long* __restrict__ gtot, int W,
+                                                                 int rank, int B, uint64_t seed, uint32_t step,
+                                                                 int32_t* __restrict__ tok_out) {
+    __shared__ RowSmem sm;
+    __shared__ int s_owner, s_mode;
+    __shared__ u128 s_local;
+    const int b = blockIdx.x, a = a_in[b], k = sr.k;
+    const int prow = b * (k + 1) + a;
+    if (threadIdx.x == 0) {
+        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)a, U_RESAMPLE);
+        auto tot = [&](int w, int which) -> u128 {
+            const unsigned long long* t = gtot + ((size_t)w * B + b) * 4 + 2 * which;
+            return ((u128)t[1] << 64) | t[0];
+        };
+        u128 R = 0;
+        for (int w = 0; w < W; ++w) R += tot(w, 0);
+        const int mode = (a < k && R != 0) ? 0 : 1;
+        u128 target;
+        if (mode == 0) {
+            const uint64_t rh = (uint64_t)(R >> 64), rl = (uint64_t)R;
+            target = (u128)u64 * rh + (u128)mulhi64(u64, rl);
+        } else {
+            target = (u128)mulhi64(u64, sr.pnuc[prow]);
+        }
+        int owner = -1;
+        u128 pre = 0, local = 0;
+        for (int w = 0; w < W && owner < 0; ++w) {
+            const u128 tw = tot(w, mode);
+            if (pre <= target && target < pre + tw) {
+                owner = w;
+                local = target - pre;
+            }
+            pre += tw;
+        }
+        s_owner = owner;
+        s_mode = mode;
+        s_local = local;
+    }
+    __syncthreads();
+    int tok = -1;
+    if (s_owner == rank) {
+        const float* zp = sr.target + (size_t)prow * sr.Vs;
+        const float pm = sr.pmax[prow];
+        const uint32_t pt = sr.ptau[prow];
+        const float c = sr.c;
+        auto pmass = [&](int j) -> u128 {
+            const float v = zp[j];
+            return logit_key(v) < pt ? (u128)0 : (u128)mass_of(v, pm, c);
+        };
+        int j;
+        if (s_mode == 0) {
+            const int qrow = b * k + a;
+            const float* zq = sr.draft + (size_t)qrow * sr.Vs;
+            const float qm = sr.qmax[qrow];
+            const uint32_t qt = sr.qtau[qrow];
+            const uint64_t Np = sr.pnuc[prow], Nq = sr.qnuc[qrow];
+            auto resid = [&](int jj) -> u128 {
+                const float w = zq[jj];
+                const u128 x = pmass(jj) * Nq;
+                const u128 y = (logit_key(w) < qt ? (u128)0 : (u128)mass_of(w, qm, c)) * Np;
+                return x > y ? x - y : (u128)0;
+            };
+            (void)cta_cdf_chunks(0, sr.Vs, resid, sm);
+            j = cta_cdf_find(0, sr.Vs, resid, s_local, sm);
+        } else {
+            (void)cta_cdf_chunks(0, sr.Vs, pmass, sm);
+            j = cta_cdf_find(0, sr.Vs, pmass, s_local, sm);
+        }
+        tok = j < 0 ? -1 : j + sr.v0;
+    }
+    if (threadIdx.x == 0) tok_out[b] = tok;
+}
+
 // ------------------------------------------------------------ host side
 float temp_coeff(float temperature) { return (float)(1.4426950408889634 / (double)temperature); }
 uint64_t top_p_q32(float top_p) {
@@ -1332,6 +1614,156 @@ extern "C" int specdec_sample_rows(const float* logits, int rows, int k, int V, 
         logits, k, V, greedy ? 0.0f : temp_coeff(sp->temperature), top_p_q32(sp->top_p), greedy, sp->seed, nullptr, sp->step,
         out, nullptr);
     SD_LAUNCH_CHECK("sample_rows_kernel");
+    return SPECDEC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary-sharded chain acceptance: the shard steps (see include/specdec.h).
+static int shard_check(int rows, int Vs, const char* what) {
+    if (rows < 0 || Vs <= 0 || Vs > kMaxVocab) {
+        set_error(std::string(what) + ": bad shape (shard width must be 1 .. 262144)");
+        return SPECDEC_EINVAL;
+    }
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_row_max(const float* z, int rows, int Vs, int v0, float* out_max, int32_t* out_arg,
+                                     void* stream) {
+    if (int rc = shard_check(rows, Vs, "shard_row_max")) return rc;
+    SD_CHECK(z && out_max && out_arg, SPECDEC_EINVAL, "shard_row_max: null argument");
+    if (rows == 0) return SPECDEC_OK;
+    shard_row_max_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(z, Vs, v0, out_max, out_arg);
+    SD_LAUNCH_CHECK("shard_row_max_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_merge_max(const float* gmax, const int32_t* garg, int W, int rows, float* out_max,
+                                       int32_t* out_arg, void* stream) {
+    SD_CHECK(gmax && garg && out_max && out_arg && W >= 1 && rows >= 0, SPECDEC_EINVAL, "shard_merge_max: bad argument");
+    if (rows == 0) return SPECDEC_OK;
+    shard_merge_max_kernel<<<(rows + 255) / 256, 256, 0, as_stream(stream)>>>(gmax, garg, W, rows, out_max, out_arg);
+    SD_LAUNCH_CHECK("shard_merge_max_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_row_mass(const float* z, int rows, int Vs, const float* gmax, float temperature,
+                                      uint64_t* out_sum, void* stream) {
+    if (int rc = shard_check(rows, Vs, "shard_row_mass")) return rc;
+    SD_CHECK(z && gmax && out_sum && temperature > 0.0f, SPECDEC_EINVAL, "shard_row_mass: bad argument");
+    if (rows == 0) return SPECDEC_OK;
+    shard_row_mass_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(
+        z, Vs, gmax, temp_coeff(temperature), reinterpret_cast<unsigned long long*>(out_sum));
+    SD_LAUNCH_CHECK("shard_row_mass_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_digit_hist(const float* z, int rows, int Vs, const float* gmax, float temperature,
+                                        const uint32_t* prefix, int digit, uint64_t* out_hist, void* stream) {
+    if (int rc = shard_check(rows, Vs, "shard_digit_hist")) return rc;
+    SD_CHECK(z && gmax && out_hist && temperature > 0.0f && digit >= 0 && digit <= 3 && (digit == 3 || prefix),
+             SPECDEC_EINVAL, "shard_digit_hist: bad argument");
+    if (rows == 0) return SPECDEC_OK;
+    const size_t hs = kWarpHistWords * sizeof(uint32_t);
+    SD_CUDA(cudaFuncSetAttribute(shard_digit_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hs));
+    shard_digit_hist_kernel<<<rows, kRowThreads, hs, as_stream(stream)>>>(
+        z, Vs, gmax, temp_coeff(temperature), prefix, digit, reinterpret_cast<unsigned long long*>(out_hist));
+    SD_LAUNCH_CHECK("shard_digit_hist_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_select_digit(const uint64_t* hist, int rows, int digit, const uint64_t* gsum, float top_p,
+                                          uint32_t* prefix, uint64_t* G, uint64_t* last, void* stream) {
+    SD_CHECK(hist && gsum && prefix && G && last && rows >= 0 && digit >= 0 && digit <= 3, SPECDEC_EINVAL,
+             "shard_select_digit: bad argument");
+    if (rows == 0) return SPECDEC_OK;
+    shard_select_digit_kernel<<<(rows + 7) / 8, 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const unsigned long long*>(hist), rows, digit,
+        reinterpret_cast<const unsigned long long*>(gsum), top_p_q32(top_p), prefix,
+        reinterpret_cast<unsigned long long*>(G), reinterpret_cast<unsigned long long*>(last));
+    SD_LAUNCH_CHECK("shard_select_digit_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_point_mass(const float* target, const float* draft, const int32_t* drafts, int B, int k,
+                                        int Vs, int v0, float temperature, const float* pmax, const uint32_t* ptau,
+                                        const float* qmax, const uint32_t* qtau, uint64_t* ep, uint64_t* eq,
+                                        void* stream) {
+    if (int rc = shard_check(B, Vs, "shard_point_mass")) return rc;
+    SD_CHECK(target && draft && drafts && pmax && ptau && qmax && qtau && ep && eq && k >= 1 && temperature > 0.0f,
+             SPECDEC_EINVAL, "shard_point_mass: bad argument");
+    if (B == 0) return SPECDEC_OK;
+    shard_point_mass_kernel<<<(B * k + 255) / 256, 256, 0, as_stream(stream)>>>(
+        target, draft, drafts, B, k, Vs, v0, temp_coeff(temperature), pmax, ptau, qmax, qtau,
+        reinterpret_cast<unsigned long long*>(ep), reinterpret_cast<unsigned long long*>(eq));
+    SD_LAUNCH_CHECK("shard_point_mass_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_accept_test(const int32_t* drafts, int B, int k, const specdec_sampling* sp,
+                                         const int32_t* parg, const uint64_t* pnuc, const uint64_t* qnuc,
+                                         const uint64_t* ep, const uint64_t* eq, int32_t* accepted, void* stream) {
+    SD_CHECK(drafts && sp && parg && accepted && B >= 0 && k >= 1, SPECDEC_EINVAL, "shard_accept_test: bad argument");
+    const bool greedy = !(sp->temperature > 0.0f);
+    SD_CHECK(greedy || (pnuc && qnuc && ep && eq), SPECDEC_EINVAL, "shard_accept_test: statistics required");
+    if (B == 0) return SPECDEC_OK;
+    shard_accept_test_kernel<<<(B + 127) / 128, 128, 0, as_stream(stream)>>>(
+        drafts, B, k, greedy, sp->seed, sp->step, parg, reinterpret_cast<const unsigned long long*>(pnuc),
+        reinterpret_cast<const unsigned long long*>(qnuc), reinterpret_cast<const unsigned long long*>(ep),
+        reinterpret_cast<const unsigned long long*>(eq), accepted);
+    SD_LAUNCH_CHECK("shard_accept_test_kernel");
+    return SPECDEC_OK;
+}
+
+static ShardRows shard_rows(const float* target, const float* draft, int k, int Vs, int v0, float temperature,
+                            const float* pmax, const uint32_t* ptau, const float* qmax, const uint32_t* qtau,
+                            const uint64_t* pnuc, const uint64_t* qnuc) {
+    ShardRows sr;
+    sr.target = target;
+    sr.draft = draft;
+    sr.k = k;
+    sr.Vs = Vs;
+    sr.v0 = v0;
+    sr.c = temp_coeff(temperature);
+    sr.pmax = pmax;
+    sr.ptau = ptau;
+    sr.qmax = qmax;
+    sr.qtau = qtau;
+    sr.pnuc = reinterpret_cast<const unsigned long long*>(pnuc);
+    sr.qnuc = reinterpret_cast<const unsigned long long*>(qnuc);
+    return sr;
+}
+
+extern "C" int specdec_shard_draw_totals(const float* target, const float* draft, int B, int k, int Vs,
+                                         float temperature, const int32_t* accepted, const float* pmax,
+                                         const uint32_t* ptau, const float* qmax, const uint32_t* qtau,
+                                         const uint64_t* pnuc, const uint64_t* qnuc, uint64_t* out_tot,
+                                         void* stream) {
+    if (int rc = shard_check(B, Vs, "shard_draw_totals")) return rc;
+    SD_CHECK(target && draft && accepted && pmax && ptau && qmax && qtau && pnuc && qnuc && out_tot && k >= 1 &&
+                 temperature > 0.0f,
+             SPECDEC_EINVAL, "shard_draw_totals: bad argument");
+    if (B == 0) return SPECDEC_OK;
+    shard_draw_totals_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
+        shard_rows(target, draft, k, Vs, 0, temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted,
+        reinterpret_cast<unsigned long long*>(out_tot));
+    SD_LAUNCH_CHECK("shard_draw_totals_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_draw(const float* target, const float* draft, int B, int k, int Vs, int v0,
+                                  const specdec_sampling* sp, const int32_t* accepted, const float* pmax,
+                                  const uint32_t* ptau, const float* qmax, const uint32_t* qtau, const uint64_t* pnuc,
+                                  const uint64_t* qnuc, const uint64_t* gtot, int W, int rank, int32_t* tok_out,
+                                  void* stream) {
+    if (int rc = shard_check(B, Vs, "shard_draw")) return rc;
+    SD_CHECK(target && draft && sp && accepted && pmax && ptau && qmax && qtau && pnuc && qnuc && gtot && tok_out &&
+                 k >= 1 && W >= 1 && rank >= 0 && rank < W && sp->temperature > 0.0f,
+             SPECDEC_EINVAL, "shard_draw: bad argument");
+    if (B == 0) return SPECDEC_OK;
+    shard_draw_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
+        shard_rows(target, draft, k, Vs, v0, sp->temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted,
+        reinterpret_cast<const unsigned long long*>(gtot), W, rank, B, sp->seed, sp->step, tok_out);
+    SD_LAUNCH_CHECK("shard_draw_kernel");
     return SPECDEC_OK;
 }
 

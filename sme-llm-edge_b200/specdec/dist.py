@@ -47,3 +47,169 @@ def step_throughput(dist, ms: float, tokens: float, device: str = "cpu") -> dict
     ms_max = reduce_max(dist, ms, device)
     tok = reduce_sum(dist, tokens, device)
     return {"ms_max": ms_max, "tokens": tok, "value": tok / (ms_max / 1e3) if ms_max > 0 else 0.0}
+
+
+# ----------------------------------------------------------------------
+# Vocabulary-sharded chain acceptance
+# ----------------------------------------------------------------------
+class TorchComm:
+    """Collectives of a torch.distributed process group (NCCL for CUDA tensors)."""
+
+    def __init__(self, dist, group=None):
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, t):
+        import torch
+
+        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        self.dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out
+
+    def all_reduce_sum(self, t):
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def all_reduce_max(self, t):
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group)
+        return t
+
+
+class ThreadComm:
+    """The same collectives among W threads of one process (W virtual ranks
+    on one GPU, all on one CUDA stream): each rank deposits its tensor, the
+    threads meet at a barrier, and every rank reads all deposits."""
+
+    def __init__(self, world: int):
+        import threading
+
+        self.world = world
+        self.barrier = threading.Barrier(world)
+        self.slots = [None] * world
+
+    def rank_view(self, rank: int):
+        comm = self
+
+        class _View:
+            world = comm.world
+
+            def __init__(self):
+                self.rank = rank
+
+            def _exchange(self, t):
+                import torch
+
+                comm.slots[self.rank] = t.clone()
+                comm.barrier.wait()
+                out = torch.stack(list(comm.slots))
+                comm.barrier.wait()
+                return out
+
+            def all_gather(self, t):
+                return self._exchange(t)
+
+            def all_reduce_sum(self, t):
+                t.copy_(self._exchange(t).sum(0))
+                return t
+
+            def all_reduce_max(self, t):
+                t.copy_(self._exchange(t).max(0).values)
+                return t
+
+        return _View()
+
+
+def vocab_shard(V: int, world: int, rank: int) -> tuple[int, int]:
+    """Vocabulary columns [v0, v0 + Vs) of `rank`, in rank order (as shard_range)."""
+    lo, hi = shard_range(V, world, rank)
+    return lo, hi - lo
+
+
+def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling, comm):
+    """Chain acceptance with the vocabulary split across ranks.
+
+    target: this rank's columns [v0, v0 + Vs) of the target logits, fp32
+    [B, k+1, Vs] on its GPU; draft: [B, k, Vs] (unused when greedy); drafts:
+    the drafted global token ids [B, k] int32.  `comm` provides all_gather /
+    all_reduce_sum / all_reduce_max over the ranks (ranks in vocabulary
+    order).  Returns (accepted [B] int32, out_tokens [B, k+1] int32) on the
+    device, the same on every rank and equal to specdec_accept_chain on the
+    whole rows.  The steps and what crosses ranks between them are listed
+    with the specdec_shard_* functions in include/specdec.h."""
+    import ctypes as C
+
+    import torch
+
+    import specdec as S
+
+    L = S.lib()
+    dev = target.device
+    B, Vs = int(target.shape[0]), int(target.shape[2])
+    rows_p, rows_q = B * (k + 1), B * k
+    st = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    W, rank = comm.world, comm.rank
+    T, tp = float(sampling.temperature), float(sampling.top_p)
+    greedy = not (T > 0.0)
+    target = target.contiguous()
+    drafts = drafts.to(device=dev, dtype=torch.int32).contiguous()
+
+    def row_max(z, rows):
+        m = torch.empty(rows, dtype=torch.float32, device=dev)
+        a = torch.empty(rows, dtype=torch.int32, device=dev)
+        S.check(L.specdec_shard_row_max(p(z), rows, Vs, v0, p(m), p(a), st))
+        gm, ga = comm.all_gather(m), comm.all_gather(a)
+        S.check(L.specdec_shard_merge_max(p(gm), p(ga), W, rows, p(m), p(a), st))
+        return m, a
+
+    def nucleus(z, rows, mx):
+        s = torch.empty(rows, dtype=torch.int64, device=dev)
+        S.check(L.specdec_shard_row_mass(p(z), rows, Vs, p(mx), T, p(s), st))
+        comm.all_reduce_sum(s)
+        if not tp < 1.0:
+            return torch.zeros(rows, dtype=torch.int32, device=dev), s
+        prefix = torch.zeros(rows, dtype=torch.int32, device=dev)
+        G = torch.zeros(rows, dtype=torch.int64, device=dev)
+        last = torch.zeros(rows, dtype=torch.int64, device=dev)
+        hist = torch.empty((rows, 256), dtype=torch.int64, device=dev)
+        for d in (3, 2, 1, 0):
+            S.check(L.specdec_shard_digit_hist(p(z), rows, Vs, p(mx), T, p(prefix), d, p(hist), st))
+            comm.all_reduce_sum(hist)
+            S.check(L.specdec_shard_select_digit(p(hist), rows, d, p(s), tp, p(prefix), p(G), p(last), st))
+        return prefix, G + last
+
+    pmax, parg = row_max(target, rows_p)
+    acc = torch.empty(B, dtype=torch.int32, device=dev)
+    if greedy:
+        S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), None, None, None, None,
+                                            p(acc), st))
+        tok = parg.view(B, k + 1).gather(1, acc.long()[:, None])[:, 0]
+    else:
+        draft = draft.contiguous()
+        qmax, _ = row_max(draft, rows_q)
+        ptau, pnuc = nucleus(target, rows_p, pmax)
+        qtau, qnuc = nucleus(draft, rows_q, qmax)
+        ep = torch.empty(rows_q, dtype=torch.int64, device=dev)
+        eq = torch.empty(rows_q, dtype=torch.int64, device=dev)
+        S.check(L.specdec_shard_point_mass(p(target), p(draft), p(drafts), B, k, Vs, v0, T, p(pmax), p(ptau),
+                                           p(qmax), p(qtau), p(ep), p(eq), st))
+        comm.all_reduce_sum(ep)
+        comm.all_reduce_sum(eq)
+        S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), p(pnuc), p(qnuc), p(ep),
+                                            p(eq), p(acc), st))
+        tot = torch.empty((B, 4), dtype=torch.int64, device=dev)
+        S.check(L.specdec_shard_draw_totals(p(target), p(draft), B, k, Vs, T, p(acc), p(pmax), p(ptau), p(qmax),
+                                            p(qtau), p(pnuc), p(qnuc), p(tot), st))
+        gtot = comm.all_gather(tot)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
+        S.check(L.specdec_shard_draw(p(target), p(draft), B, k, Vs, v0, C.byref(sampling), p(acc), p(pmax), p(ptau),
+                                     p(qmax), p(qtau), p(pnuc), p(qnuc), p(gtot), W, rank, p(tok), st))
+        comm.all_reduce_max(tok)
+    idx = torch.arange(k + 1, device=dev)[None, :]
+    a = acc.long()[:, None]
+    ext = torch.cat([drafts, torch.full((B, 1), -1, dtype=torch.int32, device=dev)], 1)
+    out = torch.where(idx < a, ext, torch.full_like(ext, -1))
+    out = torch.where(idx == a, tok.to(torch.int32)[:, None], out)
+    return acc, out

@@ -411,3 +411,54 @@ def test_w4a16_shared_workspace_across_token_tiles(cuda_device):
                                            stream_ptr()))
         sync()
         np.testing.assert_allclose(Y.cpu().numpy(), O.w4a16_gemm(X16, packed, scales), rtol=2e-3, atol=2e-3)
+
+
+# ------------------------------------------------ vocabulary-sharded acceptance
+@pytest.mark.parametrize("W,B,k,V,T,tp", [(2, 6, 4, 3001, 0.8, 0.9), (3, 5, 3, 4099, 1.0, 1.0), (2, 4, 4, 2000, 0.0, 1.0),
+                                          (3, 7, 8, 32000, 0.7, 0.9)])
+def test_accept_chain_vocab_sharded_matches_oracle(cuda_device, W, B, k, V, T, tp):
+    """W ranks (threads sharing one GPU) each hold a contiguous vocabulary
+    slice of every logits row and exchange only per-row statistics; the
+    decisions equal the oracle's on the whole rows, on every rank.  Shards of
+    unequal width (V not a multiple of W); greedy, T > 0 without a nucleus,
+    and top-p 0.9."""
+    import threading
+
+    import torch
+
+    from specdec.dist import ThreadComm, accept_chain_vocab_sharded, vocab_shard
+
+    rng = np.random.default_rng(B * 1000 + V + W)
+    tgt = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.5).astype(np.float32)
+    drafts = O.sample_rows(dr.reshape(B * k, V), k, max(T, 1.0), tp, 9, 0).reshape(B, k)
+    if T == 0.0:
+        drafts = tgt[:, :k].argmax(-1).astype(np.int32)
+        drafts[0, 1] = (drafts[0, 1] + 1) % V
+    drafts[B - 1, 0] = V + 3  # out of range: rejected, the residual is the whole target row
+    acc_o, out_o = O.accept_chain(tgt, dr, drafts, T, tp, 1234, 7)
+    comm = ThreadComm(W)
+    results = [None] * W
+    errors = []
+
+    def rank_main(r):
+        try:
+            v0, vs = vocab_shard(V, W, r)
+            t = dev(np.ascontiguousarray(tgt[:, :, v0:v0 + vs]))
+            d = dev(np.ascontiguousarray(dr[:, :, v0:v0 + vs]))
+            sp = S.sampling(T, tp, 1234, 7)
+            acc, out = accept_chain_vocab_sharded(t, d, dev(drafts), k, v0, sp, comm.rank_view(r))
+            torch.cuda.synchronize()
+            results[r] = (acc.cpu().numpy().tolist(), out.cpu().numpy().tolist())
+        except Exception as e:  # noqa: BLE001 -- reported below
+            errors.append(repr(e))
+            comm.barrier.abort()
+
+    threads = [threading.Thread(target=rank_main, args=(r,)) for r in range(W)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=300)
+    assert not errors, errors
+    for r in range(W):
+        assert results[r] == (acc_o.tolist(), out_o.tolist()), f"rank {r}"
