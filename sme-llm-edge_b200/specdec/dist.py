@@ -64,9 +64,10 @@ class TorchComm:
     def all_gather(self, t):
         import torch
 
-        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-        self.dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
-        return out
+        # flat in, flat out (the form every backend accepts), then [world, *shape]
+        out = torch.empty(self.world * t.numel(), dtype=t.dtype, device=t.device)
+        self.dist.all_gather_into_tensor(out, t.contiguous().view(-1), group=self.group)
+        return out.view((self.world,) + tuple(t.shape))
 
     def all_reduce_sum(self, t):
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)

@@ -82,3 +82,76 @@ def test_two_rank_gloo_reductions():
         assert out["ms_max"] == 125.0
         assert out["tokens"] == 81.0
         assert out["value"] == pytest.approx(81.0 / 0.125)
+
+
+# ---- collectives of the vocabulary-sharded acceptance (host side)
+def _comm_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    from specdec.dist import TorchComm, vocab_shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        comm = TorchComm(dist)
+        g = comm.all_gather(torch.tensor([rank * 10, rank * 10 + 1], dtype=torch.int64))
+        s = comm.all_reduce_sum(torch.tensor([1 << 40, rank], dtype=torch.int64))
+        m = comm.all_reduce_max(torch.tensor([-1, rank], dtype=torch.int32))
+        q.put((rank, comm.world, comm.rank, g.tolist(), s.tolist(), m.tolist(), vocab_shard(10, world, rank)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_shard_collectives():
+    """TorchComm's all-gather (rank order), int64 sum (exact above 2^32) and
+    int32 max across two gloo ranks, and the vocabulary split they use."""
+    import torch.multiprocessing as mp
+
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_comm_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, (rank, w, crank, g, s, m, shard) in enumerate(res):
+        assert (rank, w, crank) == (r, 2, r)
+        assert g == [[0, 1], [10, 11]]
+        assert s == [2 << 40, 1]
+        assert m == [-1, 1]
+    assert [x[-1] for x in res] == [(0, 5), (5, 5)]
+
+
+def test_thread_comm_matches_the_collectives():
+    """ThreadComm (virtual ranks as threads, used to test the sharded
+    acceptance on one GPU) gathers in rank order and reduces like NCCL."""
+    import threading
+
+    import torch
+
+    from specdec.dist import ThreadComm
+
+    world = 3
+    comm = ThreadComm(world)
+    out = [None] * world
+
+    def run(r):
+        v = comm.rank_view(r)
+        g = v.all_gather(torch.tensor([r, -r], dtype=torch.int64))
+        s = v.all_reduce_sum(torch.tensor([r + 1], dtype=torch.int64))
+        m = v.all_reduce_max(torch.tensor([3 - r], dtype=torch.int32))
+        out[r] = (v.world, v.rank, g.tolist(), s.tolist(), m.tolist())
+
+    ths = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join(timeout=60)
+    for r in range(world):
+        assert out[r] == (3, r, [[0, 0], [1, -1], [2, -2]], [6], [3])
