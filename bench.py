@@ -555,9 +555,21 @@ def run_accept_sharded(args):
         g = torch.Generator(device="cuda").manual_seed(4 + 1000 * rank)
         tgt = torch.randn((B, k + 1, vs), device="cuda", generator=g) * 3
         dr = tgt[:, :k] + torch.randn((B, k, vs), device="cuda", generator=g) * 0.5
-        drafts = torch.randint(0, V, (B, k), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5),
-                               dtype=torch.int32)
         comm = TorchComm(torch.distributed)
+        # drafts = the draft rows' arg-max over the whole vocabulary (as the
+        # single-GPU micro-benchmark), from the ranks' shard maxima
+        L = S.lib()
+        import ctypes as C
+
+        pt = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        mx = torch.empty(B * k, dtype=torch.float32, device="cuda")
+        am = torch.empty(B * k, dtype=torch.int32, device="cuda")
+        drc = dr.contiguous()
+        S.check(L.specdec_shard_row_max(pt(drc), B * k, None, 0, vs, v0, pt(mx), pt(am), st))
+        gm, ga = comm.all_gather(mx), comm.all_gather(am)
+        S.check(L.specdec_shard_merge_max(pt(gm), pt(ga), world, B * k, pt(mx), pt(am), st))
+        drafts = am.view(B, k).contiguous()
         sp = S.sampling(T, tp, 4, 0)
         for _ in range(args.warmup):
             accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm)

@@ -164,15 +164,19 @@ int specdec_sample_rows(const float* logits, int rows, int k, int V, const specd
  *     Greedy: the emitted token is parg[b*(k+1) + accepted[b]].
  *  6. specdec_shard_draw_totals -> [B][4] u64; all-gather [W][B][4].
  *  7. specdec_shard_draw -> token or -1 per sequence; all-reduce (max).
- * Unsigned 64-bit values may travel as signed 64-bit: every sum stays below
- * 2^63.  Shard widths up to 262144; k >= 1. */
-int specdec_shard_row_max(const float* z, int rows, int Vs, int v0, float* out_max, int32_t* out_arg, void* stream);
+ * The per-row steps (row_max, row_mass, digit_hist) take the target rows
+ * (z, rows) and the draft rows (z2, rows2; NULL, 0 when greedy) in one call;
+ * their per-row inputs and outputs list the target rows first.  Unsigned
+ * 64-bit values may travel as signed 64-bit: every sum stays below 2^63.
+ * Shard widths up to 262144; k >= 1. */
+int specdec_shard_row_max(const float* z, int rows, const float* z2, int rows2, int Vs, int v0, float* out_max,
+                          int32_t* out_arg, void* stream);
 int specdec_shard_merge_max(const float* gmax, const int32_t* garg, int W, int rows, float* out_max, int32_t* out_arg,
                             void* stream);
-int specdec_shard_row_mass(const float* z, int rows, int Vs, const float* gmax, float temperature, uint64_t* out_sum,
-                           void* stream);
-int specdec_shard_digit_hist(const float* z, int rows, int Vs, const float* gmax, float temperature,
-                             const uint32_t* prefix, int digit, uint64_t* out_hist, void* stream);
+int specdec_shard_row_mass(const float* z, int rows, const float* z2, int rows2, int Vs, const float* gmax,
+                           float temperature, uint64_t* out_sum, void* stream);
+int specdec_shard_digit_hist(const float* z, int rows, const float* z2, int rows2, int Vs, const float* gmax,
+                             float temperature, const uint32_t* prefix, int digit, uint64_t* out_hist, void* stream);
 int specdec_shard_select_digit(const uint64_t* hist, int rows, int digit, const uint64_t* gsum, float top_p,
                                uint32_t* prefix, uint64_t* G, uint64_t* last, void* stream);
 int specdec_shard_point_mass(const float* target, const float* draft, const int32_t* drafts, int B, int k, int Vs,

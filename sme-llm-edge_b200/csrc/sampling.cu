@@ -1087,13 +1087,20 @@ __global__ void compat_count_kernel(const int32_t* __restrict__ best, const int3
 // the single-GPU acceptance takes on the whole rows.
 
 // (1) row max / arg-max of the shard (global index, -1 for a row of NaN)
-__global__ void __launch_bounds__(kRowThreads) shard_row_max_kernel(const float* __restrict__ z, int Vs, int v0,
+// Rows r < rows1 are rows of z1, the rest rows of z2 (one launch for the
+// target and draft shards); per-row outputs follow that order.
+__device__ __forceinline__ const float* shard_row(const float* z1, int rows1, const float* z2, int Vs, int r) {
+    return r < rows1 ? z1 + (size_t)r * Vs : z2 + (size_t)(r - rows1) * Vs;
+}
+
+__global__ void __launch_bounds__(kRowThreads) shard_row_max_kernel(const float* __restrict__ z1, int rows1,
+                                                                    const float* __restrict__ z2, int Vs, int v0,
                                                                     float* __restrict__ out_max,
                                                                     int32_t* __restrict__ out_arg) {
     __shared__ RowSmem sm;
     float m;
     int am;
-    cta_argmax(z + (size_t)blockIdx.x * Vs, Vs, sm, &m, &am);
+    cta_argmax(shard_row(z1, rows1, z2, Vs, blockIdx.x), Vs, sm, &m, &am);
     if (threadIdx.x == 0) {
         out_max[blockIdx.x] = m;
         out_arg[blockIdx.x] = am < 0 ? -1 : am + v0;
@@ -1113,23 +1120,25 @@ __global__ void shard_merge_max_kernel(const float* __restrict__ gmax, const int
 }
 
 // (3) integer mass sum of the shard row at the global row max
-__global__ void __launch_bounds__(kRowThreads) shard_row_mass_kernel(const float* __restrict__ z, int Vs,
+__global__ void __launch_bounds__(kRowThreads) shard_row_mass_kernel(const float* __restrict__ z1, int rows1,
+                                                                     const float* __restrict__ z2, int Vs,
                                                                      const float* __restrict__ gmax, float c,
                                                                      unsigned long long* __restrict__ out_sum) {
     __shared__ RowSmem sm;
-    const uint64_t s = cta_mass_sum(z + (size_t)blockIdx.x * Vs, Vs, gmax[blockIdx.x], c, sm);
+    const uint64_t s = cta_mass_sum(shard_row(z1, rows1, z2, Vs, blockIdx.x), Vs, gmax[blockIdx.x], c, sm);
     if (threadIdx.x == 0) out_sum[blockIdx.x] = s;
 }
 
 // (4) mass-weighted histogram of key digit d (3 = top byte) over the shard
 // elements whose higher digits equal prefix's
-__global__ void __launch_bounds__(kRowThreads) shard_digit_hist_kernel(const float* __restrict__ z, int Vs,
+__global__ void __launch_bounds__(kRowThreads) shard_digit_hist_kernel(const float* __restrict__ z1, int rows1,
+                                                                       const float* __restrict__ z2, int Vs,
                                                                        const float* __restrict__ gmax, float c,
                                                                        const uint32_t* __restrict__ prefix, int d,
                                                                        unsigned long long* __restrict__ out_hist) {
     __shared__ RowSmem sm;
     extern __shared__ uint32_t whist_dyn[];  // kWarpHistWords words
-    const float* zr = z + (size_t)blockIdx.x * Vs;
+    const float* zr = shard_row(z1, rows1, z2, Vs, blockIdx.x);
     const float m = gmax[blockIdx.x];
     uint32_t* Hw = whist_dyn + (threadIdx.x >> 5) * 512;
     for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist_dyn[i] = 0;
@@ -1627,12 +1636,13 @@ static int shard_check(int rows, int Vs, const char* what) {
     return SPECDEC_OK;
 }
 
-extern "C" int specdec_shard_row_max(const float* z, int rows, int Vs, int v0, float* out_max, int32_t* out_arg,
-                                     void* stream) {
+extern "C" int specdec_shard_row_max(const float* z, int rows, const float* z2, int rows2, int Vs, int v0,
+                                     float* out_max, int32_t* out_arg, void* stream) {
     if (int rc = shard_check(rows, Vs, "shard_row_max")) return rc;
-    SD_CHECK(z && out_max && out_arg, SPECDEC_EINVAL, "shard_row_max: null argument");
-    if (rows == 0) return SPECDEC_OK;
-    shard_row_max_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(z, Vs, v0, out_max, out_arg);
+    SD_CHECK(z && out_max && out_arg && rows2 >= 0 && (rows2 == 0 || z2), SPECDEC_EINVAL,
+             "shard_row_max: null argument");
+    if (rows + rows2 == 0) return SPECDEC_OK;
+    shard_row_max_kernel<<<rows + rows2, kRowThreads, 0, as_stream(stream)>>>(z, rows, z2, Vs, v0, out_max, out_arg);
     SD_LAUNCH_CHECK("shard_row_max_kernel");
     return SPECDEC_OK;
 }
@@ -1646,27 +1656,30 @@ extern "C" int specdec_shard_merge_max(const float* gmax, const int32_t* garg, i
     return SPECDEC_OK;
 }
 
-extern "C" int specdec_shard_row_mass(const float* z, int rows, int Vs, const float* gmax, float temperature,
-                                      uint64_t* out_sum, void* stream) {
+extern "C" int specdec_shard_row_mass(const float* z, int rows, const float* z2, int rows2, int Vs,
+                                      const float* gmax, float temperature, uint64_t* out_sum, void* stream) {
     if (int rc = shard_check(rows, Vs, "shard_row_mass")) return rc;
-    SD_CHECK(z && gmax && out_sum && temperature > 0.0f, SPECDEC_EINVAL, "shard_row_mass: bad argument");
-    if (rows == 0) return SPECDEC_OK;
-    shard_row_mass_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(
-        z, Vs, gmax, temp_coeff(temperature), reinterpret_cast<unsigned long long*>(out_sum));
+    SD_CHECK(z && gmax && out_sum && temperature > 0.0f && rows2 >= 0 && (rows2 == 0 || z2), SPECDEC_EINVAL,
+             "shard_row_mass: bad argument");
+    if (rows + rows2 == 0) return SPECDEC_OK;
+    shard_row_mass_kernel<<<rows + rows2, kRowThreads, 0, as_stream(stream)>>>(
+        z, rows, z2, Vs, gmax, temp_coeff(temperature), reinterpret_cast<unsigned long long*>(out_sum));
     SD_LAUNCH_CHECK("shard_row_mass_kernel");
     return SPECDEC_OK;
 }
 
-extern "C" int specdec_shard_digit_hist(const float* z, int rows, int Vs, const float* gmax, float temperature,
-                                        const uint32_t* prefix, int digit, uint64_t* out_hist, void* stream) {
+extern "C" int specdec_shard_digit_hist(const float* z, int rows, const float* z2, int rows2, int Vs,
+                                        const float* gmax, float temperature, const uint32_t* prefix, int digit,
+                                        uint64_t* out_hist, void* stream) {
     if (int rc = shard_check(rows, Vs, "shard_digit_hist")) return rc;
-    SD_CHECK(z && gmax && out_hist && temperature > 0.0f && digit >= 0 && digit <= 3 && (digit == 3 || prefix),
+    SD_CHECK(z && gmax && out_hist && temperature > 0.0f && digit >= 0 && digit <= 3 && (digit == 3 || prefix) &&
+                 rows2 >= 0 && (rows2 == 0 || z2),
              SPECDEC_EINVAL, "shard_digit_hist: bad argument");
-    if (rows == 0) return SPECDEC_OK;
+    if (rows + rows2 == 0) return SPECDEC_OK;
     const size_t hs = kWarpHistWords * sizeof(uint32_t);
     SD_CUDA(cudaFuncSetAttribute(shard_digit_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hs));
-    shard_digit_hist_kernel<<<rows, kRowThreads, hs, as_stream(stream)>>>(
-        z, Vs, gmax, temp_coeff(temperature), prefix, digit, reinterpret_cast<unsigned long long*>(out_hist));
+    shard_digit_hist_kernel<<<rows + rows2, kRowThreads, hs, as_stream(stream)>>>(
+        z, rows, z2, Vs, gmax, temp_coeff(temperature), prefix, digit, reinterpret_cast<unsigned long long*>(out_hist));
     SD_LAUNCH_CHECK("shard_digit_hist_kernel");
     return SPECDEC_OK;
 }

@@ -79,10 +79,10 @@ _SIGS = {
     "specdec_accept_tree": (I, [P, P, P, I, I, I, C.POINTER(Sampling), P, P, P, P, SZ, P]),
     "specdec_sample_rows": (I, [P, I, I, I, C.POINTER(Sampling), P, P, SZ, P]),
     "specdec_compat_verify": (I, [P, P, P, I, I, I, P, P, P]),
-    "specdec_shard_row_max": (I, [P, I, I, I, P, P, P]),
+    "specdec_shard_row_max": (I, [P, I, P, I, I, I, P, P, P]),
     "specdec_shard_merge_max": (I, [P, P, I, I, P, P, P]),
-    "specdec_shard_row_mass": (I, [P, I, I, P, F, P, P]),
-    "specdec_shard_digit_hist": (I, [P, I, I, P, F, P, I, P, P]),
+    "specdec_shard_row_mass": (I, [P, I, P, I, I, P, F, P, P]),
+    "specdec_shard_digit_hist": (I, [P, I, P, I, I, P, F, P, I, P, P]),
     "specdec_shard_select_digit": (I, [P, I, I, P, F, P, P, P, P]),
     "specdec_shard_point_mass": (I, [P, P, P, I, I, I, I, F, P, P, P, P, P, P, P]),
     "specdec_shard_accept_test": (I, [P, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P]),

@@ -157,47 +157,50 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
     target = target.contiguous()
     drafts = drafts.to(device=dev, dtype=torch.int32).contiguous()
 
-    def row_max(z, rows):
-        m = torch.empty(rows, dtype=torch.float32, device=dev)
-        a = torch.empty(rows, dtype=torch.int32, device=dev)
-        S.check(L.specdec_shard_row_max(p(z), rows, Vs, v0, p(m), p(a), st))
-        gm, ga = comm.all_gather(m), comm.all_gather(a)
-        S.check(L.specdec_shard_merge_max(p(gm), p(ga), W, rows, p(m), p(a), st))
-        return m, a
-
-    def nucleus(z, rows, mx):
-        s = torch.empty(rows, dtype=torch.int64, device=dev)
-        S.check(L.specdec_shard_row_mass(p(z), rows, Vs, p(mx), T, p(s), st))
-        comm.all_reduce_sum(s)
-        if not tp < 1.0:
-            return torch.zeros(rows, dtype=torch.int32, device=dev), s
-        prefix = torch.zeros(rows, dtype=torch.int32, device=dev)
-        G = torch.zeros(rows, dtype=torch.int64, device=dev)
-        last = torch.zeros(rows, dtype=torch.int64, device=dev)
-        hist = torch.empty((rows, 256), dtype=torch.int64, device=dev)
-        for d in (3, 2, 1, 0):
-            S.check(L.specdec_shard_digit_hist(p(z), rows, Vs, p(mx), T, p(prefix), d, p(hist), st))
-            comm.all_reduce_sum(hist)
-            S.check(L.specdec_shard_select_digit(p(hist), rows, d, p(s), tp, p(prefix), p(G), p(last), st))
-        return prefix, G + last
-
-    pmax, parg = row_max(target, rows_p)
+    # per-row steps run on the target rows and (when sampling) the draft rows
+    # together: rows [0, rows_p) target, [rows_p, rows_p + nq) draft
+    draft = draft.contiguous() if not greedy else None
+    nq = 0 if greedy else rows_q
+    rows = rows_p + nq
+    z2 = p(draft) if nq else None
+    mx = torch.empty(rows, dtype=torch.float32, device=dev)
+    am = torch.empty(rows, dtype=torch.int32, device=dev)
+    S.check(L.specdec_shard_row_max(p(target), rows_p, z2, nq, Vs, v0, p(mx), p(am), st))
+    gm, ga = comm.all_gather(mx), comm.all_gather(am)
+    S.check(L.specdec_shard_merge_max(p(gm), p(ga), W, rows, p(mx), p(am), st))
+    pmax, parg = mx[:rows_p], am[:rows_p]
     acc = torch.empty(B, dtype=torch.int32, device=dev)
     if greedy:
         S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), None, None, None, None,
                                             p(acc), st))
         tok = parg.view(B, k + 1).gather(1, acc.long()[:, None])[:, 0]
     else:
-        draft = draft.contiguous()
-        qmax, _ = row_max(draft, rows_q)
-        ptau, pnuc = nucleus(target, rows_p, pmax)
-        qtau, qnuc = nucleus(draft, rows_q, qmax)
+        sums = torch.empty(rows, dtype=torch.int64, device=dev)
+        S.check(L.specdec_shard_row_mass(p(target), rows_p, z2, nq, Vs, p(mx), T, p(sums), st))
+        comm.all_reduce_sum(sums)
+        if tp < 1.0:
+            tau = torch.zeros(rows, dtype=torch.int32, device=dev)
+            G = torch.zeros(rows, dtype=torch.int64, device=dev)
+            last = torch.zeros(rows, dtype=torch.int64, device=dev)
+            hist = torch.empty((rows, 256), dtype=torch.int64, device=dev)
+            for d in (3, 2, 1, 0):
+                S.check(L.specdec_shard_digit_hist(p(target), rows_p, z2, nq, Vs, p(mx), T, p(tau), d, p(hist), st))
+                comm.all_reduce_sum(hist)
+                S.check(L.specdec_shard_select_digit(p(hist), rows, d, p(sums), tp, p(tau), p(G), p(last), st))
+            nuc = G + last
+        else:
+            tau = torch.zeros(rows, dtype=torch.int32, device=dev)
+            nuc = sums
+        ptau, qtau = tau[:rows_p], tau[rows_p:]
+        pnuc, qnuc = nuc[:rows_p].contiguous(), nuc[rows_p:].contiguous()
+        qmax = mx[rows_p:]
         ep = torch.empty(rows_q, dtype=torch.int64, device=dev)
         eq = torch.empty(rows_q, dtype=torch.int64, device=dev)
         S.check(L.specdec_shard_point_mass(p(target), p(draft), p(drafts), B, k, Vs, v0, T, p(pmax), p(ptau),
                                            p(qmax), p(qtau), p(ep), p(eq), st))
-        comm.all_reduce_sum(ep)
-        comm.all_reduce_sum(eq)
+        pq = torch.stack([ep, eq])
+        comm.all_reduce_sum(pq)
+        ep, eq = pq[0].contiguous(), pq[1].contiguous()
         S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), p(pnuc), p(qnuc), p(ep),
                                             p(eq), p(acc), st))
         tot = torch.empty((B, 4), dtype=torch.int64, device=dev)
