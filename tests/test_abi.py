@@ -70,3 +70,28 @@ def test_gemm_plan_is_consistent():
     assert specdec.lib().specdec_w4a16_plan(160, 4096, 14336, 0, out) == 0 and out[1] == 1
     assert specdec.lib().specdec_w4a16_plan(160, 4096, 14336, 2, out) == 0 and out[1] == 2
     assert specdec.lib().specdec_w4a16_plan(0, 4096, 4096, 0, out) != 0
+
+
+def test_shard_steps_reject_bad_arguments_without_gpu():
+    """The vocabulary-sharded acceptance steps check shapes, ranks and
+    pointers before touching the GPU."""
+    import ctypes as C
+
+    import specdec
+
+    L = specdec.lib()
+    dummy = C.c_void_p(16)
+    sp = specdec.sampling(0.7, 0.9, 1, 0)
+    # shard width 0 and above the 262144 limit
+    assert L.specdec_shard_row_max(dummy, 4, None, 0, 0, 0, dummy, dummy, None) == specdec.EINVAL
+    assert "shard width" in specdec.last_error()
+    assert L.specdec_shard_row_mass(dummy, 4, None, 0, 262145, dummy, 0.7, dummy, None) == specdec.EINVAL
+    # draft rows announced without a pointer
+    assert L.specdec_shard_digit_hist(dummy, 4, None, 3, 128, dummy, 0.7, None, 3, dummy, None) == specdec.EINVAL
+    # digits other than 0..3, and a rank outside the world
+    assert L.specdec_shard_select_digit(dummy, 4, 4, dummy, 0.9, dummy, dummy, dummy, None) == specdec.EINVAL
+    assert L.specdec_shard_draw(dummy, dummy, 2, 3, 128, 0, C.byref(sp), dummy, dummy, dummy, dummy, dummy, dummy,
+                                dummy, dummy, 2, 2, dummy, None) == specdec.EINVAL
+    # the mass steps need a temperature
+    assert L.specdec_shard_point_mass(dummy, dummy, dummy, 2, 3, 128, 0, 0.0, dummy, dummy, dummy, dummy, dummy,
+                                      dummy, None) == specdec.EINVAL
