@@ -1,0 +1,95 @@
+"""CPU check that the vocabulary-sharded acceptance loses nothing: row
+statistics assembled from per-shard partials -- the rank-order arg-max
+merge, integer mass sums, the top-p threshold from summed per-shard digit
+histograms, and the draw by the rank whose shard holds the target -- equal
+the oracle's statistics and draw on the whole row.  These are the
+combinations specdec.dist.accept_chain_vocab_sharded performs between the
+specdec_shard_* steps; the device kernels themselves are checked against
+the oracle in the GPU tests."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from specdec.dist import vocab_shard
+
+
+def _key(z):
+    b = z.astype(np.float32).view(np.uint32).astype(np.uint64)
+    return np.where(b & 0x80000000, (~b) & 0xFFFFFFFF, b | 0x80000000).astype(np.uint64)
+
+
+def _masses(z, mx, temperature):
+    """Integer masses E_j at the row max mx (the oracle's own formula)."""
+    st = O.RowStats()
+    st.max = float(mx)
+    st.tau = 0
+    c = O.temp_coeff(temperature)
+    zc = np.ascontiguousarray(z, dtype=np.float32)
+    return np.array([O.lib().orc_row_mass(O.ptr(zc), C.byref(st), c, j) for j in range(zc.size)], dtype=np.uint64)
+
+
+def _select(hist, thr, G):
+    """Highest digit whose mass from the top reaches thr (select_digit)."""
+    cum = G
+    for b in range(255, -1, -1):
+        if cum + int(hist[b]) >= thr:
+            return b, cum, int(hist[b])
+        cum += int(hist[b])
+    raise AssertionError("threshold above the total")
+
+
+@pytest.mark.parametrize("W,V,T,tp,seed", [(2, 3001, 0.8, 0.9, 1), (3, 4099, 1.0, 0.5, 2), (5, 2000, 0.7, 0.95, 3),
+                                           (4, 777, 1.3, 1.0, 4)])
+def test_shard_partials_rebuild_the_row(W, V, T, tp, seed):
+    rng = np.random.default_rng(seed)
+    z = (rng.standard_normal(V) * 3).astype(np.float32)
+    z[rng.integers(0, V)] = z.max()  # a tie for the maximum: the lower index wins
+    whole = O.row_stats(z, T, tp)
+    shards = [vocab_shard(V, W, r) for r in range(W)]
+    # 1. max / arg-max merged in rank order (value desc, index asc)
+    best_v, best_i = -np.inf, -1
+    for v0, vs in shards:
+        j = int(np.argmax(z[v0:v0 + vs]))
+        v, i = float(z[v0 + j]), v0 + j
+        if best_i < 0 or v > best_v or (v == best_v and i < best_i):
+            best_v, best_i = v, i
+    assert best_v == whole.max and best_i == int(np.argmax(z))
+    # 2. integer mass sums
+    E = _masses(z, best_v, T)
+    sums = [int(E[v0:v0 + vs].sum()) for v0, vs in shards]
+    assert sum(sums) == whole.sum
+    # 3. top-p: digits 3..0 from summed shard histograms
+    key = _key(z)
+    if tp < 1.0:
+        total = sum(sums)
+        thr = max(1, (total * O.top_p_q32(tp)) >> 32)
+        prefix, G, last = 0, 0, 0
+        for d in (3, 2, 1, 0):
+            hist = np.zeros(256, dtype=np.uint64)
+            for v0, vs in shards:
+                ks, es = key[v0:v0 + vs], E[v0:v0 + vs]
+                sel = np.ones(vs, bool) if d == 3 else (ks >> np.uint64(8 * d + 8)) == (prefix >> (8 * d + 8))
+                np.add.at(hist, ((ks[sel] >> np.uint64(8 * d)) & np.uint64(255)).astype(np.int64), es[sel])
+            digit, G, last = _select(hist, thr, G)
+            prefix |= digit << (8 * d)
+        assert prefix == whole.tau and G + last == whole.nuc
+        tau, nuc = prefix, G + last
+    else:
+        tau, nuc = 0, sum(sums)
+    # 4. the nucleus draw by the owner of the target
+    En = np.where(key >= np.uint64(tau), E, np.uint64(0))
+    P = [int(En[v0:v0 + vs].sum()) for v0, vs in shards]
+    for u64 in [int(x) for x in rng.integers(0, 2**63, 8, dtype=np.int64)] + [2**64 - 1, 0]:
+        target = (u64 * nuc) >> 64
+        pre, tok = 0, -1
+        for (v0, vs), pw in zip(shards, P):
+            if pre <= target < pre + pw:
+                run = np.cumsum(En[v0:v0 + vs].astype(object))
+                tok = v0 + int(np.argmax(run > target - pre))
+                break
+            pre += pw
+        st = O.row_stats(z, T, tp)
+        zc = np.ascontiguousarray(z)
+        assert tok == O.lib().orc_sample_row(O.ptr(zc), V, O.temp_coeff(T), C.byref(st), u64), u64
