@@ -36,6 +36,12 @@ CONFIGS = {
     "tiny": dict(shape="tiny", batch=1, ctx=512, draft_len=3, temperature=1.0, seed=0, tree=None),
 }
 METRIC = "accepted tokens/s, 8B-shape W4A16 MTP spec-decode, 1/2/4/8 B200; verify µs"
+# DRAM bytes read + written by one launch, from the ncu captures summarised
+# under profiles/: (traffic, launch, algorithmic bytes of that launch)
+TRAFFIC = {
+    "lm_head": (334.4e6, "lm_head M=160 N=128256 K=4096", 271.3e6),
+    "attention": (277.6e6, "attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048", 269.1e6),
+}
 
 
 def load_peaks():
@@ -210,120 +216,123 @@ def workload_bytes_flops(shape, ctx, rows, weight_bytes):
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_models(cfg):
-    """Oracle models of the config with 1 and 3 decoder layers (weights synthesised
-    on the host; not timed).  Layers are identical in cost, so the full model's
-    step time is the 1-layer step plus (layers - 1) x the per-layer time, the
-    latter measured as the 3-layer minus the 1-layer verify forward."""
-    import oracle as O
-    import specdec as S
+# The oracle port (C, OpenMP) on the host cores: the same batched step as the
+# GPU arm -- MTP draft chain, verify forward over the paged KV, acceptance --
+# timed on a sample of CPU_SAMPLE_SEQS of the batch's sequences per step.  The
+# CPU's work is linear in the sequences (no weight reuse across rows in the
+# oracle's contraction), so tokens / time of the sample is the batch's rate.
+CPU_SAMPLE_SEQS = 4
 
-    shape = S.MODEL_SHAPES[cfg["shape"]]
+
+def _model_shape(cfg):
+    from model_shapes import MODEL_SHAPES  # pure Python: loads no library
+
+    return MODEL_SHAPES[cfg["shape"]]
+
+
+def cpu_setup(cfg, rng):
+    """A 1-decoder-layer oracle model of the config and a paged KV of the
+    sample's sequences (weights synthesised, KV filled at random; not timed).
+    The other layers are identical in cost: their time is the per-layer time
+    measured here as the forward with one layer minus the forward with none."""
+    import oracle as O
+
+    shape = _model_shape(cfg)
     t0 = time.time()
-    ms = []
-    for L in (1, 3):
-        ocfg = dict(shape, layers=L, block_size=16, rms_eps=1e-5, rope_theta=10000.0)
-        ms.append(O.OracleModel(ocfg, seed=cfg["seed"], rope_max_pos=int(cfg["ctx"]) + 80))
-    return ms[0], ms[1], time.time() - t0
-
-
-def _cpu_inputs(cfg, layers, rng):
-    import oracle as O
-    import specdec as S
-
-    shape = S.MODEL_SHAPES[cfg["shape"]]
-    k = cfg["draft_len"] if not cfg["tree"] else 4
-    R, ctx = k + 1, int(cfg["ctx"])
+    ocfg = dict(shape, layers=1, block_size=16, rms_eps=1e-5, rope_theta=10000.0)
+    m = O.OracleModel(ocfg, seed=cfg["seed"], rope_max_pos=int(cfg["ctx"]) + 80)
+    k = cfg["draft_len"] or 4
+    R, ctx, n = k + 1, int(cfg["ctx"]), min(CPU_SAMPLE_SEQS, cfg["batch"])
     mbpr = (ctx + R + 15) // 16 + 1
-    kv = O.OracleKV(layers, mbpr, shape["n_kv_heads"], 16, shape["head_dim"])
+    kv = O.OracleKV(1, n * mbpr, shape["n_kv_heads"], 16, shape["head_dim"])
     kv.pool[:] = O.f16_bits(rng.uniform(-1, 1, kv.pool.shape).astype(np.float32))
-    tables = np.arange(mbpr, dtype=np.int32)[None, :]
-    pos = np.arange(ctx, ctx + R, dtype=np.int32)
-    mask = np.array([(1 << (r + 1)) - 1 for r in range(R)], np.uint64)
-    return kv, tables, pos, mask
-
-
-def cpu_layer_time(cfg, m1, m3, rng):
-    """Seconds one decoder layer adds to the verify forward (3-layer minus 1-layer)."""
-    import oracle as O
-
-    k = cfg["draft_len"] if not cfg["tree"] else 4
-    toks = rng.integers(0, 1000, k + 1).astype(np.int32)
+    st = dict(model=m, kv=kv, n=n, k=k, R=R, ctx=ctx, shape=shape,
+              tables=np.arange(n * mbpr, dtype=np.int32).reshape(n, mbpr),
+              ctxs=np.full(n, ctx, np.int32),
+              pos=np.tile(np.arange(ctx, ctx + R, dtype=np.int32), n),
+              mask=np.array([(1 << (r + 1)) - 1 for r in range(R)], np.uint64),
+              setup_s=time.time() - t0)
+    toks = rng.integers(0, shape["vocab"], n * R).astype(np.int32)
     t = []
-    for m, L in ((m1, 1), (m3, 3)):
-        kv, tables, pos, mask = _cpu_inputs(cfg, L, rng)
-        t0 = time.time()
-        O.forward(m, kv, tables, [int(cfg["ctx"])], toks, pos, pos, mask, 1, k + 1, want_hidden=False)
-        t.append(time.time() - t0)
-    return max(0.0, (t[1] - t[0]) / 2)
+    for nl in (0, 1):
+        t1 = time.time()
+        O.forward(m, kv, st["tables"], st["ctxs"], toks, st["pos"], st["pos"], st["mask"], n, R, n_layers=nl,
+                  want_hidden=False)
+        t.append(time.time() - t1)
+    st["t_layer"] = max(0.0, t[1] - t[0])
+    return st
 
 
-def cpu_step(cfg, m1, t_layer, setup_s, rng):
-    """One sequence-step of the oracle restatement on the host cores (OpenMP, all
-    threads): MTP draft chain, verify forward, acceptance on the 1-layer model,
-    timed, plus the other layers at the measured per-layer time."""
+def cpu_sample(cfg, st, rng, step):
+    """One timed sample: the batched step of st['n'] sequences on the 1-layer
+    model, plus (layers - 1) x the per-layer time.  Returns (tokens, seconds)."""
     import oracle as O
-    import specdec as S
 
-    shape = S.MODEL_SHAPES[cfg["shape"]]
-    k = cfg["draft_len"] if not cfg["tree"] else 4
-    R, ctx = k + 1, int(cfg["ctx"])
+    shape, n, k, R = st["shape"], st["n"], st["k"], st["R"]
     H, V = shape["hidden"], shape["vocab"]
-    kv, tables, pos, mask = _cpu_inputs(cfg, 1, rng)
-    h0 = rng.standard_normal((1, H)).astype(np.float32)
-    pend = int(rng.integers(0, V))
+    h0 = rng.standard_normal((n, H)).astype(np.float32)
+    pend = rng.integers(0, V, n).astype(np.int32)
+    T = cfg["temperature"]
     t1 = time.time()
-    dl, drafts, _ = O.draft_chain(m1, h0, k, cfg["temperature"], 1.0, cfg["seed"], 0)
-    toks = np.concatenate([[pend], drafts[0]]).astype(np.int32)
-    lg, _ = O.forward(m1, kv, tables, [ctx], toks, pos, pos, mask, 1, R, want_hidden=False)
-    acc, _ = O.accept_chain(lg.reshape(1, R, V), dl, drafts, cfg["temperature"], 1.0, cfg["seed"], 0)
-    t_step = (time.time() - t1) + (shape["layers"] - 1) * t_layer
-    tokens = int(acc[0]) + 1
-    return {"value": tokens / t_step, "unit": "accepted tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one sequence-step of the {cfg['shape']} model ({R} verify rows, ctx {ctx}, draft {k}): "
-                      f"draft chain, verify forward and acceptance timed on a 1-decoder-layer copy, plus "
-                      f"{shape['layers'] - 1} layers x {t_layer:.3f} s (3-layer minus 1-layer verify forward, "
-                      f"measured once); tokens/s = (accepted + 1) / that time; OpenMP threads = {os.cpu_count()}; "
-                      f"x86-64 scalar/auto-vectorised C, ARM SVE2/SME unavailable; weight synthesis "
-                      f"{setup_s:.1f}s not timed",
-            "t_step_s": round(t_step, 2)}
+    dl, drafts, _ = O.draft_chain(st["model"], h0, k, T, 1.0, cfg["seed"], step)
+    toks = np.concatenate([pend[:, None], drafts], axis=1).reshape(-1).astype(np.int32)
+    lg, _ = O.forward(st["model"], st["kv"], st["tables"], st["ctxs"], toks, st["pos"], st["pos"], st["mask"], n, R,
+                      want_hidden=False)
+    acc, _ = O.accept_chain(lg.reshape(n, R, V), dl, drafts, T, 1.0, cfg["seed"], step)
+    secs = (time.time() - t1) + (shape["layers"] - 1) * st["t_layer"]
+    return int(np.sum(acc + 1)), secs
 
 
-def cpu_baseline(cfg):
-    m1, m3, setup_s = cpu_models(cfg)
+def cpu_describe(cfg, st, samples):
+    shape = st["shape"]
+    return (f"{samples} sample(s) of {st['n']} of the batch's {cfg['batch']} sequences ({st['n'] * st['R']} verify "
+            f"rows, ctx {st['ctx']}, chain {st['k']}, T {cfg['temperature']}): MTP draft chain, verify forward and "
+            f"acceptance on a 1-decoder-layer copy, timed, plus {shape['layers'] - 1} layers x "
+            f"{st['t_layer']:.3f} s (forward with one layer minus forward with none, measured once); rate = "
+            f"sum(accepted + 1) / time, linear in the sequences; OpenMP threads = {os.cpu_count()}; "
+            f"x86-64 scalar/auto-vectorised C, ARM SVE2/SME unavailable; weight synthesis {st['setup_s']:.1f}s "
+            f"not timed")
+
+
+def cpu_baseline(cfg, samples=2):
+    rng = np.random.default_rng(7)
+    st = cpu_setup(cfg, rng)
     try:
-        rng = np.random.default_rng(7)
-        t_layer = cpu_layer_time(cfg, m1, m3, rng)
-        return cpu_step(cfg, m1, t_layer, setup_s, rng)
+        tok = secs = 0.0
+        for i in range(samples):
+            a, b = cpu_sample(cfg, st, rng, i)
+            tok, secs = tok + a, secs + b
+        return {"value": tok / secs, "unit": "accepted tokens/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": cpu_describe(cfg, st, samples)}
     finally:
-        m1.close()
-        m3.close()
+        st["model"].close()
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     cfg = dict(CONFIGS[args.config])
-    m1, m3, setup_s = cpu_models(cfg)  # once; each step below times one sequence-step sample
     rng = np.random.default_rng(7)
-    vals, cb = [], None
+    st = cpu_setup(cfg, rng)  # once; each step below times one sample of the batched step
+    tok = secs = 0.0
     try:
-        t_layer = cpu_layer_time(cfg, m1, m3, rng)
         for i in range(args.warmup + args.steps):
-            cb = cpu_step(cfg, m1, t_layer, setup_s, rng)
+            a, b = cpu_sample(cfg, st, rng, i)
             if i >= args.warmup:
-                vals.append(cb["value"])
+                tok, secs = tok + a, secs + b
     finally:
-        m1.close()
-        m3.close()
-    v = float(np.mean(vals))
+        st["model"].close()
+    v = tok / secs
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "accepted tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{cfg['shape']} W4A16 chain spec-decode step (CPU oracle restatement)",
-                       "batch_per_gpu": cfg["batch"], "ctx": cfg["ctx"], "draft_len": cfg["draft_len"]},
-            "cpu_baseline": {"kind": cb["kind"], "cores": cb["cores"], "sample": cb["sample"], "value": v,
-                             "unit": "accepted tokens/s"},
+            "steps": args.steps, "warmup": args.warmup,
+            # the whole batch's step: the sample's time scaled by batch / sample sequences
+            "ms_per_step": round(secs / args.steps * cfg["batch"] / st["n"] * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{cfg['shape']} W4A16 MTP spec-decode step (CPU oracle restatement)",
+                       "batch_per_gpu": cfg["batch"], "global_batch": cfg["batch"], "ctx": cfg["ctx"],
+                       "draft": f"chain {cfg['draft_len'] or 4}", "temperature": cfg["temperature"]},
+            "cpu_baseline": {"kind": "port", "cores": os.cpu_count(), "sample": cpu_describe(cfg, st, args.steps),
+                             "value": v, "unit": "accepted tokens/s"},
             "e2e": {"value": v, "unit": "accepted tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -338,7 +347,7 @@ def run_gpu(args, world, rank, local, pg):
     cfg = dict(CONFIGS[args.config])
     shape = S.MODEL_SHAPES[cfg["shape"]]
     ctx = ctx_lengths(cfg, rank, world)
-    extra = (args.warmup + 2 * args.steps + 8) * 65
+    extra = (args.warmup + 3 * args.steps + 8) * 65
     eng = S.Engine(shape, batch=cfg["batch"], draft_len=cfg["draft_len"] or 4, max_ctx=int(ctx.max()) + extra,
                    temperature=cfg["temperature"], top_p=1.0, seed=cfg["seed"] + 1000 * rank,
                    tree_branching=cfg["tree"], tree_nodes=64 if cfg["tree"] else 0, use_graph=True, device=local)
@@ -392,7 +401,15 @@ def run_gpu(args, world, rank, local, pg):
            "d2h_bytes_per_step": 4 * B + 4 * B * R, "ms_per_step": round(e_ms / args.steps, 4),
            "tokens_per_step": round(e_tok / args.steps / max(1, world), 2)}
 
-    # per-kernel device time (eager steps with an event after every launch)
+    # verify forward (embedding .. lm_head) of graphed steps: the interval
+    # between the two event nodes every step records around it
+    vms = []
+    for _ in range(args.steps):
+        eng.step()
+        vms.append(eng.verify_ms())
+    verify_ms = float(np.mean(vms))
+    # per-kernel-category split (eager steps with an event after every launch;
+    # the intervals include each launch's latency, so they sum above a graphed step)
     prof = eng.profile(3)
     peaks, peak_src = load_peaks()
     ctx_now = eng.read("lens", np.int32, (B,)) - 0
@@ -400,32 +417,40 @@ def run_gpu(args, world, rank, local, pg):
     vbytes, kvbytes, flops_per_row = workload_bytes_flops(shape, ctx_now, R, wbytes)
     M = B * R
     gemm_flops = flops_per_row * M
-    verify_ms = prof["gemm_verify"] + prof["attention"] + prof["other"]
     gemm_tflops = gemm_flops / (prof["gemm_verify"] * 1e-3) / 1e12
     attn_gbs = kvbytes / (prof["attention"] * 1e-3) / 1e9
+    # tensor peak: the burst figure when the SM clock sampled under load sat at
+    # its maximum (the kernel ran unthrottled), the sustained one otherwise
+    at_max = bool(clk.get("sm_mhz") and clk.get("sm_max_mhz") and clk["sm_mhz"] >= 0.97 * clk["sm_max_mhz"])
+    tpeak, tsrc = ((peaks.get("bf16_tflops", 1590.0), "bf16 burst (SM clock at max under load)") if at_max
+                   else (peaks.get("bf16_tflops_sustained", 1400.0), "bf16 sustained (SM clock below max)"))
     if prof["gemm_verify"] >= prof["attention"]:
         roof = {"kernel": "w4a16_tc_kernel (verify projections + lm_head)", "bound": "tensor",
-                "achieved": round(gemm_tflops, 1), "peak": peaks.get("bf16_tflops_sustained", 1400.0),
-                "unit": "TFLOP/s", "peak_source": f"{peak_src} bf16 sustained"}
+                "achieved": round(gemm_tflops, 1), "peak": tpeak, "unit": "TFLOP/s",
+                "peak_source": f"{peak_src} {tsrc}"}
     else:
         roof = {"kernel": "attn_tc_kernel (verify attention)", "bound": "hbm", "achieved": round(attn_gbs, 1),
                 "peak": peaks.get("hbm_gbs", 6650.0), "unit": "GB/s", "peak_source": f"{peak_src} hbm copy"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    roof["timing"] = "per-category device time of eager steps (event after every launch)"
     # DRAM bytes (read + write) of one launch from the committed ncu captures
     # (profiles/), with that launch's algorithmic bytes beside them
     if roof["bound"] == "tensor":
-        roof.update(traffic=334.4e6, traffic_launch="lm_head M=160 N=128256 K=4096", traffic_algorithmic=271.3e6)
+        roof.update(traffic=TRAFFIC["lm_head"][0], traffic_launch=TRAFFIC["lm_head"][1],
+                    traffic_algorithmic=TRAFFIC["lm_head"][2])
     else:
-        roof.update(traffic=277.6e6, traffic_launch="attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048",
-                    traffic_algorithmic=269.1e6)
-    verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_bytes": vbytes,
+        roof.update(traffic=TRAFFIC["attention"][0], traffic_launch=TRAFFIC["attention"][1],
+                    traffic_algorithmic=TRAFFIC["attention"][2])
+    verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_us_source": "event nodes inside the graphed step",
+              "verify_bytes": vbytes,
               "verify_hbm_frac_of_measured": round(vbytes / (verify_ms * 1e-3) / 1e9 / peaks.get("hbm_gbs", 6650.0), 4),
               "verify_hbm_frac_of_8tbs": round(vbytes / (verify_ms * 1e-3) / 1e9 / 8000.0, 4),
+              "verify_tflops": round(gemm_flops / (verify_ms * 1e-3) / 1e12, 1),
               "gemm_verify_tflops": round(gemm_tflops, 1), "attention_gbs": round(attn_gbs, 1),
               "profile_ms_per_step": {k: round(v, 4) for k, v in prof.items()}}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu and cfg["shape"] != "14b" and not cfg["tree"]:
+    if rank == 0 and world == 1 and not args.no_cpu and not cfg["tree"]:
         try:
             cpu = cpu_baseline(cfg)
         except Exception as exc:  # the CPU leg must not hide the GPU number

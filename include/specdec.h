@@ -58,9 +58,20 @@ void sve2_speculative_verify_f32(const float* logits_ptr, const int32_t* draft_t
                                  uint32_t batch_size, int32_t* accepted_counts_ptr, int32_t* replacement_tokens_ptr);
 
 /* Replaces rust_sme_mtp_predict_f32, lib.rs:1792-1831 (declared at
- * server/mtp_heads.h:6-13): logits[k, j] = sum_d h[d] * W[k, d, j]. */
+ * server/mtp_heads.h:6-13): logits[k, j] = sum_d h[d] * W[k, d, j].
+ * The fp32 weights [K, H, V] stay resident on the current device between
+ * calls, keyed by host pointer, size and a sampled content fingerprint: a
+ * call with the same weights copies only the hidden state in and the logits
+ * out.  A caller that edits the weights in place (other than by loading a new
+ * checkpoint into the buffer) calls specdec_compat_release_weights first. */
 void rust_sme_mtp_predict_f32(const float* hidden_state_ptr, const float* weights_ptr, float* logits_out_ptr,
                               uint32_t hidden_dim, uint32_t vocab_size, uint32_t k_heads);
+/* Drops the MTP weights resident on the current device; *uploads (may be
+ * NULL) receives the number of weight uploads made so far on that device.
+ * No reference counterpart (the Rust kernels read host memory directly). */
+int specdec_compat_release_weights(uint64_t* uploads);
+/* Number of MTP weight uploads made so far on the current device. */
+int specdec_compat_weight_uploads(uint64_t* uploads);
 
 /* Replaces rust_sme_mtp_sample_f32, lib.rs:1840-1886 (server/mtp_heads.h:15-20):
  * per-head argmax with the SVE lane tie rule, default 0. */
@@ -337,6 +348,11 @@ int specdec_engine_info(specdec_engine* e, const char* what, int64_t* value);
  * [2] draft GEMMs, [3] sampling / acceptance, [4] other kernels, [5] whole
  * step, [6] verify GEMM launches per step.  ms_out holds 7 floats. */
 int specdec_engine_profile(specdec_engine* e, int steps, float* ms_out);
+/* Device time (ms) of the verify forward -- embedding, every layer and the
+ * lm_head -- of the last step that ran, measured by two events the step
+ * records around it (inside the CUDA graph when the step is graphed).
+ * Synchronises the engine stream. */
+int specdec_engine_verify_ms(specdec_engine* e, float* ms);
 
 #ifdef __cplusplus
 }

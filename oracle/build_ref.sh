@@ -13,11 +13,12 @@
 #                                        files call (C restatements of lib.rs).
 #
 # Outputs only into oracle/_ref/ (git-ignored).  Needs the reference tree at
-# $REF (default /root/reference); without it the script exits 0 and leaves any
-# previously built library in place.
+# $SME_LLM_EDGE_REF (default: a directory named "reference" beside the
+# repository root); without it the script exits 0 and leaves any previously
+# built library in place.
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${REF:-/root/reference}"
+REF="${SME_LLM_EDGE_REF:-$(cd "$HERE/../.." && pwd)/reference}"
 OUT="$HERE/_ref"
 if [ ! -d "$REF/server" ]; then
   echo "build_ref: reference tree not found at $REF; skipping" >&2
@@ -42,3 +43,21 @@ for f in orc_sample orc_model orc_kv; do
 done
 $CXX -shared -fopenmp -o "$OUT/libref.so" "$OUT"/obj/*.o -lm
 echo "build_ref: built $OUT/libref.so"
+
+# The reference's callers linked against the CUDA library instead of the Rust
+# kernels: server/speculative_decoder.cpp, server/mtp_heads.cpp,
+# server/paged_kv_cache.cpp (scratch copy above) and
+# server/flash_decoding_tracker.cpp, unmodified, plus oracle/ref_callers.cpp.
+# --no-undefined: every kernel symbol they call must come from
+# libspecdec_sm100.so (found at run time through the rpath, relative to
+# oracle/_ref/).
+SPECDEC_DIR="$(cd "$HERE/.." && pwd)/sme-llm-edge_b200/specdec"
+if [ -f "$SPECDEC_DIR/libspecdec_sm100.so" ]; then
+  mkdir -p "$OUT/obj_callers"
+  $CXX $CXXFLAGS -c "$REF/server/flash_decoding_tracker.cpp" -o "$OUT/obj_callers/flash_decoding_tracker.o"
+  $CXX $CXXFLAGS -I"$REF/server" -c "$HERE/ref_callers.cpp" -o "$OUT/obj_callers/ref_callers.o"
+  $CXX -shared -o "$OUT/libref_callers.so" "$OUT/obj_callers/ref_callers.o" "$OUT/obj_callers/flash_decoding_tracker.o" \
+    "$OUT/obj/speculative_decoder.o" "$OUT/obj/mtp_heads.o" "$OUT/obj/paged_kv_cache.o" \
+    -L"$SPECDEC_DIR" -lspecdec_sm100 -Wl,-rpath,'$ORIGIN/../../sme-llm-edge_b200/specdec' -Wl,--no-undefined -ldl
+  echo "build_ref: built $OUT/libref_callers.so (reference callers -> libspecdec_sm100.so)"
+fi

@@ -52,7 +52,7 @@ def build(clean: bool = False, verbose: bool = False) -> str:
         objs = list(ex.map(_compile, SOURCES))
     if not os.path.exists(OUT) or any(os.path.getmtime(o) > os.path.getmtime(OUT) for o in objs):
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-cudart", "static",
-               "-ccbin", "/usr/bin/g++", "-o", OUT, *objs]
+               "-ccbin", "/usr/bin/g++", "-Xlinker", "-soname=libspecdec_sm100.so", "-o", OUT, *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -8,7 +8,15 @@
 // the current device, runs a kernel and copies the outputs back.  The
 // functions return void like the reference; on failure the outputs hold the
 // reference wrapper's defaults and specdec_last_error() says why.
+//
+// Staging is per device: one stream and grow-only device buffers, reused by
+// every call (a call allocates only when its inputs outgrow the buffers), and
+// the MTP heads' fp32 weights stay resident on the device between calls,
+// keyed by host pointer, size and a content fingerprint, so that
+// MTPHeads::generate_drafts (server/mtp_heads.cpp:53-79) uploads only the
+// hidden state once its weights are cached.
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -112,19 +120,76 @@ __global__ void fd_reduce_kernel(const float* __restrict__ po, const float* __re
 __global__ void compat_argmax_kernel(const float* __restrict__ logits, const int32_t* __restrict__ lens, int V,
                                      int max_draft, int32_t* __restrict__ best);
 
-// RAII device buffer for the staging paths.
-struct DevBuf {
-    void* p = nullptr;
-    cudaError_t err = cudaSuccess;
-    explicit DevBuf(size_t bytes) { err = cudaMalloc(&p, bytes ? bytes : 1); }
-    ~DevBuf() {
-        if (p) cudaFree(p);
-    }
-    template <typename T>
-    T* as() const {
-        return reinterpret_cast<T*>(p);
-    }
+// Per-device staging for the host-pointer entry points.  Calls on one device
+// serialise on its mutex; every copy and kernel of a call is ordered on the
+// device's own stream, which the call synchronises before it returns.
+enum { kStageIn = 0, kStageAux, kStageAux2, kStageOut, kStageOut2, kStageOff, kStageTab, kStageLen, kStageBufs };
+struct CompatStage {
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    void* buf[kStageBufs] = {nullptr};
+    size_t cap[kStageBufs] = {0};
+    // MTP heads weights resident on the device
+    const float* w_host = nullptr;
+    size_t w_floats = 0;
+    uint64_t w_print = 0;
+    float* w_dev = nullptr;
+    uint64_t w_uploads = 0;
 };
+static std::mutex g_stage_mu;
+static CompatStage* g_stage[64] = {nullptr};
+
+static CompatStage* compat_stage() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_stage_mu);
+    if (!g_stage[dev]) {
+        CompatStage* st = new CompatStage();
+        if (cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            delete st;
+            return nullptr;
+        }
+        g_stage[dev] = st;
+    }
+    return g_stage[dev];
+}
+
+// Device buffer i of at least `bytes` (grown, never shrunk).
+static void* stage_buf(CompatStage* st, int i, size_t bytes) {
+    if (bytes == 0) bytes = 1;
+    if (st->cap[i] < bytes) {
+        if (st->buf[i]) cudaFree(st->buf[i]);
+        st->buf[i] = nullptr;
+        st->cap[i] = 0;
+        if (cudaMalloc(&st->buf[i], bytes) != cudaSuccess) {
+            cudaGetLastError();
+            st->buf[i] = nullptr;
+            return nullptr;
+        }
+        st->cap[i] = bytes;
+    }
+    return st->buf[i];
+}
+
+// FNV-1a over 64K evenly spaced floats and the first and last 1024 of the
+// weights: a cheap content check (a few hundred KB read per call) that sees a
+// new checkpoint loaded into the same buffer.  An in-place edit that changes
+// only elements the sample misses is not seen; such callers release the
+// resident copy with specdec_compat_release_weights().
+static uint64_t weights_print(const float* w, size_t n) {
+    uint64_t h = 1469598103934665603ull ^ (uint64_t)n;
+    auto mix = [&](size_t i) {
+        uint32_t v;
+        std::memcpy(&v, w + i, 4);
+        h = (h ^ v) * 1099511628211ull;
+    };
+    const size_t edge = n < 1024 ? n : 1024;
+    for (size_t i = 0; i < edge; ++i) mix(i);
+    for (size_t i = n - edge; i < n; ++i) mix(i);
+    const size_t samples = 65536, stride = n > samples ? n / samples : 1;
+    for (size_t i = 0; i < n; i += stride) mix(i);
+    return h;
+}
 
 }  // namespace specdec
 
@@ -140,28 +205,36 @@ extern "C" void sve2_speculative_verify_f32(const float* logits_ptr, const int32
         replacement_tokens_ptr[b] = -1;
     }
     if (!B || !D || !V || !logits_ptr || !draft_tokens_ptr || !draft_lengths_ptr) return;
-    DevBuf dl(4 * B * D * V), dd(4 * B * D), dn(4 * B), da(4 * B), dr(4 * B);
-    if (dl.err || dd.err || dn.err || da.err || dr.err) {
+    CompatStage* st = compat_stage();
+    if (!st) {
+        set_error("sve2_speculative_verify_f32: no CUDA device");
+        return;
+    }
+    std::lock_guard<std::mutex> lk(st->mu);
+    float* dl = static_cast<float*>(stage_buf(st, kStageIn, 4 * B * D * V));
+    int32_t* dd = static_cast<int32_t*>(stage_buf(st, kStageAux, 4 * B * D));
+    int32_t* dn = static_cast<int32_t*>(stage_buf(st, kStageAux2, 4 * B));
+    int32_t* dout = static_cast<int32_t*>(stage_buf(st, kStageOut, 8 * B));
+    if (!dl || !dd || !dn || !dout) {
         set_error("sve2_speculative_verify_f32: device allocation failed");
         return;
     }
-    if (cudaMemcpy(dl.p, logits_ptr, 4 * B * D * V, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dd.p, draft_tokens_ptr, 4 * B * D, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dn.p, draft_lengths_ptr, 4 * B, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaStream_t s = st->stream;
+    if (cudaMemcpyAsync(dl, logits_ptr, 4 * B * D * V, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(dd, draft_tokens_ptr, 4 * B * D, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(dn, draft_lengths_ptr, 4 * B, cudaMemcpyHostToDevice, s) != cudaSuccess) {
         set_error("sve2_speculative_verify_f32: copy to device failed");
         return;
     }
-    int rc = specdec_compat_verify(dl.as<float>(), dd.as<int32_t>(), dn.as<int32_t>(), (int)V, (int)D, (int)B,
-                                   da.as<int32_t>(), dr.as<int32_t>(), nullptr);
-    if (rc) return;
-    std::vector<int32_t> a(B), r(B);
-    if (cudaMemcpy(a.data(), da.p, 4 * B, cudaMemcpyDeviceToHost) != cudaSuccess ||
-        cudaMemcpy(r.data(), dr.p, 4 * B, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    if (specdec_compat_verify(dl, dd, dn, (int)V, (int)D, (int)B, dout, dout + B, s)) return;
+    std::vector<int32_t> h(2 * B);
+    if (cudaMemcpyAsync(h.data(), dout, 8 * B, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
         set_error("sve2_speculative_verify_f32: copy to host failed");
         return;
     }
-    std::memcpy(accepted_counts_ptr, a.data(), 4 * B);
-    std::memcpy(replacement_tokens_ptr, r.data(), 4 * B);
+    std::memcpy(accepted_counts_ptr, h.data(), 4 * B);
+    std::memcpy(replacement_tokens_ptr, h.data() + B, 4 * B);
 }
 
 extern "C" void rust_sme_mtp_predict_f32(const float* hidden_state_ptr, const float* weights_ptr,
@@ -169,20 +242,51 @@ extern "C" void rust_sme_mtp_predict_f32(const float* hidden_state_ptr, const fl
                                          uint32_t k_heads) {
     const size_t H = hidden_dim, V = vocab_size, K = k_heads;
     if (!H || !V || !K || !hidden_state_ptr || !weights_ptr || !logits_out_ptr) return;
-    DevBuf dh(4 * H), dw(4 * K * H * V), dout(4 * K * V);
-    if (dh.err || dw.err || dout.err) {
+    CompatStage* st = compat_stage();
+    if (!st) {
+        set_error("rust_sme_mtp_predict_f32: no CUDA device");
+        return;
+    }
+    std::lock_guard<std::mutex> lk(st->mu);
+    cudaStream_t s = st->stream;
+    const size_t wn = K * H * V;
+    const uint64_t print = weights_print(weights_ptr, wn);
+    if (st->w_host != weights_ptr || st->w_floats != wn || st->w_print != print || !st->w_dev) {
+        if (st->w_dev && st->w_floats != wn) {
+            cudaFree(st->w_dev);
+            st->w_dev = nullptr;
+        }
+        st->w_host = nullptr;
+        if (!st->w_dev && cudaMalloc(&st->w_dev, 4 * wn) != cudaSuccess) {
+            cudaGetLastError();
+            st->w_dev = nullptr;
+            set_error("rust_sme_mtp_predict_f32: device allocation failed");
+            return;
+        }
+        if (cudaMemcpyAsync(st->w_dev, weights_ptr, 4 * wn, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            set_error("rust_sme_mtp_predict_f32: copy to device failed");
+            return;
+        }
+        st->w_host = weights_ptr;
+        st->w_floats = wn;
+        st->w_print = print;
+        ++st->w_uploads;
+    }
+    float* dh = static_cast<float*>(stage_buf(st, kStageAux, 4 * H));
+    float* dout = static_cast<float*>(stage_buf(st, kStageOut, 4 * K * V));
+    if (!dh || !dout) {
         set_error("rust_sme_mtp_predict_f32: device allocation failed");
         return;
     }
-    if (cudaMemcpy(dh.p, hidden_state_ptr, 4 * H, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dw.p, weights_ptr, 4 * K * H * V, cudaMemcpyHostToDevice) != cudaSuccess) {
+    if (cudaMemcpyAsync(dh, hidden_state_ptr, 4 * H, cudaMemcpyHostToDevice, s) != cudaSuccess) {
         set_error("rust_sme_mtp_predict_f32: copy to device failed");
         return;
     }
-    mtp_predict_kernel<<<dim3((unsigned)((V + 255) / 256), (unsigned)K), 256>>>(dh.as<float>(), dw.as<float>(),
-                                                                               dout.as<float>(), (int)H, (int)V);
+    mtp_predict_kernel<<<dim3((unsigned)((V + 255) / 256), (unsigned)K), 256, 0, s>>>(dh, st->w_dev, dout, (int)H,
+                                                                                    (int)V);
     if (cudaGetLastError() != cudaSuccess ||
-        cudaMemcpy(logits_out_ptr, dout.p, 4 * K * V, cudaMemcpyDeviceToHost) != cudaSuccess)
+        cudaMemcpyAsync(logits_out_ptr, dout, 4 * K * V, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
         set_error("rust_sme_mtp_predict_f32: kernel or copy failed");
 }
 
@@ -190,19 +294,28 @@ extern "C" void rust_sme_mtp_sample_f32(const float* logits_ptr, int32_t* draft_
                                         uint32_t k_heads) {
     const size_t V = vocab_size, K = k_heads;
     if (!V || !K || !logits_ptr || !draft_tokens_out) return;
-    DevBuf dl(4 * K * V), dout(4 * K);
-    if (dl.err || dout.err) {
+    CompatStage* st = compat_stage();
+    if (!st) {
+        set_error("rust_sme_mtp_sample_f32: no CUDA device");
+        return;
+    }
+    std::lock_guard<std::mutex> lk(st->mu);
+    cudaStream_t s = st->stream;
+    float* dl = static_cast<float*>(stage_buf(st, kStageIn, 4 * K * V));
+    int32_t* dout = static_cast<int32_t*>(stage_buf(st, kStageOut2, 4 * K));
+    if (!dl || !dout) {
         set_error("rust_sme_mtp_sample_f32: device allocation failed");
         return;
     }
-    if (cudaMemcpy(dl.p, logits_ptr, 4 * K * V, cudaMemcpyHostToDevice) != cudaSuccess) {
+    if (cudaMemcpyAsync(dl, logits_ptr, 4 * K * V, cudaMemcpyHostToDevice, s) != cudaSuccess) {
         set_error("rust_sme_mtp_sample_f32: copy to device failed");
         return;
     }
     // each head is one row of a [K, 1, V] "draft" tensor with no length limit
-    compat_argmax_kernel<<<(unsigned)K, 256>>>(dl.as<float>(), nullptr, (int)V, 1, dout.as<int32_t>());
+    compat_argmax_kernel<<<(unsigned)K, 256, 0, s>>>(dl, nullptr, (int)V, 1, dout);
     if (cudaGetLastError() != cudaSuccess ||
-        cudaMemcpy(draft_tokens_out, dout.p, 4 * K, cudaMemcpyDeviceToHost) != cudaSuccess)
+        cudaMemcpyAsync(draft_tokens_out, dout, 4 * K, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
         set_error("rust_sme_mtp_sample_f32: kernel or copy failed");
 }
 
@@ -219,20 +332,33 @@ extern "C" void rust_sme_flashdecoding_chunk_f32(const float* q_ptr, const float
     const size_t L = chunk_len, D = head_dim;
     if (!D || !q_ptr || !k_chunk_ptr || !v_chunk_ptr || !partial_o_out || !partial_max_out || !partial_sum_exp_out)
         return;
-    DevBuf dq(4 * D), dk(4 * L * D), dv(4 * L * D), dout(4 * (D + 2));
-    if (dq.err || dk.err || dv.err || dout.err) {
+    CompatStage* st = compat_stage();
+    if (!st) {
+        set_error("rust_sme_flashdecoding_chunk_f32: no CUDA device");
+        return;
+    }
+    std::lock_guard<std::mutex> lk(st->mu);
+    cudaStream_t s = st->stream;
+    float* dq = static_cast<float*>(stage_buf(st, kStageAux, 4 * D));
+    float* dk = static_cast<float*>(stage_buf(st, kStageIn, 4 * L * D));
+    float* dv = static_cast<float*>(stage_buf(st, kStageAux2, 4 * L * D));
+    float* dout = static_cast<float*>(stage_buf(st, kStageOut, 4 * (D + 2)));
+    if (!dq || !dk || !dv || !dout) {
         set_error("rust_sme_flashdecoding_chunk_f32: device allocation failed");
         return;
     }
-    cudaMemcpy(dq.p, q_ptr, 4 * D, cudaMemcpyHostToDevice);
+    bool ok = cudaMemcpyAsync(dq, q_ptr, 4 * D, cudaMemcpyHostToDevice, s) == cudaSuccess;
     if (L) {
-        cudaMemcpy(dk.p, k_chunk_ptr, 4 * L * D, cudaMemcpyHostToDevice);
-        cudaMemcpy(dv.p, v_chunk_ptr, 4 * L * D, cudaMemcpyHostToDevice);
+        ok = ok && cudaMemcpyAsync(dk, k_chunk_ptr, 4 * L * D, cudaMemcpyHostToDevice, s) == cudaSuccess;
+        ok = ok && cudaMemcpyAsync(dv, v_chunk_ptr, 4 * L * D, cudaMemcpyHostToDevice, s) == cudaSuccess;
     }
-    fd_chunk_kernel<<<1, 128>>>(dq.as<float>(), dk.as<float>(), dv.as<float>(), (int)L, (int)D, softmax_scale,
-                                dout.as<float>(), dout.as<float>() + D, dout.as<float>() + D + 1);
+    if (ok) {
+        fd_chunk_kernel<<<1, 128, 0, s>>>(dq, dk, dv, (int)L, (int)D, softmax_scale, dout, dout + D, dout + D + 1);
+        ok = cudaGetLastError() == cudaSuccess;
+    }
     std::vector<float> h(D + 2);
-    if (cudaGetLastError() != cudaSuccess || cudaMemcpy(h.data(), dout.p, 4 * (D + 2), cudaMemcpyDeviceToHost)) {
+    if (!ok || cudaMemcpyAsync(h.data(), dout, 4 * (D + 2), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
         set_error("rust_sme_flashdecoding_chunk_f32: kernel or copy failed");
         return;
     }
@@ -244,21 +370,61 @@ extern "C" void rust_sme_flashdecoding_chunk_f32(const float* q_ptr, const float
 extern "C" void rust_sve2_flashdecoding_reduce_f32(const float* partial_o_ptr, const float* partial_max_ptr,
                                                    const float* partial_sum_exp_ptr, uint32_t num_chunks,
                                                    uint32_t head_dim, float* final_o_out) {
-    const size_t C = num_chunks, D = head_dim;
+    const size_t Cn = num_chunks, D = head_dim;
     if (!D || !partial_o_ptr || !partial_max_ptr || !partial_sum_exp_ptr || !final_o_out) return;
-    DevBuf dpo(4 * C * D), dpm(4 * C), dps(4 * C), dout(4 * D);
-    if (dpo.err || dpm.err || dps.err || dout.err) {
+    CompatStage* st = compat_stage();
+    if (!st) {
+        set_error("rust_sve2_flashdecoding_reduce_f32: no CUDA device");
+        return;
+    }
+    std::lock_guard<std::mutex> lk(st->mu);
+    cudaStream_t s = st->stream;
+    float* dpo = static_cast<float*>(stage_buf(st, kStageIn, 4 * Cn * D));
+    float* dpm = static_cast<float*>(stage_buf(st, kStageAux, 4 * Cn));
+    float* dps = static_cast<float*>(stage_buf(st, kStageAux2, 4 * Cn));
+    float* dout = static_cast<float*>(stage_buf(st, kStageOut, 4 * D));
+    if (!dpo || !dpm || !dps || !dout) {
         set_error("rust_sve2_flashdecoding_reduce_f32: device allocation failed");
         return;
     }
-    if (C) {
-        cudaMemcpy(dpo.p, partial_o_ptr, 4 * C * D, cudaMemcpyHostToDevice);
-        cudaMemcpy(dpm.p, partial_max_ptr, 4 * C, cudaMemcpyHostToDevice);
-        cudaMemcpy(dps.p, partial_sum_exp_ptr, 4 * C, cudaMemcpyHostToDevice);
+    bool ok = true;
+    if (Cn) {
+        ok = cudaMemcpyAsync(dpo, partial_o_ptr, 4 * Cn * D, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+             cudaMemcpyAsync(dpm, partial_max_ptr, 4 * Cn, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+             cudaMemcpyAsync(dps, partial_sum_exp_ptr, 4 * Cn, cudaMemcpyHostToDevice, s) == cudaSuccess;
     }
-    fd_reduce_kernel<<<1, 128>>>(dpo.as<float>(), dpm.as<float>(), dps.as<float>(), (int)C, (int)D, dout.as<float>());
-    if (cudaGetLastError() != cudaSuccess || cudaMemcpy(final_o_out, dout.p, 4 * D, cudaMemcpyDeviceToHost))
+    if (ok) {
+        fd_reduce_kernel<<<1, 128, 0, s>>>(dpo, dpm, dps, (int)Cn, (int)D, dout);
+        ok = cudaGetLastError() == cudaSuccess;
+    }
+    if (!ok || cudaMemcpyAsync(final_o_out, dout, 4 * D, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
         set_error("rust_sve2_flashdecoding_reduce_f32: kernel or copy failed");
+}
+
+// Drops the MTP weights kept resident on the current device (the next
+// rust_sme_mtp_predict_f32 uploads them again) and reports how many uploads
+// the cache has made so far.
+extern "C" int specdec_compat_release_weights(uint64_t* uploads) {
+    CompatStage* st = compat_stage();
+    SD_CHECK(st, SPECDEC_ECUDA, "compat_release_weights: no CUDA device");
+    std::lock_guard<std::mutex> lk(st->mu);
+    if (uploads) *uploads = st->w_uploads;
+    if (st->w_dev) cudaFree(st->w_dev);
+    st->w_dev = nullptr;
+    st->w_host = nullptr;
+    st->w_floats = 0;
+    st->w_print = 0;
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_compat_weight_uploads(uint64_t* uploads) {
+    SD_CHECK(uploads, SPECDEC_EINVAL, "compat_weight_uploads: null");
+    CompatStage* st = compat_stage();
+    SD_CHECK(st, SPECDEC_ECUDA, "compat_weight_uploads: no CUDA device");
+    std::lock_guard<std::mutex> lk(st->mu);
+    *uploads = st->w_uploads;
+    return SPECDEC_OK;
 }
 
 extern "C" int specdec_paged_attention_compat_f32(const float* q, const float* k_pool, const float* v_pool,
@@ -285,20 +451,29 @@ extern "C" int specdec_paged_attention_compat_f32(const float* q, const float* k
             done += tib;
         }
     }
-    DevBuf dq(4 * M * H), dk(4 * pool_floats), dv(4 * pool_floats), doff(4 * (M + 1)), dt(4 * (ntab ? ntab : 1)),
-        dl(4 * M), dout(4 * M * H);
-    SD_CHECK(!(dq.err || dk.err || dv.err || doff.err || dt.err || dl.err || dout.err), SPECDEC_ENOMEM,
+    CompatStage* st = compat_stage();
+    SD_CHECK(st, SPECDEC_ECUDA, "paged_attention_compat: no CUDA device");
+    std::lock_guard<std::mutex> lk(st->mu);
+    cudaStream_t s = st->stream;
+    float* dq = static_cast<float*>(stage_buf(st, kStageAux, 4 * M * H));
+    float* dk = static_cast<float*>(stage_buf(st, kStageIn, 4 * pool_floats));
+    float* dv = static_cast<float*>(stage_buf(st, kStageAux2, 4 * pool_floats));
+    int32_t* doff = static_cast<int32_t*>(stage_buf(st, kStageOff, 4 * (M + 1)));
+    int32_t* dt = static_cast<int32_t*>(stage_buf(st, kStageTab, 4 * (ntab ? ntab : 1)));
+    int32_t* dl = static_cast<int32_t*>(stage_buf(st, kStageLen, 4 * M));
+    float* dout = static_cast<float*>(stage_buf(st, kStageOut, 4 * M * H));
+    SD_CHECK(dq && dk && dv && doff && dt && dl && dout, SPECDEC_ENOMEM,
              "paged_attention_compat: device allocation failed");
-    SD_CUDA(cudaMemcpy(dq.p, q, 4 * M * H, cudaMemcpyHostToDevice));
-    SD_CUDA(cudaMemcpy(dk.p, k_pool, 4 * pool_floats, cudaMemcpyHostToDevice));
-    SD_CUDA(cudaMemcpy(dv.p, v_pool, 4 * pool_floats, cudaMemcpyHostToDevice));
-    SD_CUDA(cudaMemcpy(doff.p, table_off, 4 * (M + 1), cudaMemcpyHostToDevice));
-    if (ntab) SD_CUDA(cudaMemcpy(dt.p, tables, 4 * ntab, cudaMemcpyHostToDevice));
-    SD_CUDA(cudaMemcpy(dl.p, seq_lens, 4 * M, cudaMemcpyHostToDevice));
-    SD_CUDA(cudaMemcpy(dout.p, o, 4 * M * H, cudaMemcpyHostToDevice));
-    compat_paged_attention_kernel<<<M, 128>>>(dq.as<float>(), dk.as<float>(), dv.as<float>(), doff.as<int32_t>(),
-                                              dt.as<int32_t>(), dl.as<int32_t>(), dout.as<float>(), (int)H, block_size);
+    SD_CUDA(cudaMemcpyAsync(dq, q, 4 * M * H, cudaMemcpyHostToDevice, s));
+    SD_CUDA(cudaMemcpyAsync(dk, k_pool, 4 * pool_floats, cudaMemcpyHostToDevice, s));
+    SD_CUDA(cudaMemcpyAsync(dv, v_pool, 4 * pool_floats, cudaMemcpyHostToDevice, s));
+    SD_CUDA(cudaMemcpyAsync(doff, table_off, 4 * (M + 1), cudaMemcpyHostToDevice, s));
+    if (ntab) SD_CUDA(cudaMemcpyAsync(dt, tables, 4 * ntab, cudaMemcpyHostToDevice, s));
+    SD_CUDA(cudaMemcpyAsync(dl, seq_lens, 4 * M, cudaMemcpyHostToDevice, s));
+    SD_CUDA(cudaMemcpyAsync(dout, o, 4 * M * H, cudaMemcpyHostToDevice, s));
+    compat_paged_attention_kernel<<<M, 128, 0, s>>>(dq, dk, dv, doff, dt, dl, dout, (int)H, block_size);
     SD_LAUNCH_CHECK("compat_paged_attention_kernel");
-    SD_CUDA(cudaMemcpy(o, dout.p, 4 * M * H, cudaMemcpyDeviceToHost));
+    SD_CUDA(cudaMemcpyAsync(o, dout, 4 * M * H, cudaMemcpyDeviceToHost, s));
+    SD_CUDA(cudaStreamSynchronize(s));
     return SPECDEC_OK;
 }

@@ -520,6 +520,9 @@ struct specdec_engine {
     // event is that launch's device time (one stream, in-order execution)
     bool prof_on = false;
     int gemm_cat = 0;
+    // verify interval (embedding through the lm_head) of every step, recorded
+    // inside the step itself (event nodes of the captured graph)
+    cudaEvent_t verify_ev[2] = {nullptr, nullptr};
     std::vector<cudaEvent_t> prof_pool;
     std::vector<int> prof_cat;
     size_t prof_used = 0;
@@ -697,7 +700,9 @@ int record_step(specdec_engine* e) {
         build_chain_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->drafts, kvs.ctx, B, k, e->tokens,
                                                                    e->pos, e->slot);
         ENG_LAUNCH("build_chain_rows_kernel");
+        SD_CUDA(cudaEventRecord(e->verify_ev[0], s));
         ENG_TRY(forward(e, R, true));
+        SD_CUDA(cudaEventRecord(e->verify_ev[1], s));
         e->kernels_per_step += 2;
         ENG_TRY(launch_accept_chain_dev(e->logits, e->dlogits, e->drafts, B, k, V, sp.temperature, sp.top_p, sp.seed,
                                         e->step, e->acc, e->out_tokens, e->acc_ws, true, s));
@@ -718,7 +723,9 @@ int record_step(specdec_engine* e) {
                                                                   e->rank, kvs.ctx, B, R, e->tokens, e->node_tokens,
                                                                   e->pos, e->slot);
         ENG_LAUNCH("build_tree_rows_kernel");
+        SD_CUDA(cudaEventRecord(e->verify_ev[0], s));
         ENG_TRY(forward(e, R, true));
+        SD_CUDA(cudaEventRecord(e->verify_ev[1], s));
         ++e->kernels_per_step;
         ENG_TRY(launch_accept_tree_dev(e->logits, e->node_tokens, e->parent, B, R, V, sp.temperature, sp.top_p,
                                        sp.seed, e->step, e->acc, e->path, e->out_tokens, s));
@@ -743,6 +750,8 @@ int record_step(specdec_engine* e) {
 extern "C" int specdec_engine_destroy(specdec_engine* e) {
     if (!e) return SPECDEC_OK;
     for (cudaEvent_t ev : e->prof_pool) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : e->verify_ev)
+        if (ev) cudaEventDestroy(ev);
     if (e->gexec) cudaGraphExecDestroy(e->gexec);
     if (e->graph) cudaGraphDestroy(e->graph);
     if (e->kvm) specdec_kv_destroy(e->kvm);
@@ -772,6 +781,8 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
         return code;
     };
     if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(SPECDEC_ECUDA);
+    if (cudaEventCreate(&e->verify_ev[0]) != cudaSuccess || cudaEventCreate(&e->verify_ev[1]) != cudaSuccess)
+        return fail(SPECDEC_ECUDA);
     const int H = mc->hidden, F = mc->ffn, V = mc->vocab, hd = mc->head_dim, Hkv = mc->n_kv_heads;
     e->tree = rc->tree_nodes > 0;
     e->B = rc->batch;
@@ -1179,6 +1190,16 @@ extern "C" int specdec_engine_profile(specdec_engine* e, int steps, float* ms_ou
         acc[CAT_N + 1] += ngemm;
     }
     for (int i = 0; i < CAT_N + 2; ++i) ms_out[i] = (float)(acc[i] / steps);
+    return SPECDEC_OK;
+}
+
+// Device time of the verify forward (embedding through the lm_head) of the
+// last step that ran, graphed or eager: the interval between the two events
+// the step records around it.
+extern "C" int specdec_engine_verify_ms(specdec_engine* e, float* ms) {
+    SD_CHECK(e && ms, SPECDEC_EINVAL, "engine_verify_ms: bad argument");
+    SD_CUDA(cudaStreamSynchronize(e->stream));
+    SD_CUDA(cudaEventElapsedTime(ms, e->verify_ev[0], e->verify_ev[1]));
     return SPECDEC_OK;
 }
 

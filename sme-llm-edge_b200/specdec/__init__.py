@@ -69,6 +69,8 @@ _SIGS = {
     "sve2_speculative_verify_f32": (None, [P, P, P, U32, U32, U32, P, P]),
     "rust_sme_mtp_predict_f32": (None, [P, P, P, U32, U32, U32]),
     "rust_sme_mtp_sample_f32": (None, [P, P, U32, U32]),
+    "specdec_compat_release_weights": (I, [C.POINTER(U64)]),
+    "specdec_compat_weight_uploads": (I, [C.POINTER(U64)]),
     "sme_sm_prefetch_kv_blocks": (None, [P, P, U32]),
     "rust_sme_flashdecoding_chunk_f32": (None, [P, P, P, U32, U32, F, P, P, P]),
     "rust_sve2_flashdecoding_reduce_f32": (None, [P, P, P, U32, U32, P]),
@@ -124,6 +126,7 @@ _SIGS = {
     "specdec_engine_write": (I, [P, C.c_char_p, P, SZ]),
     "specdec_engine_info": (I, [P, C.c_char_p, C.POINTER(C.c_int64)]),
     "specdec_engine_profile": (I, [P, I, P]),
+    "specdec_engine_verify_ms": (I, [P, C.POINTER(F)]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(_lib, _name)
@@ -328,13 +331,7 @@ class PagedKVCache:
 # ======================================================================
 # Step engine
 # ======================================================================
-MODEL_SHAPES = {
-    "tiny": dict(hidden=512, layers=4, n_q_heads=8, n_kv_heads=2, head_dim=64, ffn=1376, vocab=32000, n_mtp_heads=3),
-    "llama3-8b": dict(hidden=4096, layers=32, n_q_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
-                      n_mtp_heads=3),
-    "14b": dict(hidden=5120, layers=48, n_q_heads=40, n_kv_heads=8, head_dim=128, ffn=13824, vocab=152064,
-                n_mtp_heads=3),
-}
+from model_shapes import MODEL_SHAPES  # noqa: E402  (sme-llm-edge_b200/model_shapes.py, pure Python)
 
 
 def model_config(shape: dict) -> ModelConfig:
@@ -425,6 +422,12 @@ class Engine:
         check(_lib.specdec_engine_profile(self._h, steps, _p(out)))
         keys = ("gemm_verify", "attention", "gemm_draft", "accept", "other", "step", "verify_gemm_launches")
         return {k: float(v) for k, v in zip(keys, out)}
+
+    def verify_ms(self) -> float:
+        """Device ms of the last step's verify forward (graph event nodes)."""
+        v = F(0.0)
+        check(_lib.specdec_engine_verify_ms(self._h, C.byref(v)))
+        return float(v.value)
 
     def write(self, what: str, arr):
         a = np.ascontiguousarray(arr)
