@@ -401,12 +401,9 @@ def run_gpu(args, world, rank, local, pg):
            "d2h_bytes_per_step": 4 * B + 4 * B * R, "ms_per_step": round(e_ms / args.steps, 4),
            "tokens_per_step": round(e_tok / args.steps / max(1, world), 2)}
 
-    # verify forward (embedding .. lm_head) of graphed steps: the interval
-    # between the two event nodes every step records around it
-    vms = []
-    for _ in range(args.steps):
-        eng.step()
-        vms.append(eng.verify_ms())
+    # verify forward (embedding .. lm_head) of graphed steps: global-timer
+    # stamps around it in a second graph of the same step
+    vms = [eng.step_verify_timed() for _ in range(args.steps + 1)][1:]
     verify_ms = float(np.mean(vms))
     # per-kernel-category split (eager steps with an event after every launch;
     # the intervals include each launch's latency, so they sum above a graphed step)
@@ -441,7 +438,7 @@ def run_gpu(args, world, rank, local, pg):
     else:
         roof.update(traffic=TRAFFIC["attention"][0], traffic_launch=TRAFFIC["attention"][1],
                     traffic_algorithmic=TRAFFIC["attention"][2])
-    verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_us_source": "event nodes inside the graphed step",
+    verify = {"verify_us": round(verify_ms * 1e3, 1), "verify_us_source": "global-timer stamps around the forward inside a graphed step",
               "verify_bytes": vbytes,
               "verify_hbm_frac_of_measured": round(vbytes / (verify_ms * 1e-3) / 1e9 / peaks.get("hbm_gbs", 6650.0), 4),
               "verify_hbm_frac_of_8tbs": round(vbytes / (verify_ms * 1e-3) / 1e9 / 8000.0, 4),
@@ -479,8 +476,9 @@ def run_kernel(args):
     --shape B,R,Hq,Hkv,hd,ctx` (verify attention over a shuffled paged KV pool)
     or `--kernel accept --shape B,k,V,T,top_p` (chain acceptance on fp32 logits;
     default the acceptance micro-benchmark 256,7,128256,0.7,0.9).
-    Runs `--steps` timed launches after `--warmup` and prints the mean time;
-    this is a kernel timing, not the benchmark metric."""
+    Runs `--warmup` launches, then times `--steps` launches replayed from one
+    CUDA graph and prints the mean time per launch; this is a kernel timing,
+    not the benchmark metric."""
     import ctypes as C
 
     import torch
@@ -490,6 +488,7 @@ def run_kernel(args):
     L = S.lib()
     g = torch.Generator(device="cuda").manual_seed(0)
     ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    cur = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
     if args.kernel == "accept":
         # chain acceptance on fp32 logits: target N(0, 3) [B, k+1, V], draft =
         # target + N(0, 0.5) [B, k, V], drafts = the draft rows' arg-max
@@ -506,19 +505,38 @@ def run_kernel(args):
         ws = torch.empty(ws_b, dtype=torch.uint8, device="cuda")
         sp = S.sampling(T, tp, 4, 0)
         call = lambda: L.specdec_accept_chain(ptr(tgt), ptr(dr), ptr(drafts), B, k, V, C.byref(sp),  # noqa: E731
-                                              ptr(acc), ptr(out), ptr(ws), ws_b, None)
+                                              ptr(acc), ptr(out), ptr(ws), ws_b, cur())
         algo = {"bytes": (2 * k + 1) * B * V * 4}
         args.shape = f"{B},{k},{V},{T},{tp}"
     dims = [int(x) for x in args.shape.split(",")] if args.kernel != "accept" else []
-    if args.kernel == "gemm":
+    if args.kernel in ("gemm", "gemm_tc", "gemv"):
         M, N, K = dims
         packed = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
         scales = (torch.rand((N, (K + 127) // 128), device="cuda", generator=g) * 0.01 + 0.001).half()
-        tiled = torch.empty(L.specdec_w4_tiled_bytes(N, K), dtype=torch.uint8, device="cuda")
-        S.check(L.specdec_w4_tile(ptr(packed), ptr(scales), N, K, ptr(tiled), None))
+        nbytes = L.specdec_w4_tiled_bytes(N, K)
+        # enough weight copies that consecutive launches read them from HBM, not L2
+        copies = max(1, -(-300_000_000 // nbytes))
+        tiled = [torch.empty(nbytes, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+        for t in tiled:
+            S.check(L.specdec_w4_tile(ptr(packed), ptr(scales), N, K, ptr(t), None))
         X = torch.randn((M, K), device="cuda", generator=g).half()
         Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-        call = lambda: L.specdec_w4a16_gemm(ptr(X), M, K, ptr(tiled), N, K, ptr(Y), N, 0, None, 0, None)  # noqa: E731
+        rot = {"i": 0}
+
+        def wnext():
+            rot["i"] += 1
+            return ptr(tiled[rot["i"] % copies])
+
+        if args.kernel == "gemm_tc":  # the tcgen05 tiles on the planner's plan, whatever M
+            plan = (C.c_int32 * 4)()
+            S.check(L.specdec_w4a16_plan(M, N, K, 0, plan))
+            qn, split = int(plan[1]), int(plan[2])
+            call = lambda: L.specdec_w4a16_gemm_with_plan(ptr(X), M, K, wnext(), N, K, ptr(Y), N, 0,  # noqa: E731
+                                                          qn, split, cur())
+        elif args.kernel == "gemv":
+            call = lambda: L.specdec_w4a16_gemv(ptr(X), M, K, wnext(), N, K, ptr(Y), N, 0, cur())  # noqa: E731
+        else:  # as the planner routes it
+            call = lambda: L.specdec_w4a16_gemm(ptr(X), M, K, wnext(), N, K, ptr(Y), N, 0, None, 0, cur())  # noqa: E731
         algo = {"bytes": N * K // 2 + N * ((K + 127) // 128) * 2, "flops": 2.0 * M * N * K}
     elif args.kernel == "attention":
         B, R, Hq, Hkv, hd, ctx = dims
@@ -533,16 +551,25 @@ def run_kernel(args):
         q = torch.randn((B * R, Hq, hd), device="cuda", generator=g).half()
         out = torch.empty_like(q)
         call = lambda: L.specdec_attention(ptr(q), ptr(pool), nblk, Hkv, hd, ptr(tables), max_blocks,  # noqa: E731
-                                           ptr(ctxs), ptr(mask), B, R, Hq, ptr(out), None, 0, None)
+                                           ptr(ctxs), ptr(mask), B, R, Hq, ptr(out), None, 0, cur())
         algo = {"bytes": B * Hkv * (ctx + R) * hd * 2 * 2}
-    for _ in range(args.warmup):
-        S.check(call())
+    # warm-up launches, then `steps` launches captured once in a CUDA graph and
+    # replayed: the device time per launch without the host's launch path
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            S.check(call())
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.steps):
+            S.check(call())
+    graph.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        call()
-    e1.record()
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) / args.steps * 1e3
     res = {"kernel": args.kernel, "shape": args.shape, "us_per_launch": round(us, 2),
@@ -629,7 +656,9 @@ def main():
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--nvtx", action="store_true", help="mark the timed steps with an NVTX range (profiler filter)")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "accept"], help="time one hot kernel instead of the step")
+    ap.add_argument("--kernel", choices=["gemm", "gemm_tc", "gemv", "attention", "accept"],
+                    help="time one hot kernel instead of the step (gemm: as the planner routes it; gemm_tc: the "
+                         "tcgen05 tiles; gemv: the few-row kernel)")
     ap.add_argument("--shape", default="160,128256,4096",
                     help="--kernel shape: M,N,K (gemm), B,R,Hq,Hkv,hd,ctx (attention) or B,k,V,T,top_p (accept)")
     args = ap.parse_args()

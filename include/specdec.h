@@ -173,8 +173,10 @@ int specdec_sample_rows(const float* logits, int rows, int k, int V, const specd
  *  4. specdec_shard_point_mass -> ep, eq [B*k]; all-reduce (sum).
  *  5. specdec_shard_accept_test -> accepted [B] (identical on every rank).
  *     Greedy: the emitted token is parg[b*(k+1) + accepted[b]].
- *  6. specdec_shard_draw_totals -> [B][4] u64; all-gather [W][B][4].
- *  7. specdec_shard_draw -> token or -1 per sequence; all-reduce (max).
+ *  6. specdec_shard_draw_winners -> [B][4] int32, this shard's Gumbel-max
+ *     winners of the residual / bonus draw; all-gather [W][B][4].
+ *  7. specdec_shard_draw_merge -> the emitted token per sequence (identical on
+ *     every rank).
  * The per-row steps (row_max, row_mass, digit_hist) take the target rows
  * (z, rows) and the draft rows (z2, rows2; NULL, 0 when greedy) in one call;
  * their per-row inputs and outputs list the target rows first.  Unsigned
@@ -196,14 +198,12 @@ int specdec_shard_point_mass(const float* target, const float* draft, const int3
 int specdec_shard_accept_test(const int32_t* drafts, int B, int k, const specdec_sampling* sp, const int32_t* parg,
                               const uint64_t* pnuc, const uint64_t* qnuc, const uint64_t* ep, const uint64_t* eq,
                               int32_t* accepted, void* stream);
-int specdec_shard_draw_totals(const float* target, const float* draft, int B, int k, int Vs, float temperature,
-                              const int32_t* accepted, const float* pmax, const uint32_t* ptau, const float* qmax,
-                              const uint32_t* qtau, const uint64_t* pnuc, const uint64_t* qnuc, uint64_t* out_tot,
-                              void* stream);
-int specdec_shard_draw(const float* target, const float* draft, int B, int k, int Vs, int v0,
-                       const specdec_sampling* sp, const int32_t* accepted, const float* pmax, const uint32_t* ptau,
-                       const float* qmax, const uint32_t* qtau, const uint64_t* pnuc, const uint64_t* qnuc,
-                       const uint64_t* gtot, int W, int rank, int32_t* tok_out, void* stream);
+int specdec_shard_draw_winners(const float* target, const float* draft, int B, int k, int Vs, int v0,
+                               const specdec_sampling* sp, const int32_t* accepted, const float* pmax,
+                               const uint32_t* ptau, const float* qmax, const uint32_t* qtau, const uint64_t* pnuc,
+                               const uint64_t* qnuc, int32_t* out_win, void* stream);
+int specdec_shard_draw_merge(const int32_t* gwin, int W, int B, int k, const int32_t* accepted, int32_t* tok_out,
+                             void* stream);
 
 /* Reference-semantics greedy verify on device pointers (see
  * sve2_speculative_verify_f32 above). */
@@ -220,14 +220,26 @@ int specdec_w4_tile(const uint8_t* packed, const uint16_t* scales, int N, int K,
 int specdec_w4_untile(const void* tiled, int N, int K, uint8_t* packed, uint16_t* scales, void* stream);
 /* Y[m, n] = sum_k X[m, k] * W[n, k] (mode 0 store, 1 add).  X fp16 [M, K]
  * (row stride ldx elements, 16-byte aligned), Y fp32 with row stride ldy.
- * The int4 weights are dequantised in registers and multiplied on the tcgen05
- * tensor cores with TMEM accumulators.  Partial tiles of k-ranges split
- * across the CTAs of a cluster are summed on chip in a fixed order, so the
- * result is deterministic; the workspace (specdec_w4a16_workspace_bytes, 0)
- * is kept for the interface and may be NULL. */
+ * Replaces compute_sme_gemm_i4_f32 (server/sme_gemm.cpp:249-285) and the W8
+ * GEMV of the model forward (gemv_s8_f32_batched, server/sme_gemm.cpp:41-66)
+ * for int4 group-128 weights.  From 65 token rows up, the int4 weights are
+ * dequantised in registers and multiplied on the tcgen05 tensor cores with
+ * TMEM accumulators; below, the call runs specdec_w4a16_gemv.  Partial tiles
+ * of k-ranges split across the CTAs of a cluster are summed on chip in a
+ * fixed order, so the result is deterministic; the workspace
+ * (specdec_w4a16_workspace_bytes, 0) is kept for the interface and may be
+ * NULL. */
 size_t specdec_w4a16_workspace_bytes(int M, int N, int K);
 int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
                        int mode, void* workspace, size_t workspace_bytes, void* stream);
+/* The same contraction for 0 <= M <= 64 token rows (decode at small batch,
+ * the MTP draft heads): each CTA streams 128-row weight units by bulk copy,
+ * dequantises them into tensor-core fragments in registers, a cluster splits
+ * the k range and reduces in rank order through distributed shared memory.
+ * Same results as specdec_w4a16_gemm within fp32 summation order.  Replaces
+ * rust_sme_mtp_predict_f32's contraction (lib.rs:1792-1831) for W4A16 heads. */
+int specdec_w4a16_gemv(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
+                       int mode, void* stream);
 /* The launch plan for a shape: out[0] token tile, out[1] 128-row weight
  * units per CTA (1 or 2), out[2] CTAs splitting the k range of a tile (1, 2,
  * 4, 8), out[3] CTAs launched.  units = 0: the plan specdec_w4a16_gemm picks;
@@ -348,11 +360,12 @@ int specdec_engine_info(specdec_engine* e, const char* what, int64_t* value);
  * [2] draft GEMMs, [3] sampling / acceptance, [4] other kernels, [5] whole
  * step, [6] verify GEMM launches per step.  ms_out holds 7 floats. */
 int specdec_engine_profile(specdec_engine* e, int steps, float* ms_out);
-/* Device time (ms) of the verify forward -- embedding, every layer and the
- * lm_head -- of the last step that ran, measured by two events the step
- * records around it (inside the CUDA graph when the step is graphed).
- * Synchronises the engine stream. */
-int specdec_engine_verify_ms(specdec_engine* e, float* ms);
+/* Runs one step through a second CUDA graph of the step that stamps the
+ * global timer around the verify forward (embedding, every layer, the
+ * lm_head) and returns that forward's device time in ms.  The first call
+ * captures that graph (after one eager step).  Synchronises the engine
+ * stream. */
+int specdec_engine_step_verify_timed(specdec_engine* e, float* verify_ms);
 
 #ifdef __cplusplus
 }

@@ -72,8 +72,18 @@ typedef struct {
 void orc_row_stats_compute(const float* z, int V, float c, uint64_t top_p_q32, orc_row_stats* st);
 /* E of token x under the row statistics (0 outside the nucleus). */
 uint32_t orc_row_mass(const float* z, const orc_row_stats* st, float c, int x);
-/* Inverse-CDF draw from the nucleus distribution with a 64-bit uniform. */
-int orc_sample_row(const float* z, int V, float c, const orc_row_stats* st, uint64_t u64);
+/* Gumbel-max draw from the nucleus distribution (weights E_j) of row z with
+ * the element uniforms of draw (seed, step, b, i, purpose), the tokens
+ * excl[0 .. n_excl) left out; -1 when no token has weight.  See
+ * orc_sample.c for the arithmetic. */
+int orc_draw_row(const float* z, int V, float c, const orc_row_stats* st, uint64_t seed, uint32_t step, uint32_t b,
+                 uint32_t i, uint32_t purpose, const int32_t* excl, int n_excl);
+/* The pieces: log2 by the atanh series, -log2 of a Philox uniform, the
+ * uniform of element j of a draw, and a candidate's score. */
+float orc_det_log2(float x);
+float orc_neg_log2_uniform(uint32_t x);
+uint32_t orc_gumbel_uniform(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose, uint32_t j);
+float orc_gumbel_score(float log2w, uint32_t u);
 /* Lowest index of the maximum (NaN never wins); -1 if V == 0. */
 int orc_argmax(const float* z, int V);
 /* Maximum and the second maximum (value of the best other index). */
@@ -82,8 +92,9 @@ void orc_top2(const float* z, int V, float* top1, float* top2);
 void orc_topk(const float* z, int V, int k, int* out);
 
 /* Uniform streams.  ctr = {b, i, purpose, step}, key = {seed_lo, seed_hi}.
- * purpose 0 = draft sampling, 1 = accept test, 2 = residual / bonus draw. */
-enum { ORC_U_DRAFT = 0, ORC_U_ACCEPT = 1, ORC_U_RESAMPLE = 2 };
+ * purpose 1 = accept test; the draws use one uniform per element:
+ * 3 = draft sampling, 4 = residual / bonus / tree draw (orc_gumbel_uniform). */
+enum { ORC_U_ACCEPT = 1, ORC_U_GUMBEL_DRAFT = 3, ORC_U_GUMBEL_RESAMPLE = 4 };
 uint32_t orc_uniform_u32(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose);
 uint64_t orc_uniform_u64(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose);
 
@@ -110,7 +121,7 @@ void orc_accept_tree(const float* target, const int32_t* node_tokens, const int3
                      float temperature, float top_p, uint64_t seed, uint32_t step, int32_t* accepted_len,
                      int32_t* path_nodes, int32_t* out_tokens);
 
-/* Draft-token sampling from draft logits rows [rows, V] (purpose 0 stream,
+/* Draft-token sampling from draft logits rows [rows, V] (purpose 3 draw,
  * b = row / k, i = row % k).  temperature == 0 -> argmax. */
 void orc_sample_rows(const float* logits, int rows, int k, int V, float temperature, float top_p, uint64_t seed,
                      uint32_t step, int32_t* out);

@@ -69,7 +69,11 @@ def _declare(L):
         "orc_logit_key": (U32, [F]),
         "orc_row_stats_compute": (None, [P, I, F, U64, C.POINTER(RowStats)]),
         "orc_row_mass": (U32, [P, C.POINTER(RowStats), F, I]),
-        "orc_sample_row": (I, [P, I, F, C.POINTER(RowStats), U64]),
+        "orc_draw_row": (I, [P, I, F, C.POINTER(RowStats), U64, U32, U32, U32, U32, P, I]),
+        "orc_det_log2": (F, [F]),
+        "orc_neg_log2_uniform": (F, [U32]),
+        "orc_gumbel_uniform": (U32, [U64, U32, U32, U32, U32, U32]),
+        "orc_gumbel_score": (F, [F, U32]),
         "orc_argmax": (I, [P, I]),
         "orc_topk": (None, [P, I, I, P]),
         "orc_uniform_u32": (U32, [U64, U32, U32, U32, U32]),
@@ -127,6 +131,18 @@ def philox(ctr, key):
     o = np.zeros(4, dtype=np.uint32)
     lib().orc_philox4x32_10(ptr(c), ptr(k), ptr(o))
     return o
+
+
+U_ACCEPT, U_GUMBEL_DRAFT, U_GUMBEL_RESAMPLE = 1, 3, 4
+
+
+def draw_row(z, temperature, top_p, seed, step, b, i, purpose=U_GUMBEL_DRAFT, exclude=()):
+    """Gumbel-max draw from the nucleus distribution of row z (orc_draw_row)."""
+    z = np.ascontiguousarray(z, dtype=np.float32)
+    st = row_stats(z, temperature, top_p)
+    ex = np.ascontiguousarray(exclude, dtype=np.int32) if len(exclude) else None
+    return lib().orc_draw_row(ptr(z), z.size, temp_coeff(temperature), C.byref(st), seed, step, b, i, purpose,
+                              ptr(ex) if ex is not None else None, 0 if ex is None else ex.size)
 
 
 def temp_coeff(temperature: float) -> float:

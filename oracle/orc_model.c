@@ -405,7 +405,7 @@ void orc_draft_chain(const orc_model* m, const float* h0, int B, int k, float te
             float cc = (float)(1.4426950408889634 / (double)temperature);
             uint64_t tp = (top_p < 1.0f) ? (uint64_t)llround((double)top_p * 4294967296.0) : (1ull << 32);
             orc_row_stats_compute(z, V, cc, tp, &st);
-            tok[b] = orc_sample_row(z, V, cc, &st, orc_uniform_u64(seed, step, (uint32_t)b, (uint32_t)i, ORC_U_DRAFT));
+            tok[b] = orc_draw_row(z, V, cc, &st, seed, step, (uint32_t)b, (uint32_t)i, ORC_U_GUMBEL_DRAFT, NULL, 0);
         }
         for (int b = 0; b < B; ++b) drafts[(size_t)b * k + i] = tok[b];
     }

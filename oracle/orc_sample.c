@@ -156,18 +156,98 @@ uint32_t orc_row_mass(const float* z, const orc_row_stats* st, float c, int x) {
 
 static inline uint64_t mulhi64(uint64_t a, uint64_t b) { return (uint64_t)(((u128)a * b) >> 64); }
 
-int orc_sample_row(const float* z, int V, float c, const orc_row_stats* st, uint64_t u64) {
-    uint64_t target = mulhi64(u64, st->nuc);
-    uint64_t cum = 0;
-    int last = -1;
-    for (int j = 0; j < V; ++j) {
-        uint32_t e = orc_row_mass(z, st, c, j);
-        if (!e) continue;
-        last = j;
-        cum += e;
-        if (cum > target) return j;
+/* ---------------------------------------------------- Gumbel-max draws
+ * A token is drawn with probability proportional to its integer weight w_j
+ * (the row mass E_j, or the residual max(0, E_p S_q - E_q S_p)) as the
+ * arg-max of log2(w_j) - log2(-log2 U_j), U_j from Philox per element
+ * (ctr = {b, i, (j / 4) << 4 | purpose, step}, word j % 4).  For row masses
+ * log2(E_j) is replaced by (z_j - max) * c, the exponent E_j was formed from
+ * (equal up to the floor of E_j, below 2^-31 of the row maximum's mass).
+ * log2 by the atanh series ln x = 2 atanh((x - 1) / (x + 1)) on the mantissa
+ * in [sqrt(1/2), sqrt(2)), five terms; -log2 U above one half through the
+ * complement w = 1 - U, ln(1 / (1 - w)) = 2 atanh(w / (2 - w)), eight terms.
+ * Every operation is a single round-to-nearest fp32 operation (the file is
+ * compiled with -ffp-contract=off; fmaf is the fused multiply-add), the same
+ * sequence as the CUDA kernels, so draws agree bit for bit. */
+static float from_bits(uint32_t b) {
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+static uint32_t to_bits(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    return b;
+}
+static float atanh_series5(float s) {
+    float s2 = s * s;
+    float p = 0x1.c71c72p-4f;          /* 1/9 */
+    p = fmaf(p, s2, 0x1.24924ap-3f);   /* 1/7 */
+    p = fmaf(p, s2, 0x1.99999ap-3f);   /* 1/5 */
+    p = fmaf(p, s2, 0x1.555556p-2f);   /* 1/3 */
+    return fmaf(p, s2, 1.0f);
+}
+float orc_det_log2(float x) {
+    uint32_t bits = to_bits(x);
+    int e = (int)((bits >> 23) & 255u) - 127;
+    float m = from_bits((bits & 0x7FFFFFu) | 0x3F800000u);
+    if (m > 0x1.6a09e6p+0f) {
+        m = m * 0.5f;
+        e += 1;
     }
-    return last;
+    float s = (m - 1.0f) / (m + 1.0f);
+    return fmaf(s * atanh_series5(s), 0x1.715476p+1f, (float)e);
+}
+float orc_neg_log2_uniform(uint32_t x) {
+    if (x < 0x80000000u) return -orc_det_log2(((float)x + 0.5f) * 0x1p-32f);
+    uint32_t y = (uint32_t)(0x100000000ull - (uint64_t)x);
+    float w = ((float)y - 0.5f) * 0x1p-32f;
+    float s = w / (2.0f - w);
+    float s2 = s * s;
+    float p = 0x1.111112p-4f;
+    p = fmaf(p, s2, 0x1.3b13b2p-4f);
+    p = fmaf(p, s2, 0x1.745d18p-4f);
+    p = fmaf(p, s2, 0x1.c71c72p-4f);
+    p = fmaf(p, s2, 0x1.24924ap-3f);
+    p = fmaf(p, s2, 0x1.99999ap-3f);
+    p = fmaf(p, s2, 0x1.555556p-2f);
+    p = fmaf(p, s2, 1.0f);
+    return (s * p) * 0x1.715476p+1f;
+}
+static float gumbel2(uint32_t x) { return -orc_det_log2(orc_neg_log2_uniform(x)); }
+static float det_log2_u128(u128 w) {
+    uint64_t hi = (uint64_t)(w >> 64), v = (uint64_t)w;
+    int sh = 0;
+    if (hi) {
+        sh = 64 - __builtin_clzll(hi);
+        v = (uint64_t)(w >> sh);
+    }
+    return orc_det_log2((float)v) + (float)sh;
+}
+uint32_t orc_gumbel_uniform(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose, uint32_t j) {
+    uint32_t ctr[4] = {b, i, ((j >> 2) << 4) | purpose, step}, key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)},
+             o[4];
+    orc_philox4x32_10(ctr, key, o);
+    return o[j & 3];
+}
+float orc_gumbel_score(float log2w, uint32_t u) { return log2w + gumbel2(u); }
+
+int orc_draw_row(const float* z, int V, float c, const orc_row_stats* st, uint64_t seed, uint32_t step, uint32_t b,
+                 uint32_t i, uint32_t purpose, const int32_t* excl, int n_excl) {
+    int best = -1;
+    float bs = 0.0f;
+    for (int j = 0; j < V; ++j) {
+        if (!orc_row_mass(z, st, c, j)) continue;
+        int ex = 0;
+        for (int t = 0; t < n_excl; ++t) ex |= excl[t] == j;
+        if (ex) continue;
+        float sc = orc_gumbel_score((z[j] - st->max) * c, orc_gumbel_uniform(seed, step, b, i, purpose, (uint32_t)j));
+        if (best < 0 || sc > bs) {
+            bs = sc;
+            best = j;
+        }
+    }
+    return best;
 }
 
 int orc_argmax(const float* z, int V) {
@@ -210,29 +290,25 @@ static uint64_t top_p_q32(float top_p) {
     return (uint64_t)llround((double)top_p * 4294967296.0);
 }
 
-/* Residual draw from max(0, P - Q) (integer cross-multiplied masses). */
-static int sample_residual(const float* zp, const orc_row_stats* sp, const float* zq, const orc_row_stats* sq,
-                           int V, float c, uint64_t u64) {
-    u128 R = 0;
+/* Residual draw from max(0, P - Q) (integer cross-multiplied masses); from P
+ * when the residual is zero everywhere. */
+static int draw_residual(const float* zp, const orc_row_stats* sp, const float* zq, const orc_row_stats* sq, int V,
+                         float c, uint64_t seed, uint32_t step, uint32_t b, uint32_t i) {
+    int best = -1;
+    float bs = 0.0f;
     for (int j = 0; j < V; ++j) {
         u128 a = (u128)orc_row_mass(zp, sp, c, j) * sq->nuc;
-        u128 b = (u128)orc_row_mass(zq, sq, c, j) * sp->nuc;
-        if (a > b) R += a - b;
+        u128 q = (u128)orc_row_mass(zq, sq, c, j) * sp->nuc;
+        if (a <= q) continue;
+        float sc = orc_gumbel_score(det_log2_u128(a - q),
+                                    orc_gumbel_uniform(seed, step, b, i, ORC_U_GUMBEL_RESAMPLE, (uint32_t)j));
+        if (best < 0 || sc > bs) {
+            bs = sc;
+            best = j;
+        }
     }
-    if (R == 0) return orc_sample_row(zp, V, c, sp, u64);
-    uint64_t rh = (uint64_t)(R >> 64), rl = (uint64_t)R;
-    u128 target = (u128)u64 * rh + mulhi64(u64, rl);
-    u128 cum = 0;
-    int last = -1;
-    for (int j = 0; j < V; ++j) {
-        u128 a = (u128)orc_row_mass(zp, sp, c, j) * sq->nuc;
-        u128 b = (u128)orc_row_mass(zq, sq, c, j) * sp->nuc;
-        if (a <= b) continue;
-        last = j;
-        cum += a - b;
-        if (cum > target) return j;
-    }
-    return last;
+    if (best < 0) best = orc_draw_row(zp, V, c, sp, seed, step, b, i, ORC_U_GUMBEL_RESAMPLE, NULL, 0);
+    return best;
 }
 
 void orc_accept_chain(const float* target, const float* draft, const int32_t* drafts, int B, int k, int V,
@@ -256,8 +332,8 @@ void orc_accept_chain(const float* target, const float* draft, const int32_t* dr
             for (;;) {
                 if (a == k) {
                     orc_row_stats_compute(P + (size_t)k * V, V, c, tp, &sp);
-                    tok = orc_sample_row(P + (size_t)k * V, V, c, &sp,
-                                         orc_uniform_u64(seed, step, b, k, ORC_U_RESAMPLE));
+                    tok = orc_draw_row(P + (size_t)k * V, V, c, &sp, seed, step, (uint32_t)b, (uint32_t)k,
+                                       ORC_U_GUMBEL_RESAMPLE, NULL, 0);
                     break;
                 }
                 const float* zp = P + (size_t)a * V;
@@ -271,7 +347,7 @@ void orc_accept_chain(const float* target, const float* draft, const int32_t* dr
                 u128 lhs = (u128)u * eq * sp.nuc;
                 u128 rhs = ((u128)ep * sq.nuc) << 32;
                 if (lhs < rhs) { ++a; continue; }
-                tok = sample_residual(zp, &sp, zq, &sq, V, c, orc_uniform_u64(seed, step, b, a, ORC_U_RESAMPLE));
+                tok = draw_residual(zp, &sp, zq, &sq, V, c, seed, step, (uint32_t)b, (uint32_t)a);
                 break;
             }
         }
@@ -324,22 +400,9 @@ void orc_accept_tree(const float* target, const int32_t* node_tokens, const int3
                     remaining -= e;
                 }
                 if (next < 0) {
-                    uint64_t u64 = orc_uniform_u64(seed, step, b, (uint32_t)cur, ORC_U_RESAMPLE);
-                    if (remaining == 0) { emit = orc_sample_row(z, V, c, &st, u64); break; }
-                    uint64_t target_m = mulhi64(u64, remaining);
-                    uint64_t cum = 0;
-                    int last = -1;
-                    for (int j = 0; j < V; ++j) {
-                        uint32_t e = orc_row_mass(z, &st, c, j);
-                        if (!e) continue;
-                        int rm = 0;
-                        for (int t = 0; t < n_removed; ++t) rm |= removed[t] == j;
-                        if (rm) continue;
-                        last = j;
-                        cum += e;
-                        if (cum > target_m) break;
-                    }
-                    emit = last;
+                    /* P without the rejected children's tokens; all of P when they cover it */
+                    emit = orc_draw_row(z, V, c, &st, seed, step, (uint32_t)b, (uint32_t)cur, ORC_U_GUMBEL_RESAMPLE,
+                                        removed, remaining ? n_removed : 0);
                     break;
                 }
             }
@@ -364,8 +427,8 @@ void orc_sample_rows(const float* logits, int rows, int k, int V, float temperat
         if (greedy) { out[r] = orc_argmax(z, V); continue; }
         orc_row_stats st;
         orc_row_stats_compute(z, V, c, tp, &st);
-        out[r] = orc_sample_row(z, V, c, &st, orc_uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k),
-                                                               ORC_U_DRAFT));
+        out[r] = orc_draw_row(z, V, c, &st, seed, step, (uint32_t)(r / k), (uint32_t)(r % k), ORC_U_GUMBEL_DRAFT,
+                              NULL, 0);
     }
 }
 

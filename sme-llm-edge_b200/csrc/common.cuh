@@ -68,17 +68,15 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t
     out[3] = c3;
 }
 
-enum { U_DRAFT = 0, U_ACCEPT = 1, U_RESAMPLE = 2 };
+// Uniform streams: ctr = {b, i, purpose, step}, key = seed.  The accept tests
+// use one uniform per test; the draws one per element (gumbel.cuh, purposes 3
+// and 4 with the element group in the counter's third word).
+enum { U_ACCEPT = 1 };
 
 __device__ __forceinline__ uint32_t uniform_u32(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose) {
     uint32_t o[4];
     philox4x32_10(b, i, purpose, step, (uint32_t)seed, (uint32_t)(seed >> 32), o);
     return o[0];
-}
-__device__ __forceinline__ uint64_t uniform_u64(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose) {
-    uint32_t o[4];
-    philox4x32_10(b, i, purpose, step, (uint32_t)seed, (uint32_t)(seed >> 32), o);
-    return ((uint64_t)o[0] << 32) | o[1];
 }
 
 // floor(2^t * 2^31), t <= 0: rint range reduction, degree-7 Taylor polynomial

@@ -301,6 +301,15 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int ldq, const int
     }
 }
 
+// Global timer (ns) into out[i]: brackets the verify forward in the timed graph.
+__global__ void stamp_kernel(unsigned long long* out, int i) {
+    if (threadIdx.x == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        out[i] = t;
+    }
+}
+
 // Chain verify rows: [pending, d_0 .. d_{k-1}] at positions ctx .. ctx + k.
 __global__ void build_chain_rows_kernel(const int32_t* __restrict__ pending, const int32_t* __restrict__ drafts,
                                         const int32_t* __restrict__ ctx, int B, int k, int32_t* tokens, int32_t* pos,
@@ -520,9 +529,12 @@ struct specdec_engine {
     // event is that launch's device time (one stream, in-order execution)
     bool prof_on = false;
     int gemm_cat = 0;
-    // verify interval (embedding through the lm_head) of every step, recorded
-    // inside the step itself (event nodes of the captured graph)
-    cudaEvent_t verify_ev[2] = {nullptr, nullptr};
+    // verify interval (embedding through the lm_head): a second graph of the
+    // same step with a global-timer stamp kernel on each side of the forward
+    bool stamp_on = false;
+    unsigned long long* stamps = nullptr;
+    cudaGraph_t graph_timed = nullptr;
+    cudaGraphExec_t gexec_timed = nullptr;
     std::vector<cudaEvent_t> prof_pool;
     std::vector<int> prof_cat;
     size_t prof_used = 0;
@@ -556,6 +568,12 @@ int dalloc(specdec_engine* e, T** p, size_t count) {
 }
 
 int gemm(specdec_engine* e, const __half* X, int M, int K, const uint8_t* w, int N, float* Y, int ldy, int mode) {
+    if (plan_gemm_uses_gemv(M, N, K)) {  // few token rows: draft heads, batch-1 steps
+        ++e->kernels_per_step;
+        int rc = gemv_launch(X, K, K, plan_gemv(M, N, K), w, M, N, Y, ldy, mode, e->stream, /*pdl=*/true);
+        prof_mark(e, e->gemm_cat);
+        return rc;
+    }
     GemmPlan p = plan_gemm(M, N, K);
     CUtensorMap map;
     int rc = make_x_tmap(&map, X, M, K, K, p.MT);
@@ -700,9 +718,9 @@ int record_step(specdec_engine* e) {
         build_chain_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->drafts, kvs.ctx, B, k, e->tokens,
                                                                    e->pos, e->slot);
         ENG_LAUNCH("build_chain_rows_kernel");
-        SD_CUDA(cudaEventRecord(e->verify_ev[0], s));
+        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 0);
         ENG_TRY(forward(e, R, true));
-        SD_CUDA(cudaEventRecord(e->verify_ev[1], s));
+        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 1);
         e->kernels_per_step += 2;
         ENG_TRY(launch_accept_chain_dev(e->logits, e->dlogits, e->drafts, B, k, V, sp.temperature, sp.top_p, sp.seed,
                                         e->step, e->acc, e->out_tokens, e->acc_ws, true, s));
@@ -723,9 +741,9 @@ int record_step(specdec_engine* e) {
                                                                   e->rank, kvs.ctx, B, R, e->tokens, e->node_tokens,
                                                                   e->pos, e->slot);
         ENG_LAUNCH("build_tree_rows_kernel");
-        SD_CUDA(cudaEventRecord(e->verify_ev[0], s));
+        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 0);
         ENG_TRY(forward(e, R, true));
-        SD_CUDA(cudaEventRecord(e->verify_ev[1], s));
+        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 1);
         ++e->kernels_per_step;
         ENG_TRY(launch_accept_tree_dev(e->logits, e->node_tokens, e->parent, B, R, V, sp.temperature, sp.top_p,
                                        sp.seed, e->step, e->acc, e->path, e->out_tokens, s));
@@ -750,8 +768,8 @@ int record_step(specdec_engine* e) {
 extern "C" int specdec_engine_destroy(specdec_engine* e) {
     if (!e) return SPECDEC_OK;
     for (cudaEvent_t ev : e->prof_pool) cudaEventDestroy(ev);
-    for (cudaEvent_t ev : e->verify_ev)
-        if (ev) cudaEventDestroy(ev);
+    if (e->gexec_timed) cudaGraphExecDestroy(e->gexec_timed);
+    if (e->graph_timed) cudaGraphDestroy(e->graph_timed);
     if (e->gexec) cudaGraphExecDestroy(e->gexec);
     if (e->graph) cudaGraphDestroy(e->graph);
     if (e->kvm) specdec_kv_destroy(e->kvm);
@@ -781,8 +799,6 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
         return code;
     };
     if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(SPECDEC_ECUDA);
-    if (cudaEventCreate(&e->verify_ev[0]) != cudaSuccess || cudaEventCreate(&e->verify_ev[1]) != cudaSuccess)
-        return fail(SPECDEC_ECUDA);
     const int H = mc->hidden, F = mc->ffn, V = mc->vocab, hd = mc->head_dim, Hkv = mc->n_kv_heads;
     e->tree = rc->tree_nodes > 0;
     e->B = rc->batch;
@@ -894,7 +910,8 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
         (rcode = dalloc(e, &e->path, (size_t)e->B * e->R)) || (rcode = dalloc(e, &e->node_tokens, (size_t)e->B * e->R)) ||
         (rcode = dalloc(e, &e->topk, (size_t)e->B * e->k * std::max(1, e->topk_w))) ||
         (rcode = dalloc(e, &e->new_len, e->B)) || (rcode = dalloc(e, &e->active, e->B)) ||
-        (rcode = dalloc(e, &e->step, 1)) || (rcode = dalloc(e, &e->emitted, 1)))
+        (rcode = dalloc(e, &e->step, 1)) || (rcode = dalloc(e, &e->emitted, 1)) ||
+        (rcode = dalloc(e, &e->stamps, 2)))
         return fail(rcode);
     cudaMemset(e->step, 0, 4);
     cudaMemset(e->emitted, 0, 8);
@@ -1193,13 +1210,43 @@ extern "C" int specdec_engine_profile(specdec_engine* e, int steps, float* ms_ou
     return SPECDEC_OK;
 }
 
-// Device time of the verify forward (embedding through the lm_head) of the
-// last step that ran, graphed or eager: the interval between the two events
-// the step records around it.
-extern "C" int specdec_engine_verify_ms(specdec_engine* e, float* ms) {
-    SD_CHECK(e && ms, SPECDEC_EINVAL, "engine_verify_ms: bad argument");
-    SD_CUDA(cudaStreamSynchronize(e->stream));
-    SD_CUDA(cudaEventElapsedTime(ms, e->verify_ev[0], e->verify_ev[1]));
+// One step through a second graph of the same step that stamps the global
+// timer (ns) right before the verify forward's first kernel and right after
+// its last (the lm_head), and the verify forward's device time (ms) between the
+// stamps.  The stamp kernels are launched normally, so each waits for the
+// kernel before it to finish and the next one starts only after it.
+extern "C" int specdec_engine_step_verify_timed(specdec_engine* e, float* verify_ms) {
+    SD_CHECK(e && verify_ms, SPECDEC_EINVAL, "engine_step_verify_timed: bad argument");
+    cudaStream_t s = e->stream;
+    if (!e->gexec_timed) {
+        // an eager step first (kernel attributes), then the capture
+        e->stamp_on = true;
+        int rc = record_step(e);
+        if (!rc) {
+            SD_CUDA(cudaStreamSynchronize(s));
+            SD_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+            rc = record_step(e);
+            cudaGraph_t g = nullptr;
+            cudaError_t ce = cudaStreamEndCapture(s, &g);
+            e->stamp_on = false;
+            if (rc) {
+                if (g) cudaGraphDestroy(g);
+                return rc;
+            }
+            if (ce != cudaSuccess) return cuda_status(ce, "engine_step_verify_timed capture");
+            e->graph_timed = g;
+            SD_CUDA(cudaGraphInstantiate(&e->gexec_timed, g, 0));
+        }
+        e->stamp_on = false;
+        if (rc) return rc;
+        // the eager run above was this call's step
+    } else {
+        SD_CUDA(cudaGraphLaunch(e->gexec_timed, s));
+    }
+    unsigned long long t[2] = {0, 0};
+    SD_CUDA(cudaMemcpyAsync(t, e->stamps, sizeof(t), cudaMemcpyDeviceToHost, s));
+    SD_CUDA(cudaStreamSynchronize(s));
+    *verify_ms = (float)((double)(t[1] - t[0]) * 1e-6);
     return SPECDEC_OK;
 }
 

@@ -1072,6 +1072,9 @@ extern "C" int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void*
     SD_CHECK(X && w_tiled && Y && M >= 0 && N > 0 && K > 0 && ldx >= K && ldy >= N && (mode == 0 || mode == 1),
              SPECDEC_EINVAL, "w4a16_gemm: bad argument");
     if (M == 0) return SPECDEC_OK;
+    if (plan_gemm_uses_gemv(M, N, K))  // few token rows: the bandwidth-shaped kernel
+        return gemv_launch(reinterpret_cast<const __half*>(X), ldx, K, plan_gemv(M, N, K), w_tiled, M, N, Y, ldy,
+                           mode, as_stream(stream), false);
     GemmPlan p = plan_gemm(M, N, K);
     CUtensorMap map;
     int rc = make_x_tmap(&map, X, M, K, ldx, p.MT);

@@ -60,6 +60,22 @@ GemmPlan plan_gemm_qkv(int M, int N, int K);
 int gemm_launch_qkv_rope(const CUtensorMap& map, const GemmPlan& p, const void* w_qkv, int M, int N, const RopeArgs& ra,
                          cudaStream_t s, bool pdl = false);
 size_t gemm_workspace_bound(int max_m, int max_n, int max_k);
+
+// W4A16 contraction for few token rows (gemv_w4a16.cu): mode 0 store / 1 add,
+// 1 <= M <= kGemvMaxRows.  plan_gemm_uses_gemv() is the crossover the planner
+// applies (measured against the tcgen05 tiles).
+constexpr int kGemvMaxRows = 64;
+struct GemvPlan {
+    int NT;      // tiles of 8 token rows
+    int KG;      // 128-wide k units
+    int blocks;  // 128-row unit blocks
+    int S;       // CTAs per unit block (cluster split of the k range)
+    int grid;
+};
+GemvPlan plan_gemv(int M, int N, int K);
+bool plan_gemm_uses_gemv(int M, int N, int K);
+int gemv_launch(const __half* X, int ldx, int K, const GemvPlan& p, const void* w_tiled, int M, int N, float* Y,
+                int ldy, int mode, cudaStream_t s, bool pdl = false);
 size_t w4_tiled_bytes(int N, int K);
 
 // ---------------------------------------------------------------- attention

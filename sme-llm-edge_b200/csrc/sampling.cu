@@ -8,11 +8,15 @@
 // E_j = floor(2^((z_j - max) * log2(e) / T) * 2^31) (deterministic exp2), sums
 // are integer, the min(1, p/q) test and the residual are integer
 // cross-multiplications, so the result does not depend on reduction order.
+// Draws (draft tokens, the residual / bonus token, the tree's fallback) are
+// Gumbel-max arg-maxes over per-element scores (gumbel.cuh), merged as
+// (score desc, index asc), which is order-independent as well.
 #include <cfloat>
 #include <climits>
 #include <mutex>
 
 #include "common.cuh"
+#include "gumbel.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -29,22 +33,16 @@ struct DevRowStats {
 static_assert(sizeof(DevRowStats) == kAcceptStatsBytes, "row stats layout");
 
 constexpr int kRowThreads = 1024;
-
-constexpr int kCdfChunk = 256;      // inverse CDF: elements per recorded chunk total (8 per lane)
-constexpr int kCdfChunksPerWarp = 32;  // so V <= 32 warps x 32 chunks x 256 = 262144
-constexpr int kMaxVocab = (kRowThreads / 32) * kCdfChunksPerWarp * kCdfChunk;
+// The top-p histograms of a row keep one per warp of 16-bit mass halves: a warp
+// sees at most 8192 elements of a row (32 warps), which bounds V.
+constexpr int kMaxVocab = 262144;
 
 struct RowSmem {
     uint64_t hist[256];
-    u128 scan[32];
-    u128 chunk[32][kCdfChunksPerWarp];  // inverse CDF: mass of every 256-element chunk of a warp's range
     uint64_t red64[32];
     float redf[32];
     int redi[32];
     DevRowStats st;
-    int result;
-    u128 big;
-    u128 total;
 };
 
 __device__ __forceinline__ uint32_t mass_of(float z, float m, float c) {
@@ -348,166 +346,158 @@ __device__ __forceinline__ uint32_t nucleus_mass(const float* z, const DevRowSta
     return mass_of(zx, st.max, c);
 }
 
-// Block-wide inclusive scan of u128 (blockDim.x multiple of 32, <= 1024).
-__device__ u128 block_incl_scan_u128(u128 v, RowSmem& sm, u128* total) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+// ------------------------------------------------------ Gumbel-max draws
+// The CTA's best (score, index) of the per-thread candidates (every thread gets it).
+__device__ void cta_best(float bs, int bj, RowSmem& sm, float* out_s, int* out_j) {
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        uint64_t lo = __shfl_up_sync(0xffffffffu, (uint64_t)v, o);
-        uint64_t hi = __shfl_up_sync(0xffffffffu, (uint64_t)(v >> 64), o);
-        if (lane >= o) v += ((u128)hi << 64) | lo;
+    for (int o = 16; o; o >>= 1) {
+        const float s2 = __shfl_xor_sync(0xffffffffu, bs, o);
+        const int j2 = __shfl_xor_sync(0xffffffffu, bj, o);
+        gumbel_merge(bs, bj, s2, j2);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) {
+        sm.redf[wid] = bs;
+        sm.redi[wid] = bj;
     }
     __syncthreads();
-    if (lane == 31) sm.scan[wid] = v;
-    __syncthreads();
     if (wid == 0) {
-        u128 w = lane < nw ? sm.scan[lane] : (u128)0;
+        bs = lane < nw ? sm.redf[lane] : -INFINITY;
+        bj = lane < nw ? sm.redi[lane] : -1;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            uint64_t lo = __shfl_up_sync(0xffffffffu, (uint64_t)w, o);
-            uint64_t hi = __shfl_up_sync(0xffffffffu, (uint64_t)(w >> 64), o);
-            if (lane >= o) w += ((u128)hi << 64) | lo;
+        for (int o = 16; o; o >>= 1) {
+            const float s2 = __shfl_xor_sync(0xffffffffu, bs, o);
+            const int j2 = __shfl_xor_sync(0xffffffffu, bj, o);
+            gumbel_merge(bs, bj, s2, j2);
         }
-        if (lane < nw) sm.scan[lane] = w;
-    }
-    __syncthreads();
-    const u128 before = wid ? sm.scan[wid - 1] : (u128)0;
-    *total = sm.scan[nw - 1];
-    return v + before;
-}
-
-__device__ __forceinline__ u128 shfl_u128(u128 v, int src) {
-    const uint64_t lo = __shfl_sync(0xffffffffu, (uint64_t)v, src);
-    const uint64_t hi = __shfl_sync(0xffffffffu, (uint64_t)(v >> 64), src);
-    return ((u128)hi << 64) | lo;
-}
-__device__ __forceinline__ u128 warp_incl_scan_u128(u128 v) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint64_t lo = __shfl_up_sync(0xffffffffu, (uint64_t)v, o);
-        const uint64_t hi = __shfl_up_sync(0xffffffffu, (uint64_t)(v >> 64), o);
-        if (lane >= o) v += ((u128)hi << 64) | lo;
-    }
-    return v;
-}
-
-// Inverse CDF over the index range [L, H), in two phases so that a cluster
-// can exchange range totals in between.
-// Phase 1 (cta_cdf_chunks): warp w owns the contiguous range
-// [L + w*C, L + (w+1)*C), C a multiple of 256, and walks it in 256-element
-// chunks (lane l: 8 contiguous elements), keeping every chunk's mass in
-// shared memory and every warp's total in sm.scan; returns the range total.
-// Phase 2 (cta_cdf_find): the smallest j in [L, H) whose running mass from L
-// exceeds `target` -- the warp whose range holds the target finds the chunk
-// from the recorded totals and re-reads only that chunk; -1 when the target
-// is not below the total.  One pass over the range plus 256 elements; every
-// sum is an integer sum, so the result does not depend on the order.
-template <class MassFn>
-__device__ u128 cta_cdf_chunks(int L, int H, MassFn mass, RowSmem& sm) {
-    constexpr int E = kCdfChunk / 32;  // elements per lane and chunk
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int C = ((H - L + nw - 1) / nw + kCdfChunk - 1) / kCdfChunk * kCdfChunk;
-    const int nch = C / kCdfChunk;  // <= kCdfChunksPerWarp (H - L <= 262144, checked by the launchers)
-    const int lo = L + wid * C, hi = min(H, lo + C);
-    u128 t = 0;
-    __syncthreads();  // sm.scan / sm.chunk / sm.total may still be read by a previous caller
-    for (int ch = 0; ch < nch; ++ch) {
-        const int base = lo + ch * kCdfChunk + lane * E;
-        u128 sc = 0;
-#pragma unroll
-        for (int e = 0; e < E; ++e) sc += base + e < hi ? mass(base + e) : (u128)0;  // unrolled: loads in flight together
-        sc = warp_sum_u128(sc);
-        if (lane == 0) sm.chunk[wid][ch] = sc;
-        t += sc;
-    }
-    if (lane == 0) sm.scan[wid] = t;
-    __syncthreads();
-    if (wid == 0) {
-        const u128 tot = warp_sum_u128(lane < nw ? sm.scan[lane] : (u128)0);
-        if (lane == 0) sm.total = tot;
-    }
-    __syncthreads();
-    return sm.total;
-}
-
-template <class MassFn>
-__device__ int cta_cdf_find(int L, int H, MassFn mass, u128 target, RowSmem& sm) {
-    constexpr int E = kCdfChunk / 32;
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int C = ((H - L + nw - 1) / nw + kCdfChunk - 1) / kCdfChunk * kCdfChunk;
-    const int nch = C / kCdfChunk;
-    if (wid == 0) {
-        const u128 v = lane < nw ? sm.scan[lane] : (u128)0;
-        const u128 incl = warp_incl_scan_u128(v);
-        const bool hit = lane < nw && incl - v <= target && target < incl;
-        const unsigned b = __ballot_sync(0xffffffffu, hit);
-        if (hit && lane == __ffs(b) - 1) sm.big = target - (incl - v);
         if (lane == 0) {
-            sm.redi[0] = b ? __ffs(b) - 1 : -1;
-            sm.result = -1;
+            sm.redf[0] = bs;
+            sm.redi[0] = bj;
         }
     }
     __syncthreads();
-    const int W = sm.redi[0];
-    if (W >= 0 && wid == W) {
-        const int lo = L + W * C, hi = min(H, lo + C);
-        const u128 tgt = sm.big;
-        // the chunk holding the target
-        const u128 v = lane < nch ? sm.chunk[W][lane] : (u128)0;
-        const u128 incl = warp_incl_scan_u128(v);
-        const bool hit = lane < nch && incl - v <= tgt && tgt < incl;
-        const unsigned hb = __ballot_sync(0xffffffffu, hit);
-        if (hb) {
-            const int ch = __ffs(hb) - 1;
-            const u128 rem = tgt - shfl_u128(incl - v, ch);
-            // its 256 elements: lane sums, a warp scan, then the lane's 8 in order
-            const int base = lo + ch * kCdfChunk + lane * E;
-            u128 sl = 0;
+    *out_s = sm.redf[0];
+    *out_j = sm.redi[0];
+    __syncthreads();
+}
+
+// Visits the elements j of [L, H) in groups of four aligned on the element
+// index (the draw's uniforms come four per Philox block): f(g, v[4], in[4])
+// with the four values of group g (v = z[4g + e]) and which of them lie in
+// [L, H).  One float4 load per group when z is 16-byte aligned and L, H are
+// multiples of 4; element loads otherwise.
+template <class F>
+__device__ __forceinline__ void for_each_group(const float* __restrict__ z, int L, int H, F f) {
+    const int g0 = L >> 2, g1 = (H + 3) >> 2;
+    const bool vec = ((reinterpret_cast<uintptr_t>(z) & 15) == 0) && ((L & 3) == 0) && ((H & 3) == 0);
+    for (int g = g0 + (int)threadIdx.x; g < g1; g += blockDim.x) {
+        float v[4];
+        bool in[4];
+        if (vec) {
+            const float4 q = reinterpret_cast<const float4*>(z)[g];
+            v[0] = q.x;
+            v[1] = q.y;
+            v[2] = q.z;
+            v[3] = q.w;
 #pragma unroll
-            for (int e = 0; e < E; ++e) sl += base + e < hi ? mass(base + e) : (u128)0;
-            const u128 li = warp_incl_scan_u128(sl);
-            const bool h2 = li - sl <= rem && rem < li;
-            const unsigned b2 = __ballot_sync(0xffffffffu, h2);
-            if (h2 && lane == __ffs(b2) - 1) {  // the lane's 8 elements in order (recomputed)
-                u128 run = li - sl;
-                for (int e = 0; e < E; ++e) {
-                    const u128 me = base + e < hi ? mass(base + e) : (u128)0;
-                    if (run + me > rem) {
-                        sm.result = base + e;
-                        break;
-                    }
-                    run += me;
-                }
+            for (int e = 0; e < 4; ++e) in[e] = true;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * g + e;
+                in[e] = j >= L && j < H;
+                v[e] = in[e] ? z[j] : 0.f;
             }
         }
+        f(g, v, in);
     }
-    __syncthreads();
-    const int r = sm.result;
-    __syncthreads();
-    return r;
 }
 
-// Smallest j (index order) whose running mass exceeds target_of(total), where
-// total = sum of all masses; returns -1 when the total is zero (or does not
-// exceed the target).  *total_out receives the total.
-template <class MassFn, class TargetFn>
-__device__ int cta_inverse_cdf_total(int V, MassFn mass, TargetFn target_of, RowSmem& sm, u128* total_out) {
-    const u128 total = cta_cdf_chunks(0, V, mass, sm);
-    *total_out = total;
-    return cta_cdf_find(0, V, mass, target_of(total), sm);
+// Draw from the masses of row z over [L, H): candidates are the elements with
+// key >= tau and mass E_j > 0, minus excl[0, nex); score (z_j - m) c + G_j
+// with the uniforms of draw (seed, step, b, i, purpose) by element index (the
+// oracle's orc_draw_row).  *sum (if given) receives the candidates' mass total.
+__device__ void cta_gumbel_mass(const float* __restrict__ z, int L, int H, float m, float c, uint32_t tau,
+                                const int* excl, int nex, uint64_t seed, uint32_t step, uint32_t b, uint32_t i,
+                                uint32_t purpose, RowSmem& sm, float* out_s, int* out_j, uint64_t* sum = nullptr) {
+    float bs = -INFINITY;
+    int bj = -1;
+    uint64_t tot = 0;
+    for_each_group(z, L, H, [&](int g, const float* v, const bool* in) {
+        uint32_t e4[4];
+        bool any = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = 4 * g + e;
+            uint32_t me = (in[e] && logit_key(v[e]) >= tau) ? mass_of(v[e], m, c) : 0u;
+            for (int t = 0; t < nex; ++t)
+                if (excl[t] == j) me = 0u;
+            e4[e] = me;
+            tot += me;
+            any |= me != 0u;
+        }
+        if (!any) return;
+        uint32_t o[4];
+        gumbel_uniforms(seed, step, b, i, purpose, (uint32_t)g, o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (!e4[e]) continue;
+            const float sc = __fadd_rn(__fmul_rn(__fsub_rn(v[e], m), c), gumbel2(o[e]));
+            gumbel_merge(bs, bj, sc, 4 * g + e);
+        }
+    });
+    if (sum) *sum = block_sum<uint64_t>(tot, sm.red64);
+    cta_best(bs, bj, sm, out_s, out_j);
 }
 
-// Smallest j (index order) whose running mass exceeds `target`.
-template <class MassFn>
-__device__ int cta_inverse_cdf(int V, u128 target, MassFn mass, RowSmem& sm) {
-    u128 total;
-    return cta_inverse_cdf_total(V, mass, [target](u128) { return target; }, sm, &total);
-}
-
-__device__ int cta_sample_nucleus(const float* z, int V, float c, const DevRowStats& st, uint64_t u64, RowSmem& sm) {
-    const u128 target = (u128)mulhi64(u64, st.nuc);
-    return cta_inverse_cdf(V, target, [&](int j) -> u128 { return (u128)nucleus_mass(z, st, c, j); }, sm);
+// Draw from the residual max(0, E_p N_q - E_q N_p) of target row zp and draft
+// row zq over [L, H) (nucleus masses at their row statistics; N = nucleus
+// totals); score log2(residual) + G_j (the oracle's draw_residual).  Index -1
+// when the residual is zero everywhere in [L, H).
+__device__ void cta_gumbel_resid(const float* __restrict__ zp, float pm, uint32_t pt, uint64_t Np,
+                                 const float* __restrict__ zq, float qm, uint32_t qt, uint64_t Nq, int L, int H,
+                                 float c, uint64_t seed, uint32_t step, uint32_t b, uint32_t i, RowSmem& sm,
+                                 float* out_s, int* out_j) {
+    float bs = -INFINITY;
+    int bj = -1;
+    const bool vec = ((reinterpret_cast<uintptr_t>(zq) & 15) == 0);
+    for_each_group(zp, L, H, [&](int g, const float* vp, const bool* in) {
+        float vq[4];
+        if (vec && in[0] && in[3]) {
+            const float4 q = reinterpret_cast<const float4*>(zq)[g];
+            vq[0] = q.x;
+            vq[1] = q.y;
+            vq[2] = q.z;
+            vq[3] = q.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) vq[e] = in[e] ? zq[4 * g + e] : 0.f;
+        }
+        u128 r4[4];
+        bool any = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            r4[e] = 0;
+            if (!in[e]) continue;
+            const uint32_t ep = logit_key(vp[e]) >= pt ? mass_of(vp[e], pm, c) : 0u;
+            const uint32_t eq = logit_key(vq[e]) >= qt ? mass_of(vq[e], qm, c) : 0u;
+            const u128 x = (u128)ep * Nq, y = (u128)eq * Np;
+            if (x > y) {
+                r4[e] = x - y;
+                any = true;
+            }
+        }
+        if (!any) return;
+        uint32_t o[4];
+        gumbel_uniforms(seed, step, b, i, U_GUMBEL_RESAMPLE, (uint32_t)g, o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (!r4[e]) continue;
+            gumbel_merge(bs, bj, __fadd_rn(det_log2_u128(r4[e]), gumbel2(o[e])), 4 * g + e);
+        }
+    });
+    cta_best(bs, bj, sm, out_s, out_j);
 }
 
 // --------------------------------------------------------------- kernels
@@ -574,29 +564,20 @@ __global__ void __launch_bounds__(kRowThreads) accept_chain_kernel(const float* 
     if (greedy) {
         tok = sp[a].argmax;
     } else {
-        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)a, U_RESAMPLE);
+        // the residual max(0, p - q) on the first rejected position, the bonus
+        // token from p_k, and p itself where the residual is zero everywhere
         const float* zp = P + (size_t)a * V;
-        if (a == k) {
-            tok = cta_sample_nucleus(zp, V, c, sp[a], u64, sm);
-        } else {
-            const float* zq = Q + (size_t)a * V;
-            const DevRowStats stp = sp[a], stq = sq[a];
-            auto resid = [&](int j) -> u128 {
-                const u128 x = (u128)nucleus_mass(zp, stp, c, j) * stq.nuc;
-                const u128 y = (u128)nucleus_mass(zq, stq, c, j) * stp.nuc;
-                return x > y ? x - y : (u128)0;
-            };
-            // draw from the residual: target = U * R / 2^64 with R the total residual mass
-            u128 R = 0;
-            tok = cta_inverse_cdf_total(
-                V, resid,
-                [u64](u128 tot) {
-                    const uint64_t rh = (uint64_t)(tot >> 64), rl = (uint64_t)tot;
-                    return (u128)u64 * rh + (u128)mulhi64(u64, rl);
-                },
-                sm, &R);
-            if (R == 0) tok = cta_sample_nucleus(zp, V, c, stp, u64, sm);
+        const DevRowStats stp = sp[a];
+        float sc;
+        tok = -1;
+        if (a < k) {
+            const DevRowStats stq = sq[a];
+            cta_gumbel_resid(zp, stp.max, stp.tau, stp.nuc, Q + (size_t)a * V, stq.max, stq.tau, stq.nuc, 0, V, c, seed,
+                             step, (uint32_t)b, (uint32_t)a, sm, &sc, &tok);
         }
+        if (tok < 0)
+            cta_gumbel_mass(zp, 0, V, stp.max, c, stp.tau, nullptr, 0, seed, step, (uint32_t)b, (uint32_t)a,
+                            U_GUMBEL_RESAMPLE, sm, &sc, &tok);
     }
     if (threadIdx.x == 0) {
         int32_t* out = out_tokens + (size_t)b * (k + 1);
@@ -612,10 +593,10 @@ __global__ void __launch_bounds__(kRowThreads) accept_chain_kernel(const float* 
 // S CTAs of a cluster split every logits row of their sequence into S
 // contiguous vocabulary slices (CTA r: [r*Vs, (r+1)*Vs), Vs a multiple of 4).
 // Row arg-max and mass sums are per-slice partials merged in rank order
-// through distributed shared memory; the final draw exchanges the slices'
-// mass totals and the CTA whose slice holds the target searches it.  All
-// masses are integers, so every total, and with it every decision, is the one
-// the single-CTA kernels above take.
+// through distributed shared memory; the final draw takes every slice's
+// Gumbel-max winner and merges them (score desc, index asc).  All masses are
+// integers and the scores are per element, so every total, and with it every
+// decision, is the one the single-CTA kernels above take.
 constexpr int kAcceptClusterMaxK = 16;
 constexpr int kAcceptClusterRows = 2 * kAcceptClusterMaxK + 1;
 constexpr int kAcceptClusterMax = 8;
@@ -624,48 +605,11 @@ struct AcceptXchg {
     float pmax[kAcceptClusterRows];      // this CTA's slice partials, read by its peers
     int parg[kAcceptClusterRows];
     uint64_t psum[kAcceptClusterRows];
-    uint64_t ptot[2][2];                 // slice total of a draw (low, high words); two draws at most
     DevRowStats st[kAcceptClusterRows];  // merged statistics (identical in every CTA)
-    u128 local;                          // the draw's target, relative to the owner's slice
-    u128 total_scratch;
-    int owner;
+    float gs[2];                         // this CTA's draw winner (score, index): residual, then p
+    int gj[2];
     int a;
-    int tok;                             // the owner's result, read by rank 0
 };
-
-// Publishes this CTA's slice total t in slot `slot`; every CTA then reads the
-// S totals in rank order, forms target_of(total) and finds the slice holding
-// it.  Returns the cluster total; xs.owner (-1 if none) and xs.local are set.
-template <class TargetFn>
-__device__ u128 cluster_draw_owner(AcceptXchg& xs, int slot, u128 t, int S, TargetFn target_of) {
-    if (threadIdx.x == 0) {
-        xs.ptot[slot][0] = (uint64_t)t;
-        xs.ptot[slot][1] = (uint64_t)(t >> 64);
-    }
-    cluster_sync_all();
-    if (threadIdx.x == 0) {
-        const uint32_t a0 = s_addr(&xs.ptot[slot][0]), a1 = s_addr(&xs.ptot[slot][1]);
-        u128 total = 0;
-        for (int r = 0; r < S; ++r)
-            total += ((u128)ld_dsmem_u64(a1, (uint32_t)r) << 64) | ld_dsmem_u64(a0, (uint32_t)r);
-        const u128 target = target_of(total);
-        int owner = -1;
-        u128 pre = 0, local = 0;
-        for (int r = 0; r < S && owner < 0; ++r) {
-            const u128 tr = ((u128)ld_dsmem_u64(a1, (uint32_t)r) << 64) | ld_dsmem_u64(a0, (uint32_t)r);
-            if (pre <= target && target < pre + tr) {
-                owner = r;
-                local = target - pre;
-            }
-            pre += tr;
-        }
-        xs.owner = owner;
-        xs.local = local;
-        xs.total_scratch = total;
-    }
-    __syncthreads();
-    return xs.total_scratch;
-}
 
 __global__ void __launch_bounds__(kRowThreads) accept_chain_cluster_kernel(
     const float* __restrict__ target, const float* __restrict__ draft, const int32_t* __restrict__ drafts, int k,
@@ -751,52 +695,50 @@ __global__ void __launch_bounds__(kRowThreads) accept_chain_cluster_kernel(
             }
         }
         xs.a = a;
-        xs.tok = -1;
     }
     __syncthreads();
     const int a = xs.a;
+    int tok = -1;
     if (greedy) {
-        if (threadIdx.x == 0) xs.tok = xs.st[a].argmax;
+        tok = xs.st[a].argmax;
     } else {
-        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)a, U_RESAMPLE);
+        // every CTA draws over its slice; the slices' winners are merged in
+        // rank order (score desc, index asc) identically in every CTA
         const float* zp = P + (size_t)a * V;
         const DevRowStats stp = xs.st[a];
-        bool bonus = a == k;
-        int slot = 0;
-        if (!bonus) {
-            // the residual max(0, p - q) on the first rejected position
-            const float* zq = Q + (size_t)a * V;
+        auto merged = [&](int slot) {
+            float bs = -INFINITY;
+            int bj = -1;
+            for (int r = 0; r < S; ++r)
+                gumbel_merge(bs, bj, ld_dsmem_f32(s_addr(&xs.gs[slot]), (uint32_t)r),
+                             (int)ld_dsmem_u32(s_addr(&xs.gj[slot]), (uint32_t)r));
+            return bj;
+        };
+        float sc;
+        int j;
+        if (a < k) {
             const DevRowStats stq = own_q ? xs.st[k + 1 + a] : qstats[(size_t)b * k + a];
-            auto resid = [&](int j) -> u128 {
-                const u128 x = (u128)mass_of(zp[j], stp.max, c) * stq.nuc;
-                const u128 y = (u128)mass_of(zq[j], stq.max, c) * stp.nuc;
-                return x > y ? x - y : (u128)0;
-            };
-            const u128 R = cluster_draw_owner(xs, slot++, cta_cdf_chunks(L, H, resid, sm), S, [u64](u128 tot) {
-                const uint64_t rh = (uint64_t)(tot >> 64), rl = (uint64_t)tot;
-                return (u128)u64 * rh + (u128)mulhi64(u64, rl);
-            });
-            if (R == 0) {
-                bonus = true;  // p and q agree: draw from p
-            } else if (rank == xs.owner) {
-                const int t = cta_cdf_find(L, H, resid, xs.local, sm);
-                if (threadIdx.x == 0) xs.tok = t;
+            cta_gumbel_resid(zp, stp.max, 0u, stp.nuc, Q + (size_t)a * V, stq.max, 0u, stq.nuc, L, H, c, seed, step,
+                             (uint32_t)b, (uint32_t)a, sm, &sc, &j);
+            if (threadIdx.x == 0) {
+                xs.gs[0] = sc;
+                xs.gj[0] = j;
             }
+            cluster_sync_all();
+            tok = merged(0);
         }
-        if (bonus) {
-            auto pmass = [&](int j) -> u128 { return (u128)mass_of(zp[j], stp.max, c); };
-            (void)cluster_draw_owner(xs, slot, cta_cdf_chunks(L, H, pmass, sm), S,
-                                     [u64](u128 tot) { return (u128)mulhi64(u64, (uint64_t)tot); });
-            if (rank == xs.owner) {
-                const int t = cta_cdf_find(L, H, pmass, xs.local, sm);
-                if (threadIdx.x == 0) xs.tok = t;
+        if (tok < 0) {  // the bonus row, or p and q agree
+            cta_gumbel_mass(zp, L, H, stp.max, c, 0u, nullptr, 0, seed, step, (uint32_t)b, (uint32_t)a,
+                            U_GUMBEL_RESAMPLE, sm, &sc, &j);
+            if (threadIdx.x == 0) {
+                xs.gs[1] = sc;
+                xs.gj[1] = j;
             }
+            cluster_sync_all();
+            tok = merged(1);
         }
     }
-    cluster_sync_all();  // the owner's token is in its shared memory
     if (rank == 0 && threadIdx.x == 0) {
-        const int owner = greedy ? 0 : xs.owner;
-        const int tok = owner < 0 ? -1 : (int)ld_dsmem_u32(s_addr(&xs.tok), (uint32_t)owner);
         int32_t* out = out_tokens + (size_t)b * (k + 1);
         for (int i = 0; i < a; ++i) out[i] = D[i];
         out[a] = tok;
@@ -872,22 +814,11 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
             if (greedy) {
                 emit = st.argmax;
             } else {
-                const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)cur, U_RESAMPLE);
-                const uint64_t remaining = s_remaining;
-                const int nrem = s_nremoved;
-                if (remaining == 0) {
-                    emit = cta_sample_nucleus(z, V, c, st, u64, sm);
-                } else {
-                    const u128 tgt = (u128)mulhi64(u64, remaining);
-                    emit = cta_inverse_cdf(
-                        V, tgt,
-                        [&](int j) -> u128 {
-                            for (int t = 0; t < nrem; ++t)
-                                if (s_removed[t] == j) return (u128)0;
-                            return (u128)nucleus_mass(z, st, c, j);
-                        },
-                        sm);
-                }
+                // p without the rejected children's tokens (all of p when they cover its mass)
+                const int nrem = s_remaining ? s_nremoved : 0;
+                float sc;
+                cta_gumbel_mass(z, 0, V, st.max, c, st.tau, s_removed, nrem, seed, step, (uint32_t)b, (uint32_t)cur,
+                                U_GUMBEL_RESAMPLE, sm, &sc, &emit);
             }
             break;
         }
@@ -906,9 +837,9 @@ __global__ void __launch_bounds__(kRowThreads) accept_tree_kernel(const float* _
 }
 
 // Draft sampling: one CTA per row.  Without a nucleus the row's mass total
-// comes out of the inverse-CDF pass itself (the draw's target is a fraction
-// of that total), so a row is read twice: arg-max, then masses.  When
-// `stats` is given, the row's statistics are kept there for the acceptance.
+// comes out of the draw's pass itself, so a row is read twice: arg-max, then
+// masses and scores.  When `stats` is given, the row's statistics are kept
+// there for the acceptance.
 __global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* __restrict__ logits, int k, int V,
                                                                   float c, uint64_t tp, bool greedy, uint64_t seed,
                                                                   const uint32_t* step_dev, uint32_t step_host,
@@ -921,21 +852,19 @@ __global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* _
     const float* z = logits + (size_t)r * V;
     DevRowStats st;
     int tok;
+    float sc;
     if (!greedy && tp >= (1ull << 32)) {
         cta_row_stats(z, V, c, tp, false, sm, &st);  // max and arg-max only
-        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k), U_DRAFT);
-        const float m = st.max;
-        u128 total = 0;
-        tok = cta_inverse_cdf_total(
-            V, [&](int j) -> u128 { return (u128)mass_of(z[j], m, c); },
-            [u64](u128 tot) { return (u128)mulhi64(u64, (uint64_t)tot); }, sm, &total);
-        st.sum = st.nuc = (uint64_t)total;  // <= V * 2^31 < 2^64
+        uint64_t total = 0;  // the mass total comes out of the draw's pass
+        cta_gumbel_mass(z, 0, V, st.max, c, 0u, nullptr, 0, seed, step, (uint32_t)(r / k), (uint32_t)(r % k),
+                        U_GUMBEL_DRAFT, sm, &sc, &tok, &total);
+        st.sum = st.nuc = total;  // <= V * 2^31 < 2^64
     } else {
         cta_row_stats(z, V, c, tp, !greedy, sm, &st, whist_dyn);
         tok = st.argmax;
         if (!greedy)
-            tok = cta_sample_nucleus(z, V, c, st,
-                                     uniform_u64(seed, step, (uint32_t)(r / k), (uint32_t)(r % k), U_DRAFT), sm);
+            cta_gumbel_mass(z, 0, V, st.max, c, st.tau, nullptr, 0, seed, step, (uint32_t)(r / k),
+                            (uint32_t)(r % k), U_GUMBEL_DRAFT, sm, &sc, &tok);
     }
     if (threadIdx.x == 0) {
         out[r] = tok;
@@ -1252,121 +1181,54 @@ struct ShardRows {
     const unsigned long long* qnuc;
 };
 
-// (8) per sequence b with a = a_in[b]: the shard's residual total (a < k) and
-// nucleus total of target row a, as u128 halves out[b] = {R lo, R hi, P lo, P hi}
-__global__ void __launch_bounds__(kRowThreads) shard_draw_totals_kernel(ShardRows sr, const int32_t* __restrict__ a_in,
-                                                                        unsigned long long* __restrict__ out) {
+// (8) per sequence b with a = a_in[b]: this shard's Gumbel-max winners of the
+// draw on target row a, over the residual max(0, p - q) (a < k) and over the
+// nucleus of p, as out[b] = {residual score bits, index, p score bits, index}
+// (global indices; -1 when the shard has no candidate).  The element uniforms
+// are those of the global index, so the winners merged over the shards are
+// the draw on the whole row.
+__global__ void __launch_bounds__(kRowThreads) shard_draw_winners_kernel(ShardRows sr, const int32_t* __restrict__ a_in,
+                                                                         uint64_t seed, uint32_t step,
+                                                                         int32_t* __restrict__ out) {
     __shared__ RowSmem sm;
     const int b = blockIdx.x, a = a_in[b], k = sr.k;
     const int prow = b * (k + 1) + a;
-    const float* zp = sr.target + (size_t)prow * sr.Vs;
-    const float pm = sr.pmax[prow];
-    const uint32_t pt = sr.ptau[prow];
-    const float c = sr.c;
-    auto pmass = [&](int j) -> u128 {
-        const float v = zp[j];
-        return logit_key(v) < pt ? (u128)0 : (u128)mass_of(v, pm, c);
-    };
-    u128 R = 0;
+    // rows addressed by global vocabulary index: element j of the shard at [j - v0]
+    const float* zp = sr.target + (size_t)prow * sr.Vs - sr.v0;
+    const int L = sr.v0, H = sr.v0 + sr.Vs;
+    float rs = -INFINITY, ps = -INFINITY;
+    int rj = -1, pj = -1;
     if (a < k) {
         const int qrow = b * k + a;
-        const float* zq = sr.draft + (size_t)qrow * sr.Vs;
-        const float qm = sr.qmax[qrow];
-        const uint32_t qt = sr.qtau[qrow];
-        const uint64_t Np = sr.pnuc[prow], Nq = sr.qnuc[qrow];
-        auto resid = [&](int j) -> u128 {
-            const float w = zq[j];
-            const u128 x = pmass(j) * Nq;
-            const u128 y = (logit_key(w) < qt ? (u128)0 : (u128)mass_of(w, qm, c)) * Np;
-            return x > y ? x - y : (u128)0;
-        };
-        R = cta_cdf_chunks(0, sr.Vs, resid, sm);
+        const float* zq = sr.draft + (size_t)qrow * sr.Vs - sr.v0;
+        cta_gumbel_resid(zp, sr.pmax[prow], sr.ptau[prow], sr.pnuc[prow], zq, sr.qmax[qrow], sr.qtau[qrow],
+                         sr.qnuc[qrow], L, H, sr.c, seed, step, (uint32_t)b, (uint32_t)a, sm, &rs, &rj);
     }
-    const u128 P = cta_cdf_chunks(0, sr.Vs, pmass, sm);
+    cta_gumbel_mass(zp, L, H, sr.pmax[prow], sr.c, sr.ptau[prow], nullptr, 0, seed, step, (uint32_t)b, (uint32_t)a,
+                    U_GUMBEL_RESAMPLE, sm, &ps, &pj);
     if (threadIdx.x == 0) {
-        out[(size_t)b * 4 + 0] = (uint64_t)R;
-        out[(size_t)b * 4 + 1] = (uint64_t)(R >> 64);
-        out[(size_t)b * 4 + 2] = (uint64_t)P;
-        out[(size_t)b * 4 + 3] = (uint64_t)(P >> 64);
+        out[(size_t)b * 4 + 0] = __float_as_int(rs);
+        out[(size_t)b * 4 + 1] = rj;
+        out[(size_t)b * 4 + 2] = __float_as_int(ps);
+        out[(size_t)b * 4 + 3] = pj;
     }
 }
 
-// (9) per sequence: the draw from the gathered totals ([W][B][4]).  The
-// residual when a < k and its total is nonzero, else target row a's nucleus;
-// the rank whose shard holds the target (ranks in vocabulary order) searches
-// it, the others write -1.
-__global__ void __launch_bounds__(kRowThreads) shard_draw_kernel(ShardRows sr, const int32_t* __restrict__ a_in,
-                                                                 const unsigned long long* __restrict__ gtot, int W,
-                                                                 int rank, int B, uint64_t seed, uint32_t step,
-                                                                 int32_t* __restrict__ tok_out) {
-    __shared__ RowSmem sm;
-    __shared__ int s_owner, s_mode;
-    __shared__ u128 s_local;
-    const int b = blockIdx.x, a = a_in[b], k = sr.k;
-    const int prow = b * (k + 1) + a;
-    if (threadIdx.x == 0) {
-        const uint64_t u64 = uniform_u64(seed, step, (uint32_t)b, (uint32_t)a, U_RESAMPLE);
-        auto tot = [&](int w, int which) -> u128 {
-            const unsigned long long* t = gtot + ((size_t)w * B + b) * 4 + 2 * which;
-            return ((u128)t[1] << 64) | t[0];
-        };
-        u128 R = 0;
-        for (int w = 0; w < W; ++w) R += tot(w, 0);
-        const int mode = (a < k && R != 0) ? 0 : 1;
-        u128 target;
-        if (mode == 0) {
-            const uint64_t rh = (uint64_t)(R >> 64), rl = (uint64_t)R;
-            target = (u128)u64 * rh + (u128)mulhi64(u64, rl);
-        } else {
-            target = (u128)mulhi64(u64, sr.pnuc[prow]);
-        }
-        int owner = -1;
-        u128 pre = 0, local = 0;
-        for (int w = 0; w < W && owner < 0; ++w) {
-            const u128 tw = tot(w, mode);
-            if (pre <= target && target < pre + tw) {
-                owner = w;
-                local = target - pre;
-            }
-            pre += tw;
-        }
-        s_owner = owner;
-        s_mode = mode;
-        s_local = local;
+// (9) per sequence: the gathered winners ([W][B][4]) merged in rank order
+// (score desc, index asc): the residual's when a < k and it has a candidate
+// anywhere, else p's.
+__global__ void shard_draw_merge_kernel(const int32_t* __restrict__ gwin, int W, int B, int k,
+                                        const int32_t* __restrict__ a_in, int32_t* __restrict__ tok_out) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    float rs = -INFINITY, ps = -INFINITY;
+    int rj = -1, pj = -1;
+    for (int w = 0; w < W; ++w) {
+        const int32_t* g = gwin + ((size_t)w * B + b) * 4;
+        gumbel_merge(rs, rj, __int_as_float(g[0]), g[1]);
+        gumbel_merge(ps, pj, __int_as_float(g[2]), g[3]);
     }
-    __syncthreads();
-    int tok = -1;
-    if (s_owner == rank) {
-        const float* zp = sr.target + (size_t)prow * sr.Vs;
-        const float pm = sr.pmax[prow];
-        const uint32_t pt = sr.ptau[prow];
-        const float c = sr.c;
-        auto pmass = [&](int j) -> u128 {
-            const float v = zp[j];
-            return logit_key(v) < pt ? (u128)0 : (u128)mass_of(v, pm, c);
-        };
-        int j;
-        if (s_mode == 0) {
-            const int qrow = b * k + a;
-            const float* zq = sr.draft + (size_t)qrow * sr.Vs;
-            const float qm = sr.qmax[qrow];
-            const uint32_t qt = sr.qtau[qrow];
-            const uint64_t Np = sr.pnuc[prow], Nq = sr.qnuc[qrow];
-            auto resid = [&](int jj) -> u128 {
-                const float w = zq[jj];
-                const u128 x = pmass(jj) * Nq;
-                const u128 y = (logit_key(w) < qt ? (u128)0 : (u128)mass_of(w, qm, c)) * Np;
-                return x > y ? x - y : (u128)0;
-            };
-            (void)cta_cdf_chunks(0, sr.Vs, resid, sm);
-            j = cta_cdf_find(0, sr.Vs, resid, s_local, sm);
-        } else {
-            (void)cta_cdf_chunks(0, sr.Vs, pmass, sm);
-            j = cta_cdf_find(0, sr.Vs, pmass, s_local, sm);
-        }
-        tok = j < 0 ? -1 : j + sr.v0;
-    }
-    if (threadIdx.x == 0) tok_out[b] = tok;
+    tok_out[b] = (a_in[b] < k && rj >= 0) ? rj : pj;
 }
 
 // ------------------------------------------------------------ host side
@@ -1746,37 +1608,29 @@ static ShardRows shard_rows(const float* target, const float* draft, int k, int 
     return sr;
 }
 
-extern "C" int specdec_shard_draw_totals(const float* target, const float* draft, int B, int k, int Vs,
-                                         float temperature, const int32_t* accepted, const float* pmax,
+extern "C" int specdec_shard_draw_winners(const float* target, const float* draft, int B, int k, int Vs, int v0,
+                                         const specdec_sampling* sp, const int32_t* accepted, const float* pmax,
                                          const uint32_t* ptau, const float* qmax, const uint32_t* qtau,
-                                         const uint64_t* pnuc, const uint64_t* qnuc, uint64_t* out_tot,
-                                         void* stream) {
-    if (int rc = shard_check(B, Vs, "shard_draw_totals")) return rc;
-    SD_CHECK(target && draft && accepted && pmax && ptau && qmax && qtau && pnuc && qnuc && out_tot && k >= 1 &&
-                 temperature > 0.0f,
-             SPECDEC_EINVAL, "shard_draw_totals: bad argument");
+                                         const uint64_t* pnuc, const uint64_t* qnuc, int32_t* out_win, void* stream) {
+    if (int rc = shard_check(B, Vs, "shard_draw_winners")) return rc;
+    SD_CHECK(target && draft && sp && accepted && pmax && ptau && qmax && qtau && pnuc && qnuc && out_win && k >= 1 &&
+                 v0 >= 0 && sp->temperature > 0.0f,
+             SPECDEC_EINVAL, "shard_draw_winners: bad argument");
     if (B == 0) return SPECDEC_OK;
-    shard_draw_totals_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
-        shard_rows(target, draft, k, Vs, 0, temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted,
-        reinterpret_cast<unsigned long long*>(out_tot));
-    SD_LAUNCH_CHECK("shard_draw_totals_kernel");
+    shard_draw_winners_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
+        shard_rows(target, draft, k, Vs, v0, sp->temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted, sp->seed,
+        sp->step, out_win);
+    SD_LAUNCH_CHECK("shard_draw_winners_kernel");
     return SPECDEC_OK;
 }
 
-extern "C" int specdec_shard_draw(const float* target, const float* draft, int B, int k, int Vs, int v0,
-                                  const specdec_sampling* sp, const int32_t* accepted, const float* pmax,
-                                  const uint32_t* ptau, const float* qmax, const uint32_t* qtau, const uint64_t* pnuc,
-                                  const uint64_t* qnuc, const uint64_t* gtot, int W, int rank, int32_t* tok_out,
-                                  void* stream) {
-    if (int rc = shard_check(B, Vs, "shard_draw")) return rc;
-    SD_CHECK(target && draft && sp && accepted && pmax && ptau && qmax && qtau && pnuc && qnuc && gtot && tok_out &&
-                 k >= 1 && W >= 1 && rank >= 0 && rank < W && sp->temperature > 0.0f,
-             SPECDEC_EINVAL, "shard_draw: bad argument");
+extern "C" int specdec_shard_draw_merge(const int32_t* gwin, int W, int B, int k, const int32_t* accepted,
+                                        int32_t* tok_out, void* stream) {
+    SD_CHECK(gwin && accepted && tok_out && W >= 1 && B >= 0 && k >= 0, SPECDEC_EINVAL,
+             "shard_draw_merge: bad argument");
     if (B == 0) return SPECDEC_OK;
-    shard_draw_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
-        shard_rows(target, draft, k, Vs, v0, sp->temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted,
-        reinterpret_cast<const unsigned long long*>(gtot), W, rank, B, sp->seed, sp->step, tok_out);
-    SD_LAUNCH_CHECK("shard_draw_kernel");
+    shard_draw_merge_kernel<<<(B + 127) / 128, 128, 0, as_stream(stream)>>>(gwin, W, B, k, accepted, tok_out);
+    SD_LAUNCH_CHECK("shard_draw_merge_kernel");
     return SPECDEC_OK;
 }
 

@@ -88,14 +88,15 @@ _SIGS = {
     "specdec_shard_select_digit": (I, [P, I, I, P, F, P, P, P, P]),
     "specdec_shard_point_mass": (I, [P, P, P, I, I, I, I, F, P, P, P, P, P, P, P]),
     "specdec_shard_accept_test": (I, [P, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P]),
-    "specdec_shard_draw_totals": (I, [P, P, I, I, I, F, P, P, P, P, P, P, P, P, P]),
-    "specdec_shard_draw": (I, [P, P, I, I, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P, P, I, I, P, P]),
+    "specdec_shard_draw_winners": (I, [P, P, I, I, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P, P, P]),
+    "specdec_shard_draw_merge": (I, [P, I, I, I, P, P, P]),
     "specdec_w4_tiled_bytes": (SZ, [I, I]),
     "specdec_w4_tile": (I, [P, P, I, I, P, P]),
     "specdec_w4_untile": (I, [P, I, I, P, P, P]),
     "specdec_w4a16_workspace_bytes": (SZ, [I, I, I]),
     "specdec_w4a16_gemm": (I, [P, I, I, P, I, I, P, I, I, P, SZ, P]),
     "specdec_w4a16_gemm_swiglu": (I, [P, I, I, P, I, I, P, I, P]),
+    "specdec_w4a16_gemv": (I, [P, I, I, P, I, I, P, I, I, P]),
     "specdec_w4a16_plan": (I, [I, I, I, I, P]),
     "specdec_w4a16_gemm_with_plan": (I, [P, I, I, P, I, I, P, I, I, I, I, P]),
     "specdec_w4a16_gemm_simt": (I, [P, I, I, P, I, I, P, I, I, P]),
@@ -126,7 +127,7 @@ _SIGS = {
     "specdec_engine_write": (I, [P, C.c_char_p, P, SZ]),
     "specdec_engine_info": (I, [P, C.c_char_p, C.POINTER(C.c_int64)]),
     "specdec_engine_profile": (I, [P, I, P]),
-    "specdec_engine_verify_ms": (I, [P, C.POINTER(F)]),
+    "specdec_engine_step_verify_timed": (I, [P, C.POINTER(F)]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(_lib, _name)
@@ -423,10 +424,11 @@ class Engine:
         keys = ("gemm_verify", "attention", "gemm_draft", "accept", "other", "step", "verify_gemm_launches")
         return {k: float(v) for k, v in zip(keys, out)}
 
-    def verify_ms(self) -> float:
-        """Device ms of the last step's verify forward (graph event nodes)."""
+    def step_verify_timed(self) -> float:
+        """One step (a graph with global-timer stamps around the verify
+        forward); returns the verify forward's device ms."""
         v = F(0.0)
-        check(_lib.specdec_engine_verify_ms(self._h, C.byref(v)))
+        check(_lib.specdec_engine_step_verify_timed(self._h, C.byref(v)))
         return float(v.value)
 
     def write(self, what: str, arr):

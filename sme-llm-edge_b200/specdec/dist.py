@@ -203,14 +203,12 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
         ep, eq = pq[0].contiguous(), pq[1].contiguous()
         S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), p(pnuc), p(qnuc), p(ep),
                                             p(eq), p(acc), st))
-        tot = torch.empty((B, 4), dtype=torch.int64, device=dev)
-        S.check(L.specdec_shard_draw_totals(p(target), p(draft), B, k, Vs, T, p(acc), p(pmax), p(ptau), p(qmax),
-                                            p(qtau), p(pnuc), p(qnuc), p(tot), st))
-        gtot = comm.all_gather(tot)
+        win = torch.empty((B, 4), dtype=torch.int32, device=dev)
+        S.check(L.specdec_shard_draw_winners(p(target), p(draft), B, k, Vs, v0, C.byref(sampling), p(acc), p(pmax),
+                                             p(ptau), p(qmax), p(qtau), p(pnuc), p(qnuc), p(win), st))
+        gwin = comm.all_gather(win).contiguous()
         tok = torch.empty(B, dtype=torch.int32, device=dev)
-        S.check(L.specdec_shard_draw(p(target), p(draft), B, k, Vs, v0, C.byref(sampling), p(acc), p(pmax), p(ptau),
-                                     p(qmax), p(qtau), p(pnuc), p(qnuc), p(gtot), W, rank, p(tok), st))
-        comm.all_reduce_max(tok)
+        S.check(L.specdec_shard_draw_merge(p(gwin), W, B, k, p(acc), p(tok), st))
     idx = torch.arange(k + 1, device=dev)[None, :]
     a = acc.long()[:, None]
     ext = torch.cat([drafts, torch.full((B, 1), -1, dtype=torch.int32, device=dev)], 1)

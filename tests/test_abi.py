@@ -47,6 +47,11 @@ def test_invalid_arguments_fail_loudly_without_gpu():
     assert rc == specdec.EINVAL and "bad argument" in specdec.last_error()
     h = C.c_void_p()
     assert specdec.lib().specdec_kv_create(0, 16, 1, 1, C.byref(h)) == specdec.EINVAL
+    # the few-row contraction takes 0..64 rows and modes 0 / 1 only
+    x = C.c_void_p(16)
+    assert specdec.lib().specdec_w4a16_gemv(x, 65, 128, x, 128, 128, x, 128, 0, None) == specdec.EINVAL
+    assert specdec.lib().specdec_w4a16_gemv(x, 4, 128, x, 128, 128, x, 128, 2, None) == specdec.EINVAL
+    assert "0 <= M <= 64" in specdec.last_error()
 
 
 def test_gemm_plan_is_consistent():
@@ -88,10 +93,11 @@ def test_shard_steps_reject_bad_arguments_without_gpu():
     assert L.specdec_shard_row_mass(dummy, 4, None, 0, 262145, dummy, 0.7, dummy, None) == specdec.EINVAL
     # draft rows announced without a pointer
     assert L.specdec_shard_digit_hist(dummy, 4, None, 3, 128, dummy, 0.7, None, 3, dummy, None) == specdec.EINVAL
-    # digits other than 0..3, and a rank outside the world
+    # digits other than 0..3, a draft length of 0, and an empty world
     assert L.specdec_shard_select_digit(dummy, 4, 4, dummy, 0.9, dummy, dummy, dummy, None) == specdec.EINVAL
-    assert L.specdec_shard_draw(dummy, dummy, 2, 3, 128, 0, C.byref(sp), dummy, dummy, dummy, dummy, dummy, dummy,
-                                dummy, dummy, 2, 2, dummy, None) == specdec.EINVAL
+    assert L.specdec_shard_draw_winners(dummy, dummy, 2, 0, 128, 0, C.byref(sp), dummy, dummy, dummy, dummy, dummy,
+                                        dummy, dummy, dummy, None) == specdec.EINVAL
+    assert L.specdec_shard_draw_merge(dummy, 0, 2, 3, dummy, dummy, None) == specdec.EINVAL
     # the mass steps need a temperature
     assert L.specdec_shard_point_mass(dummy, dummy, dummy, 2, 3, 128, 0, 0.0, dummy, dummy, dummy, dummy, dummy,
                                       dummy, None) == specdec.EINVAL

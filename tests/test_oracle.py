@@ -61,19 +61,56 @@ def test_row_stats_nucleus_mass_threshold():
 
 
 def test_sampling_distribution_matches_softmax():
+    """Gumbel-max draws (one per step) follow softmax(z / T)."""
     rng = np.random.default_rng(5)
     V = 12
     z = rng.standard_normal(V).astype(np.float32)
-    st = O.row_stats(z, 1.0, 1.0)
-    L = O.lib()
     n = 20000
     counts = np.zeros(V)
     for s in range(n):
-        u = L.orc_uniform_u64(11, s, 0, 0, 2)
-        counts[L.orc_sample_row(O.ptr(z), V, O.temp_coeff(1.0), C.byref(st), u)] += 1
+        counts[O.draw_row(z, 1.0, 1.0, 11, s, 0, 0)] += 1
     p = np.exp(z - z.max())
     p /= p.sum()
     assert np.abs(counts / n - p).max() < 0.015
+
+
+def test_gumbel_draw_is_the_argmax_of_the_scores():
+    """orc_draw_row = arg-max over the nucleus of (z_j - max) * c + G_j, with
+    G_j = -log2(-log2 U_j) from the draw's own element uniforms; excluded
+    tokens never win, ties go to the lower index."""
+    rng = np.random.default_rng(8)
+    V, T, tp = 300, 0.7, 0.9
+    z = (rng.standard_normal(V) * 2).astype(np.float32)
+    st = O.row_stats(z, T, tp)
+    c = O.temp_coeff(T)
+    L = O.lib()
+    for step in range(5):
+        best, bs = -1, None
+        for j in range(V):
+            if not L.orc_row_mass(O.ptr(z), C.byref(st), c, j) or j in (3, 17):
+                continue
+            t = float(np.float32(np.float32(z[j] - np.float32(st.max)) * np.float32(c)))
+            sc = L.orc_gumbel_score(t, L.orc_gumbel_uniform(9, step, 2, 1, O.U_GUMBEL_DRAFT, j))
+            if best < 0 or sc > bs:
+                best, bs = j, sc
+        assert O.draw_row(z, T, tp, 9, step, 2, 1, exclude=[3, 17]) == best
+
+
+def test_det_log2_and_uniform_transform_accuracy():
+    """The atanh-series log2 against float64 log2, and -log2 U across the
+    whole 32-bit range (including both ends and the switch at U = 1/2)."""
+    L = O.lib()
+    xs = np.concatenate([np.geomspace(2.0 ** -126, 2.0 ** 127, 2000), np.linspace(0.5, 2.0, 2001)]).astype(np.float32)
+    for x in xs:
+        got = L.orc_det_log2(float(x))
+        ref = np.log2(np.float64(x))
+        assert abs(got - ref) <= 2e-7 * max(1.0, abs(ref)), (x, got, ref)
+    us = [0, 1, 2, 12345, 2**31 - 1, 2**31, 2**31 + 1, 3 * 2**30, 2**32 - 2, 2**32 - 1]
+    us += [int(v) for v in np.random.default_rng(1).integers(0, 2**32, 2000, dtype=np.uint64)]
+    for u in us:
+        got = L.orc_neg_log2_uniform(u)
+        ref = -np.log2((np.float64(u) + 0.5) / 2.0 ** 32)
+        assert abs(got - ref) <= 4e-7 * ref + 1e-12, (u, got, ref)  # relative: tiny values keep their precision
 
 
 # --------------------------------------------------- acceptance semantics
@@ -106,8 +143,7 @@ def test_rejection_sampling_acceptance_rate():
     n = 4000
     tgt = np.broadcast_to(np.stack([zp, zp]), (n, 2, V)).copy()
     dr = np.broadcast_to(zq, (n, 1, V)).copy()
-    drafts = np.array([[O.lib().orc_sample_row(O.ptr(zq), V, O.temp_coeff(T), C.byref(O.row_stats(zq, T)),
-                                               O.lib().orc_uniform_u64(1, 0, b, 0, 0))] for b in range(n)], np.int32)
+    drafts = np.array([[O.draw_row(zq, T, 1.0, 1, 0, b, 0)] for b in range(n)], np.int32)
     acc, out = O.accept_chain(tgt, dr, drafts, T, 1.0, 77, 0)
     assert abs(acc.mean() - np.minimum(p, q).sum()) < 0.03
     # the emitted first token is distributed as p (speculative sampling is lossless)

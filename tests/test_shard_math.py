@@ -1,8 +1,8 @@
 """CPU check that the vocabulary-sharded acceptance loses nothing: row
 statistics assembled from per-shard partials -- the rank-order arg-max
 merge, integer mass sums, the top-p threshold from summed per-shard digit
-histograms, and the draw by the rank whose shard holds the target -- equal
-the oracle's statistics and draw on the whole row.  These are the
+histograms, and the Gumbel-max draw as the best of the shards' local
+winners -- equal the oracle's statistics and draw on the whole row.  These are the
 combinations specdec.dist.accept_chain_vocab_sharded performs between the
 specdec_shard_* steps; the device kernels themselves are checked against
 the oracle in the GPU tests."""
@@ -78,18 +78,21 @@ def test_shard_partials_rebuild_the_row(W, V, T, tp, seed):
         tau, nuc = prefix, G + last
     else:
         tau, nuc = 0, sum(sums)
-    # 4. the nucleus draw by the owner of the target
-    En = np.where(key >= np.uint64(tau), E, np.uint64(0))
-    P = [int(En[v0:v0 + vs].sum()) for v0, vs in shards]
-    for u64 in [int(x) for x in rng.integers(0, 2**63, 8, dtype=np.int64)] + [2**64 - 1, 0]:
-        target = (u64 * nuc) >> 64
-        pre, tok = 0, -1
-        for (v0, vs), pw in zip(shards, P):
-            if pre <= target < pre + pw:
-                run = np.cumsum(En[v0:v0 + vs].astype(object))
-                tok = v0 + int(np.argmax(run > target - pre))
-                break
-            pre += pw
-        st = O.row_stats(z, T, tp)
-        zc = np.ascontiguousarray(z)
-        assert tok == O.lib().orc_sample_row(O.ptr(zc), V, O.temp_coeff(T), C.byref(st), u64), u64
+    # 4. the draw: each shard's best (score, index) over its slice, merged
+    #    (score desc, index asc); the uniforms are those of the global index
+    c = O.temp_coeff(T)
+    L = O.lib()
+    for step in range(6):
+        best, bs = -1, None
+        for v0, vs in shards:
+            lb, ls = -1, None
+            for j in range(v0, v0 + vs):
+                if key[j] < tau or E[j] == 0:
+                    continue
+                t = float(np.float32(np.float32(z[j] - np.float32(best_v)) * np.float32(c)))
+                sc = L.orc_gumbel_score(t, L.orc_gumbel_uniform(seed, step, 1, 2, O.U_GUMBEL_RESAMPLE, j))
+                if lb < 0 or sc > ls:
+                    lb, ls = j, sc
+            if lb >= 0 and (best < 0 or ls > bs or (ls == bs and lb < best)):
+                best, bs = lb, ls
+        assert best == O.draw_row(z, T, tp, seed, step, 1, 2, O.U_GUMBEL_RESAMPLE), step
