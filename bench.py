@@ -527,10 +527,11 @@ def run_kernel(args):
             rot["i"] += 1
             return ptr(tiled[rot["i"] % copies])
 
-        if args.kernel == "gemm_tc":  # the tcgen05 tiles on the planner's plan, whatever M
+        if args.kernel == "gemm_tc":  # the tcgen05 tiles on the planner's plan (or --plan), whatever M
             plan = (C.c_int32 * 4)()
             S.check(L.specdec_w4a16_plan(M, N, K, 0, plan))
-            qn, split = int(plan[1]), int(plan[2])
+            qn, split = (int(plan[1]), int(plan[2])) if not args.plan else (int(x) for x in args.plan.split(","))
+            args.shape += f" plan {qn},{split}"
             call = lambda: L.specdec_w4a16_gemm_with_plan(ptr(X), M, K, wnext(), N, K, ptr(Y), N, 0,  # noqa: E731
                                                           qn, split, cur())
         elif args.kernel == "gemv":
@@ -564,12 +565,13 @@ def run_kernel(args):
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(args.steps):
             S.check(call())
-    graph.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    graph.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) / args.steps * 1e3
     res = {"kernel": args.kernel, "shape": args.shape, "us_per_launch": round(us, 2),
@@ -659,6 +661,7 @@ def main():
     ap.add_argument("--kernel", choices=["gemm", "gemm_tc", "gemv", "attention", "accept"],
                     help="time one hot kernel instead of the step (gemm: as the planner routes it; gemm_tc: the "
                          "tcgen05 tiles; gemv: the few-row kernel)")
+    ap.add_argument("--plan", default="", help="--kernel gemm_tc: units per CTA and k split, e.g. 2,8")
     ap.add_argument("--shape", default="160,128256,4096",
                     help="--kernel shape: M,N,K (gemm), B,R,Hq,Hkv,hd,ctx (attention) or B,k,V,T,top_p (accept)")
     args = ap.parse_args()

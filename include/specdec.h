@@ -134,9 +134,11 @@ int specdec_accept_chain(const float* target, const float* draft, const int32_t*
  * its whole memory budget up front, or a host program that owns the GPU
  * allocator).  No counterpart exists in the reference.  The row statistics
  * live in a fixed array compiled into the library: 8192 rows of 32 bytes
- * (256 KB on every GPU that loads the library, held until exit), so
- * B*(k+1) + B*k must not exceed 8192 (B*(k+1) when greedy); larger calls fail
- * with SPECDEC_EINVAL.  The first call on a device looks up the array's
+ * (256 KB on every GPU that loads the library, held until exit).  Where that
+ * array is used -- sampling with top_p < 1, or more than 16 drafts -- B*(k+1)
+ * + B*k must not exceed 8192 (B*(k+1) when greedy); larger calls fail with
+ * SPECDEC_EINVAL.  Greedy and top_p = 1 acceptance with at most 16 drafts
+ * needs no row scratch and takes any batch.  The first call on a device looks up the array's
  * address with that device current and should come before any stream
  * capture.  All calls share the array: calls whose kernels overlap on the
  * GPU race.  No cudaMalloc, cudaFree or allocating library routine is used. */

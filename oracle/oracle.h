@@ -72,18 +72,18 @@ typedef struct {
 void orc_row_stats_compute(const float* z, int V, float c, uint64_t top_p_q32, orc_row_stats* st);
 /* E of token x under the row statistics (0 outside the nucleus). */
 uint32_t orc_row_mass(const float* z, const orc_row_stats* st, float c, int x);
-/* Gumbel-max draw from the nucleus distribution (weights E_j) of row z with
+/* Draw (exponential race) from the nucleus distribution (weights E_j) of row z with
  * the element uniforms of draw (seed, step, b, i, purpose), the tokens
  * excl[0 .. n_excl) left out; -1 when no token has weight.  See
  * orc_sample.c for the arithmetic. */
 int orc_draw_row(const float* z, int V, float c, const orc_row_stats* st, uint64_t seed, uint32_t step, uint32_t b,
                  uint32_t i, uint32_t purpose, const int32_t* excl, int n_excl);
 /* The pieces: log2 by the atanh series, -log2 of a Philox uniform, the
- * uniform of element j of a draw, and a candidate's score. */
+ * uniform of element j of a draw, and a candidate's race key w / (-log2 U). */
 float orc_det_log2(float x);
 float orc_neg_log2_uniform(uint32_t x);
 uint32_t orc_gumbel_uniform(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose, uint32_t j);
-float orc_gumbel_score(float log2w, uint32_t u);
+float orc_race_key(float w, uint32_t u);
 /* Lowest index of the maximum (NaN never wins); -1 if V == 0. */
 int orc_argmax(const float* z, int V);
 /* Maximum and the second maximum (value of the best other index). */

@@ -73,7 +73,7 @@ def _declare(L):
         "orc_det_log2": (F, [F]),
         "orc_neg_log2_uniform": (F, [U32]),
         "orc_gumbel_uniform": (U32, [U64, U32, U32, U32, U32, U32]),
-        "orc_gumbel_score": (F, [F, U32]),
+        "orc_race_key": (F, [F, U32]),
         "orc_argmax": (I, [P, I]),
         "orc_topk": (None, [P, I, I, P]),
         "orc_uniform_u32": (U32, [U64, U32, U32, U32, U32]),
@@ -137,7 +137,7 @@ U_ACCEPT, U_GUMBEL_DRAFT, U_GUMBEL_RESAMPLE = 1, 3, 4
 
 
 def draw_row(z, temperature, top_p, seed, step, b, i, purpose=U_GUMBEL_DRAFT, exclude=()):
-    """Gumbel-max draw from the nucleus distribution of row z (orc_draw_row)."""
+    """Draw (exponential race) from the nucleus distribution of row z (orc_draw_row)."""
     z = np.ascontiguousarray(z, dtype=np.float32)
     st = row_stats(z, temperature, top_p)
     ex = np.ascontiguousarray(exclude, dtype=np.int32) if len(exclude) else None

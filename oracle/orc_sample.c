@@ -156,13 +156,14 @@ uint32_t orc_row_mass(const float* z, const orc_row_stats* st, float c, int x) {
 
 static inline uint64_t mulhi64(uint64_t a, uint64_t b) { return (uint64_t)(((u128)a * b) >> 64); }
 
-/* ---------------------------------------------------- Gumbel-max draws
+/* ---------------------------------------------------- draws
  * A token is drawn with probability proportional to its integer weight w_j
  * (the row mass E_j, or the residual max(0, E_p S_q - E_q S_p)) as the
- * arg-max of log2(w_j) - log2(-log2 U_j), U_j from Philox per element
- * (ctr = {b, i, (j / 4) << 4 | purpose, step}, word j % 4).  For row masses
- * log2(E_j) is replaced by (z_j - max) * c, the exponent E_j was formed from
- * (equal up to the floor of E_j, below 2^-31 of the row maximum's mass).
+ * arg-max of the race key w_j / (-log2 U_j) (U_j from Philox per element,
+ * ctr = {b, i, (j / 4) << 4 | purpose, step}, word j % 4): -log2 U is
+ * exponential, and the smallest of exponentials scaled by 1 / w_j falls on j
+ * with probability w_j / sum(w) (the exponential race, equivalent to the
+ * Gumbel-max trick).  Ties go to the lower index.
  * log2 by the atanh series ln x = 2 atanh((x - 1) / (x + 1)) on the mantissa
  * in [sqrt(1/2), sqrt(2)), five terms; -log2 U above one half through the
  * complement w = 1 - U, ln(1 / (1 - w)) = 2 atanh(w / (2 - w)), eight terms.
@@ -214,15 +215,11 @@ float orc_neg_log2_uniform(uint32_t x) {
     p = fmaf(p, s2, 1.0f);
     return (s * p) * 0x1.715476p+1f;
 }
-static float gumbel2(uint32_t x) { return -orc_det_log2(orc_neg_log2_uniform(x)); }
-static float det_log2_u128(u128 w) {
-    uint64_t hi = (uint64_t)(w >> 64), v = (uint64_t)w;
-    int sh = 0;
-    if (hi) {
-        sh = 64 - __builtin_clzll(hi);
-        v = (uint64_t)(w >> sh);
-    }
-    return orc_det_log2((float)v) + (float)sh;
+static float u128_to_f32(u128 w) {
+    uint64_t hi = (uint64_t)(w >> 64);
+    if (!hi) return (float)(uint64_t)w;
+    int sh = 64 - __builtin_clzll(hi);
+    return (float)(uint64_t)(w >> sh) * from_bits((uint32_t)(127 + sh) << 23);
 }
 uint32_t orc_gumbel_uniform(uint64_t seed, uint32_t step, uint32_t b, uint32_t i, uint32_t purpose, uint32_t j) {
     uint32_t ctr[4] = {b, i, ((j >> 2) << 4) | purpose, step}, key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)},
@@ -230,18 +227,19 @@ uint32_t orc_gumbel_uniform(uint64_t seed, uint32_t step, uint32_t b, uint32_t i
     orc_philox4x32_10(ctr, key, o);
     return o[j & 3];
 }
-float orc_gumbel_score(float log2w, uint32_t u) { return log2w + gumbel2(u); }
+float orc_race_key(float w, uint32_t u) { return w / orc_neg_log2_uniform(u); }
 
 int orc_draw_row(const float* z, int V, float c, const orc_row_stats* st, uint64_t seed, uint32_t step, uint32_t b,
                  uint32_t i, uint32_t purpose, const int32_t* excl, int n_excl) {
     int best = -1;
     float bs = 0.0f;
     for (int j = 0; j < V; ++j) {
-        if (!orc_row_mass(z, st, c, j)) continue;
+        uint32_t e = orc_row_mass(z, st, c, j);
+        if (!e) continue;
         int ex = 0;
         for (int t = 0; t < n_excl; ++t) ex |= excl[t] == j;
         if (ex) continue;
-        float sc = orc_gumbel_score((z[j] - st->max) * c, orc_gumbel_uniform(seed, step, b, i, purpose, (uint32_t)j));
+        float sc = orc_race_key((float)e, orc_gumbel_uniform(seed, step, b, i, purpose, (uint32_t)j));
         if (best < 0 || sc > bs) {
             bs = sc;
             best = j;
@@ -300,8 +298,8 @@ static int draw_residual(const float* zp, const orc_row_stats* sp, const float* 
         u128 a = (u128)orc_row_mass(zp, sp, c, j) * sq->nuc;
         u128 q = (u128)orc_row_mass(zq, sq, c, j) * sp->nuc;
         if (a <= q) continue;
-        float sc = orc_gumbel_score(det_log2_u128(a - q),
-                                    orc_gumbel_uniform(seed, step, b, i, ORC_U_GUMBEL_RESAMPLE, (uint32_t)j));
+        float sc = orc_race_key(u128_to_f32(a - q), orc_gumbel_uniform(seed, step, b, i, ORC_U_GUMBEL_RESAMPLE,
+                                                                         (uint32_t)j));
         if (best < 0 || sc > bs) {
             bs = sc;
             best = j;

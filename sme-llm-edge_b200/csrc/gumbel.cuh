@@ -4,12 +4,15 @@
 //
 // A token is drawn with probability proportional to a weight w_j (an integer
 // mass: E_j of the row, or the residual max(0, E_p S_q - E_q S_p)) as the
-// arg-max over j of  log2(w_j) - log2(-log2(U_j)),  U_j uniform in (0, 1) from
-// Philox4x32-10 per element (Gumbel, 1954; the Gumbel-max trick: Yellott 1977,
-// Maddison et al. 2014).  Unlike an inverse-CDF search over the running mass,
-// whose result moves when any earlier mass moves, the arg-max changes only when
-// two candidates' scores come within the logits' error of each other: the
-// top-2 margin rule of the arg-max decisions carries over to sampled ones.
+// arg-max over j of the key  w_j / (-log2 U_j),  U_j uniform in (0, 1) from
+// Philox4x32-10 per element: -log2 U_j is exponentially distributed, and the
+// smallest of independent exponentials scaled by 1 / w_j falls on j with
+// probability w_j / sum(w) (the exponential race; equivalently the Gumbel-max
+// trick on log2 w_j - log2(-log2 U_j): Gumbel 1954, Yellott 1977, Maddison et
+// al. 2014).  Unlike an inverse-CDF search over the running mass, whose
+// result moves when any earlier mass moves, the arg-max changes only when two
+// candidates' keys come within the logits' error of each other: the top-2
+// margin rule of the arg-max decisions carries over to sampled ones.
 //
 // Arithmetic: log2 by the atanh series of the logarithm,
 //   ln x = 2 atanh((x - 1) / (x + 1)),  atanh s = s + s^3/3 + s^5/5 + ...,
@@ -68,19 +71,16 @@ __device__ __forceinline__ float neg_log2_uniform(uint32_t x) {
     return __fmul_rn(__fmul_rn(s, p), 0x1.715476p+1f);
 }
 
-// The Gumbel term -log2(-log2 U) of a draw.
-__device__ __forceinline__ float gumbel2(uint32_t x) { return -det_log2(neg_log2_uniform(x)); }
+// The key of a candidate of weight w (a float of the weight) in a draw.
+__device__ __forceinline__ float race_key(float w, uint32_t x) { return __fdiv_rn(w, neg_log2_uniform(x)); }
 
-// log2 of an integer weight: the top 64 bits converted to fp32, plus the shift.
-__device__ __forceinline__ float det_log2_u128(u128 w) {
+// An integer weight as fp32: its top 64 bits converted (round to nearest),
+// scaled back by the exact power of two.
+__device__ __forceinline__ float u128_to_f32(u128 w) {
     const uint64_t hi = (uint64_t)(w >> 64);
-    int sh = 0;
-    uint64_t v = (uint64_t)w;
-    if (hi) {
-        sh = 64 - __clzll((long long)hi);
-        v = (uint64_t)(w >> sh);
-    }
-    return __fadd_rn(det_log2(__ull2float_rn(v)), (float)sh);
+    if (!hi) return __ull2float_rn((uint64_t)w);
+    const int sh = 64 - __clzll((long long)hi);
+    return __fmul_rn(__ull2float_rn((uint64_t)(w >> sh)), __uint_as_float((uint32_t)(127 + sh) << 23));
 }
 
 // Uniforms of elements 4*j4 .. 4*j4 + 3 of draw (b, i, purpose) at `step`.
@@ -89,7 +89,7 @@ __device__ __forceinline__ void gumbel_uniforms(uint64_t seed, uint32_t step, ui
     philox4x32_10(b, i, (j4 << 4) | purpose, step, (uint32_t)seed, (uint32_t)(seed >> 32), o);
 }
 
-// (score desc, index asc): the better of two candidates; index -1 = none.
+// (key desc, index asc): the better of two candidates; index -1 = none.
 __device__ __forceinline__ void gumbel_merge(float& s, int& j, float s2, int j2) {
     if (j2 < 0) return;
     if (j < 0 || s2 > s || (s2 == s && j2 < j)) {

@@ -9,8 +9,8 @@
 // are integer, the min(1, p/q) test and the residual are integer
 // cross-multiplications, so the result does not depend on reduction order.
 // Draws (draft tokens, the residual / bonus token, the tree's fallback) are
-// Gumbel-max arg-maxes over per-element scores (gumbel.cuh), merged as
-// (score desc, index asc), which is order-independent as well.
+// arg-maxes of per-element race keys (gumbel.cuh), merged as (key desc, index
+// asc), which is order-independent as well.
 #include <cfloat>
 #include <climits>
 #include <mutex>
@@ -415,7 +415,7 @@ __device__ __forceinline__ void for_each_group(const float* __restrict__ z, int 
 }
 
 // Draw from the masses of row z over [L, H): candidates are the elements with
-// key >= tau and mass E_j > 0, minus excl[0, nex); score (z_j - m) c + G_j
+// key >= tau and mass E_j > 0, minus excl[0, nex); race key E_j / (-log2 U_j)
 // with the uniforms of draw (seed, step, b, i, purpose) by element index (the
 // oracle's orc_draw_row).  *sum (if given) receives the candidates' mass total.
 __device__ void cta_gumbel_mass(const float* __restrict__ z, int L, int H, float m, float c, uint32_t tau,
@@ -443,8 +443,7 @@ __device__ void cta_gumbel_mass(const float* __restrict__ z, int L, int H, float
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (!e4[e]) continue;
-            const float sc = __fadd_rn(__fmul_rn(__fsub_rn(v[e], m), c), gumbel2(o[e]));
-            gumbel_merge(bs, bj, sc, 4 * g + e);
+            gumbel_merge(bs, bj, race_key(__uint2float_rn(e4[e]), o[e]), 4 * g + e);
         }
     });
     if (sum) *sum = block_sum<uint64_t>(tot, sm.red64);
@@ -453,7 +452,7 @@ __device__ void cta_gumbel_mass(const float* __restrict__ z, int L, int H, float
 
 // Draw from the residual max(0, E_p N_q - E_q N_p) of target row zp and draft
 // row zq over [L, H) (nucleus masses at their row statistics; N = nucleus
-// totals); score log2(residual) + G_j (the oracle's draw_residual).  Index -1
+// totals); race key residual / (-log2 U_j) (the oracle's draw_residual).  Index -1
 // when the residual is zero everywhere in [L, H).
 __device__ void cta_gumbel_resid(const float* __restrict__ zp, float pm, uint32_t pt, uint64_t Np,
                                  const float* __restrict__ zq, float qm, uint32_t qt, uint64_t Nq, int L, int H,
@@ -494,7 +493,7 @@ __device__ void cta_gumbel_resid(const float* __restrict__ zp, float pm, uint32_
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (!r4[e]) continue;
-            gumbel_merge(bs, bj, __fadd_rn(det_log2_u128(r4[e]), gumbel2(o[e])), 4 * g + e);
+            gumbel_merge(bs, bj, race_key(u128_to_f32(r4[e]), o[e]), 4 * g + e);
         }
     });
     cta_best(bs, bj, sm, out_s, out_j);
@@ -1249,21 +1248,31 @@ int launch_topk(const float* logits, int rows, int V, int k, int32_t* out, cudaS
 // Dynamic shared memory of the row-statistics kernels: the per-warp top-p
 // histograms, needed only when the rows need mass sums and a nucleus.  They
 // exceed the 48 KB default, so the kernels opt in once per device.
+static std::mutex g_hist_mu;
+static bool g_hist_opted[64] = {};
+
 static int hist_smem(bool need_mass, uint64_t tp, size_t* bytes) {
     *bytes = 0;
     if (!need_mass || tp >= (1ull << 32)) return SPECDEC_OK;
-    static bool done[64] = {};
     int dev = 0;
     SD_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !done[dev]) {
+    SD_CHECK(dev >= 0 && dev < 64, SPECDEC_EINVAL, "sampling: device index out of range");
+    std::lock_guard<std::mutex> lk(g_hist_mu);  // first calls from several host threads
+    if (!g_hist_opted[dev]) {
         const int sz = (int)kWarpHistBytes;
         SD_CUDA(cudaFuncSetAttribute(row_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sz));
         SD_CUDA(cudaFuncSetAttribute(accept_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sz));
         SD_CUDA(cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sz));
-        if (dev >= 0 && dev < 64) done[dev] = true;
+        g_hist_opted[dev] = true;
     }
     *bytes = kWarpHistBytes;
     return SPECDEC_OK;
+}
+
+// Whether the chain acceptance takes the row-statistics path (which uses the
+// per-row scratch) rather than the sliced cluster kernel (which needs none).
+static bool accept_uses_row_stats(bool greedy, uint64_t tp, int k) {
+    return !((greedy || tp >= (1ull << 32)) && k <= kAcceptClusterMaxK);
 }
 
 // Cluster size of the sliced chain acceptance: the largest power of two
@@ -1289,7 +1298,7 @@ static int launch_accept_chain_impl(const float* target, const float* draft, con
     const float c = greedy ? 0.0f : temp_coeff(temperature);
     const uint64_t tp = top_p_q32(top_p);
     const float* dq = greedy ? target : draft;
-    if ((greedy || tp >= (1ull << 32)) && k <= kAcceptClusterMaxK) {
+    if (!accept_uses_row_stats(greedy, tp, k)) {
         const int S = accept_cluster_size(B);
         const DevRowStats* qstats = (!greedy && draft_stats_ready) ? st + (size_t)B * (k + 1) : nullptr;
         cudaLaunchConfig_t cfg = {};
@@ -1309,7 +1318,9 @@ static int launch_accept_chain_impl(const float* target, const float* draft, con
         return SPECDEC_OK;
     }
     SD_CHECK(st, SPECDEC_EINVAL, "accept_chain: row statistics scratch required");
-    const int rows = B * (k + 1) + (greedy ? 0 : B * k);
+    const long long rows_ll = (long long)B * (k + 1) + (greedy ? 0 : (long long)B * k);
+    SD_CHECK(rows_ll <= INT_MAX, SPECDEC_EINVAL, "accept_chain: too many logits rows");
+    const int rows = (int)rows_ll;
     RowSet a{target, B * (k + 1)}, bq{dq, greedy ? 0 : B * k};
     size_t hs = 0;
     int rc = hist_smem(!greedy, tp, &hs);
@@ -1375,7 +1386,9 @@ extern "C" int specdec_accept_chain(const float* target, const float* draft, con
     if (B == 0) return SPECDEC_OK;
     const bool greedy = !(sp->temperature > 0.0f);
     SD_CHECK(greedy || draft, SPECDEC_EINVAL, "accept_chain: draft logits required when sampling");
-    SD_CHECK(workspace && workspace_bytes >= specdec_accept_workspace_bytes(B * (2 * k + 1)), SPECDEC_EINVAL,
+    const long long ws_rows = (long long)B * (2 * (long long)k + 1);
+    SD_CHECK(ws_rows <= INT_MAX, SPECDEC_EINVAL, "accept_chain: too many logits rows");
+    SD_CHECK(workspace && workspace_bytes >= specdec_accept_workspace_bytes((int)ws_rows), SPECDEC_EINVAL,
              "accept_chain: workspace too small");
     return launch_accept_chain_impl(target, draft, drafts, B, k, V, sp->temperature, sp->top_p, sp->seed, nullptr,
                                     sp->step, reinterpret_cast<DevRowStats*>(workspace), false, accepted_len,
@@ -1434,7 +1447,9 @@ extern "C" int specdec_accept_chain_noalloc(const float* target, const float* dr
     const bool greedy = !(sp->temperature > 0.0f);
     SD_CHECK(greedy || draft, SPECDEC_EINVAL, "accept_chain_noalloc: draft logits required when sampling");
     const long long rows = (long long)B * (k + 1) + (greedy ? 0 : (long long)B * k);
-    if (rows > kStaticAcceptRows) {
+    // the limit binds only where the fixed scratch is used: the row-statistics
+    // path (top_p < 1 sampling, or more than 16 drafts)
+    if (accept_uses_row_stats(greedy, top_p_q32(sp->top_p), k) && rows > kStaticAcceptRows) {
         set_error("accept_chain_noalloc: batch*(k+1) + batch*k logits rows (" + std::to_string(rows) +
                   ") exceed the fixed scratch of " + std::to_string(kStaticAcceptRows) +
                   " rows; use specdec_accept_chain with a caller workspace");
@@ -1566,6 +1581,7 @@ extern "C" int specdec_shard_point_mass(const float* target, const float* draft,
     if (int rc = shard_check(B, Vs, "shard_point_mass")) return rc;
     SD_CHECK(target && draft && drafts && pmax && ptau && qmax && qtau && ep && eq && k >= 1 && temperature > 0.0f,
              SPECDEC_EINVAL, "shard_point_mass: bad argument");
+    SD_CHECK((long long)B * k <= INT_MAX - 255, SPECDEC_EINVAL, "shard_point_mass: too many draft rows");
     if (B == 0) return SPECDEC_OK;
     shard_point_mass_kernel<<<(B * k + 255) / 256, 256, 0, as_stream(stream)>>>(
         target, draft, drafts, B, k, Vs, v0, temp_coeff(temperature), pmax, ptau, qmax, qtau,

@@ -61,7 +61,7 @@ def test_row_stats_nucleus_mass_threshold():
 
 
 def test_sampling_distribution_matches_softmax():
-    """Gumbel-max draws (one per step) follow softmax(z / T)."""
+    """Draws (one per step) follow softmax(z / T)."""
     rng = np.random.default_rng(5)
     V = 12
     z = rng.standard_normal(V).astype(np.float32)
@@ -75,9 +75,9 @@ def test_sampling_distribution_matches_softmax():
 
 
 def test_gumbel_draw_is_the_argmax_of_the_scores():
-    """orc_draw_row = arg-max over the nucleus of (z_j - max) * c + G_j, with
-    G_j = -log2(-log2 U_j) from the draw's own element uniforms; excluded
-    tokens never win, ties go to the lower index."""
+    """orc_draw_row = arg-max over the nucleus of the race key
+    E_j / (-log2 U_j) with the draw's own element uniforms; excluded tokens
+    never win, ties go to the lower index."""
     rng = np.random.default_rng(8)
     V, T, tp = 300, 0.7, 0.9
     z = (rng.standard_normal(V) * 2).astype(np.float32)
@@ -89,8 +89,8 @@ def test_gumbel_draw_is_the_argmax_of_the_scores():
         for j in range(V):
             if not L.orc_row_mass(O.ptr(z), C.byref(st), c, j) or j in (3, 17):
                 continue
-            t = float(np.float32(np.float32(z[j] - np.float32(st.max)) * np.float32(c)))
-            sc = L.orc_gumbel_score(t, L.orc_gumbel_uniform(9, step, 2, 1, O.U_GUMBEL_DRAFT, j))
+            e = L.orc_row_mass(O.ptr(z), C.byref(st), c, j)
+            sc = L.orc_race_key(float(e), L.orc_gumbel_uniform(9, step, 2, 1, O.U_GUMBEL_DRAFT, j))
             if best < 0 or sc > bs:
                 best, bs = j, sc
         assert O.draw_row(z, T, tp, 9, step, 2, 1, exclude=[3, 17]) == best

@@ -1,8 +1,8 @@
 """CPU check that the vocabulary-sharded acceptance loses nothing: row
 statistics assembled from per-shard partials -- the rank-order arg-max
 merge, integer mass sums, the top-p threshold from summed per-shard digit
-histograms, and the Gumbel-max draw as the best of the shards' local
-winners -- equal the oracle's statistics and draw on the whole row.  These are the
+histograms, and the draw as the best of the shards' local winners (race
+keys) -- equal the oracle's statistics and draw on the whole row.  These are the
 combinations specdec.dist.accept_chain_vocab_sharded performs between the
 specdec_shard_* steps; the device kernels themselves are checked against
 the oracle in the GPU tests."""
@@ -89,8 +89,7 @@ def test_shard_partials_rebuild_the_row(W, V, T, tp, seed):
             for j in range(v0, v0 + vs):
                 if key[j] < tau or E[j] == 0:
                     continue
-                t = float(np.float32(np.float32(z[j] - np.float32(best_v)) * np.float32(c)))
-                sc = L.orc_gumbel_score(t, L.orc_gumbel_uniform(seed, step, 1, 2, O.U_GUMBEL_RESAMPLE, j))
+                sc = L.orc_race_key(float(E[j]), L.orc_gumbel_uniform(seed, step, 1, 2, O.U_GUMBEL_RESAMPLE, j))
                 if lb < 0 or sc > ls:
                     lb, ls = j, sc
             if lb >= 0 and (best < 0 or ls > bs or (ls == bs and lb < best)):
