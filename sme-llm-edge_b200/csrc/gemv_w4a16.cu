@@ -29,10 +29,12 @@
 //              after it;
 //   warps 0-7  warp w owns weight rows 16w .. 16w+15 of every unit: it
 //              dequantises them straight from the unit's words into the
-//              registers of m16n8k16 A fragments (the nibble pair of a word is
-//              exactly one fragment register) and multiplies them with the
-//              activation fragments read from the swizzled slice, fp32
-//              accumulators in registers (MP / 8 tiles of 8 tokens).
+//              registers of m16n8k16 A fragments (a nibble pair of a word is
+//              exactly one fragment register; k is permuted within each k16
+//              step so that a lane's four k are contiguous: one word per row
+//              and one 8-byte activation load per fragment) and multiplies
+//              them with the activation fragments read from the swizzled
+//              slice, fp32 accumulators in registers (MP / 8 tiles of 8 tokens).
 // Epilogue: accumulators to shared memory as [token][128 rows]; CTA rank r of
 // the cluster sums token rows [r * MP / S, (r + 1) * MP / S) over the S
 // partial tiles and writes them (store, or add for mode 1).
@@ -87,11 +89,13 @@ __device__ __forceinline__ void mma_f16_16816(float* d, const uint32_t* a, uint3
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// nibble pair (k_2c, k_2c+1) of a unit word -> fp16x2 fp16((u - 8) * s)
-__device__ __forceinline__ uint32_t deq_pair(uint32_t word, int c, __half2 s2) {
-    const uint32_t t = ((word >> (4 * c)) & 0x000F000Fu) | 0x64006400u;  // fp16 1024 + u in each half
+// the nibble pair in bits 0-3 / 16-19 of a (shifted) unit word -> fp16x2
+// fp16((u - 8) * s): fp16 1024 + u in each half, exact u - 8, one rounding of
+// the product
+__device__ __forceinline__ uint32_t deq_pair(uint32_t w, __half2 s2) {
+    const uint32_t t = (w & 0x000F000Fu) | 0x64006400u;
     __half2 h = *reinterpret_cast<const __half2*>(&t);
-    h = __hmul2(__hsub2(h, __float2half2_rn(1032.0f)), s2);  // exact u - 8, one rounding of the product
+    h = __hmul2(__hsub2(h, __float2half2_rn(1032.0f)), s2);
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
@@ -174,6 +178,8 @@ __global__ void __launch_bounds__(kGvThreads, 2)
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
     const int g = lane >> 2, c = lane & 3;
     const int r = warp * 16 + g;  // this lane's rows r and r + 8 of the unit
+    const int cw = c >> 1;                  // the word of a k16 step this lane reads
+    const uint32_t sh = 8u * (uint32_t)(c & 1);  // its nibble pairs 2(c&1), 2(c&1)+1
     if (warp < kGvMathWarps) {
         // ------------------------------------------------ dequant + MMA
         bool ok = true;
@@ -188,21 +194,25 @@ __global__ void __launch_bounds__(kGvThreads, 2)
             const unsigned char* xs = sX + s * L::kXSlot;
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
+                // k16 step ks = words 2ks, 2ks + 1.  The contraction does not
+                // depend on the order of k, so lane (g, c) takes physical k
+                // 4c .. 4c + 3 of the step for its fragment slots (2c, 2c+1)
+                // and (2c+8, 2c+9): nibble pairs 2(c&1), 2(c&1)+1 of word
+                // 2ks + c/2 -- one word per row -- and 8 contiguous bytes of X.
+                const uint32_t w0 = words[(2 * ks + cw) * 128 + r] >> sh;
+                const uint32_t w1 = words[(2 * ks + cw) * 128 + r + 8] >> sh;
                 uint32_t a[4];
-                a[0] = deq_pair(words[(2 * ks) * 128 + r], c, s_lo);
-                a[1] = deq_pair(words[(2 * ks) * 128 + r + 8], c, s_hi);
-                a[2] = deq_pair(words[(2 * ks + 1) * 128 + r], c, s_lo);
-                a[3] = deq_pair(words[(2 * ks + 1) * 128 + r + 8], c, s_hi);
+                a[0] = deq_pair(w0, s_lo);
+                a[1] = deq_pair(w1, s_hi);
+                a[2] = deq_pair(w0 >> 4, s_lo);
+                a[3] = deq_pair(w1 >> 4, s_hi);
                 const unsigned char* box = xs + (ks >> 2) * L::kXBox;
-                const int kk = ks & 3;
+                const int chunk = 2 * (ks & 3) + cw;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     const int n = 8 * t + g;  // token row of the box
-                    const unsigned char* row = box + n * 128;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(row + ((((2 * kk) ^ (n & 7)) << 4) + 4 * c));
-                    const uint32_t b1 =
-                        *reinterpret_cast<const uint32_t*>(row + ((((2 * kk + 1) ^ (n & 7)) << 4) + 4 * c));
-                    mma_f16_16816(acc[t], a, b0, b1);
+                    const uint2 b = *reinterpret_cast<const uint2*>(box + n * 128 + (((chunk ^ (n & 7)) << 4) + 8 * (c & 1)));
+                    mma_f16_16816(acc[t], a, b.x, b.y);
                 }
             }
             __syncwarp();
