@@ -73,17 +73,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
         if (gtimer() - t0 > 2000000000ull) return false;
     }
 }
-// Bounded wait that polls without suspending (test_wait in a loop, the global
-// timer read every 1024 probes): for a thread whose next action is on the
-// critical path, where a suspended try_wait's wake-up would add latency.
-__device__ __forceinline__ bool mbar_wait_spin(uint32_t a, uint32_t parity) {
-    if (mbar_test(a, parity)) return true;
-    const uint64_t t0 = gtimer();
-    for (uint32_t n = 1;; ++n) {
-        if (mbar_test(a, parity)) return true;
-        if ((n & 1023u) == 0 && gtimer() - t0 > 2000000000ull) return false;
-    }
-}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(mbar)
