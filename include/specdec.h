@@ -36,7 +36,9 @@ enum {
     SPECDEC_ENOMEM = 2,   /* device memory or KV block pool exhausted */
     SPECDEC_ECUDA = 3,    /* CUDA runtime / launch error */
     SPECDEC_ETIMEOUT = 4, /* a bounded device-side wait gave up */
-    SPECDEC_ENOTSUP = 5   /* feature not available on this device */
+    SPECDEC_ENOTSUP = 5,  /* feature not available on this device */
+    SPECDEC_EFORMAT = 6,  /* malformed or truncated .sme model file */
+    SPECDEC_EIO = 7       /* model file cannot be opened or mapped */
 };
 /* Last error message of the calling thread ("" if none). */
 const char* specdec_last_error(void);
@@ -327,12 +329,23 @@ typedef struct {
 } specdec_run_config;
 
 typedef struct specdec_engine specdec_engine;
+typedef struct specdec_sme specdec_sme;
 int specdec_engine_create(const specdec_model_config* mc, const specdec_run_config* rc, int device,
                           specdec_engine** out);
 int specdec_engine_destroy(specdec_engine* e);
 /* Synthesises all weights on the device (bit-identical to the oracle's
  * host-side generator for the same seed). */
 int specdec_engine_init_weights(specdec_engine* e, uint32_t seed);
+/* Loads the weights of a `.sme` model file (section 5 below) into the
+ * engine, whose model config must equal specdec_sme_model_config(f).
+ * Projections are requantised to int4 group-128 on the device (the
+ * converter of specdec_w4_convert), q/k/v fused, gate/up interleaved; each
+ * RMSNorm weight is folded into the columns of the projections it feeds
+ * (attn_norm -> q, k, v; ffn_norm -> gate, up; norm -> lm_head;
+ * mtp.<i>.norm -> mtp.<i>.proj).  embed_tokens becomes fp16 rows.  A missing
+ * lm_head is tied to embed_tokens; missing MTP heads (the reference format
+ * has none) are synthesised from missing_seed like specdec_engine_init_weights. */
+int specdec_engine_load_sme(specdec_engine* e, const specdec_sme* f, uint32_t missing_seed);
 /* Chunked prefill of host prompts [batch, prompt_len] (all but the last
  * token enter the KV; the last becomes the pending token). */
 int specdec_engine_prefill(specdec_engine* e, const int32_t* prompts, int prompt_len);
@@ -368,6 +381,63 @@ int specdec_engine_profile(specdec_engine* e, int steps, float* ms_out);
  * captures that graph (after one eager step).  Synchronises the engine
  * stream. */
 int specdec_engine_step_verify_timed(specdec_engine* e, float* verify_ms);
+
+/* ===================================================================== */
+/* 5. `.sme` model files (model/README.md:9-36, written by                 */
+/*    convert_model.py:26-67, read by load_sme_model, server/main.cpp:     */
+/*    112-228).  Host-only: no call in this section touches the GPU        */
+/*    except specdec_w4_convert.                                           */
+/* ===================================================================== */
+/* Maps the file read-only and parses it with every field bounds-checked
+ * (SPECDEC_EFORMAT on a short or malformed file, SPECDEC_EIO when it cannot
+ * be opened).  Offsets advance by the element count of each tensor as in
+ * main.cpp:207-221; a repeated tensor name replaces the earlier tensor. */
+int specdec_sme_open(const char* path, specdec_sme** out);
+/* Same over a caller-owned buffer (kept alive until specdec_sme_close). */
+int specdec_sme_open_buffer(const void* data, size_t bytes, specdec_sme** out);
+int specdec_sme_close(specdec_sme* f);
+/* The config JSON text, and a top-level number under `key` (the text after
+ * "key" and its colon, as main.cpp:129-135 extract_int; EINVAL if absent). */
+int specdec_sme_config_json(const specdec_sme* f, const char** json, size_t* len);
+int specdec_sme_config_number(const specdec_sme* f, const char* key, double* value);
+/* Vocabulary: token text (not NUL-terminated) by id, and id by text with
+ * unknown words mapping to 1 (tokenize_word, main.cpp:230-233). */
+int specdec_sme_vocab_size(const specdec_sme* f, uint32_t* n);
+int specdec_sme_token(const specdec_sme* f, uint32_t id, const char** text, uint32_t* len);
+int specdec_sme_token_id(const specdec_sme* f, const char* text, uint32_t len, int32_t* id);
+/* Tensor views into the mapping (host pointers, no alignment guarantee). */
+typedef struct {
+    const char* name;
+    uint32_t n_dims;
+    const uint32_t* dims;
+    uint64_t elements;       /* product of dims */
+    int quantized;           /* 1: int8 data + f32 row factors rs = 127 / max|w| */
+    uint32_t data_bytes;     /* data size as written in the file */
+    const void* scales;      /* f32 [dims[0]] when quantized, else NULL */
+    const void* data;        /* int8 or f32 [elements] */
+} specdec_sme_tensor;
+int specdec_sme_tensor_count(const specdec_sme* f, uint32_t* n);
+int specdec_sme_tensor_at(const specdec_sme* f, uint32_t index, specdec_sme_tensor* out);
+int specdec_sme_find(const specdec_sme* f, const char* name, specdec_sme_tensor* out);
+/* Engine model config of the file: hidden_dim, num_layers, num_heads and
+ * vocab_size from the JSON (hidden / vocab default to embed_tokens' shape);
+ * head_dim = JSON head_dim or hidden / num_heads; n_kv_heads = JSON
+ * num_kv_heads / num_key_value_heads or rows(layers.0.k_proj) / head_dim;
+ * ffn = rows(layers.0.gate_proj); n_mtp_heads = the mtp.<i>.proj tensors
+ * present, else JSON num_mtp_heads, else 3; rms_eps = JSON rms_norm_eps or
+ * 1e-5 (main.cpp:272); rope_theta = JSON rope_theta or 10000.  Tensors are
+ * found under the reference's names (embed_tokens, layers.<l>.q_proj ...
+ * attn_norm, ffn_norm, norm, lm_head) or the Hugging Face names
+ * (model.layers.<l>.self_attn.q_proj.weight ...). */
+int specdec_sme_model_config(const specdec_sme* f, specdec_model_config* mc);
+/* Device converter: rows [rows, K] of int8 (row factors row_scales, value =
+ * q / rs) or f32 (src_f32 = 1), times fold[k] when fold is non-NULL, to
+ * int4 group-128 (s = fp16(amax / 7), 1 when amax = 0; q = clamp(round(v /
+ * s), -8, 7)) written into the tiled weight of N rows: rows row0 .. (layout
+ * 0), or the gate (1) / up (2) half of a fused SwiGLU weight.  K % 8 == 0.
+ * Device pointers. */
+int specdec_w4_convert(const void* src, int src_f32, const float* row_scales, const float* fold, int rows, int K,
+                       void* tiled, int N, int row0, int layout, void* stream);
 
 #ifdef __cplusplus
 }

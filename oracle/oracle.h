@@ -175,6 +175,9 @@ float orc_synth_value(uint32_t seed, uint32_t tid, uint64_t e);
  * packed is [n, K/2] (low nibble = even k), scales [n, K/128]. */
 void orc_synth_w4(uint32_t seed, uint32_t tid, int N, int K, int n0, int n, uint8_t* packed, uint16_t* scales);
 void orc_synth_f16(uint32_t seed, uint32_t tid, uint64_t e0, size_t n, uint16_t* out);
+/* The same quantiser over given rows w [n, K] (K even): packed [n, K/2],
+ * scales [n, K/128]. */
+void orc_w4_quantize(const float* w, int n, int K, uint8_t* packed, uint16_t* scales);
 /* Dequantise int4 rows to fp16-rounded fp32 values. */
 void orc_w4_dequant(const uint8_t* packed, const uint16_t* scales, int N, int K, float* out);
 /* Y[m,n] (op)= sum_k X[m,k] * Wdq[n,k]; X fp16 [M,K]; accumulate in fp32.

@@ -92,6 +92,7 @@ def _declare(L):
         "orc_synth_w4": (None, [U32, U32, I, I, I, I, P, P]),
         "orc_synth_f16": (None, [U32, U32, U64, C.c_size_t, P]),
         "orc_w4_dequant": (None, [P, P, I, I, P]),
+        "orc_w4_quantize": (None, [P, I, I, P, P]),
         "orc_w4a16_gemm": (None, [P, I, P, P, I, I, P, I, I]),
         "orc_rmsnorm_f16": (None, [P, P, I, F, P]),
         "orc_rope_tables": (None, [I, I, F, P, P]),
@@ -225,6 +226,16 @@ def synth_w4(seed, tid, N, K, n0=0, n=None):
     return packed, scales
 
 
+def w4_quantize(w):
+    """int4 group-128 quantiser of the oracle generator over given f32 rows."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, K = w.shape
+    packed = np.zeros((n, K // 2), np.uint8)
+    scales = np.zeros((n, (K + 127) // 128), np.uint16)
+    lib().orc_w4_quantize(ptr(w), n, K, ptr(packed), ptr(scales))
+    return packed, scales
+
+
 def w4_dequant(packed, scales):
     N, K2 = packed.shape
     out = np.zeros((N, K2 * 2), np.float32)
@@ -280,6 +291,50 @@ class OracleModel:
             self.close()
         except Exception:
             pass
+
+
+class ArrayModel:
+    """Oracle model over given weights (e.g. converted from a `.sme` file):
+    emb fp16 bits [V, H]; proj = {name: [(packed, scales) per layer]} for
+    q, k, v, o, gate, up, down; lm = (packed, scales); mtp = [(packed,
+    scales)] per head.  Arrays are kept alive by this object."""
+
+    _ORDER = ("q", "k", "v", "o", "gate", "up", "down")
+
+    def __init__(self, cfg: dict, emb16, proj: dict, lm, mtp, rope_max_pos: int = 4096):
+        self.cfg = cfg
+        hd = cfg["head_dim"]
+        self._keep = []
+
+        def keep(a):
+            a = np.ascontiguousarray(a)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        c = ModelCfg(cfg["hidden"], cfg["layers"], cfg["n_q_heads"], cfg["n_kv_heads"], hd, cfg["ffn"], cfg["vocab"],
+                     cfg["n_mtp_heads"], cfg.get("block_size", 16), cfg.get("rms_eps", 1e-5),
+                     cfg.get("rope_theta", 10000.0))
+        m = Model()
+        m.cfg = c
+        m.emb = keep(np.asarray(emb16, np.uint16))
+        for i, name in enumerate(self._ORDER):
+            m.w_packed[i] = keep(np.concatenate([p for p, _ in proj[name]]))
+            m.w_scales[i] = keep(np.concatenate([sc for _, sc in proj[name]]))
+        m.lm_packed, m.lm_scales = keep(lm[0]), keep(lm[1])
+        m.mtp_packed = keep(np.concatenate([p for p, _ in mtp]))
+        m.mtp_scales = keep(np.concatenate([sc for _, sc in mtp]))
+        half = hd // 2
+        cos_t = np.zeros((rope_max_pos, half), np.float32)
+        sin_t = np.zeros((rope_max_pos, half), np.float32)
+        lib().orc_rope_tables(rope_max_pos, hd, C.c_float(c.rope_theta), ptr(cos_t), ptr(sin_t))
+        m.rope_cos, m.rope_sin = keep(cos_t), keep(sin_t)
+        m.rope_max_pos = rope_max_pos
+        m.n_layers_present = cfg["layers"]
+        self._m = m
+        self.m = C.pointer(m)
+
+    def close(self):
+        pass
 
 
 class OracleKV:

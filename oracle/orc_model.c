@@ -22,33 +22,49 @@ float orc_synth_value(uint32_t seed, uint32_t tid, uint64_t e) {
     return (float)((s - 2.0) * 0.034641016151377546); /* sqrt(3) * 0.02 */
 }
 
+/* One row of K values to int4 with group-128 fp16 scales: s = fp16(amax / 7)
+ * (1 when amax = 0), q = clamp(round(w / s), -8, 7), u4 = q + 8, low nibble
+ * = even k. */
+static void quantize_row(const float* w, int K, uint8_t* packed, uint16_t* scales) {
+    const int G = (K + 127) / 128; /* the last group may hold fewer than 128 columns */
+    for (int g = 0; g < G; ++g) {
+        const float* wg = w + (size_t)g * 128;
+        const int gl = (K - g * 128) < 128 ? (K - g * 128) : 128;
+        float amax = 0.0f;
+        for (int t = 0; t < gl; ++t) {
+            float a = fabsf(wg[t]);
+            if (a > amax) amax = a;
+        }
+        uint16_t s16 = orc_f32_to_f16(amax / 7.0f);
+        if (amax == 0.0f) s16 = orc_f32_to_f16(1.0f);
+        scales[g] = s16;
+        float sf = orc_f16_to_f32(s16);
+        uint8_t* dst = packed + g * 64;
+        for (int t = 0; t < gl; t += 2) {
+            int q0 = (int)roundf(wg[t] / sf), q1 = (int)roundf(wg[t + 1] / sf);
+            q0 = q0 < -8 ? -8 : (q0 > 7 ? 7 : q0);
+            q1 = q1 < -8 ? -8 : (q1 > 7 ? 7 : q1);
+            dst[t / 2] = (uint8_t)((q0 + 8) | ((q1 + 8) << 4));
+        }
+    }
+}
+
+void orc_w4_quantize(const float* w, int n, int K, uint8_t* packed, uint16_t* scales) {
+    const int G = (K + 127) / 128;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < n; ++r) quantize_row(w + (size_t)r * K, K, packed + (size_t)r * (K / 2), scales + (size_t)r * G);
+}
+
 void orc_synth_w4(uint32_t seed, uint32_t tid, int N, int K, int n0, int n, uint8_t* packed, uint16_t* scales) {
     (void)N;
-    const int G = (K + 127) / 128; /* the last group may hold fewer than 128 columns */
+    const int G = (K + 127) / 128;
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < n; ++r) {
-        int row = n0 + r;
-        float w[128];
-        for (int g = 0; g < G; ++g) {
-            const int gl = (K - g * 128) < 128 ? (K - g * 128) : 128;
-            float amax = 0.0f;
-            for (int t = 0; t < gl; ++t) {
-                w[t] = orc_synth_value(seed, tid, (uint64_t)row * K + (uint64_t)g * 128 + t);
-                float a = fabsf(w[t]);
-                if (a > amax) amax = a;
-            }
-            uint16_t s16 = orc_f32_to_f16(amax / 7.0f);
-            if (amax == 0.0f) s16 = orc_f32_to_f16(1.0f);
-            scales[(size_t)r * G + g] = s16;
-            float sf = orc_f16_to_f32(s16);
-            uint8_t* dst = packed + (size_t)r * (K / 2) + g * 64;
-            for (int t = 0; t < gl; t += 2) {
-                int q0 = (int)roundf(w[t] / sf), q1 = (int)roundf(w[t + 1] / sf);
-                q0 = q0 < -8 ? -8 : (q0 > 7 ? 7 : q0);
-                q1 = q1 < -8 ? -8 : (q1 > 7 ? 7 : q1);
-                dst[t / 2] = (uint8_t)((q0 + 8) | ((q1 + 8) << 4));
-            }
-        }
+        const int row = n0 + r;
+        float* w = (float*)malloc(sizeof(float) * (size_t)G * 128);
+        for (int t = 0; t < K; ++t) w[t] = orc_synth_value(seed, tid, (uint64_t)row * K + t);
+        quantize_row(w, K, packed + (size_t)r * (K / 2), scales + (size_t)r * G);
+        free(w);
     }
 }
 

@@ -763,6 +763,23 @@ int record_step(specdec_engine* e) {
     return SPECDEC_OK;
 }
 
+int synth_tiled(cudaStream_t s, uint32_t seed, RowSegs segs, int N, int K, uint8_t* dst) {
+    const int KG = (K + 127) / 128, units_n = ((N + 255) / 256) * 2;
+    const size_t threads = (size_t)units_n * 128 * KG;
+    synth_w4_tiled_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(seed, segs, N, K, KG, units_n, dst);
+    SD_LAUNCH_CHECK("synth_w4_tiled_kernel");
+    return SPECDEC_OK;
+}
+
+RowSegs one(uint32_t tid, int N) {
+    RowSegs r;
+    r.n = 1;
+    r.inter = 0;
+    r.end[0] = N;
+    r.tid[0] = tid;
+    return r;
+}
+
 }  // namespace
 
 extern "C" int specdec_engine_destroy(specdec_engine* e) {
@@ -944,21 +961,7 @@ extern "C" int specdec_engine_init_weights(specdec_engine* e, uint32_t seed) {
     const auto& c = e->mc;
     cudaStream_t s = e->stream;
     const int H = c.hidden, F = c.ffn, V = c.vocab, hd = c.head_dim;
-    auto synth = [&](RowSegs segs, int N, int K, uint8_t* dst) -> int {
-        const int KG = (K + 127) / 128, units_n = ((N + 255) / 256) * 2;
-        const size_t threads = (size_t)units_n * 128 * KG;
-        synth_w4_tiled_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(seed, segs, N, K, KG, units_n, dst);
-        SD_LAUNCH_CHECK("synth_w4_tiled_kernel");
-        return SPECDEC_OK;
-    };
-    auto one = [](uint32_t tid, int N) {
-        RowSegs r;
-        r.n = 1;
-        r.inter = 0;
-        r.end[0] = N;
-        r.tid[0] = tid;
-        return r;
-    };
+    auto synth = [&](RowSegs segs, int N, int K, uint8_t* dst) { return synth_tiled(s, seed, segs, N, K, dst); };
     const int qd = c.n_q_heads * hd, kd = c.n_kv_heads * hd;
     int rc;
     // tensor ids: layer l, which (q 0, k 1, v 2, o 3, gate 4, up 5, down 6) -> l * 16 + which
@@ -990,6 +993,92 @@ extern "C" int specdec_engine_init_weights(specdec_engine* e, uint32_t seed) {
         if ((rc = synth(one(0x10010u + (uint32_t)i, H), H, H, e->heads[i]))) return rc;
     synth_f16_kernel<<<1184, 256, 0, s>>>(seed, 0x10000u, (size_t)V * H, 1.0f, e->emb);
     SD_LAUNCH_CHECK("synth_f16_kernel");
+    SD_CUDA(cudaStreamSynchronize(s));
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_engine_load_sme(specdec_engine* e, const specdec_sme* f, uint32_t missing_seed) {
+    SD_CHECK(e && f, SPECDEC_EINVAL, "engine_load_sme: null argument");
+    specdec_model_config fc{};
+    int rc = specdec_sme_model_config(f, &fc);
+    if (rc) return rc;
+    const auto& c = e->mc;
+    SD_CHECK(fc.hidden == c.hidden && fc.layers == c.layers && fc.n_q_heads == c.n_q_heads &&
+                 fc.n_kv_heads == c.n_kv_heads && fc.head_dim == c.head_dim && fc.ffn == c.ffn && fc.vocab == c.vocab,
+             SPECDEC_EINVAL, "engine_load_sme: the file's model config differs from the engine's");
+    cudaStream_t s = e->stream;
+    const int H = c.hidden, F = c.ffn, V = c.vocab, hd = c.head_dim;
+    const int qd = c.n_q_heads * hd, kd = c.n_kv_heads * hd;
+    // staging for row chunks plus one fold vector, released on every return
+    // (after the stream has drained)
+    struct Scratch {
+        cudaStream_t stream = nullptr;
+        uint8_t* stage = nullptr;
+        float* fold = nullptr;
+        ~Scratch() {
+            cudaStreamSynchronize(stream);
+            if (stage) cudaFree(stage);
+            if (fold) cudaFree(fold);
+        }
+    } sc;
+    sc.stream = s;
+    const size_t stage_bytes = (size_t)64 << 20;
+    SD_CUDA(cudaMalloc(&sc.stage, stage_bytes));
+    SD_CUDA(cudaMalloc(&sc.fold, sizeof(float) * (size_t)H));
+    auto view = [&](const char* role, int l, uint32_t rows, uint32_t cols, specdec_sme_tensor* v) -> int {
+        SD_CHECK(sme_role_view(f, role, l, v), SPECDEC_EFORMAT,
+                 std::string("sme: no ") + role + " tensor for layer/head " + std::to_string(l));
+        SD_CHECK(v->n_dims == 2 && v->dims[0] == rows && v->dims[1] == cols, SPECDEC_EFORMAT,
+                 std::string("sme: ") + v->name + " has the wrong shape");
+        return SPECDEC_OK;
+    };
+    // RMSNorm weight of a role -> the device fold vector (null when absent).
+    // One buffer: each copy is stream-ordered after the conversions that read
+    // the previous vector.
+    auto fold = [&](const char* role, int l, const float** out) -> int {
+        specdec_sme_tensor v;
+        *out = nullptr;
+        if (!sme_role_view(f, role, l, &v)) return SPECDEC_OK;
+        SD_CHECK(v.n_dims == 1 && v.dims[0] == (uint32_t)H && !v.quantized, SPECDEC_EFORMAT,
+                 std::string("sme: ") + v.name + " must be f32 [hidden]");
+        SD_CUDA(cudaMemcpyAsync(sc.fold, v.data, sizeof(float) * H, cudaMemcpyHostToDevice, s));
+        *out = sc.fold;
+        return SPECDEC_OK;
+    };
+    auto conv = [&](const specdec_sme_tensor& v, const float* fv, uint8_t* dst, int row0, int layout) {
+        return sme_upload_convert(v, fv, dst, ((int)v.dims[1] + 127) / 128, row0, layout, nullptr, sc.stage,
+                                  stage_bytes, s);
+    };
+    const size_t per_layer = e->sz_qkv + e->sz_o + e->sz_gu + e->sz_down;
+    const size_t wbytes = per_layer * c.layers + e->sz_lm + e->sz_head * c.n_mtp_heads;
+    if ((rc = w4_fill_zero_launch(e->weights, wbytes / 8448, s))) return rc;
+    specdec_sme_tensor v;
+    const float* fv = nullptr;
+    for (int l = 0; l < c.layers; ++l) {
+        const WeightSet& w = e->layers[l];
+        if ((rc = fold("attn_norm", l, &fv))) return rc;
+        if ((rc = view("q", l, qd, H, &v)) || (rc = conv(v, fv, w.qkv, 0, 0))) return rc;
+        if ((rc = view("k", l, kd, H, &v)) || (rc = conv(v, fv, w.qkv, qd, 0))) return rc;
+        if ((rc = view("v", l, kd, H, &v)) || (rc = conv(v, fv, w.qkv, qd + kd, 0))) return rc;
+        if ((rc = view("o", l, H, qd, &v)) || (rc = conv(v, nullptr, w.o, 0, 0))) return rc;
+        if ((rc = fold("ffn_norm", l, &fv))) return rc;
+        if ((rc = view("gate", l, F, H, &v)) || (rc = conv(v, fv, w.gu, 0, 1))) return rc;
+        if ((rc = view("up", l, F, H, &v)) || (rc = conv(v, fv, w.gu, 0, 2))) return rc;
+        if ((rc = view("down", l, H, F, &v)) || (rc = conv(v, nullptr, w.down, 0, 0))) return rc;
+    }
+    if ((rc = fold("norm", 0, &fv))) return rc;
+    const char* lm_role = sme_role_view(f, "lm_head", 0, &v) ? "lm_head" : "embed";  // embed: tied output embedding
+    if ((rc = view(lm_role, 0, V, H, &v)) || (rc = conv(v, fv, e->lm, 0, 0))) return rc;
+    for (int i = 0; i < c.n_mtp_heads; ++i) {
+        if (sme_role_view(f, "mtp", i, &v)) {
+            if ((rc = fold("mtp_norm", i, &fv))) return rc;
+            if ((rc = view("mtp", i, H, H, &v)) || (rc = conv(v, fv, e->heads[i], 0, 0))) return rc;
+        } else if ((rc = synth_tiled(s, missing_seed, one(0x10010u + (uint32_t)i, H), H, H, e->heads[i]))) {
+            return rc;
+        }
+    }
+    if ((rc = view("embed", 0, V, H, &v))) return rc;
+    if ((rc = sme_upload_convert(v, nullptr, nullptr, 0, 0, 0, e->emb, sc.stage, stage_bytes, s))) return rc;
     SD_CUDA(cudaStreamSynchronize(s));
     return SPECDEC_OK;
 }
@@ -1147,11 +1236,23 @@ View engine_view(specdec_engine* e, const char* what) {
     if (w == "emitted") return {e->emitted, 8};
     if (w == "emb") return {e->emb, 2 * V * H};
     if (w == "w_lm") return {e->lm, e->sz_lm};
-    if (w == "w_head0") return {e->heads[0], e->sz_head};
-    if (w == "w_qkv0") return {e->layers[0].qkv, e->sz_qkv};
-    if (w == "w_o0") return {e->layers[0].o, e->sz_o};
-    if (w == "w_gu0") return {e->layers[0].gu, e->sz_gu};
-    if (w == "w_down0") return {e->layers[0].down, e->sz_down};
+    // per-layer / per-head weights: "w_qkv<l>", "w_o<l>", "w_gu<l>", "w_down<l>", "w_head<i>"
+    for (const char* pre : {"w_qkv", "w_o", "w_gu", "w_down", "w_head"}) {
+        const size_t n = std::strlen(pre);
+        if (w.compare(0, n, pre) != 0 || w.size() == n || w.size() > n + 4 ||
+            w.find_first_not_of("0123456789", n) != std::string::npos)
+            continue;
+        const int i = std::atoi(w.c_str() + n);
+        if (w == std::string(pre) + std::to_string(i)) {
+            if (pre[2] == 'h') return i < (int)e->heads.size() ? View{e->heads[i], e->sz_head} : View{nullptr, 0};
+            if (i >= c.layers) return {nullptr, 0};
+            const WeightSet& ws = e->layers[i];
+            if (pre[2] == 'q') return {ws.qkv, e->sz_qkv};
+            if (pre[2] == 'o') return {ws.o, e->sz_o};
+            if (pre[2] == 'g') return {ws.gu, e->sz_gu};
+            return {ws.down, e->sz_down};
+        }
+    }
     return {nullptr, 0};
 }
 }  // namespace

@@ -114,4 +114,31 @@ KVState& kv_state(specdec_kv* kv);
 int kv_append_uniform(specdec_kv* kv, int n, int tokens, cudaStream_t s);
 int kv_truncate_dev(specdec_kv* kv, const int32_t* new_len_dev, int n, cudaStream_t s);
 
+// ------------------------------------------------------------ .sme weights
+// Rows of a source weight on the device: int8 with the writer's per-row
+// factor (value = q / rs) or fp32; fold = optional per-column multiplier
+// (an RMSNorm weight folded into the following projection).
+struct W4Source {
+    const int8_t* q8;
+    const float* rs;
+    const float* f32;
+    const float* fold;
+    int K;
+};
+// Source rows -> tiled W4 units (KG = ceil(K / 128) units per 128 rows).
+// layout 0: source row r is row row0 + r; 1 / 2: gate / up half of the fused
+// SwiGLU weight (row0 = 0).
+int w4_convert_launch(const W4Source& src, int rows, int row0, int layout, uint8_t* tiled, int KG, cudaStream_t s);
+int w4_fill_zero_launch(uint8_t* tiled, size_t units, cudaStream_t s);
+int f16_rows_launch(const W4Source& src, int rows, __half* out, cudaStream_t s);
+// The tensor of a role of a .sme file ("embed", "norm", "lm_head", "q", "k",
+// "v", "o", "gate", "up", "down", "attn_norm", "ffn_norm", "mtp",
+// "mtp_norm") for layer / head `layer`; false when the file has none.
+bool sme_role_view(const specdec_sme* f, const char* role, int layer, specdec_sme_tensor* out);
+// Copies a file tensor to the device through `stage` in row chunks and
+// converts it: into tiled W4 rows (row0 / layout as w4_convert_launch, fold =
+// device f32 [K] or null) or, with f16 non-null, into fp16 rows.
+int sme_upload_convert(const specdec_sme_tensor& t, const float* fold, uint8_t* tiled, int KG, int row0, int layout,
+                       __half* f16, uint8_t* stage, size_t stage_bytes, cudaStream_t s);
+
 }  // namespace specdec

@@ -24,7 +24,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 # on one machine); the in-tree build otherwise.
 LIB_PATH = os.environ.get("SPECDEC_LIB") or os.path.join(_HERE, "libspecdec_sm100.so")
 
-OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, ENOTSUP = range(6)
+OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, ENOTSUP, EFORMAT, EIO = range(8)
 
 
 class SpecdecError(RuntimeError):
@@ -56,6 +56,11 @@ class Sampling(C.Structure):
 class ModelConfig(C.Structure):
     _fields_ = [("hidden", I), ("layers", I), ("n_q_heads", I), ("n_kv_heads", I), ("head_dim", I), ("ffn", I),
                 ("vocab", I), ("n_mtp_heads", I), ("block_size", I), ("rms_eps", F), ("rope_theta", F)]
+
+
+class SmeTensorView(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("n_dims", U32), ("dims", C.POINTER(U32)), ("elements", U64),
+                ("quantized", I), ("data_bytes", U32), ("scales", C.c_void_p), ("data", C.c_void_p)]
 
 
 class RunConfig(C.Structure):
@@ -117,6 +122,20 @@ _SIGS = {
     "specdec_engine_create": (I, [C.POINTER(ModelConfig), C.POINTER(RunConfig), I, C.POINTER(P)]),
     "specdec_engine_destroy": (I, [P]),
     "specdec_engine_init_weights": (I, [P, U32]),
+    "specdec_engine_load_sme": (I, [P, P, U32]),
+    "specdec_sme_open": (I, [C.c_char_p, C.POINTER(P)]),
+    "specdec_sme_open_buffer": (I, [P, SZ, C.POINTER(P)]),
+    "specdec_sme_close": (I, [P]),
+    "specdec_sme_config_json": (I, [P, C.POINTER(C.c_char_p), C.POINTER(SZ)]),
+    "specdec_sme_config_number": (I, [P, C.c_char_p, C.POINTER(C.c_double)]),
+    "specdec_sme_vocab_size": (I, [P, C.POINTER(U32)]),
+    "specdec_sme_token": (I, [P, U32, C.POINTER(C.c_void_p), C.POINTER(U32)]),
+    "specdec_sme_token_id": (I, [P, C.c_char_p, U32, C.POINTER(C.c_int32)]),
+    "specdec_sme_tensor_count": (I, [P, C.POINTER(U32)]),
+    "specdec_sme_tensor_at": (I, [P, U32, C.POINTER(SmeTensorView)]),
+    "specdec_sme_find": (I, [P, C.c_char_p, C.POINTER(SmeTensorView)]),
+    "specdec_sme_model_config": (I, [P, C.POINTER(ModelConfig)]),
+    "specdec_w4_convert": (I, [P, I, P, P, I, I, P, I, I, I, P]),
     "specdec_engine_prefill": (I, [P, P, I]),
     "specdec_engine_seed_state": (I, [P, P, U32]),
     "specdec_engine_step": (I, [P]),
@@ -335,6 +354,118 @@ class PagedKVCache:
 from model_shapes import MODEL_SHAPES  # noqa: E402  (sme-llm-edge_b200/model_shapes.py, pure Python)
 
 
+class SmeTensor:
+    """One tensor of a `.sme` file (the reference's Tensor, server/main.cpp:
+    184-222): name, dims, is_quantized, row factors `scales` (f32 [dims[0]],
+    127 / max|w| per row) and `data` (int8 or f32), as numpy views into the
+    file mapping (valid while the SmeModel is open)."""
+
+    def __init__(self, v: SmeTensorView):
+        self.name = v.name.decode("utf-8", "replace")
+        self.dims = tuple(int(v.dims[i]) for i in range(v.n_dims))
+        self.is_quantized = bool(v.quantized)
+        self.data_bytes = int(v.data_bytes)
+        n = int(v.elements)
+        if self.is_quantized:
+            self.scales = np.frombuffer((C.c_char * (4 * self.dims[0])).from_address(v.scales), np.float32)
+            self.data = np.frombuffer((C.c_char * n).from_address(v.data), np.int8) if n else np.zeros(0, np.int8)
+        else:
+            self.scales = None
+            self.data = (np.frombuffer((C.c_char * (4 * n)).from_address(v.data), np.float32) if n
+                         else np.zeros(0, np.float32))
+
+    def dequantized(self) -> np.ndarray:
+        """Weights as f32: q / scale per row for int8 tensors (the writer's
+        definition, convert_model.py:8-23), the stored values otherwise."""
+        if not self.is_quantized:
+            return self.data.reshape(self.dims)
+        q = self.data.reshape(self.dims[0], -1).astype(np.float32)
+        return (q / self.scales[:, None]).reshape(self.dims)
+
+
+class SmeModel:
+    """A `.sme` model file (load_sme_model, server/main.cpp:112-228), parsed
+    by the library's C++ loader over a read-only mapping of the file."""
+
+    def __init__(self, path=None, buffer: bytes | None = None):
+        h = P()
+        if buffer is not None:
+            self._buf = C.create_string_buffer(bytes(buffer), len(buffer)) if len(buffer) else None
+            check(_lib.specdec_sme_open_buffer(self._buf, len(buffer), C.byref(h)))
+        else:
+            check(_lib.specdec_sme_open(os.fsencode(path), C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.specdec_sme_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def config_json(self) -> str:
+        p, n = C.c_char_p(), SZ(0)
+        check(_lib.specdec_sme_config_json(self._h, C.byref(p), C.byref(n)))
+        return C.string_at(p, n.value).decode("utf-8", "replace")
+
+    def config_number(self, key: str):
+        v = C.c_double(0)
+        rc = _lib.specdec_sme_config_number(self._h, key.encode(), C.byref(v))
+        return None if rc else v.value
+
+    @property
+    def vocab_size(self) -> int:
+        n = U32(0)
+        check(_lib.specdec_sme_vocab_size(self._h, C.byref(n)))
+        return int(n.value)
+
+    def token(self, i: int) -> bytes:
+        p, n = C.c_void_p(), U32(0)
+        check(_lib.specdec_sme_token(self._h, i, C.byref(p), C.byref(n)))
+        return C.string_at(p, n.value) if n.value else b""
+
+    def token_id(self, word) -> int:
+        b = word.encode() if isinstance(word, str) else bytes(word)
+        out = C.c_int32(0)
+        check(_lib.specdec_sme_token_id(self._h, b, len(b), C.byref(out)))
+        return int(out.value)
+
+    def tensor_names(self) -> list:
+        n = U32(0)
+        check(_lib.specdec_sme_tensor_count(self._h, C.byref(n)))
+        out = []
+        for i in range(n.value):
+            v = SmeTensorView()
+            check(_lib.specdec_sme_tensor_at(self._h, i, C.byref(v)))
+            out.append(v.name.decode("utf-8", "replace"))
+        return out
+
+    def tensor(self, name: str) -> SmeTensor:
+        v = SmeTensorView()
+        check(_lib.specdec_sme_find(self._h, name.encode(), C.byref(v)))
+        return SmeTensor(v)
+
+    def model_config(self) -> dict:
+        mc = ModelConfig()
+        check(_lib.specdec_sme_model_config(self._h, C.byref(mc)))
+        return {f: getattr(mc, f) for f, _ in ModelConfig._fields_}
+
+
 def model_config(shape: dict) -> ModelConfig:
     return ModelConfig(shape["hidden"], shape["layers"], shape["n_q_heads"], shape["n_kv_heads"], shape["head_dim"],
                        shape["ffn"], shape["vocab"], shape["n_mtp_heads"], 16, shape.get("rms_eps", 1e-5),
@@ -387,6 +518,20 @@ class Engine:
 
     def init_weights(self, seed: int):
         check(_lib.specdec_engine_init_weights(self._h, seed))
+
+    def load_sme(self, model: "SmeModel", missing_seed: int = 0):
+        """Weights from a `.sme` file (requantised to int4 group-128 on the
+        device); MTP heads the file lacks are synthesised from missing_seed."""
+        check(_lib.specdec_engine_load_sme(self._h, model.handle, missing_seed))
+
+    @classmethod
+    def from_sme(cls, path, batch: int, missing_seed: int = 0, **run):
+        """Engine shaped by a `.sme` file's config, loaded with its weights."""
+        with SmeModel(path) as m:
+            shape = m.model_config()
+            eng = cls(shape, batch, **run)
+            eng.load_sme(m, missing_seed)
+        return eng
 
     def prefill(self, prompts):
         p = np.ascontiguousarray(prompts, dtype=np.int32)
