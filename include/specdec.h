@@ -305,6 +305,22 @@ int specdec_kv_read(specdec_kv* kv, int32_t* tables, int32_t* lens, int32_t* ref
 int32_t* specdec_kv_tables_dev(specdec_kv* kv);
 int32_t* specdec_kv_lens_dev(specdec_kv* kv);
 
+/* Prefix index of admitted prompts: RadixKVCache (server/radix_kv_cache.h:
+ * 16-38, .cpp:39-98) with its per-token semantics -- insert adds one
+ * reference to every position of the path and records the request as the
+ * source of the positions it creates; match returns the positions matched
+ * from the root and the source of the deepest one ((0, -1) for none);
+ * release removes one reference along the request's remembered path and
+ * drops subtrees left without references.  Host memory, thread-safe. */
+typedef struct specdec_radix specdec_radix;
+int specdec_radix_create(specdec_radix** out);
+int specdec_radix_destroy(specdec_radix* r);
+int specdec_radix_match(specdec_radix* r, const int32_t* tokens, int n, int32_t* matched, int32_t* source);
+int specdec_radix_insert(specdec_radix* r, int32_t request_id, const int32_t* tokens, int n);
+int specdec_radix_release(specdec_radix* r, int32_t request_id);
+/* Nodes (edges) held and token positions they cover. */
+int specdec_radix_stats(specdec_radix* r, int64_t* nodes, int64_t* positions);
+
 /* ===================================================================== */
 /* 4. Step engine: the whole speculative step on device.                  */
 /* ===================================================================== */
@@ -349,6 +365,21 @@ int specdec_engine_load_sme(specdec_engine* e, const specdec_sme* f, uint32_t mi
 /* Chunked prefill of host prompts [batch, prompt_len] (all but the last
  * token enter the KV; the last becomes the pending token). */
 int specdec_engine_prefill(specdec_engine* e, const int32_t* prompts, int prompt_len);
+/* Starts sequence slot `seq` on a new request (ids are the caller's): the
+ * slot's previous request is retired first.  With a prefix index, the
+ * longest indexed prefix of the prompt whose source request still holds a
+ * slot is shared block by block (the source's whole 16-token blocks, at most
+ * prompt_len - 2 tokens so the last KV token is recomputed for the draft
+ * state; PagedKVCache::share_prefix, paged_kv_cache.cpp:136-154, with
+ * reference counts), only the remaining prompt tokens are prefilled (64-row
+ * chunks of this sequence alone), and the prompt's KV tokens are inserted
+ * into the index under request_id.  shared_tokens (may be NULL) receives the
+ * number of shared tokens.  Synchronises the engine stream. */
+int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt, int prompt_len,
+                         specdec_radix* cache, int32_t* shared_tokens);
+/* Releases slot `seq`: its KV blocks (shared blocks survive while another
+ * slot holds them) and, with an index, its prefix references. */
+int specdec_engine_retire(specdec_engine* e, int seq, specdec_radix* cache);
 /* Synthetic state: every sequence gets ctx_len[b] tokens of seeded random
  * fp16 K/V, a random pending token and a random draft hidden state. */
 int specdec_engine_seed_state(specdec_engine* e, const int32_t* ctx_len, uint32_t seed);

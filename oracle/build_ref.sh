@@ -4,6 +4,8 @@
 #
 #   server/paged_attention.cpp, server/speculative_decoder.cpp,
 #   server/mtp_heads.cpp                 compiled in place, unmodified;
+#   server/radix_kv_cache.cpp            compiled in place, unmodified, with
+#                                        <functional> force-included;
 #   server/paged_kv_cache.cpp            compiled unmodified from a scratch copy
 #                                        under oracle/_ref/src whose header has
 #                                        the one-word shim the reference needs
@@ -37,6 +39,9 @@ $CXX $CXXFLAGS -c "$REF/server/paged_attention.cpp" -o "$OUT/obj/paged_attention
 $CXX $CXXFLAGS -c "$REF/server/speculative_decoder.cpp" -o "$OUT/obj/speculative_decoder.o"
 $CXX $CXXFLAGS -c "$REF/server/mtp_heads.cpp" -o "$OUT/obj/mtp_heads.o"
 $CXX $CXXFLAGS -c "$OUT/src/paged_kv_cache.cpp" -o "$OUT/obj/paged_kv_cache.o"
+# radix_kv_cache.cpp uses std::function without including <functional>; the
+# header is supplied on the command line (-include), the source is unmodified
+$CXX $CXXFLAGS -include functional -c "$REF/server/radix_kv_cache.cpp" -o "$OUT/obj/radix_kv_cache.o"
 $CXX $CXXFLAGS -I"$OUT/src" -I"$REF/server" -I"$HERE" -c "$HERE/ref_shim.cpp" -o "$OUT/obj/ref_shim.o"
 for f in orc_sample orc_model orc_kv; do
   $CC $CFLAGS -c "$HERE/$f.c" -o "$OUT/obj/$f.o"

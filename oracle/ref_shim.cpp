@@ -15,6 +15,7 @@
 #include "mtp_heads.h"
 #include "paged_attention.h"
 #include "paged_kv_cache.h"
+#include "radix_kv_cache.h"
 #include "speculative_decoder.h"
 
 extern "C" {
@@ -97,4 +98,17 @@ extern "C" void ref_mtp_generate(const float* weights, const float* hidden_state
     heads.load_weights(weights);
     std::vector<int32_t> d = heads.generate_drafts(hidden_state);
     for (int i = 0; i < k; ++i) out[i] = d[i];
+}
+
+// RadixKVCache (server/radix_kv_cache.cpp), driven op by op.
+extern "C" void* ref_radix_create() { return new RadixKVCache(); }
+extern "C" void ref_radix_destroy(void* h) { delete static_cast<RadixKVCache*>(h); }
+extern "C" void ref_radix_insert(void* h, int req, const int32_t* t, int n) {
+    static_cast<RadixKVCache*>(h)->insert_prefix(req, std::vector<int>(t, t + n));
+}
+extern "C" void ref_radix_release(void* h, int req) { static_cast<RadixKVCache*>(h)->release_prefix(req); }
+extern "C" void ref_radix_match(void* h, const int32_t* t, int n, int32_t* matched, int32_t* source) {
+    auto r = static_cast<RadixKVCache*>(h)->match_prefix(std::vector<int>(t, t + n));
+    *matched = r.first;
+    *source = r.second;
 }

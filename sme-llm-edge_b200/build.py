@@ -21,7 +21,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "specdec", "libspecdec_sm100.so")
-SOURCES = ["runtime.cu", "sampling.cu", "kvcache.cu", "attention.cu", "gemm_w4a16.cu", "gemv_w4a16.cu", "engine.cu", "compat.cu", "sme_loader.cu"]
+SOURCES = ["runtime.cu", "sampling.cu", "kvcache.cu", "attention.cu", "gemm_w4a16.cu", "gemv_w4a16.cu", "engine.cu", "compat.cu", "sme_loader.cu", "radix_cache.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -525,6 +525,7 @@ struct specdec_engine {
     cudaGraphExec_t gexec = nullptr;
     int kernels_per_step = 0;
     std::vector<int> host_parent;
+    std::vector<int32_t> slot_request;  // request id admitted into each slot (-1: none)
     // profiler: an event after every launch; the interval since the previous
     // event is that launch's device time (one stream, in-order execution)
     bool prof_on = false;
@@ -622,12 +623,15 @@ int gemm_swiglu(specdec_engine* e, const __half* X, int M, int K, const uint8_t*
     } while (0)
 #define ENG_LAUNCH(name) ENG_LAUNCH_CAT(name, CAT_OTHER)
 
-// Verify forward over Rrows rows per sequence (Rrows * B rows in total).
-int forward(specdec_engine* e, int Rrows, bool want_logits) {
+// Verify forward over Rrows rows per sequence for sequences b0 .. b0 + nseq - 1
+// (all of them by default): Rrows * nseq rows in total.
+int forward(specdec_engine* e, int Rrows, bool want_logits, int b0 = 0, int nseq = -1) {
     const auto& c = e->mc;
-    const int B = e->B, M = B * Rrows, H = c.hidden, F = c.ffn, hd = c.head_dim;
+    const int B = nseq < 0 ? e->B : nseq, M = B * Rrows, H = c.hidden, F = c.ffn, hd = c.head_dim;
     cudaStream_t s = e->stream;
     KVState& kvs = kv_state(e->kvm);
+    const int32_t* tables = kvs.tables + (size_t)b0 * e->max_blocks;
+    const int32_t* ctx = kvs.ctx + b0;
     e->gemm_cat = CAT_GEMM_VERIFY;
     embed_kernel<<<M, 256, 0, s>>>(e->tokens, e->emb, H, c.vocab, e->x);
     ENG_LAUNCH("embed_kernel");
@@ -640,7 +644,7 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
             RopeArgs ra;
             ra.pos = e->pos;
             ra.slot = e->slot;
-            ra.tables = kvs.tables;
+            ra.tables = tables;
             ra.max_blocks = e->max_blocks;
             ra.R = Rrows;
             ra.cos_t = e->rope_cos;
@@ -653,12 +657,12 @@ int forward(specdec_engine* e, int Rrows, bool want_logits) {
             ENG_TRY(gemm_qkv_rope(e, e->xn, M, H, w.qkv, e->NQKV, ra));
         } else {
             ENG_TRY(gemm(e, e->xn, M, H, w.qkv, e->NQKV, e->qkv, e->NQKV, 0));
-            rope_kv_kernel<<<M, 256, 0, s>>>(e->qkv, e->NQKV, e->pos, e->slot, kvs.tables, e->max_blocks, Rrows,
+            rope_kv_kernel<<<M, 256, 0, s>>>(e->qkv, e->NQKV, e->pos, e->slot, tables, e->max_blocks, Rrows,
                                              e->rope_cos, e->rope_sin, c.n_q_heads, c.n_kv_heads, hd, kv_l, e->q16);
             ENG_LAUNCH("rope_kv_kernel");
         }
         ++e->kernels_per_step;
-        ENG_TRY(launch_attention(e->q16, kv_l, e->num_blocks, c.n_kv_heads, hd, kvs.tables, e->max_blocks, kvs.ctx,
+        ENG_TRY(launch_attention(e->q16, kv_l, e->num_blocks, c.n_kv_heads, hd, tables, e->max_blocks, ctx,
                                  e->mask, B, Rrows, c.n_q_heads, e->att, e->attn_ws, e->attn_ws_bytes,
                                  e->rc.max_ctx, s));
         prof_mark(e, CAT_ATTENTION);
@@ -819,6 +823,7 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
     const int H = mc->hidden, F = mc->ffn, V = mc->vocab, hd = mc->head_dim, Hkv = mc->n_kv_heads;
     e->tree = rc->tree_nodes > 0;
     e->B = rc->batch;
+    e->slot_request.assign(rc->batch, -1);
     if (e->tree) {
         SD_CHECK(rc->tree_nodes <= 64 && rc->tree_levels >= 1 && rc->tree_levels <= 8, SPECDEC_EINVAL,
                  "engine_create: tree must have <= 64 nodes and 1..8 levels");
@@ -1131,6 +1136,85 @@ extern "C" int specdec_engine_prefill(specdec_engine* e, const int32_t* prompts,
     SD_CUDA(cudaMemcpy(&st, kvs.status, sizeof(int), cudaMemcpyDeviceToHost));
     SD_CHECK(!st, SPECDEC_ENOMEM, "engine_prefill: KV block pool exhausted");
     return check_device_status(s);
+}
+
+extern "C" int specdec_engine_retire(specdec_engine* e, int seq, specdec_radix* cache) {
+    SD_CHECK(e && seq >= 0 && seq < e->B, SPECDEC_EINVAL, "engine_retire: bad argument");
+    if (cache && e->slot_request[seq] >= 0) {
+        const int rc = specdec_radix_release(cache, e->slot_request[seq]);
+        if (rc) return rc;
+    }
+    e->slot_request[seq] = -1;
+    return specdec_kv_free_request(e->kvm, seq, e->stream);
+}
+
+extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt, int P,
+                                    specdec_radix* cache, int32_t* shared_tokens) {
+    SD_CHECK(e && prompt && seq >= 0 && seq < e->B && P >= 2 && P <= e->rc.max_ctx, SPECDEC_EINVAL,
+             "engine_admit: bad argument");
+    cudaStream_t s = e->stream;
+    const int H = e->mc.hidden;
+    int rc = specdec_engine_retire(e, seq, cache);
+    if (rc) return rc;
+    // longest indexed prefix of the prompt's KV tokens whose source still holds a slot
+    int shared = 0;
+    if (cache) {
+        int32_t m = 0, src = -1;
+        if ((rc = specdec_radix_match(cache, prompt, P - 1, &m, &src))) return rc;
+        int src_slot = -1;
+        for (int b = 0; b < e->B && src >= 0; ++b)
+            if (b != seq && e->slot_request[b] == src) src_slot = b;
+        if (src_slot >= 0) {
+            shared = std::min<int>(m, P - 2) / 16 * 16;  // whole blocks; the last KV token is recomputed
+            if (shared > 0 && (rc = specdec_kv_share_prefix(e->kvm, seq, src_slot, shared, s))) return rc;
+        }
+    }
+    int32_t* d_prompt = nullptr;
+    SD_CUDA(cudaMallocAsync(&d_prompt, sizeof(int32_t) * (size_t)P, s));
+    SD_CUDA(cudaMemcpyAsync(d_prompt, prompt, sizeof(int32_t) * (size_t)P, cudaMemcpyHostToDevice, s));
+    std::vector<uint64_t> chain(64);
+    for (int r = 0; r < 64; ++r) chain[r] = (r == 63) ? ~0ull : ((1ull << (r + 1)) - 1);
+    uint64_t* saved_mask = nullptr;
+    if (e->tree) {
+        SD_CUDA(cudaMallocAsync(&saved_mask, 8 * 64, s));
+        SD_CUDA(cudaMemcpyAsync(saved_mask, e->mask, 8 * 64, cudaMemcpyDeviceToDevice, s));
+    }
+    SD_CUDA(cudaMemcpyAsync(e->mask, chain.data(), 8 * 64, cudaMemcpyHostToDevice, s));
+    KVState& kvs = kv_state(e->kvm);
+    const int n_end = P - 1;  // the last prompt token becomes the pending token
+    int last_rp = 0;
+    for (int c0 = shared; c0 < n_end && !rc; c0 += 64) {
+        const int Rp = std::min(64, n_end - c0);
+        if ((rc = kv_append_uniform(e->kvm, 1, Rp, s, seq))) break;
+        prefill_rows_kernel<<<(Rp + 127) / 128, 128, 0, s>>>(d_prompt, P, c0, Rp, kvs.ctx + seq, 1, e->tokens, e->pos,
+                                                            e->slot);
+        if (cudaGetLastError() != cudaSuccess) {
+            rc = SPECDEC_ECUDA;
+            break;
+        }
+        rc = forward(e, Rp, false, seq, 1);
+        last_rp = Rp;
+    }
+    if (!rc) {
+        prefill_finish_kernel<<<1, 256, 0, s>>>(d_prompt, P, e->x, last_rp, H, e->pending + seq,
+                                                e->h0 + (size_t)seq * H);
+        if (cudaGetLastError() != cudaSuccess) rc = SPECDEC_ECUDA;
+    }
+    if (e->tree) {
+        cudaMemcpyAsync(e->mask, saved_mask, 8 * 64, cudaMemcpyDeviceToDevice, s);
+        cudaFreeAsync(saved_mask, s);
+    }
+    cudaFreeAsync(d_prompt, s);
+    SD_CUDA(cudaStreamSynchronize(s));
+    if (rc) return rc;
+    int st = 0;
+    SD_CUDA(cudaMemcpy(&st, kvs.status, sizeof(int), cudaMemcpyDeviceToHost));
+    SD_CHECK(!st, SPECDEC_ENOMEM, "engine_admit: KV block pool exhausted");
+    if ((rc = check_device_status(s))) return rc;
+    if (cache && (rc = specdec_radix_insert(cache, request_id, prompt, P - 1))) return rc;
+    e->slot_request[seq] = request_id;
+    if (shared_tokens) *shared_tokens = shared;
+    return SPECDEC_OK;
 }
 
 extern "C" int specdec_engine_seed_state(specdec_engine* e, const int32_t* ctx_len, uint32_t seed) {

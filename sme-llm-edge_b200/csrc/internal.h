@@ -111,7 +111,8 @@ struct KVState {
     int32_t* status;   // [1] ENOMEM flag of the last batch append
 };
 KVState& kv_state(specdec_kv* kv);
-int kv_append_uniform(specdec_kv* kv, int n, int tokens, cudaStream_t s);
+// requests r0 .. r0 + n - 1 each append `tokens` tokens
+int kv_append_uniform(specdec_kv* kv, int n, int tokens, cudaStream_t s, int r0 = 0);
 int kv_truncate_dev(specdec_kv* kv, const int32_t* new_len_dev, int n, cudaStream_t s);
 
 // ------------------------------------------------------------ .sme weights

@@ -50,10 +50,10 @@ __device__ int block_excl_scan(int v, int* sh, int* total) {
 }
 
 // Batch append (one CTA).  reqs/ntok: n entries (device).  uniform_n >= 0
-// means every request in [0, n) appends uniform_n tokens (reqs == identity).
+// means every request in [r0, r0 + n) appends uniform_n tokens.
 __global__ void __launch_bounds__(kKVThreads) kv_append_kernel(KVState s, const int32_t* __restrict__ reqs,
                                                                const int32_t* __restrict__ ntok, int n, int uniform_n,
-                                                               int32_t* __restrict__ last_block) {
+                                                               int r0, int32_t* __restrict__ last_block) {
     __shared__ int sh[32];
     int32_t* need = s.scratch;                       // [n] blocks granted
     int32_t* got_off = s.scratch + s.max_reqs;       // [n] offset into the free list
@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(kKVThreads) kv_append_kernel(KVState s, const 
         int avail = total_free, used = 0;
         s.status[0] = 0;
         for (int i = 0; i < n; ++i) {
-            const int r = uniform_n >= 0 ? i : reqs[i];
+            const int r = uniform_n >= 0 ? r0 + i : reqs[i];
             const int t = uniform_n >= 0 ? uniform_n : ntok[i];
             if (s.nblk[r] < 0) {
                 s.nblk[r] = 0;
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kKVThreads) kv_append_kernel(KVState s, const 
     __syncthreads();
     // 3) hand out the lowest free indices in request order
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int r = uniform_n >= 0 ? i : reqs[i];
+        const int r = uniform_n >= 0 ? r0 + i : reqs[i];
         for (int j = 0; j < need[i]; ++j) {
             const int blk = freelist[got_off[i] + j];
             s.tables[(size_t)r * s.max_bpr + base_nb[i] + j] = blk;
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(kKVThreads) kv_append_kernel(KVState s, const 
     }
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int r = uniform_n >= 0 ? i : reqs[i];
+        const int r = uniform_n >= 0 ? r0 + i : reqs[i];
         if (last_block && last_block[i] <= -2) last_block[i] = s.tables[(size_t)r * s.max_bpr + (-2 - last_block[i])];
     }
 }
@@ -204,8 +204,8 @@ struct specdec_kv {
 
 namespace specdec {
 KVState& kv_state(specdec_kv* kv) { return kv->s; }
-int kv_append_uniform(specdec_kv* kv, int n, int tokens, cudaStream_t s) {
-    kv_append_kernel<<<1, kKVThreads, 0, s>>>(kv->s, nullptr, nullptr, n, tokens, nullptr);
+int kv_append_uniform(specdec_kv* kv, int n, int tokens, cudaStream_t s, int r0) {
+    kv_append_kernel<<<1, kKVThreads, 0, s>>>(kv->s, nullptr, nullptr, n, tokens, r0, nullptr);
     SD_LAUNCH_CHECK("kv_append_kernel");
     return SPECDEC_OK;
 }
@@ -281,7 +281,7 @@ extern "C" int specdec_kv_append(specdec_kv* kv, const int32_t* reqs, const int3
     }
     SD_CUDA(cudaMemcpyAsync(kv->d_tmp, h, sizeof(int32_t) * 2 * n, cudaMemcpyHostToDevice, s));
     int32_t* d_out = kv->d_tmp + 2 * n;
-    kv_append_kernel<<<1, kKVThreads, 0, s>>>(kv->s, kv->d_tmp, kv->d_tmp + n, n, -1, d_out);
+    kv_append_kernel<<<1, kKVThreads, 0, s>>>(kv->s, kv->d_tmp, kv->d_tmp + n, n, -1, 0, d_out);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaMemcpyAsync(h, d_out, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);

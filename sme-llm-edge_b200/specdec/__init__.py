@@ -123,6 +123,14 @@ _SIGS = {
     "specdec_engine_destroy": (I, [P]),
     "specdec_engine_init_weights": (I, [P, U32]),
     "specdec_engine_load_sme": (I, [P, P, U32]),
+    "specdec_engine_admit": (I, [P, I, C.c_int32, P, I, P, C.POINTER(C.c_int32)]),
+    "specdec_engine_retire": (I, [P, I, P]),
+    "specdec_radix_create": (I, [C.POINTER(P)]),
+    "specdec_radix_destroy": (I, [P]),
+    "specdec_radix_match": (I, [P, P, I, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "specdec_radix_insert": (I, [P, C.c_int32, P, I]),
+    "specdec_radix_release": (I, [P, C.c_int32]),
+    "specdec_radix_stats": (I, [P, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "specdec_sme_open": (I, [C.c_char_p, C.POINTER(P)]),
     "specdec_sme_open_buffer": (I, [P, SZ, C.POINTER(P)]),
     "specdec_sme_close": (I, [P]),
@@ -466,6 +474,51 @@ class SmeModel:
         return {f: getattr(mc, f) for f, _ in ModelConfig._fields_}
 
 
+class RadixKVCache:
+    """server/radix_kv_cache.h: prefix index of admitted prompts (host side,
+    path-compressed, the reference's per-token semantics)."""
+
+    def __init__(self):
+        h = P()
+        check(_lib.specdec_radix_create(C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.specdec_radix_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def match_prefix(self, tokens):
+        """-> (matched_token_count, source_request_id)"""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        m, src = C.c_int32(0), C.c_int32(-1)
+        check(_lib.specdec_radix_match(self._h, _p(t), t.size, C.byref(m), C.byref(src)))
+        return int(m.value), int(src.value)
+
+    def insert_prefix(self, request_id: int, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(_lib.specdec_radix_insert(self._h, int(request_id), _p(t), t.size))
+
+    def release_prefix(self, request_id: int):
+        check(_lib.specdec_radix_release(self._h, int(request_id)))
+
+    def stats(self):
+        """-> (nodes, token positions) held by the tree."""
+        n, p = C.c_int64(0), C.c_int64(0)
+        check(_lib.specdec_radix_stats(self._h, C.byref(n), C.byref(p)))
+        return int(n.value), int(p.value)
+
+
 def model_config(shape: dict) -> ModelConfig:
     return ModelConfig(shape["hidden"], shape["layers"], shape["n_q_heads"], shape["n_kv_heads"], shape["head_dim"],
                        shape["ffn"], shape["vocab"], shape["n_mtp_heads"], 16, shape.get("rms_eps", 1e-5),
@@ -536,6 +589,19 @@ class Engine:
     def prefill(self, prompts):
         p = np.ascontiguousarray(prompts, dtype=np.int32)
         check(_lib.specdec_engine_prefill(self._h, _p(p), p.shape[1]))
+
+    def admit(self, seq: int, request_id: int, prompt, cache: "RadixKVCache | None" = None) -> int:
+        """Starts slot `seq` on a new request; with a prefix index, shares the
+        KV blocks of an indexed prefix and prefills only the rest.  Returns
+        the number of shared tokens."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32).reshape(-1)
+        shared = C.c_int32(0)
+        check(_lib.specdec_engine_admit(self._h, seq, int(request_id), _p(p), p.size,
+                                        cache.handle if cache is not None else None, C.byref(shared)))
+        return int(shared.value)
+
+    def retire(self, seq: int, cache: "RadixKVCache | None" = None):
+        check(_lib.specdec_engine_retire(self._h, seq, cache.handle if cache is not None else None))
 
     def seed_state(self, ctx_len, seed: int):
         c = np.ascontiguousarray(ctx_len, dtype=np.int32)

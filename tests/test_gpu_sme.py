@@ -22,13 +22,12 @@ import pytest
 import oracle as O
 import sme_format as SF
 import specdec as S
-from helpers import dev, interleave_gu, margin_ok, ptr, stream_ptr, sync, tile_w4
+from helpers import dev, interleave_gu, ptr, steps_match_oracle, stream_ptr, sync, tile_w4
 
 pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 FIXTURE = os.path.join(HERE, "golden", "tiny_llama.sme")
-LOGIT_TOL = 2e-2
 
 ROLE_NAMES = {
     "ref": dict(embed="embed_tokens", norm="norm", lm_head="lm_head", q="layers.{}.q_proj", k="layers.{}.k_proj",
@@ -142,56 +141,11 @@ def _check_weights(eng, mc, proj, lm, mtp, emb16):
     np.testing.assert_array_equal(eng.read("emb", np.uint16, (V * H,)), emb16.reshape(-1))
 
 
-def _check_logits(got, ref, what):
-    err = np.abs(got - ref).max()
-    assert err < LOGIT_TOL, f"{what}: max |logit diff| {err}"
-    rows, refr = got.reshape(-1, got.shape[-1]), ref.reshape(-1, ref.shape[-1])
-    assert all(int(rows[i].argmax()) == int(refr[i].argmax()) for i in range(rows.shape[0]) if margin_ok(refr[i])), what
-
-
 def _run_parity(eng, model, mc, B, k, T, seed, prompt_len, steps):
-    """Prefill, then speculative steps checked against the oracle forward
-    from the engine's pre-step state (the step-engine test's procedure)."""
-    V, H = mc["vocab"], mc["hidden"]
+    """Prefill, then speculative steps checked against the oracle."""
     rng = np.random.default_rng(seed)
-    prompt = rng.integers(0, V, (B, prompt_len)).astype(np.int32)
-    eng.prefill(prompt)
-    mb, nb = eng.info("max_blocks"), eng.info("num_blocks")
-    R = k + 1
-    chain = np.array([(1 << (r + 1)) - 1 for r in range(R)], np.uint64)
-    for step in range(steps):
-        h0_prev = eng.read("h0", np.float32, (B, H))
-        pend_prev = eng.read("pending", np.int32, (B,))
-        kvo = O.OracleKV(mc["layers"], nb, mc["n_kv_heads"], 16, mc["head_dim"])
-        kvo.pool[:] = eng.read("kv", np.uint16, kvo.pool.shape)
-        lens_prev = eng.read("lens", np.int32, (B,)).copy()
-        tab_pre = eng.read("tables", np.int32, (B, mb))
-        acc, out = eng.step_host()
-        dl = eng.read("draft_logits", np.float32, (B, k, V))
-        drafts = eng.read("drafts", np.int32, (B, k))
-        lg = eng.read("logits", np.float32, (B, R, V))
-        acc_o, out_o = O.accept_chain(lg, dl, drafts, T, 1.0, seed, step)
-        assert acc.tolist() == acc_o.tolist() and out.tolist() == out_o.tolist()
-        dl_o, _, _ = O.draft_chain(model, h0_prev, k, T, 1.0, seed, step)
-        _check_logits(dl, dl_o, f"draft logits step {step}")
-        toks = np.concatenate([np.concatenate([[pend_prev[b]], drafts[b]]) for b in range(B)]).astype(np.int32)
-        pos = np.concatenate([lens_prev[b] + np.arange(R) for b in range(B)]).astype(np.int32)
-        lg_o, _ = O.forward(model, kvo, _extend_tables(tab_pre, lens_prev, R, nb), lens_prev, toks, pos, pos, chain,
-                            B, R)
-        _check_logits(lg, lg_o.reshape(B, R, V), f"target logits step {step}")
-
-
-def _extend_tables(tab_pre, lens_prev, R, nb):
-    """Pre-step block tables extended to the step's R new slots: the context
-    blocks are the engine's; a new slot past them may take any block no
-    table uses (the oracle forward writes the new rows' K/V before reading)."""
-    tab = tab_pre.copy()
-    free = iter(sorted(set(range(nb)) - set(tab[tab >= 0].tolist())))
-    for b in range(tab.shape[0]):
-        have = int((tab[b] >= 0).sum())
-        for j in range(have, (int(lens_prev[b]) + R + 15) // 16):
-            tab[b, j] = next(free)
-    return tab
+    eng.prefill(rng.integers(0, mc["vocab"], (B, prompt_len)).astype(np.int32))
+    steps_match_oracle(eng, model, mc, B, k, T, seed, steps)
 
 
 @pytest.fixture(scope="module")
