@@ -102,6 +102,28 @@ __device__ __forceinline__ uint32_t exp2_fx31(float t) {
     return (uint32_t)v;
 }
 
+// exp2_fx31 without branches (identical results for every t, NaN included):
+// t is clamped to [-40, 0] (NaN and positive t to 0, as above); for
+// t < -31.5 the exponent e = rint(t) + 31 is negative and p * 2^e < 1
+// truncates to 0, the value the early returns give.
+__device__ __forceinline__ uint32_t exp2_fx31_bf(float t) {
+    t = (t <= 0.0f) ? t : 0.0f;
+    t = fmaxf(t, -40.0f);
+    const float n = rintf(t);
+    const float f = __fsub_rn(t, n);
+    const float x = __fmul_rn(f, 0x1.62e43p-1f);
+    float p = 0x1.a01a02p-13f;
+    p = __fmaf_rn(p, x, 0x1.6c16c2p-10f);
+    p = __fmaf_rn(p, x, 0x1.111112p-7f);
+    p = __fmaf_rn(p, x, 0x1.555556p-5f);
+    p = __fmaf_rn(p, x, 0x1.555556p-3f);
+    p = __fmaf_rn(p, x, 0x1p-1f);
+    p = __fmaf_rn(p, x, 0x1p+0f);
+    p = __fmaf_rn(p, x, 0x1p+0f);
+    const int e = (int)n + 31;  // >= -9
+    return (uint32_t)__fmul_rn(p, __int_as_float((e + 127) << 23));
+}
+
 __device__ __forceinline__ uint32_t logit_key(float z) {
     uint32_t b = __float_as_uint(z);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);

@@ -129,6 +129,39 @@ __device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, floa
     __syncthreads();
 }
 
+// Row maximum only (NaN never wins; -inf for an empty or all-NaN row): one
+// max per element, four float4 loads in flight per thread.
+__device__ float cta_max(const float* __restrict__ z, int V, RowSmem& sm) {
+    float bv = -INFINITY;
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+        const float4* z4 = reinterpret_cast<const float4*>(z);
+        const int n4 = V / 4, bd = blockDim.x;
+        int q = threadIdx.x;
+        for (; q + 3 * bd < n4; q += 4 * bd) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) bv = fmaxf(bv, fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w)));
+        }
+        for (; q < n4; q += bd) {
+            const float4 v = z4[q];
+            bv = fmaxf(bv, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+        }
+    } else {
+        for (int j = threadIdx.x; j < V; j += blockDim.x) bv = fmaxf(bv, z[j]);
+    }
+    bv = warp_max(bv);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) sm.redf[wid] = bv;
+    __syncthreads();
+    float r = lane < nw ? sm.redf[lane] : -INFINITY;
+    r = warp_max(r);
+    __syncthreads();
+    return r;
+}
+
 // Calls f(z_j) for every element of the row z[0, V) once, in no particular
 // order: four float4 loads in flight per thread when z is 16-byte aligned and
 // V a multiple of 4, else one element per thread and iteration.
@@ -254,20 +287,112 @@ __device__ uint64_t cta_mass_sum(const float* __restrict__ z, int n, float m, fl
 }
 
 // Full row statistics (max, argmax, mass sum, top-p threshold, nucleus mass).
-// The top-p threshold is a radix select on the logit key, 8 bits per pass,
-// over mass-weighted histograms.  whist (only needed when tp < 2^32) holds one
-// private histogram per warp ([warps][2][256] u32) and then a list of up to
-// kNucleusList (key, mass) pairs: the second pass records the elements whose
-// top digit was selected, and the last two passes read only that list (or the
-// row again, when it overflowed).
+//
+// The top-p threshold tau is the largest logit key with
+// sum_{key >= tau} E >= thr, thr = max(1, floor(S * top_p)).  Two passes over
+// the row in the common case: the arg-max pass, then one pass that sums the
+// masses and lists the elements whose exponent t = (z - max) * c is at least
+// kTList (mass >= 2^kTList of the maximum's) as (key, mass) pairs.  When the
+// list holds all of them (at most kNucleusList) and its mass reaches thr, the
+// threshold lies among the listed elements -- every element with a larger key
+// has a larger t and is listed too -- and a 4-digit radix select over the
+// list (8 bits per digit, mass-weighted) finds it.  Otherwise (flat rows whose
+// nucleus reaches below kTList, NaN logits) the radix select runs over the
+// whole row: the first digit from a row pass into per-warp histograms (the
+// 16-bit halves of each mass, only lanes of one warp contend), the second from
+// another row pass that also lists the elements of the selected top digit, the
+// last two from that list (or the row again when it overflowed).
+// whist (only needed when tp < 2^32) holds the per-warp histograms
+// ([warps][2][256] u32) and then the list.
 constexpr int kNucleusList = 8192;
+constexpr float kTList = -14.0f;
 constexpr size_t kWarpHistWords = (size_t)(kRowThreads / 32) * 512;
 constexpr size_t kWarpHistBytes = kWarpHistWords * sizeof(uint32_t) + (size_t)kNucleusList * sizeof(uint2) + 16;
+
+// Mass-weighted radix select of tau over list[0, n) (every element with a key
+// above tau is in the list): returns tau and the mass of the keys >= tau.
+// Per-warp 32-bit histograms as in the row passes (the listed keys share their
+// leading digits, so one shared histogram would serialise on a few bins).
+__device__ void list_topp_select(const uint2* list, int n, uint64_t thr, RowSmem& sm, uint32_t* whist,
+                                 uint32_t* tau, uint64_t* nuc) {
+    uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
+    for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist[i] = 0;
+    __syncthreads();
+    uint64_t G = 0, last = 0;
+    uint32_t prefix = 0, dg = 0;
+    for (int d = 3; d >= 0; --d) {
+        const int shift = 8 * d;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint2 en = list[i];
+            if (d == 3 || (en.x >> (shift + 8)) == (prefix >> (shift + 8))) hist_add_lane(Hw, (en.x >> shift) & 255u, en.y);
+        }
+        merge_warp_hists(whist, sm);
+        select_digit(sm, thr, &G, &dg, &last);
+        prefix |= dg << shift;
+    }
+    *tau = prefix;
+    *nuc = G + last;
+}
+
+// The radix select over the whole row (see above); s = the row's mass sum.
+__device__ void row_topp_select(const float* __restrict__ z, int V, float m, float c, uint64_t thr, RowSmem& sm,
+                                uint32_t* whist, uint32_t* tau, uint64_t* nuc) {
+    uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
+    uint2* list = reinterpret_cast<uint2*>(whist + kWarpHistWords);
+    int* list_n = reinterpret_cast<int*>(list + kNucleusList);
+    for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist[i] = 0;
+    if (threadIdx.x == 0) *list_n = 0;
+    __syncthreads();
+    for_each_row_value(z, V, [&](float zj) { hist_add_lane(Hw, logit_key(zj) >> 24, mass_of(zj, m, c)); });
+    merge_warp_hists(whist, sm);
+    uint64_t G = 0, last = 0;
+    uint32_t prefix = 0, dg = 0;
+    select_digit(sm, thr, &G, &dg, &last);
+    prefix = dg << 24;
+    for (int d = 2; d >= 0; --d) {
+        const int shift = 8 * d;
+        const uint32_t want = prefix >> (shift + 8);
+        if (d == 2) {
+            for_each_row_value(z, V, [&](float zj) {
+                const uint32_t key = logit_key(zj);
+                if ((key >> (shift + 8)) == want) {
+                    const uint32_t e = mass_of(zj, m, c);
+                    hist_add_lane(Hw, (key >> shift) & 255u, e);
+                    const int at = atomicAdd(list_n, 1);
+                    if (at < kNucleusList) list[at] = make_uint2(key, e);
+                }
+            });
+        } else if (*list_n <= kNucleusList) {
+            const int n = *list_n;
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const uint2 en = list[i];
+                if ((en.x >> (shift + 8)) == want) hist_add_lane(Hw, (en.x >> shift) & 255u, en.y);
+            }
+        } else {
+            for_each_row_value(z, V, [&](float zj) {
+                const uint32_t key = logit_key(zj);
+                if ((key >> (shift + 8)) == want) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
+            });
+        }
+        merge_warp_hists(whist, sm);
+        select_digit(sm, thr, &G, &dg, &last);
+        prefix |= dg << shift;
+    }
+    *tau = prefix;
+    *nuc = G + last;
+}
+
+// need_mass: the sampling statistics (max, mass sum, top-p threshold and
+// nucleus mass; argmax = -1); else the greedy statistics (max and argmax).
 __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint64_t tp, bool need_mass, RowSmem& sm,
                               DevRowStats* st, uint32_t* whist = nullptr) {
     float m;
-    int am;
-    cta_argmax(z, V, sm, &m, &am);
+    int am = -1;
+    if (need_mass) {
+        m = cta_max(z, V, sm);
+    } else {
+        cta_argmax(z, V, sm, &m, &am);
+    }
     DevRowStats r;
     r.max = m;
     r.argmax = am;
@@ -278,63 +403,80 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
     if (need_mass) {
         const bool nucleus = tp < (1ull << 32);
         uint64_t s = 0;
-        uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
-        uint2* list = reinterpret_cast<uint2*>(whist + kWarpHistWords);
-        int* list_n = reinterpret_cast<int*>(list + kNucleusList);
         if (!nucleus) {
             s = cta_mass_sum(z, V, m, c, sm);
+            r.sum = s;
+            r.nuc = s;
         } else {
-            for (int i = threadIdx.x; i < (int)(blockDim.x >> 5) * 512; i += blockDim.x) whist[i] = 0;
-            if (threadIdx.x == 0) *list_n = 0;
+            uint2* list = reinterpret_cast<uint2*>(whist + kWarpHistWords);
+            int* list_n = reinterpret_cast<int*>(list + kNucleusList);
+            int* odd = list_n + 1;  // a NaN exponent seen (NaN logit, or an infinite maximum)
+            if (threadIdx.x == 0) {
+                *list_n = 0;
+                *odd = 0;
+            }
             __syncthreads();
-            for_each_row_value(z, V, [&](float zj) {
-                const uint32_t e = mass_of(zj, m, c);
-                s += e;
-                hist_add_lane(Hw, logit_key(zj) >> 24, e);
-            });
+            uint64_t ls = 0;
+            bool nan_t = false;
+            // the masses of a group of values first (independent, branch-free),
+            // then the rare listing
+            auto group = [&](const float* v, int nv) {
+                float t[16];
+                uint32_t e[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    if (u < nv) {
+                        t[u] = __fmul_rn(__fsub_rn(v[u], m), c);
+                        e[u] = exp2_fx31_bf(t[u]);
+                        s += e[u];
+                        nan_t |= t[u] != t[u];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    if (u < nv && t[u] >= kTList) {
+                        ls += e[u];
+                        const int at = atomicAdd(list_n, 1);
+                        if (at < kNucleusList) list[at] = make_uint2(logit_key(v[u]), e[u]);
+                    }
+                }
+            };
+            if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
+                const float4* z4 = reinterpret_cast<const float4*>(z);
+                const int n4 = V / 4, bd = blockDim.x;
+                int q = threadIdx.x;
+                for (; q + 3 * bd < n4; q += 4 * bd) {
+                    float v[16];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) *reinterpret_cast<float4*>(&v[4 * u]) = z4[q + u * bd];
+                    group(v, 16);
+                }
+                for (; q < n4; q += bd) {
+                    float v[16];
+                    *reinterpret_cast<float4*>(&v[0]) = z4[q];
+                    group(v, 4);
+                }
+            } else {
+                for (int j = threadIdx.x; j < V; j += blockDim.x) {
+                    float v[16];
+                    v[0] = z[j];
+                    group(v, 1);
+                }
+            }
+            if (nan_t) *odd = 1;
             s = block_sum<uint64_t>(s, sm.red64);
-        }
-        r.sum = s;
-        r.nuc = s;
-        if (nucleus) {
+            ls = block_sum<uint64_t>(ls, sm.red64);
             uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
             if (thr < 1) thr = 1;
-            merge_warp_hists(whist, sm);
-            uint64_t G = 0, last = 0;
-            uint32_t prefix = 0, dg = 0;
-            select_digit(sm, thr, &G, &dg, &last);
-            prefix = dg << 24;
-            for (int d = 2; d >= 0; --d) {
-                const int shift = 8 * d;
-                const uint32_t want = prefix >> (shift + 8);
-                if (d == 2) {
-                    for_each_row_value(z, V, [&](float zj) {
-                        const uint32_t key = logit_key(zj);
-                        if ((key >> (shift + 8)) == want) {
-                            const uint32_t e = mass_of(zj, m, c);
-                            hist_add_lane(Hw, (key >> shift) & 255u, e);
-                            const int at = atomicAdd(list_n, 1);
-                            if (at < kNucleusList) list[at] = make_uint2(key, e);
-                        }
-                    });
-                } else if (*list_n <= kNucleusList) {
-                    const int n = *list_n;
-                    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                        const uint2 en = list[i];
-                        if ((en.x >> (shift + 8)) == want) hist_add_lane(Hw, (en.x >> shift) & 255u, en.y);
-                    }
-                } else {
-                    for_each_row_value(z, V, [&](float zj) {
-                        const uint32_t key = logit_key(zj);
-                        if ((key >> (shift + 8)) == want) hist_add_lane(Hw, (key >> shift) & 255u, mass_of(zj, m, c));
-                    });
-                }
-                merge_warp_hists(whist, sm);
-                select_digit(sm, thr, &G, &dg, &last);
-                prefix |= dg << shift;
+            const int n = *list_n;
+            const bool in_list = !*odd && n <= kNucleusList && ls >= thr;
+            __syncthreads();
+            if (in_list) {
+                list_topp_select(list, n, thr, sm, whist, &r.tau, &r.nuc);
+            } else {
+                row_topp_select(z, V, m, c, thr, sm, whist, &r.tau, &r.nuc);
             }
-            r.tau = prefix;
-            r.nuc = G + last;
+            r.sum = s;
         }
     }
     *st = r;
@@ -853,7 +995,10 @@ __global__ void __launch_bounds__(kRowThreads) sample_rows_kernel(const float* _
     int tok;
     float sc;
     if (!greedy && tp >= (1ull << 32)) {
-        cta_row_stats(z, V, c, tp, false, sm, &st);  // max and arg-max only
+        st.max = cta_max(z, V, sm);
+        st.argmax = -1;
+        st.tau = 0;
+        st.pad = 0;
         uint64_t total = 0;  // the mass total comes out of the draw's pass
         cta_gumbel_mass(z, 0, V, st.max, c, 0u, nullptr, 0, seed, step, (uint32_t)(r / k), (uint32_t)(r % k),
                         U_GUMBEL_DRAFT, sm, &sc, &tok, &total);

@@ -50,6 +50,39 @@ def test_accept_chain_bit_exact(cuda_device, B, k, V, T, tp):
     assert out.cpu().numpy().tolist() == out_o.tolist()
 
 
+@pytest.mark.parametrize("scale,T,tp", [(0.5, 1.0, 0.9), (1.0, 1.0, 0.95), (3.0, 0.7, 0.9), (8.0, 0.7, 0.5),
+                                         (3.0, 0.3, 0.999)])
+def test_accept_chain_topp_both_threshold_paths(cuda_device, scale, T, tp):
+    """The top-p threshold from the listed high-mass elements (peaked rows:
+    scale 3, 8, low temperature) and from the whole-row radix select (flat
+    rows: scale 0.5, 1, whose nucleus reaches below the listed range) --
+    bit-exact with the oracle either way; one row has tied maxima."""
+    B, k, V = 6, 5, 50000
+    rng = np.random.default_rng(int(scale * 10) + int(tp * 1000))
+    tgt = (rng.standard_normal((B, k + 1, V)) * scale).astype(np.float32)
+    tgt[1, 2, 100:140] = tgt[1, 2].max()  # 40 tied maxima
+    dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.3 * scale).astype(np.float32)
+    drafts = O.sample_rows(dr.reshape(B * k, V), k, T, tp, 9, 0).reshape(B, k)
+    acc_o, out_o = O.accept_chain(tgt, dr, drafts, T, tp, 4321, 2)
+    import torch
+
+    d_t, d_d, d_dr = dev(tgt), dev(dr), dev(drafts)
+    acc, out = _i32(B), _i32((B, k + 1))
+    ws_b = S.lib().specdec_accept_workspace_bytes(B * (2 * k + 1))
+    ws = empty(ws_b, torch.uint8)
+    sp = S.sampling(T, tp, 4321, 2)
+    S.check(S.lib().specdec_accept_chain(ptr(d_t), ptr(d_d), ptr(d_dr), B, k, V, C.byref(sp), ptr(acc), ptr(out),
+                                         ptr(ws), ws_b, stream_ptr()))
+    sync()
+    assert acc.cpu().numpy().tolist() == acc_o.tolist()
+    assert out.cpu().numpy().tolist() == out_o.tolist()
+    # the sampler over the same rows (its own row statistics)
+    got = _i32(B * k)
+    S.check(S.lib().specdec_sample_rows(ptr(d_d), B * k, k, V, C.byref(sp), ptr(got), None, 0, stream_ptr()))
+    sync()
+    assert got.cpu().numpy().tolist() == O.sample_rows(dr.reshape(B * k, V), k, T, tp, 4321, 2).tolist()
+
+
 @pytest.mark.parametrize("k", [0, 3])
 def test_accept_chain_zero_residual_and_bonus_only(cuda_device, k):
     """q == p with out-of-range draft tokens: the forced rejection leaves a
