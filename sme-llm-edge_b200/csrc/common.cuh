@@ -102,14 +102,16 @@ __device__ __forceinline__ uint32_t exp2_fx31(float t) {
     return (uint32_t)v;
 }
 
-// exp2_fx31 without branches (identical results for every t, NaN included):
-// t is clamped to [-40, 0] (NaN and positive t to 0, as above); for
-// t < -31.5 the exponent e = rint(t) + 31 is negative and p * 2^e < 1
-// truncates to 0, the value the early returns give.
-__device__ __forceinline__ uint32_t exp2_fx31_bf(float t) {
-    t = (t <= 0.0f) ? t : 0.0f;
+// exp2_fx31 for t <= 0 or t = -inf (no NaN), without branches and with
+// the rounding of t done by the 1.5 * 2^23 addition (round to nearest even,
+// the mode of rintf) instead of conversion instructions: identical results.
+// t is clamped at -40 (below -31.5 the exponent e = n + 31 is negative and
+// p * 2^e < 1 truncates to 0, the value exp2_fx31 returns there).
+__device__ __forceinline__ uint32_t exp2_fx31_neg(float t) {
     t = fmaxf(t, -40.0f);
-    const float n = rintf(t);
+    const float big = __fadd_rn(t, 0x1.8p23f);
+    const float n = __fsub_rn(big, 0x1.8p23f);
+    const int ni = __float_as_int(big) - 0x4B400000;
     const float f = __fsub_rn(t, n);
     const float x = __fmul_rn(f, 0x1.62e43p-1f);
     float p = 0x1.a01a02p-13f;
@@ -120,8 +122,7 @@ __device__ __forceinline__ uint32_t exp2_fx31_bf(float t) {
     p = __fmaf_rn(p, x, 0x1p-1f);
     p = __fmaf_rn(p, x, 0x1p+0f);
     p = __fmaf_rn(p, x, 0x1p+0f);
-    const int e = (int)n + 31;  // >= -9
-    return (uint32_t)__fmul_rn(p, __int_as_float((e + 127) << 23));
+    return (uint32_t)__fmul_rn(p, __int_as_float((ni + 31 + 127) << 23));  // ni + 31 >= -9
 }
 
 __device__ __forceinline__ uint32_t logit_key(float z) {

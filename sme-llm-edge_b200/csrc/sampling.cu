@@ -130,9 +130,10 @@ __device__ void cta_argmax(const float* __restrict__ z, int V, RowSmem& sm, floa
 }
 
 // Row maximum only (NaN never wins; -inf for an empty or all-NaN row): one
-// max per element, four float4 loads in flight per thread.
-__device__ float cta_max(const float* __restrict__ z, int V, RowSmem& sm) {
-    float bv = -INFINITY;
+// max per element, four float4 loads in flight per thread.  *finite (if
+// given) tells whether every value is finite (sum of v * 0 stays a zero).
+__device__ float cta_max(const float* __restrict__ z, int V, RowSmem& sm, bool* finite = nullptr) {
+    float bv = -INFINITY, nz = 0.0f;
     if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0) {
         const float4* z4 = reinterpret_cast<const float4*>(z);
         const int n4 = V / 4, bd = blockDim.x;
@@ -142,15 +143,24 @@ __device__ float cta_max(const float* __restrict__ z, int V, RowSmem& sm) {
 #pragma unroll
             for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) bv = fmaxf(bv, fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w)));
+            for (int u = 0; u < 4; ++u) {
+                bv = fmaxf(bv, fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w)));
+                if (finite) nz = __fmaf_rn(v[u].x, 0.0f, __fmaf_rn(v[u].y, 0.0f, __fmaf_rn(v[u].z, 0.0f, __fmaf_rn(v[u].w, 0.0f, nz))));
+            }
         }
         for (; q < n4; q += bd) {
             const float4 v = z4[q];
             bv = fmaxf(bv, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+            if (finite) nz = __fmaf_rn(v.x, 0.0f, __fmaf_rn(v.y, 0.0f, __fmaf_rn(v.z, 0.0f, __fmaf_rn(v.w, 0.0f, nz))));
         }
     } else {
-        for (int j = threadIdx.x; j < V; j += blockDim.x) bv = fmaxf(bv, z[j]);
+        for (int j = threadIdx.x; j < V; j += blockDim.x) {
+            const float v = z[j];
+            bv = fmaxf(bv, v);
+            if (finite) nz = __fmaf_rn(v, 0.0f, nz);
+        }
     }
+    if (finite) *finite = __syncthreads_and(nz == 0.0f);
     bv = warp_max(bv);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     __syncthreads();
@@ -388,8 +398,9 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
                               DevRowStats* st, uint32_t* whist = nullptr) {
     float m;
     int am = -1;
+    bool finite = true;
     if (need_mass) {
-        m = cta_max(z, V, sm);
+        m = cta_max(z, V, sm, tp < (1ull << 32) ? &finite : nullptr);
     } else {
         cta_argmax(z, V, sm, &m, &am);
     }
@@ -407,17 +418,20 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
             s = cta_mass_sum(z, V, m, c, sm);
             r.sum = s;
             r.nuc = s;
+        } else if (!finite) {
+            // NaN / infinite logits: exp2_fx31's handling of a NaN exponent and
+            // the keys' order decide, so the general path
+            s = cta_mass_sum(z, V, m, c, sm);
+            uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
+            if (thr < 1) thr = 1;
+            row_topp_select(z, V, m, c, thr, sm, whist, &r.tau, &r.nuc);
+            r.sum = s;
         } else {
             uint2* list = reinterpret_cast<uint2*>(whist + kWarpHistWords);
             int* list_n = reinterpret_cast<int*>(list + kNucleusList);
-            int* odd = list_n + 1;  // a NaN exponent seen (NaN logit, or an infinite maximum)
-            if (threadIdx.x == 0) {
-                *list_n = 0;
-                *odd = 0;
-            }
+            if (threadIdx.x == 0) *list_n = 0;
             __syncthreads();
             uint64_t ls = 0;
-            bool nan_t = false;
             // the masses of a group of values first (independent, branch-free),
             // then the rare listing
             auto group = [&](const float* v, int nv) {
@@ -427,9 +441,8 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
                 for (int u = 0; u < 16; ++u) {
                     if (u < nv) {
                         t[u] = __fmul_rn(__fsub_rn(v[u], m), c);
-                        e[u] = exp2_fx31_bf(t[u]);
+                        e[u] = exp2_fx31_neg(t[u]);  // finite row: t <= 0
                         s += e[u];
-                        nan_t |= t[u] != t[u];
                     }
                 }
 #pragma unroll
@@ -463,13 +476,12 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
                     group(v, 1);
                 }
             }
-            if (nan_t) *odd = 1;
             s = block_sum<uint64_t>(s, sm.red64);
             ls = block_sum<uint64_t>(ls, sm.red64);
             uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
             if (thr < 1) thr = 1;
             const int n = *list_n;
-            const bool in_list = !*odd && n <= kNucleusList && ls >= thr;
+            const bool in_list = n <= kNucleusList && ls >= thr;
             __syncthreads();
             if (in_list) {
                 list_topp_select(list, n, thr, sm, whist, &r.tau, &r.nuc);

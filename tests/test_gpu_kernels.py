@@ -83,6 +83,26 @@ def test_accept_chain_topp_both_threshold_paths(cuda_device, scale, T, tp):
     assert got.cpu().numpy().tolist() == O.sample_rows(dr.reshape(B * k, V), k, T, tp, 4321, 2).tolist()
 
 
+def test_sample_rows_topp_nonfinite_rows(cuda_device):
+    """Rows with NaN or infinite logits take the general top-p path (the
+    exponent of a NaN logit counts as 0, as in the oracle): draws bit-exact."""
+    rng = np.random.default_rng(31)
+    rows, k, V = 6, 3, 20000
+    z = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    z[0, 17] = np.nan
+    z[1, 5] = np.inf
+    z[2, 9] = -np.inf
+    z[3, [1, 2, 3]] = np.nan
+    z[3, 4] = np.inf
+    ref = O.sample_rows(z, k, 0.7, 0.9, 77, 1)
+    out = _i32(rows)
+    sp = S.sampling(0.7, 0.9, 77, 1)
+    d_z = dev(z)
+    S.check(S.lib().specdec_sample_rows(ptr(d_z), rows, k, V, C.byref(sp), ptr(out), None, 0, stream_ptr()))
+    sync()
+    assert out.cpu().numpy().tolist() == ref.tolist()
+
+
 @pytest.mark.parametrize("k", [0, 3])
 def test_accept_chain_zero_residual_and_bonus_only(cuda_device, k):
     """q == p with out-of-range draft tokens: the forced rejection leaves a
