@@ -138,12 +138,13 @@ __device__ float cta_max(const float* __restrict__ z, int V, RowSmem& sm, bool* 
         const float4* z4 = reinterpret_cast<const float4*>(z);
         const int n4 = V / 4, bd = blockDim.x;
         int q = threadIdx.x;
-        for (; q + 3 * bd < n4; q += 4 * bd) {
-            float4 v[4];
+        // eight float4 loads in flight per thread: the row comes from HBM
+        for (; q + 7 * bd < n4; q += 8 * bd) {
+            float4 v[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = z4[q + u * bd];
+            for (int u = 0; u < 8; ++u) v[u] = z4[q + u * bd];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 8; ++u) {
                 bv = fmaxf(bv, fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w)));
                 if (finite) nz = __fmaf_rn(v[u].x, 0.0f, __fmaf_rn(v[u].y, 0.0f, __fmaf_rn(v[u].z, 0.0f, __fmaf_rn(v[u].w, 0.0f, nz))));
             }
