@@ -915,6 +915,9 @@ extern "C" int specdec_engine_create(const specdec_model_config* mc, const specd
     // KV pool and block manager
     e->layer_stride = (size_t)e->num_blocks * 2 * Hkv * 16 * hd;
     if ((rcode = dalloc(e, &e->kv, e->layer_stride * mc->layers))) return fail(rcode);
+    // zeroed: attention reads whole 16-slot blocks and multiplies the masked
+    // slots' V by a zero probability, which stale NaN / Inf bits would defeat
+    if (cudaMemset(e->kv, 0, sizeof(__half) * e->layer_stride * mc->layers) != cudaSuccess) return fail(SPECDEC_ECUDA);
     if ((rcode = specdec_kv_create(e->num_blocks, 16, e->B, e->max_blocks, &e->kvm))) return fail(rcode);
     // activations
     const int Mx = e->Mmax;

@@ -219,3 +219,19 @@ def test_tiny_tree_step_matches_oracle(cuda_device, oracle_model):
         np.testing.assert_array_equal(tables, oracle_tables())
         assert (lens == lens_prev + acc + 1).all()
     eng.close()
+
+
+def test_engine_kv_pool_starts_zeroed(cuda_device):
+    """The verify attention reads whole 16-slot blocks and gives the slots past
+    a sequence's length zero probability; that only holds if those slots hold
+    finite values, so the pool starts as zeros (never stale device memory)."""
+    import torch
+
+    junk = torch.full((64 << 20,), float("nan"), device="cuda")  # leave NaN bits behind in freed memory
+    del junk
+    torch.cuda.empty_cache()
+    eng = S.Engine(TINY, batch=2, draft_len=3, max_ctx=256, use_graph=False)
+    L, hd, Hkv = TINY["layers"], TINY["head_dim"], TINY["n_kv_heads"]
+    pool = eng.read("kv", np.uint16, (L, eng.info("num_blocks"), 2, Hkv, 16, hd))
+    assert not pool.any()
+    eng.close()
