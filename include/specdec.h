@@ -174,6 +174,19 @@ int specdec_sample_rows(const float* logits, int rows, int k, int V, const specd
  *  3. top_p < 1: for digit 3, 2, 1, 0: specdec_shard_digit_hist (rows x 256
  *     u64); all-reduce (sum); specdec_shard_select_digit -> prefix, G, last.
  *     Then tau = prefix and nuc = G + last; with top_p = 1: tau = 0, nuc = sum.
+ *  2'-3'. Instead of 2-3 when top_p < 1 and W <= 8 (one shard pass, two
+ *     collectives): specdec_shard_mass_hist -> per row {sum, listed mass,
+ *     NaN count, overflow count, 256-bin histogram of t = (z - max) * c over
+ *     the listed elements t >= -14} (rows x 260 u64) and this shard's listed
+ *     (key, mass) pairs; all-reduce the stats (sum); specdec_shard_cross -> G
+ *     and this shard's candidates in the bin where the mass from the top
+ *     reaches the threshold (rows x 33 (key, mass) pairs, the last holding the
+ *     count); all-gather them [W]; specdec_shard_union_select -> tau, nuc and
+ *     ok per row.  ok is 0 for rows with a NaN exponent, a list past `cap`, a
+ *     nucleus reaching below t = -14 or more than 32 candidates on a rank:
+ *     when any row is not ok (the same answer on every rank), run 2-3 (and
+ *     4-7 again).  The flags can be read after 4-7 are queued, so the host
+ *     never waits in the middle.
  *  4. specdec_shard_point_mass -> ep, eq [B*k]; all-reduce (sum).
  *  5. specdec_shard_accept_test -> accepted [B] (identical on every rank).
  *     Greedy: the emitted token is parg[b*(k+1) + accepted[b]].
@@ -196,6 +209,14 @@ int specdec_shard_digit_hist(const float* z, int rows, const float* z2, int rows
                              float temperature, const uint32_t* prefix, int digit, uint64_t* out_hist, void* stream);
 int specdec_shard_select_digit(const uint64_t* hist, int rows, int digit, const uint64_t* gsum, float top_p,
                                uint32_t* prefix, uint64_t* G, uint64_t* last, void* stream);
+int specdec_shard_mass_hist(const float* z, int rows, const float* z2, int rows2, int Vs, const float* gmax,
+                            float temperature, int cap, void* list, int32_t* list_n, uint64_t* out_stats,
+                            void* stream);
+int specdec_shard_cross(const uint64_t* stats, int rows, float top_p, const float* gmax, float temperature,
+                        const void* list, int cap, const int32_t* list_n, uint64_t* out_G, void* out_cand,
+                        void* stream);
+int specdec_shard_union_select(const void* gcand, int W, int rows, const uint64_t* stats, const uint64_t* G,
+                               float top_p, uint32_t* out_tau, uint64_t* out_nuc, int32_t* out_ok, void* stream);
 int specdec_shard_point_mass(const float* target, const float* draft, const int32_t* drafts, int B, int k, int Vs,
                              int v0, float temperature, const float* pmax, const uint32_t* ptau, const float* qmax,
                              const uint32_t* qtau, uint64_t* ep, uint64_t* eq, void* stream);

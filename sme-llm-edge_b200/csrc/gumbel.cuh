@@ -74,6 +74,16 @@ __device__ __forceinline__ float neg_log2_uniform(uint32_t x) {
 // The key of a candidate of weight w (a float of the weight) in a draw.
 __device__ __forceinline__ float race_key(float w, uint32_t x) { return __fdiv_rn(w, neg_log2_uniform(x)); }
 
+// False only when a candidate of weight w and uniform x surely loses to a key
+// bs already held: its key w / (-log2 U) is below w ln2 / (1 - U) (as
+// -ln U >= 1 - U) and 1 - U >= ~x / 2^32, so (~x / 2^32) bs > w ln2 (1 + 1e-3)
+// puts it below bs with a margin far above the roundings of race_key and of
+// this test.  Skipping such a candidate leaves the draw unchanged (its key is
+// strictly smaller) and saves the logarithm and the division.
+__device__ __forceinline__ bool race_may_beat(float w, uint32_t x, float bs) {
+    return !(__fmul_rn(__fmul_rn(__uint2float_rn(~x), bs), 0x1p-32f) > __fmul_rn(w, 0.69384f));
+}
+
 // An integer weight as fp32: its top 64 bits converted (round to nearest),
 // scaled back by the exact power of two.
 __device__ __forceinline__ float u128_to_f32(u128 w) {

@@ -598,7 +598,8 @@ __device__ void cta_gumbel_mass(const float* __restrict__ z, int L, int H, float
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (!e4[e]) continue;
-            gumbel_merge(bs, bj, race_key(__uint2float_rn(e4[e]), o[e]), 4 * g + e);
+            const float wf = __uint2float_rn(e4[e]);
+            if (race_may_beat(wf, o[e], bs)) gumbel_merge(bs, bj, race_key(wf, o[e]), 4 * g + e);
         }
     });
     if (sum) *sum = block_sum<uint64_t>(tot, sm.red64);
@@ -648,7 +649,8 @@ __device__ void cta_gumbel_resid(const float* __restrict__ zp, float pm, uint32_
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (!r4[e]) continue;
-            gumbel_merge(bs, bj, race_key(u128_to_f32(r4[e]), o[e]), 4 * g + e);
+            const float wf = u128_to_f32(r4[e]);
+            if (race_may_beat(wf, o[e], bs)) gumbel_merge(bs, bj, race_key(wf, o[e]), 4 * g + e);
         }
     });
     cta_best(bs, bj, sm, out_s, out_j);
@@ -1280,6 +1282,212 @@ __global__ void shard_select_digit_kernel(const unsigned long long* __restrict__
     }
 }
 
+// ---- top-p over the listed high-mass elements (the fast form of steps 2-3)
+// (2') per shard row: the integer mass sum S, the mass of the elements with
+// t = (z - gmax) * c >= kTList and their 256-bin t histogram (bin =
+// floor((t - kTList) * 256 / -kTList), monotone in the key), a count of
+// non-finite exponents and of list overflow; the listed (key, mass) pairs go
+// to list[row][0, cap).  Layout of out_stats[row]: {S, listed mass, odd,
+// overflow, hist[256]} (kShardStatCols u64), summed over ranks.
+constexpr int kShardStatCols = 4 + 256;
+constexpr int kShardCand = 32;  // candidates per rank and row in the crossing bin
+__device__ __forceinline__ int shard_tbin(float t) {
+    const int b = (int)__fmul_rn(__fsub_rn(t, kTList), 256.0f / -kTList);
+    return b < 255 ? b : 255;
+}
+__device__ __forceinline__ float key_value(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
+__global__ void __launch_bounds__(kRowThreads) shard_mass_hist_kernel(const float* __restrict__ z1, int rows1,
+                                                                      const float* __restrict__ z2, int Vs,
+                                                                      const float* __restrict__ gmax, float c,
+                                                                      int cap, uint2* __restrict__ list,
+                                                                      int32_t* __restrict__ list_n,
+                                                                      unsigned long long* __restrict__ out_stats) {
+    __shared__ RowSmem sm;
+    // the t histogram as 16-bit halves of each mass: with at most `cap`
+    // (<= 2^16) listed elements a bin stays below 2^32; a row whose list
+    // overflowed is not read (step 3' falls back)
+    __shared__ uint32_t hlo[256], hhi[256];
+    __shared__ int s_n, s_odd;
+    const float* zr = shard_row(z1, rows1, z2, Vs, blockIdx.x);
+    const float m = gmax[blockIdx.x];
+    uint2* lrow = list + (size_t)blockIdx.x * cap;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hlo[i] = hhi[i] = 0;
+    if (threadIdx.x == 0) {
+        s_n = 0;
+        s_odd = 0;
+    }
+    __syncthreads();
+    uint64_t s = 0, ls = 0;
+    bool odd = false;
+    for_each_row_value(zr, Vs, [&](float zj) {
+        const float t = __fmul_rn(__fsub_rn(zj, m), c);
+        odd |= t != t;
+        const uint32_t e = exp2_fx31_neg(t);
+        s += e;
+        if (t >= kTList) {
+            ls += e;
+            const int at = atomicAdd(&s_n, 1);
+            if (at < cap) {
+                lrow[at] = make_uint2(logit_key(zj), e);
+                const int b = shard_tbin(t);
+                atomicAdd(&hlo[b], e & 0xFFFFu);
+                atomicAdd(&hhi[b], e >> 16);
+            }
+        }
+    });
+    if (odd) s_odd = 1;
+    s = block_sum<uint64_t>(s, sm.red64);
+    ls = block_sum<uint64_t>(ls, sm.red64);
+    __syncthreads();
+    unsigned long long* o = out_stats + (size_t)blockIdx.x * kShardStatCols;
+    if (threadIdx.x == 0) {
+        o[0] = s;
+        o[1] = ls;
+        o[2] = s_odd;
+        o[3] = s_n > cap ? 1ull : 0ull;
+        list_n[blockIdx.x] = min(s_n, cap);
+    }
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) o[4 + b] = ((unsigned long long)hhi[b] << 16) + hlo[b];
+}
+
+// (3') per row (one warp), on the rank-summed stats: thr = max(1, floor(S *
+// top_p)); the row takes the listed path when no exponent was NaN, no rank's
+// list overflowed and the listed mass reaches thr.  Then the t bin where the
+// mass from the top reaches thr, G = the mass of the bins above it, and this
+// rank's listed elements of that bin (at most kShardCand, else the row falls
+// back) as candidates: out_cand[row] = {kShardCand (key, mass) pairs, count}
+// (count = kShardCand + 1 for a fallback row).
+__global__ void shard_cross_kernel(const unsigned long long* __restrict__ stats, int rows, uint64_t tp,
+                                   const float* __restrict__ gmax, float c, const uint2* __restrict__ list, int cap,
+                                   const int32_t* __restrict__ list_n, unsigned long long* __restrict__ out_G,
+                                   uint2* __restrict__ out_cand) {
+    const int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;  // whole warps
+    const unsigned long long* st = stats + (size_t)r * kShardStatCols;
+    uint2* cand = out_cand + (size_t)r * (kShardCand + 1);
+    uint64_t thr = (uint64_t)(((u128)st[0] * tp) >> 32);
+    if (thr < 1) thr = 1;
+    if (st[2] != 0 || st[3] != 0 || st[1] < thr) {
+        if (lane == 0) {
+            out_G[r] = 0;
+            cand[kShardCand] = make_uint2(kShardCand + 1, 0);
+        }
+        return;
+    }
+    const unsigned long long* h = st + 4;
+    uint64_t local = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) local += h[255 - 8 * lane - i];
+    uint64_t incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, incl >= thr);
+    const int f = hit ? (__ffs(hit) - 1) : 31;
+    int chosen = 0;
+    uint64_t G = 0;
+    if (lane == f) {
+        uint64_t cum = incl - local;
+        chosen = 255 - 8 * f - 7;
+        for (int i = 0; i < 8; ++i) {
+            const int bin = 255 - 8 * f - i;
+            if (cum + h[bin] >= thr) {
+                chosen = bin;
+                break;
+            }
+            cum += h[bin];
+        }
+        G = cum;
+    }
+    chosen = __shfl_sync(0xffffffffu, chosen, f);
+    G = __shfl_sync(0xffffffffu, G, f);
+    // this rank's listed elements in the chosen bin (the list is complete: no overflow)
+    const float m = gmax[r];
+    const uint2* lrow = list + (size_t)r * cap;
+    int n = 0;
+    const int ln = list_n[r];
+    for (int i0 = 0; i0 < ln; i0 += 32) {
+        const int i = i0 + lane;
+        bool in = false;
+        uint2 en = make_uint2(0, 0);
+        if (i < ln) {
+            en = lrow[i];
+            in = en.y != 0u && shard_tbin(__fmul_rn(__fsub_rn(key_value(en.x), m), c)) == chosen;
+        }
+        const unsigned msk = __ballot_sync(0xffffffffu, in);
+        const int at = n + __popc(msk & ((1u << lane) - 1u));
+        if (in && at < kShardCand) cand[at] = en;
+        n += __popc(msk);
+    }
+    if (lane == 0) {
+        out_G[r] = G;
+        cand[kShardCand] = make_uint2((uint32_t)min(n, kShardCand + 1), 0);
+    }
+}
+
+// (4') per row (one CTA): the radix select over the W ranks' gathered
+// candidates ([W][rows][kShardCand + 1]) above G, as list_topp_select; a row
+// any rank marked for fallback gets ok = 0.
+__global__ void __launch_bounds__(256) shard_union_select_kernel(const uint2* __restrict__ gcand, int W, int rows,
+                                                                 const unsigned long long* __restrict__ stats,
+                                                                 const unsigned long long* __restrict__ gG,
+                                                                 uint64_t tp, uint32_t* __restrict__ out_tau,
+                                                                 unsigned long long* __restrict__ out_nuc,
+                                                                 int32_t* __restrict__ out_ok) {
+    __shared__ RowSmem sm;
+    __shared__ uint32_t whist[8 * 512];
+    __shared__ uint2 cands[256];
+    __shared__ int s_n, s_bad;
+    const int r = blockIdx.x;
+    if (threadIdx.x == 0) {
+        s_n = 0;
+        s_bad = 0;
+    }
+    __syncthreads();
+    for (int w = 0; w < W; ++w) {
+        const uint2* cw = gcand + ((size_t)w * rows + r) * (kShardCand + 1);
+        const int cnt = (int)cw[kShardCand].x;
+        if (cnt > kShardCand) {
+            if (threadIdx.x == 0) s_bad = 1;
+            continue;
+        }
+        for (int i = threadIdx.x; i < cnt; i += blockDim.x) cands[atomicAdd(&s_n, 1)] = cw[i];
+    }
+    __syncthreads();
+    if (s_bad) {
+        if (threadIdx.x == 0) out_ok[r] = 0;
+        return;
+    }
+    uint64_t thr = (uint64_t)(((u128)stats[(size_t)r * kShardStatCols] * tp) >> 32);
+    if (thr < 1) thr = 1;
+    const int n = s_n;
+    uint32_t* Hw = whist + (threadIdx.x >> 5) * 512;
+    for (int i = threadIdx.x; i < 8 * 512; i += blockDim.x) whist[i] = 0;
+    __syncthreads();
+    uint64_t G = gG[r], last = 0;
+    uint32_t prefix = 0, dg = 0;
+    for (int d = 3; d >= 0; --d) {
+        const int shift = 8 * d;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint2 en = cands[i];
+            if (d == 3 || (en.x >> (shift + 8)) == (prefix >> (shift + 8))) hist_add_lane(Hw, (en.x >> shift) & 255u, en.y);
+        }
+        merge_warp_hists(whist, sm);
+        select_digit(sm, thr, &G, &dg, &last);
+        prefix |= dg << shift;
+    }
+    if (threadIdx.x == 0) {
+        out_tau[r] = prefix;
+        out_nuc[r] = G + last;
+        out_ok[r] = 1;
+    }
+}
+
 // (6) the nucleus masses of the drafted tokens in the shard that owns them (0 elsewhere)
 __global__ void shard_point_mass_kernel(const float* __restrict__ target, const float* __restrict__ draft,
                                         const int32_t* __restrict__ drafts, int B, int k, int Vs, int v0, float c,
@@ -1716,6 +1924,52 @@ extern "C" int specdec_shard_digit_hist(const float* z, int rows, const float* z
     shard_digit_hist_kernel<<<rows + rows2, kRowThreads, hs, as_stream(stream)>>>(
         z, rows, z2, Vs, gmax, temp_coeff(temperature), prefix, digit, reinterpret_cast<unsigned long long*>(out_hist));
     SD_LAUNCH_CHECK("shard_digit_hist_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_mass_hist(const float* z, int rows, const float* z2, int rows2, int Vs, const float* gmax,
+                                       float temperature, int cap, void* list, int32_t* list_n, uint64_t* out_stats,
+                                       void* stream) {
+    if (int rc = shard_check(rows, Vs, "shard_mass_hist")) return rc;
+    SD_CHECK(z && gmax && list && list_n && out_stats && temperature > 0.0f && cap > 0 && rows2 >= 0 &&
+                 (rows2 == 0 || z2),
+             SPECDEC_EINVAL, "shard_mass_hist: bad argument");
+    if (rows + rows2 == 0) return SPECDEC_OK;
+    SD_CHECK(cap <= 65536, SPECDEC_EINVAL, "shard_mass_hist: cap above 65536");
+    shard_mass_hist_kernel<<<rows + rows2, kRowThreads, 0, as_stream(stream)>>>(
+        z, rows, z2, Vs, gmax, temp_coeff(temperature), cap, static_cast<uint2*>(list), list_n,
+        reinterpret_cast<unsigned long long*>(out_stats));
+    SD_LAUNCH_CHECK("shard_mass_hist_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_cross(const uint64_t* stats, int rows, float top_p, const float* gmax, float temperature,
+                                   const void* list, int cap, const int32_t* list_n, uint64_t* out_G, void* out_cand,
+                                   void* stream) {
+    SD_CHECK(stats && gmax && list && list_n && out_G && out_cand && rows >= 0 && cap > 0 && temperature > 0.0f &&
+                 top_p > 0.0f && top_p < 1.0f,
+             SPECDEC_EINVAL, "shard_cross: bad argument");
+    if (rows == 0) return SPECDEC_OK;
+    shard_cross_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const unsigned long long*>(stats), rows, top_p_q32(top_p), gmax, temp_coeff(temperature),
+        static_cast<const uint2*>(list), cap, list_n, reinterpret_cast<unsigned long long*>(out_G),
+        static_cast<uint2*>(out_cand));
+    SD_LAUNCH_CHECK("shard_cross_kernel");
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_shard_union_select(const void* gcand, int W, int rows, const uint64_t* stats,
+                                          const uint64_t* G, float top_p, uint32_t* out_tau, uint64_t* out_nuc,
+                                          int32_t* out_ok, void* stream) {
+    SD_CHECK(gcand && stats && G && out_tau && out_nuc && out_ok && rows >= 0 && W >= 1 && W * kShardCand <= 256 &&
+                 top_p > 0.0f && top_p < 1.0f,
+             SPECDEC_EINVAL, "shard_union_select: bad argument (at most 8 ranks)");
+    if (rows == 0) return SPECDEC_OK;
+    shard_union_select_kernel<<<(unsigned)rows, 256, 0, as_stream(stream)>>>(
+        static_cast<const uint2*>(gcand), W, rows, reinterpret_cast<const unsigned long long*>(stats),
+        reinterpret_cast<const unsigned long long*>(G), top_p_q32(top_p), out_tau,
+        reinterpret_cast<unsigned long long*>(out_nuc), out_ok);
+    SD_LAUNCH_CHECK("shard_union_select_kernel");
     return SPECDEC_OK;
 }
 

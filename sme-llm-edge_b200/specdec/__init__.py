@@ -91,6 +91,9 @@ _SIGS = {
     "specdec_shard_row_mass": (I, [P, I, P, I, I, P, F, P, P]),
     "specdec_shard_digit_hist": (I, [P, I, P, I, I, P, F, P, I, P, P]),
     "specdec_shard_select_digit": (I, [P, I, I, P, F, P, P, P, P]),
+    "specdec_shard_mass_hist": (I, [P, I, P, I, I, P, F, I, P, P, P, P]),
+    "specdec_shard_cross": (I, [P, I, F, P, F, P, I, P, P, P, P]),
+    "specdec_shard_union_select": (I, [P, I, I, P, P, F, P, P, P, P]),
     "specdec_shard_point_mass": (I, [P, P, P, I, I, I, I, F, P, P, P, P, P, P, P]),
     "specdec_shard_accept_test": (I, [P, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P]),
     "specdec_shard_draw_winners": (I, [P, P, I, I, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P, P, P]),

@@ -128,6 +128,10 @@ def vocab_shard(V: int, world: int, rank: int) -> tuple[int, int]:
     return lo, hi - lo
 
 
+SHARD_LIST_CAP = 1024  # listed (key, mass) pairs kept per shard row
+SHARD_CAND = 32  # crossing-bin candidates per rank and row (kShardCand)
+
+
 def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling, comm):
     """Chain acceptance with the vocabulary split across ranks.
 
@@ -169,46 +173,79 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
     gm, ga = comm.all_gather(mx), comm.all_gather(am)
     S.check(L.specdec_shard_merge_max(p(gm), p(ga), W, rows, p(mx), p(am), st))
     pmax, parg = mx[:rows_p], am[:rows_p]
-    acc = torch.empty(B, dtype=torch.int32, device=dev)
     if greedy:
+        acc = torch.empty(B, dtype=torch.int32, device=dev)
         S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), None, None, None, None,
                                             p(acc), st))
         tok = parg.view(B, k + 1).gather(1, acc.long()[:, None])[:, 0]
     else:
-        sums = torch.empty(rows, dtype=torch.int64, device=dev)
-        S.check(L.specdec_shard_row_mass(p(target), rows_p, z2, nq, Vs, p(mx), T, p(sums), st))
-        comm.all_reduce_sum(sums)
-        if tp < 1.0:
-            tau = torch.zeros(rows, dtype=torch.int32, device=dev)
-            G = torch.zeros(rows, dtype=torch.int64, device=dev)
-            last = torch.zeros(rows, dtype=torch.int64, device=dev)
-            hist = torch.empty((rows, 256), dtype=torch.int64, device=dev)
-            for d in (3, 2, 1, 0):
-                S.check(L.specdec_shard_digit_hist(p(target), rows_p, z2, nq, Vs, p(mx), T, p(tau), d, p(hist), st))
-                comm.all_reduce_sum(hist)
-                S.check(L.specdec_shard_select_digit(p(hist), rows, d, p(sums), tp, p(tau), p(G), p(last), st))
-            nuc = G + last
-        else:
-            tau = torch.zeros(rows, dtype=torch.int32, device=dev)
-            nuc = sums
-        ptau, qtau = tau[:rows_p], tau[rows_p:]
-        pnuc, qnuc = nuc[:rows_p].contiguous(), nuc[rows_p:].contiguous()
         qmax = mx[rows_p:]
-        ep = torch.empty(rows_q, dtype=torch.int64, device=dev)
-        eq = torch.empty(rows_q, dtype=torch.int64, device=dev)
-        S.check(L.specdec_shard_point_mass(p(target), p(draft), p(drafts), B, k, Vs, v0, T, p(pmax), p(ptau),
-                                           p(qmax), p(qtau), p(ep), p(eq), st))
-        pq = torch.stack([ep, eq])
-        comm.all_reduce_sum(pq)
-        ep, eq = pq[0].contiguous(), pq[1].contiguous()
-        S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), p(pnuc), p(qnuc), p(ep),
-                                            p(eq), p(acc), st))
-        win = torch.empty((B, 4), dtype=torch.int32, device=dev)
-        S.check(L.specdec_shard_draw_winners(p(target), p(draft), B, k, Vs, v0, C.byref(sampling), p(acc), p(pmax),
-                                             p(ptau), p(qmax), p(qtau), p(pnuc), p(qnuc), p(win), st))
-        gwin = comm.all_gather(win).contiguous()
-        tok = torch.empty(B, dtype=torch.int32, device=dev)
-        S.check(L.specdec_shard_draw_merge(p(gwin), W, B, k, p(acc), p(tok), st))
+
+        def finish(tau, nuc):
+            """Steps 4-7 at the given nucleus thresholds and masses."""
+            ptau, qtau = tau[:rows_p], tau[rows_p:]
+            pnuc, qnuc = nuc[:rows_p].contiguous(), nuc[rows_p:].contiguous()
+            ep = torch.empty(rows_q, dtype=torch.int64, device=dev)
+            eq = torch.empty(rows_q, dtype=torch.int64, device=dev)
+            S.check(L.specdec_shard_point_mass(p(target), p(draft), p(drafts), B, k, Vs, v0, T, p(pmax), p(ptau),
+                                               p(qmax), p(qtau), p(ep), p(eq), st))
+            pq = torch.stack([ep, eq])
+            comm.all_reduce_sum(pq)
+            ep, eq = pq[0].contiguous(), pq[1].contiguous()
+            acc = torch.empty(B, dtype=torch.int32, device=dev)
+            S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), p(pnuc), p(qnuc),
+                                                p(ep), p(eq), p(acc), st))
+            win = torch.empty((B, 4), dtype=torch.int32, device=dev)
+            S.check(L.specdec_shard_draw_winners(p(target), p(draft), B, k, Vs, v0, C.byref(sampling), p(acc),
+                                                 p(pmax), p(ptau), p(qmax), p(qtau), p(pnuc), p(qnuc), p(win), st))
+            gwin = comm.all_gather(win).contiguous()
+            tok = torch.empty(B, dtype=torch.int32, device=dev)
+            S.check(L.specdec_shard_draw_merge(p(gwin), W, B, k, p(acc), p(tok), st))
+            return acc, tok
+
+        done = False
+        if tp < 1.0 and W * SHARD_CAND <= 256:
+            # the listed path: one shard pass, the stats all-reduce and a small
+            # candidate all-gather (steps 2'-3' in include/specdec.h).  The rows'
+            # ok flags are read only after the whole acceptance is queued, so
+            # the host does not stall the GPU; a row that needs the digit
+            # passes (rare: flat rows, NaN logits) redoes the acceptance below.
+            lst = torch.empty((rows, SHARD_LIST_CAP, 2), dtype=torch.int32, device=dev)
+            lnum = torch.empty(rows, dtype=torch.int32, device=dev)
+            stats = torch.empty((rows, 260), dtype=torch.int64, device=dev)
+            S.check(L.specdec_shard_mass_hist(p(target), rows_p, z2, nq, Vs, p(mx), T, SHARD_LIST_CAP, p(lst),
+                                              p(lnum), p(stats), st))
+            comm.all_reduce_sum(stats)
+            G = torch.empty(rows, dtype=torch.int64, device=dev)
+            cand = torch.empty((rows, SHARD_CAND + 1, 2), dtype=torch.int32, device=dev)
+            S.check(L.specdec_shard_cross(p(stats), rows, tp, p(mx), T, p(lst), SHARD_LIST_CAP, p(lnum), p(G),
+                                          p(cand), st))
+            gcand = comm.all_gather(cand).contiguous()
+            tau = torch.empty(rows, dtype=torch.int32, device=dev)
+            nuc = torch.empty(rows, dtype=torch.int64, device=dev)
+            ok = torch.empty(rows, dtype=torch.int32, device=dev)
+            S.check(L.specdec_shard_union_select(p(gcand), W, rows, p(stats), p(G), tp, p(tau), p(nuc), p(ok), st))
+            acc, tok = finish(tau, nuc)
+            done = bool(ok.all().item())  # the same on every rank: computed from exchanged data only
+        if not done:
+            sums = torch.empty(rows, dtype=torch.int64, device=dev)
+            S.check(L.specdec_shard_row_mass(p(target), rows_p, z2, nq, Vs, p(mx), T, p(sums), st))
+            comm.all_reduce_sum(sums)
+            if tp < 1.0:
+                tau = torch.zeros(rows, dtype=torch.int32, device=dev)
+                G = torch.zeros(rows, dtype=torch.int64, device=dev)
+                last = torch.zeros(rows, dtype=torch.int64, device=dev)
+                hist = torch.empty((rows, 256), dtype=torch.int64, device=dev)
+                for d in (3, 2, 1, 0):
+                    S.check(L.specdec_shard_digit_hist(p(target), rows_p, z2, nq, Vs, p(mx), T, p(tau), d, p(hist),
+                                                       st))
+                    comm.all_reduce_sum(hist)
+                    S.check(L.specdec_shard_select_digit(p(hist), rows, d, p(sums), tp, p(tau), p(G), p(last), st))
+                nuc = G + last
+            else:
+                tau = torch.zeros(rows, dtype=torch.int32, device=dev)
+                nuc = sums
+            acc, tok = finish(tau, nuc)
     idx = torch.arange(k + 1, device=dev)[None, :]
     a = acc.long()[:, None]
     ext = torch.cat([drafts, torch.full((B, 1), -1, dtype=torch.int32, device=dev)], 1)

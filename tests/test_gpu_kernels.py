@@ -469,14 +469,16 @@ def test_w4a16_shared_workspace_across_token_tiles(cuda_device):
 
 
 # ------------------------------------------------ vocabulary-sharded acceptance
-@pytest.mark.parametrize("W,B,k,V,T,tp", [(2, 6, 4, 3001, 0.8, 0.9), (3, 5, 3, 4099, 1.0, 1.0), (2, 4, 4, 2000, 0.0, 1.0),
-                                          (3, 7, 8, 32000, 0.7, 0.9)])
-def test_accept_chain_vocab_sharded_matches_oracle(cuda_device, W, B, k, V, T, tp):
+@pytest.mark.parametrize("W,B,k,V,T,tp,scale", [(2, 6, 4, 3001, 0.8, 0.9, 3.0), (3, 5, 3, 4099, 1.0, 1.0, 3.0),
+                                                (2, 4, 4, 2000, 0.0, 1.0, 3.0), (3, 7, 8, 32000, 0.7, 0.9, 3.0),
+                                                (8, 4, 7, 40000, 0.7, 0.9, 3.0), (4, 3, 3, 5003, 1.0, 0.9, 0.5)])
+def test_accept_chain_vocab_sharded_matches_oracle(cuda_device, W, B, k, V, T, tp, scale):
     """W ranks (threads sharing one GPU) each hold a contiguous vocabulary
     slice of every logits row and exchange only per-row statistics; the
     decisions equal the oracle's on the whole rows, on every rank.  Shards of
     unequal width (V not a multiple of W); greedy, T > 0 without a nucleus,
-    and top-p 0.9."""
+    top-p through the listed path (peaked rows, up to 8 ranks) and through
+    the digit passes (flat rows, scale 0.5)."""
     import threading
 
     import torch
@@ -484,8 +486,8 @@ def test_accept_chain_vocab_sharded_matches_oracle(cuda_device, W, B, k, V, T, t
     from specdec.dist import ThreadComm, accept_chain_vocab_sharded, vocab_shard
 
     rng = np.random.default_rng(B * 1000 + V + W)
-    tgt = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
-    dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.5).astype(np.float32)
+    tgt = (rng.standard_normal((B, k + 1, V)) * scale).astype(np.float32)
+    dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.5 * scale / 3).astype(np.float32)
     drafts = O.sample_rows(dr.reshape(B * k, V), k, max(T, 1.0), tp, 9, 0).reshape(B, k)
     if T == 0.0:
         drafts = tgt[:, :k].argmax(-1).astype(np.int32)

@@ -95,3 +95,56 @@ def test_shard_partials_rebuild_the_row(W, V, T, tp, seed):
             if lb >= 0 and (best < 0 or ls > bs or (ls == bs and lb < best)):
                 best, bs = lb, ls
         assert best == O.draw_row(z, T, tp, seed, step, 1, 2, O.U_GUMBEL_RESAMPLE), step
+
+
+def _tbin(t):
+    """Device bin of an exponent t >= -14: floor((t + 14) * fp32(256 / 14)), at most 255."""
+    b = ((t - np.float32(-14.0)).astype(np.float32) * (np.float32(256.0) / np.float32(14.0))).astype(np.float32)
+    return np.minimum(b.astype(np.int64), 255)
+
+
+@pytest.mark.parametrize("W,V,T,tp,scale,seed", [(2, 30001, 0.7, 0.9, 3.0, 5), (4, 20000, 0.8, 0.95, 3.0, 6),
+                                                 (8, 40000, 0.7, 0.5, 4.0, 7), (3, 9999, 0.3, 0.99, 2.0, 8)])
+def test_listed_shard_path_rebuilds_the_threshold(W, V, T, tp, scale, seed):
+    """The listed path (specdec_shard_mass_hist / _cross / _union_select):
+    per shard the mass sum, the listed mass and the t-bin histogram of the
+    elements with t = (z - max) * c >= -14; summed over shards, the crossing
+    bin and the mass G above it; the shards' listed elements in that bin; a
+    radix select over them above G -- the oracle's tau and nucleus mass."""
+    rng = np.random.default_rng(seed)
+    z = (rng.standard_normal(V) * scale).astype(np.float32)
+    whole = O.row_stats(z, T, tp)
+    m = np.float32(whole.max)
+    c = np.float32(O.temp_coeff(T))
+    t = ((z - m).astype(np.float32) * c).astype(np.float32)
+    E = _masses(z, m, T)
+    key = _key(z)
+    shards = [vocab_shard(V, W, r) for r in range(W)]
+    S = 0
+    ls = 0
+    hist = np.zeros(256, dtype=np.uint64)
+    for v0, vs in shards:
+        sl = slice(v0, v0 + vs)
+        S += int(E[sl].sum())
+        lst = t[sl] >= np.float32(-14.0)
+        ls += int(E[sl][lst].sum())
+        np.add.at(hist, _tbin(t[sl][lst]), E[sl][lst])
+    assert S == whole.sum
+    thr = max(1, (S * O.top_p_q32(tp)) >> 32)
+    assert ls >= thr  # peaked rows: the nucleus lies among the listed elements
+    b, G, _ = _select(hist, thr, 0)
+    cand = []
+    for v0, vs in shards:
+        sl = slice(v0, v0 + vs)
+        sel = (t[sl] >= np.float32(-14.0)) & (_tbin(np.maximum(t[sl], np.float32(-14.0))) == b)
+        cand += list(zip(key[sl][sel].tolist(), E[sl][sel].tolist()))
+        assert sel.sum() <= 32
+    prefix, last = 0, 0
+    for d in (3, 2, 1, 0):
+        h = np.zeros(256, dtype=np.uint64)
+        for kk, e in cand:
+            if d == 3 or (kk >> (8 * d + 8)) == (prefix >> (8 * d + 8)):
+                h[(kk >> (8 * d)) & 255] += np.uint64(e)
+        digit, G, last = _select(h, thr, G)
+        prefix |= digit << (8 * d)
+    assert prefix == whole.tau and G + last == whole.nuc
