@@ -247,9 +247,10 @@ int specdec_w4_untile(const void* tiled, int N, int K, uint8_t* packed, uint16_t
  * (row stride ldx elements, 16-byte aligned), Y fp32 with row stride ldy.
  * Replaces compute_sme_gemm_i4_f32 (server/sme_gemm.cpp:249-285) and the W8
  * GEMV of the model forward (gemv_s8_f32_batched, server/sme_gemm.cpp:41-66)
- * for int4 group-128 weights.  From 65 token rows up, the int4 weights are
+ * for int4 group-128 weights.  From 17 token rows up, the int4 weights are
  * dequantised in registers and multiplied on the tcgen05 tensor cores with
- * TMEM accumulators; below, the call runs specdec_w4a16_gemv.  Partial tiles
+ * TMEM accumulators; below, the call runs specdec_w4a16_gemv (the measured
+ * crossover between the two).  Partial tiles
  * of k-ranges split across the CTAs of a cluster are summed on chip in a
  * fixed order, so the result is deterministic; the workspace
  * (specdec_w4a16_workspace_bytes, 0) is kept for the interface and may be
@@ -258,7 +259,7 @@ size_t specdec_w4a16_workspace_bytes(int M, int N, int K);
 int specdec_w4a16_gemm(const uint16_t* X, int M, int ldx, const void* w_tiled, int N, int K, float* Y, int ldy,
                        int mode, void* workspace, size_t workspace_bytes, void* stream);
 /* The same contraction for 0 <= M <= 64 token rows (decode at small batch,
- * the MTP draft heads): each CTA streams 128-row weight units by bulk copy,
+ * batch-1 steps): each CTA streams 128-row weight units by bulk copy,
  * dequantises them into tensor-core fragments in registers, a cluster splits
  * the k range and reduces in rank order through distributed shared memory.
  * Same results as specdec_w4a16_gemm within fp32 summation order.  Replaces

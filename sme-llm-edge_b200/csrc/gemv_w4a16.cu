@@ -288,11 +288,16 @@ static int gemv_num_sms() {
     return n;
 }
 
-// The planner's crossover between this kernel and the tcgen05 tiles.
+// The planner's crossover between this kernel and the tcgen05 tiles, from
+// graph-replay timings on a B200 (K = 4096): at N = 4096 this kernel takes
+// 8.3 / 10.1 / 12.8 / 19.6 us at M = 8 / 16 / 32 / 64 against 10.2 / 10.4 /
+// 10.9 / 11.6 for the tiles; at N = 128256, 93.6 / 114 / 172 / 306 against
+// 139 / 140 / 142 / 146.  Above 16 rows the tiles win.
+constexpr int kGemvRouteRows = 16;
 bool plan_gemm_uses_gemv(int M, int N, int K) {
     (void)N;
     (void)K;
-    return M >= 1 && M <= kGemvMaxRows;
+    return M >= 1 && M <= kGemvRouteRows;
 }
 
 int gemv_tiles(int M) { return M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8)); }

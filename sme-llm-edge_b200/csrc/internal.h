@@ -63,7 +63,7 @@ size_t gemm_workspace_bound(int max_m, int max_n, int max_k);
 
 // W4A16 contraction for few token rows (gemv_w4a16.cu): mode 0 store / 1 add,
 // 1 <= M <= kGemvMaxRows.  plan_gemm_uses_gemv() is the crossover the planner
-// applies (measured against the tcgen05 tiles).
+// applies (measured against the tcgen05 tiles: up to 16 rows).
 constexpr int kGemvMaxRows = 64;
 struct GemvPlan {
     int NT;      // tiles of 8 token rows
