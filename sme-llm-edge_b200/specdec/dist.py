@@ -128,7 +128,7 @@ def vocab_shard(V: int, world: int, rank: int) -> tuple[int, int]:
     return lo, hi - lo
 
 
-SHARD_LIST_CAP = 1024  # listed (key, mass) pairs kept per shard row
+SHARD_LIST_CAP = 4096  # listed (key, mass) pairs kept per shard row (~1600 per whole row at N(0, 3), T = 0.7)
 SHARD_CAND = 32  # crossing-bin candidates per rank and row (kShardCand)
 
 
@@ -173,6 +173,16 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
     gm, ga = comm.all_gather(mx), comm.all_gather(am)
     S.check(L.specdec_shard_merge_max(p(gm), p(ga), W, rows, p(mx), p(am), st))
     pmax, parg = mx[:rows_p], am[:rows_p]
+
+    def assemble(acc, tok):
+        """(accepted, out_tokens [B, k+1]): accepted drafts, the emitted token, -1."""
+        idx = torch.arange(k + 1, device=dev)[None, :]
+        a = acc.long()[:, None]
+        ext = torch.cat([drafts, torch.full((B, 1), -1, dtype=torch.int32, device=dev)], 1)
+        out = torch.where(idx < a, ext, torch.full_like(ext, -1))
+        out = torch.where(idx == a, tok.to(torch.int32)[:, None], out)
+        return acc, out
+
     if greedy:
         acc = torch.empty(B, dtype=torch.int32, device=dev)
         S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), None, None, None, None,
@@ -226,6 +236,7 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
             ok = torch.empty(rows, dtype=torch.int32, device=dev)
             S.check(L.specdec_shard_union_select(p(gcand), W, rows, p(stats), p(G), tp, p(tau), p(nuc), p(ok), st))
             acc, tok = finish(tau, nuc)
+            res = assemble(acc, tok)
             done = bool(ok.all().item())  # the same on every rank: computed from exchanged data only
         if not done:
             sums = torch.empty(rows, dtype=torch.int64, device=dev)
@@ -245,10 +256,6 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
             else:
                 tau = torch.zeros(rows, dtype=torch.int32, device=dev)
                 nuc = sums
-            acc, tok = finish(tau, nuc)
-    idx = torch.arange(k + 1, device=dev)[None, :]
-    a = acc.long()[:, None]
-    ext = torch.cat([drafts, torch.full((B, 1), -1, dtype=torch.int32, device=dev)], 1)
-    out = torch.where(idx < a, ext, torch.full_like(ext, -1))
-    out = torch.where(idx == a, tok.to(torch.int32)[:, None], out)
-    return acc, out
+            res = assemble(*finish(tau, nuc))
+        return res
+    return assemble(acc, tok)
