@@ -625,22 +625,45 @@ def run_accept_sharded(args):
         S.check(L.specdec_shard_merge_max(pt(gm), pt(ga), world, B * k, pt(mx), pt(am), st))
         drafts = am.view(B, k).contiguous()
         sp = S.sampling(T, tp, 4, 0)
-        for _ in range(args.warmup):
-            accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm)
-        torch.cuda.synchronize()
-        barrier(pg, local)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            acc, _ = accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm)
-        e1.record()
-        torch.cuda.synchronize()
+        # the captured form (one CUDA graph of the kernels and collectives per
+        # call) where it applies; its result is checked against the
+        # host-issued sequence once
+        captured = None
+        if T > 0.0 and tp < 1.0 and world <= 8:
+            from specdec.dist import ShardedChainAcceptor
+
+            tgt, dr = tgt.contiguous(), dr.contiguous()
+            captured = ShardedChainAcceptor(tgt, dr, drafts, k, v0, sp, comm, graph=True)
+            a1, o1 = captured(0)
+            a2, o2 = accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm)
+            same = bool(torch.equal(a1, a2) and torch.equal(o1, o2))
+        call = (lambda: captured(0)) if captured is not None else (
+            lambda: accept_chain_vocab_sharded(tgt, dr, drafts, k, v0, sp, comm))
+        try:
+            for _ in range(args.warmup):
+                call()
+            torch.cuda.synchronize()
+            barrier(pg, local)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                acc, _ = call()
+            e1.record()
+            torch.cuda.synchronize()
+        finally:
+            if captured is not None:
+                captured.close()  # a graph holding collectives must go before the process group
+                captured = None
+                torch.cuda.synchronize()
         us = reduce_max(pg, e0.elapsed_time(e1) / args.steps * 1e3, local)
         if rank == 0:
             peaks, src = load_peaks()
             total = (2 * k + 1) * B * V * 4
             print(json.dumps({"kernel": "accept (vocabulary-sharded)", "shape": f"{B},{k},{V},{T},{tp}",
                               "n_gpus": world, "us_per_launch": round(us, 2),
+                              "issue": "one CUDA graph per call" if T > 0.0 and tp < 1.0 and world <= 8
+                              else "host-issued kernels and collectives",
+                              "graph_matches_host_issued": same if T > 0.0 and tp < 1.0 and world <= 8 else None,
                               "gbs_algorithmic_per_gpu": round(total / world / us / 1e3, 1),
                               "hbm_frac_per_gpu": round(total / world / us / 1e3 / peaks["hbm_gbs"], 3),
                               "mean_accepted": round(float(acc.float().mean()), 3)}), flush=True)

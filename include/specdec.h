@@ -220,13 +220,15 @@ int specdec_shard_union_select(const void* gcand, int W, int rows, const uint64_
 int specdec_shard_point_mass(const float* target, const float* draft, const int32_t* drafts, int B, int k, int Vs,
                              int v0, float temperature, const float* pmax, const uint32_t* ptau, const float* qmax,
                              const uint32_t* qtau, uint64_t* ep, uint64_t* eq, void* stream);
+/* step_dev (may be NULL): a device step counter read instead of sp->step,
+ * so that a captured sequence of the steps serves every decoding step. */
 int specdec_shard_accept_test(const int32_t* drafts, int B, int k, const specdec_sampling* sp, const int32_t* parg,
                               const uint64_t* pnuc, const uint64_t* qnuc, const uint64_t* ep, const uint64_t* eq,
-                              int32_t* accepted, void* stream);
+                              int32_t* accepted, const uint32_t* step_dev, void* stream);
 int specdec_shard_draw_winners(const float* target, const float* draft, int B, int k, int Vs, int v0,
                                const specdec_sampling* sp, const int32_t* accepted, const float* pmax,
                                const uint32_t* ptau, const float* qmax, const uint32_t* qtau, const uint64_t* pnuc,
-                               const uint64_t* qnuc, int32_t* out_win, void* stream);
+                               const uint64_t* qnuc, int32_t* out_win, const uint32_t* step_dev, void* stream);
 int specdec_shard_draw_merge(const int32_t* gwin, int W, int B, int k, const int32_t* accepted, int32_t* tok_out,
                              void* stream);
 

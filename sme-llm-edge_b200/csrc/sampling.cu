@@ -1510,11 +1510,13 @@ __global__ void shard_point_mass_kernel(const float* __restrict__ target, const 
 
 // (7) the sequential min(1, p/q) tests (as accept_chain_kernel), one thread per sequence
 __global__ void shard_accept_test_kernel(const int32_t* __restrict__ drafts, int B, int k, bool greedy, uint64_t seed,
-                                         uint32_t step, const int32_t* __restrict__ parg,
+                                         const uint32_t* __restrict__ step_dev, uint32_t step_host,
+                                         const int32_t* __restrict__ parg,
                                          const unsigned long long* __restrict__ pnuc,
                                          const unsigned long long* __restrict__ qnuc,
                                          const unsigned long long* __restrict__ ep,
                                          const unsigned long long* __restrict__ eq, int32_t* __restrict__ a_out) {
+    const uint32_t step = step_dev ? *step_dev : step_host;
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const int32_t* D = drafts + (size_t)b * k;
@@ -1553,8 +1555,10 @@ struct ShardRows {
 // are those of the global index, so the winners merged over the shards are
 // the draw on the whole row.
 __global__ void __launch_bounds__(kRowThreads) shard_draw_winners_kernel(ShardRows sr, const int32_t* __restrict__ a_in,
-                                                                         uint64_t seed, uint32_t step,
-                                                                         int32_t* __restrict__ out) {
+                                                                         uint64_t seed,
+                                                                         const uint32_t* __restrict__ step_dev,
+                                                                         uint32_t step_host, int32_t* __restrict__ out) {
+    const uint32_t step = step_dev ? *step_dev : step_host;
     __shared__ RowSmem sm;
     const int b = blockIdx.x, a = a_in[b], k = sr.k;
     const int prow = b * (k + 1) + a;
@@ -2004,13 +2008,14 @@ extern "C" int specdec_shard_point_mass(const float* target, const float* draft,
 
 extern "C" int specdec_shard_accept_test(const int32_t* drafts, int B, int k, const specdec_sampling* sp,
                                          const int32_t* parg, const uint64_t* pnuc, const uint64_t* qnuc,
-                                         const uint64_t* ep, const uint64_t* eq, int32_t* accepted, void* stream) {
+                                         const uint64_t* ep, const uint64_t* eq, int32_t* accepted,
+                                         const uint32_t* step_dev, void* stream) {
     SD_CHECK(drafts && sp && parg && accepted && B >= 0 && k >= 1, SPECDEC_EINVAL, "shard_accept_test: bad argument");
     const bool greedy = !(sp->temperature > 0.0f);
     SD_CHECK(greedy || (pnuc && qnuc && ep && eq), SPECDEC_EINVAL, "shard_accept_test: statistics required");
     if (B == 0) return SPECDEC_OK;
     shard_accept_test_kernel<<<(B + 127) / 128, 128, 0, as_stream(stream)>>>(
-        drafts, B, k, greedy, sp->seed, sp->step, parg, reinterpret_cast<const unsigned long long*>(pnuc),
+        drafts, B, k, greedy, sp->seed, step_dev, sp->step, parg, reinterpret_cast<const unsigned long long*>(pnuc),
         reinterpret_cast<const unsigned long long*>(qnuc), reinterpret_cast<const unsigned long long*>(ep),
         reinterpret_cast<const unsigned long long*>(eq), accepted);
     SD_LAUNCH_CHECK("shard_accept_test_kernel");
@@ -2039,7 +2044,8 @@ static ShardRows shard_rows(const float* target, const float* draft, int k, int 
 extern "C" int specdec_shard_draw_winners(const float* target, const float* draft, int B, int k, int Vs, int v0,
                                          const specdec_sampling* sp, const int32_t* accepted, const float* pmax,
                                          const uint32_t* ptau, const float* qmax, const uint32_t* qtau,
-                                         const uint64_t* pnuc, const uint64_t* qnuc, int32_t* out_win, void* stream) {
+                                         const uint64_t* pnuc, const uint64_t* qnuc, int32_t* out_win,
+                                         const uint32_t* step_dev, void* stream) {
     if (int rc = shard_check(B, Vs, "shard_draw_winners")) return rc;
     SD_CHECK(target && draft && sp && accepted && pmax && ptau && qmax && qtau && pnuc && qnuc && out_win && k >= 1 &&
                  v0 >= 0 && sp->temperature > 0.0f,
@@ -2047,7 +2053,7 @@ extern "C" int specdec_shard_draw_winners(const float* target, const float* draf
     if (B == 0) return SPECDEC_OK;
     shard_draw_winners_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
         shard_rows(target, draft, k, Vs, v0, sp->temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted, sp->seed,
-        sp->step, out_win);
+        step_dev, sp->step, out_win);
     SD_LAUNCH_CHECK("shard_draw_winners_kernel");
     return SPECDEC_OK;
 }

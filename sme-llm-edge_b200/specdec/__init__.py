@@ -95,8 +95,8 @@ _SIGS = {
     "specdec_shard_cross": (I, [P, I, F, P, F, P, I, P, P, P, P]),
     "specdec_shard_union_select": (I, [P, I, I, P, P, F, P, P, P, P]),
     "specdec_shard_point_mass": (I, [P, P, P, I, I, I, I, F, P, P, P, P, P, P, P]),
-    "specdec_shard_accept_test": (I, [P, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P]),
-    "specdec_shard_draw_winners": (I, [P, P, I, I, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P, P, P]),
+    "specdec_shard_accept_test": (I, [P, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P, P]),
+    "specdec_shard_draw_winners": (I, [P, P, I, I, I, I, C.POINTER(Sampling), P, P, P, P, P, P, P, P, P, P]),
     "specdec_shard_draw_merge": (I, [P, I, I, I, P, P, P]),
     "specdec_w4_tiled_bytes": (SZ, [I, I]),
     "specdec_w4_tile": (I, [P, P, I, I, P, P]),

@@ -186,7 +186,7 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
     if greedy:
         acc = torch.empty(B, dtype=torch.int32, device=dev)
         S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), None, None, None, None,
-                                            p(acc), st))
+                                            p(acc), None, st))
         tok = parg.view(B, k + 1).gather(1, acc.long()[:, None])[:, 0]
     else:
         qmax = mx[rows_p:]
@@ -204,10 +204,11 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
             ep, eq = pq[0].contiguous(), pq[1].contiguous()
             acc = torch.empty(B, dtype=torch.int32, device=dev)
             S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sampling), p(parg), p(pnuc), p(qnuc),
-                                                p(ep), p(eq), p(acc), st))
+                                                p(ep), p(eq), p(acc), None, st))
             win = torch.empty((B, 4), dtype=torch.int32, device=dev)
             S.check(L.specdec_shard_draw_winners(p(target), p(draft), B, k, Vs, v0, C.byref(sampling), p(acc),
-                                                 p(pmax), p(ptau), p(qmax), p(qtau), p(pnuc), p(qnuc), p(win), st))
+                                                 p(pmax), p(ptau), p(qmax), p(qtau), p(pnuc), p(qnuc), p(win), None,
+                                                 st))
             gwin = comm.all_gather(win).contiguous()
             tok = torch.empty(B, dtype=torch.int32, device=dev)
             S.check(L.specdec_shard_draw_merge(p(gwin), W, B, k, p(acc), p(tok), st))
@@ -259,3 +260,121 @@ def accept_chain_vocab_sharded(target, draft, drafts, k: int, v0: int, sampling,
             res = assemble(*finish(tau, nuc))
         return res
     return assemble(acc, tok)
+
+
+class ShardedChainAcceptor:
+    """accept_chain_vocab_sharded for fixed shapes and sampling (T > 0, top_p
+    < 1, at most 8 ranks) with its buffers allocated once and, when `graph`
+    is set, the listed path -- its kernels and collectives -- recorded in one
+    CUDA graph, so that a call costs the host one graph launch instead of
+    about twenty kernel and collective launches.
+
+    target [B, k+1, Vs], draft [B, k, Vs] and drafts [B, k] are the static
+    inputs: write each step's shard logits and drafted tokens into them.  The
+    step of the uniforms is a device counter (`__call__(step)` sets it).
+    Rows the listed path cannot settle (flat rows, NaN logits) make the call
+    redo the acceptance with accept_chain_vocab_sharded.  `close()` releases
+    the graph and must run before the process group is destroyed."""
+
+    def __init__(self, target, draft, drafts, k: int, v0: int, sampling, comm, graph: bool = True):
+        import torch
+
+        T, tp = float(sampling.temperature), float(sampling.top_p)
+        if not (T > 0.0 and tp < 1.0 and comm.world * SHARD_CAND <= 256):
+            raise ValueError("ShardedChainAcceptor: needs T > 0, top_p < 1 and at most 8 ranks")
+        self.target, self.draft, self.drafts = target, draft, drafts
+        self.k, self.v0, self.sampling, self.comm = k, v0, sampling, comm
+        dev = target.device
+        B, Vs = int(target.shape[0]), int(target.shape[2])
+        self.B, self.Vs = B, Vs
+        rows_p, rows_q = B * (k + 1), B * k
+        rows = rows_p + rows_q
+        self.rows_p, self.rows_q, self.rows = rows_p, rows_q, rows
+        i32, i64 = torch.int32, torch.int64
+        self.step_dev = torch.full((1,), int(sampling.step), dtype=i32, device=dev)
+        self.mx = torch.empty(rows, dtype=torch.float32, device=dev)
+        self.am = torch.empty(rows, dtype=i32, device=dev)
+        self.lst = torch.empty((rows, SHARD_LIST_CAP, 2), dtype=i32, device=dev)
+        self.lnum = torch.empty(rows, dtype=i32, device=dev)
+        self.stats = torch.empty((rows, 260), dtype=i64, device=dev)
+        self.G = torch.empty(rows, dtype=i64, device=dev)
+        self.cand = torch.empty((rows, SHARD_CAND + 1, 2), dtype=i32, device=dev)
+        self.tau = torch.empty(rows, dtype=i32, device=dev)
+        self.nuc = torch.empty(rows, dtype=i64, device=dev)
+        self.ok = torch.empty(rows, dtype=i32, device=dev)
+        self.pq = torch.empty((2, rows_q), dtype=i64, device=dev)
+        self.acc = torch.empty(B, dtype=i32, device=dev)
+        self.win = torch.empty((B, 4), dtype=i32, device=dev)
+        self.tok = torch.empty(B, dtype=i32, device=dev)
+        self.out = torch.empty((B, k + 1), dtype=i32, device=dev)
+        self.graph = None
+        self._issue()  # eager once: warms the collectives up and checks the sequence
+        torch.cuda.synchronize(dev)
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._issue()
+            self.graph = g
+
+    def _issue(self):
+        import ctypes as C
+
+        import torch
+
+        import specdec as S
+
+        L = S.lib()
+        p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+        st = C.c_void_p(torch.cuda.current_stream(self.target.device).cuda_stream)
+        comm, sp, k, B, Vs, v0 = self.comm, self.sampling, self.k, self.B, self.Vs, self.v0
+        T, tp = float(sp.temperature), float(sp.top_p)
+        rows_p, rows_q, rows = self.rows_p, self.rows_q, self.rows
+        tgt, dr, drafts = self.target, self.draft, self.drafts
+        S.check(L.specdec_shard_row_max(p(tgt), rows_p, p(dr), rows_q, Vs, v0, p(self.mx), p(self.am), st))
+        gm, ga = comm.all_gather(self.mx), comm.all_gather(self.am)
+        S.check(L.specdec_shard_merge_max(p(gm), p(ga), comm.world, rows, p(self.mx), p(self.am), st))
+        S.check(L.specdec_shard_mass_hist(p(tgt), rows_p, p(dr), rows_q, Vs, p(self.mx), T, SHARD_LIST_CAP,
+                                          p(self.lst), p(self.lnum), p(self.stats), st))
+        comm.all_reduce_sum(self.stats)
+        S.check(L.specdec_shard_cross(p(self.stats), rows, tp, p(self.mx), T, p(self.lst), SHARD_LIST_CAP,
+                                      p(self.lnum), p(self.G), p(self.cand), st))
+        gcand = comm.all_gather(self.cand)
+        S.check(L.specdec_shard_union_select(p(gcand), comm.world, rows, p(self.stats), p(self.G), tp, p(self.tau),
+                                             p(self.nuc), p(self.ok), st))
+        pmax, qmax = self.mx[:rows_p], self.mx[rows_p:]
+        ptau, qtau = self.tau[:rows_p], self.tau[rows_p:]
+        pnuc, qnuc = self.nuc[:rows_p], self.nuc[rows_p:]
+        S.check(L.specdec_shard_point_mass(p(tgt), p(dr), p(drafts), B, k, Vs, v0, T, p(pmax), p(ptau), p(qmax),
+                                           p(qtau), p(self.pq[0]), p(self.pq[1]), st))
+        comm.all_reduce_sum(self.pq)
+        S.check(L.specdec_shard_accept_test(p(drafts), B, k, C.byref(sp), p(self.am[:rows_p]), p(pnuc), p(qnuc),
+                                            p(self.pq[0]), p(self.pq[1]), p(self.acc), p(self.step_dev), st))
+        S.check(L.specdec_shard_draw_winners(p(tgt), p(dr), B, k, Vs, v0, C.byref(sp), p(self.acc), p(pmax),
+                                             p(ptau), p(qmax), p(qtau), p(pnuc), p(qnuc), p(self.win),
+                                             p(self.step_dev), st))
+        gwin = comm.all_gather(self.win)
+        S.check(L.specdec_shard_draw_merge(p(gwin), comm.world, B, k, p(self.acc), p(self.tok), st))
+        idx = torch.arange(k + 1, device=tgt.device)[None, :]
+        a = self.acc.long()[:, None]
+        ext = torch.cat([drafts, torch.full((B, 1), -1, dtype=torch.int32, device=tgt.device)], 1)
+        out = torch.where(idx < a, ext, torch.full_like(ext, -1))
+        self.out.copy_(torch.where(idx == a, self.tok[:, None], out))
+
+    def __call__(self, step: int | None = None):
+        """(accepted [B], out_tokens [B, k+1]) on the device, the same on every rank."""
+        if step is not None:
+            self.step_dev.fill_(int(step))
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._issue()
+        if bool(self.ok.all().item()):  # the same on every rank: computed from exchanged data only
+            return self.acc, self.out
+        import specdec as S
+
+        s0 = self.sampling
+        sp = S.sampling(s0.temperature, s0.top_p, s0.seed, int(self.step_dev.item()) if step is None else int(step))
+        return accept_chain_vocab_sharded(self.target, self.draft, self.drafts, self.k, self.v0, sp, self.comm)
+
+    def close(self):
+        self.graph = None

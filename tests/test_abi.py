@@ -96,7 +96,7 @@ def test_shard_steps_reject_bad_arguments_without_gpu():
     # digits other than 0..3, a draft length of 0, and an empty world
     assert L.specdec_shard_select_digit(dummy, 4, 4, dummy, 0.9, dummy, dummy, dummy, None) == specdec.EINVAL
     assert L.specdec_shard_draw_winners(dummy, dummy, 2, 0, 128, 0, C.byref(sp), dummy, dummy, dummy, dummy, dummy,
-                                        dummy, dummy, dummy, None) == specdec.EINVAL
+                                        dummy, dummy, dummy, None, None) == specdec.EINVAL
     assert L.specdec_shard_draw_merge(dummy, 0, 2, 3, dummy, dummy, None) == specdec.EINVAL
     # the mass steps need a temperature
     assert L.specdec_shard_point_mass(dummy, dummy, dummy, 2, 3, 128, 0, 0.0, dummy, dummy, dummy, dummy, dummy,

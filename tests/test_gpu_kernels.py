@@ -519,3 +519,51 @@ def test_accept_chain_vocab_sharded_matches_oracle(cuda_device, W, B, k, V, T, t
     assert not errors, errors
     for r in range(W):
         assert results[r] == (acc_o.tolist(), out_o.tolist()), f"rank {r}"
+
+
+def test_sharded_acceptor_buffers_match_oracle(cuda_device):
+    """ShardedChainAcceptor (buffers allocated once, the step counter on the
+    device; issued eagerly here, as thread-ranks cannot record collectives in
+    a graph): two steps over the same static inputs, each equal to the
+    oracle's acceptance at that step."""
+    import threading
+
+    import torch
+
+    from specdec.dist import ShardedChainAcceptor, ThreadComm, vocab_shard
+
+    W, B, k, V, T, tp = 3, 5, 4, 20000, 0.7, 0.9
+    rng = np.random.default_rng(77)
+    tgt = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.5).astype(np.float32)
+    drafts = O.sample_rows(dr.reshape(B * k, V), k, T, tp, 9, 0).reshape(B, k)
+    want = {st: O.accept_chain(tgt, dr, drafts, T, tp, 55, st) for st in (3, 4)}
+    comm = ThreadComm(W)
+    results, errors = [None] * W, []
+
+    def rank_main(r):
+        try:
+            v0, vs = vocab_shard(V, W, r)
+            t = dev(np.ascontiguousarray(tgt[:, :, v0:v0 + vs]))
+            d = dev(np.ascontiguousarray(dr[:, :, v0:v0 + vs]))
+            acc = ShardedChainAcceptor(t, d, dev(drafts), k, v0, S.sampling(T, tp, 55, 3), comm.rank_view(r),
+                                       graph=False)
+            got = {}
+            for st in (3, 4):
+                a, o = acc(st)
+                torch.cuda.synchronize()
+                got[st] = (a.cpu().numpy().tolist(), o.cpu().numpy().tolist())
+            results[r] = got
+        except Exception as e:  # noqa: BLE001 -- reported below
+            errors.append(repr(e))
+            comm.barrier.abort()
+
+    threads = [threading.Thread(target=rank_main, args=(r,)) for r in range(W)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+    for r in range(W):
+        for st in (3, 4):
+            assert results[r][st][0] == want[st][0].tolist() and results[r][st][1] == want[st][1].tolist(), (r, st)
