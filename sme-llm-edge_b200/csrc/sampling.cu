@@ -1875,6 +1875,15 @@ extern "C" int specdec_sample_rows(const float* logits, int rows, int k, int V, 
 
 // ---------------------------------------------------------------------------
 // Vocabulary-sharded chain acceptance: the shard steps (see include/specdec.h).
+// Threads per shard row: narrow shards (many ranks) get smaller CTAs, so that
+// several rows share an SM instead of one 1024-thread CTA per row idling in
+// its reductions.
+static int shard_threads(int Vs) {
+    int t = 256;
+    while (t < kRowThreads && t * 64 < Vs) t *= 2;
+    return t;
+}
+
 static int shard_check(int rows, int Vs, const char* what) {
     if (rows < 0 || Vs <= 0 || Vs > kMaxVocab) {
         set_error(std::string(what) + ": bad shape (shard width must be 1 .. 262144)");
@@ -1889,7 +1898,7 @@ extern "C" int specdec_shard_row_max(const float* z, int rows, const float* z2, 
     SD_CHECK(z && out_max && out_arg && rows2 >= 0 && (rows2 == 0 || z2), SPECDEC_EINVAL,
              "shard_row_max: null argument");
     if (rows + rows2 == 0) return SPECDEC_OK;
-    shard_row_max_kernel<<<rows + rows2, kRowThreads, 0, as_stream(stream)>>>(z, rows, z2, Vs, v0, out_max, out_arg);
+    shard_row_max_kernel<<<rows + rows2, shard_threads(Vs), 0, as_stream(stream)>>>(z, rows, z2, Vs, v0, out_max, out_arg);
     SD_LAUNCH_CHECK("shard_row_max_kernel");
     return SPECDEC_OK;
 }
@@ -1909,7 +1918,7 @@ extern "C" int specdec_shard_row_mass(const float* z, int rows, const float* z2,
     SD_CHECK(z && gmax && out_sum && temperature > 0.0f && rows2 >= 0 && (rows2 == 0 || z2), SPECDEC_EINVAL,
              "shard_row_mass: bad argument");
     if (rows + rows2 == 0) return SPECDEC_OK;
-    shard_row_mass_kernel<<<rows + rows2, kRowThreads, 0, as_stream(stream)>>>(
+    shard_row_mass_kernel<<<rows + rows2, shard_threads(Vs), 0, as_stream(stream)>>>(
         z, rows, z2, Vs, gmax, temp_coeff(temperature), reinterpret_cast<unsigned long long*>(out_sum));
     SD_LAUNCH_CHECK("shard_row_mass_kernel");
     return SPECDEC_OK;
@@ -1940,7 +1949,7 @@ extern "C" int specdec_shard_mass_hist(const float* z, int rows, const float* z2
              SPECDEC_EINVAL, "shard_mass_hist: bad argument");
     if (rows + rows2 == 0) return SPECDEC_OK;
     SD_CHECK(cap <= 65536, SPECDEC_EINVAL, "shard_mass_hist: cap above 65536");
-    shard_mass_hist_kernel<<<rows + rows2, kRowThreads, 0, as_stream(stream)>>>(
+    shard_mass_hist_kernel<<<rows + rows2, shard_threads(Vs), 0, as_stream(stream)>>>(
         z, rows, z2, Vs, gmax, temp_coeff(temperature), cap, static_cast<uint2*>(list), list_n,
         reinterpret_cast<unsigned long long*>(out_stats));
     SD_LAUNCH_CHECK("shard_mass_hist_kernel");
@@ -2051,7 +2060,7 @@ extern "C" int specdec_shard_draw_winners(const float* target, const float* draf
                  v0 >= 0 && sp->temperature > 0.0f,
              SPECDEC_EINVAL, "shard_draw_winners: bad argument");
     if (B == 0) return SPECDEC_OK;
-    shard_draw_winners_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(
+    shard_draw_winners_kernel<<<B, shard_threads(Vs), 0, as_stream(stream)>>>(
         shard_rows(target, draft, k, Vs, v0, sp->temperature, pmax, ptau, qmax, qtau, pnuc, qnuc), accepted, sp->seed,
         step_dev, sp->step, out_win);
     SD_LAUNCH_CHECK("shard_draw_winners_kernel");
