@@ -469,6 +469,48 @@ def run_gpu(args, world, rank, local, pg):
     eng.close()
 
 
+# ------------------------------------------------------------ prefill
+def run_prefill(args):
+    """Chunked prefill of the engine (64-token verify forwards over the paged
+    KV): `--kernel prefill --shape model,batch,prompt_len` (default
+    llama3-8b,32,2048), random-init weights and uniform random prompts; prints the
+    prompt tokens per second of `--steps` timed prefills (each into a fresh
+    KV after `specdec_engine_retire` of every slot) after `--warmup`."""
+    import torch
+
+    import specdec as S
+
+    parts = (args.shape or "llama3-8b,32,2048").split(",")
+    model, B, P = parts[0], int(parts[1]), int(parts[2])
+    shape = S.MODEL_SHAPES[model]
+    eng = S.Engine(shape, batch=B, draft_len=4, max_ctx=P + 64, temperature=0.8, seed=1, use_graph=False)
+    eng.init_weights(1)
+    rng = np.random.default_rng(0)
+    prompts = rng.integers(0, shape["vocab"], (B, P)).astype(np.int32)
+
+    def one():
+        for b in range(B):
+            eng.retire(b)
+        eng.prefill(prompts)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(torch.cuda.ExternalStream(eng.stream()))
+    for _ in range(args.steps):
+        one()
+    e1.record(torch.cuda.ExternalStream(eng.stream()))
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    toks = B * (P - 1)
+    print(json.dumps({"kernel": "prefill", "model": model, "batch": B, "prompt_len": P, "ms_per_prefill": round(ms, 3),
+                      "prompt_tokens_per_s": round(toks / (ms / 1e3), 1), "chunk_rows": 64 * B,
+                      "timing": "CUDA events on the engine stream around --steps prefills (host-synchronised calls)"}),
+          flush=True)
+    eng.close()
+
+
 # ------------------------------------------------------------ single-kernel mode
 def run_kernel(args):
     """One hot kernel on synthetic inputs, for profiler captures: `--kernel gemm
@@ -681,7 +723,7 @@ def main():
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--nvtx", action="store_true", help="mark the timed steps with an NVTX range (profiler filter)")
-    ap.add_argument("--kernel", choices=["gemm", "gemm_tc", "gemv", "attention", "accept"],
+    ap.add_argument("--kernel", choices=["gemm", "gemm_tc", "gemv", "attention", "accept", "prefill"],
                     help="time one hot kernel instead of the step (gemm: as the planner routes it; gemm_tc: the "
                          "tcgen05 tiles; gemv: the few-row kernel)")
     ap.add_argument("--plan", default="", help="--kernel gemm_tc: units per CTA and k split, e.g. 2,8")
@@ -691,6 +733,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.kernel == "accept" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_accept_sharded(args)
+        return
+    if args.kernel == "prefill":
+        run_prefill(args)
         return
     if args.kernel:
         run_kernel(args)
