@@ -43,6 +43,14 @@ enum {
 /* Last error message of the calling thread ("" if none). */
 const char* specdec_last_error(void);
 int specdec_abi_version(void);
+/* Failure-path self-test: launches one thread that waits on an mbarrier phase
+ * no thread completes, with the bounded wait every TMA / tensor-core kernel of
+ * the library uses (about 2 s of wall time).  The wait gives up, the kernel
+ * records SPECDEC_ETIMEOUT in the device status word and returns; the call
+ * reads the word back on `stream` and returns SPECDEC_ETIMEOUT (message
+ * "device-side wait gave up at site 90").  The status word is cleared and the
+ * context stays usable.  No fault, trap or unbounded wait is involved. */
+int specdec_selftest_wait_timeout(void* stream);
 
 /* ===================================================================== */
 /* 1. Reference FFI symbols (host pointers).                               */

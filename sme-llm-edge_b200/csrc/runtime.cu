@@ -3,6 +3,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace specdec {
 
@@ -46,7 +47,29 @@ int check_device_status(cudaStream_t s) {
     return SPECDEC_OK;
 }
 
+// One thread waits on phase 0 of an mbarrier that expects one arrival and
+// gets none: mbar_wait gives up after its ~2 s limit and the give-up path
+// records the timeout, as in every kernel whose producer never delivers.
+constexpr int kSelftestWaitSite = 90;
+__global__ void wait_timeout_selftest_kernel(DeviceStatus* st) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(s_addr(&bar), 1);
+        if (!mbar_wait(s_addr(&bar), 0)) record_timeout(st, kSelftestWaitSite);
+    }
+}
+
 }  // namespace specdec
 
 extern "C" const char* specdec_last_error(void) { return specdec::g_last_error.c_str(); }
 extern "C" int specdec_abi_version(void) { return 1; }
+
+extern "C" int specdec_selftest_wait_timeout(void* stream) {
+    using namespace specdec;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    DeviceStatus* st = device_status_ptr();
+    SD_CHECK(st, SPECDEC_ECUDA, "selftest_wait_timeout: no device status word");
+    wait_timeout_selftest_kernel<<<1, 32, 0, s>>>(st);
+    SD_LAUNCH_CHECK("wait_timeout_selftest_kernel");
+    return check_device_status(s);
+}

@@ -71,6 +71,7 @@ class RunConfig(C.Structure):
 _SIGS = {
     "specdec_last_error": (C.c_char_p, []),
     "specdec_abi_version": (I, []),
+    "specdec_selftest_wait_timeout": (I, [P]),
     "sve2_speculative_verify_f32": (None, [P, P, P, U32, U32, U32, P, P]),
     "rust_sme_mtp_predict_f32": (None, [P, P, P, U32, U32, U32]),
     "rust_sme_mtp_sample_f32": (None, [P, P, U32, U32]),

@@ -23,29 +23,34 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
-def _reduce(dist, x: float, device: str, op) -> float:
+def _reduce(dist, x: float, device: str, op, timeout: float | None = None) -> float:
     if dist is None:
         return float(x)
     import torch
 
     t = torch.tensor([float(x)], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=op)
+    if timeout is None:
+        dist.all_reduce(t, op=op)
+    else:
+        guarded_wait(dist.all_reduce(t, op=op, async_op=True), timeout, "all_reduce")
     return float(t.item())
 
 
-def reduce_max(dist, x: float, device: str = "cpu") -> float:
-    return _reduce(dist, x, device, None if dist is None else dist.ReduceOp.MAX)
+def reduce_max(dist, x: float, device: str = "cpu", timeout: float | None = None) -> float:
+    return _reduce(dist, x, device, None if dist is None else dist.ReduceOp.MAX, timeout)
 
 
-def reduce_sum(dist, x: float, device: str = "cpu") -> float:
-    return _reduce(dist, x, device, None if dist is None else dist.ReduceOp.SUM)
+def reduce_sum(dist, x: float, device: str = "cpu", timeout: float | None = None) -> float:
+    return _reduce(dist, x, device, None if dist is None else dist.ReduceOp.SUM, timeout)
 
 
-def step_throughput(dist, ms: float, tokens: float, device: str = "cpu") -> dict:
+def step_throughput(dist, ms: float, tokens: float, device: str = "cpu", timeout: float | None = None) -> dict:
     """Whole-job throughput of a timed run: tokens of all ranks over the
-    slowest rank's device time.  Every rank must call it (it is collective)."""
-    ms_max = reduce_max(dist, ms, device)
-    tok = reduce_sum(dist, tokens, device)
+    slowest rank's device time.  Every rank must call it (it is collective);
+    with `timeout` a rank that never joins raises RankLost after that many
+    seconds."""
+    ms_max = reduce_max(dist, ms, device, timeout)
+    tok = reduce_sum(dist, tokens, device, timeout)
     return {"ms_max": ms_max, "tokens": tok, "value": tok / (ms_max / 1e3) if ms_max > 0 else 0.0}
 
 
@@ -53,28 +58,43 @@ def step_throughput(dist, ms: float, tokens: float, device: str = "cpu") -> dict
 # Vocabulary-sharded chain acceptance
 # ----------------------------------------------------------------------
 class TorchComm:
-    """Collectives of a torch.distributed process group (NCCL for CUDA tensors)."""
+    """Collectives of a torch.distributed process group (NCCL for CUDA tensors).
 
-    def __init__(self, dist, group=None):
+    With `timeout` (seconds) every collective is issued asynchronously and
+    waited for at most that long on the host, raising RankLost when a peer
+    never joins or has gone; without it the collectives are plain (the form
+    a CUDA graph can capture)."""
+
+    def __init__(self, dist, group=None, timeout: float | None = None):
         self.dist = dist
         self.group = group
+        self.timeout = timeout
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+
+    def _run(self, issue, what: str):
+        if self.timeout is None:
+            issue(False)
+        else:
+            guarded_wait(issue(True), self.timeout, what)
 
     def all_gather(self, t):
         import torch
 
         # flat in, flat out (the form every backend accepts), then [world, *shape]
         out = torch.empty(self.world * t.numel(), dtype=t.dtype, device=t.device)
-        self.dist.all_gather_into_tensor(out, t.contiguous().view(-1), group=self.group)
+        src = t.contiguous().view(-1)
+        self._run(lambda a: self.dist.all_gather_into_tensor(out, src, group=self.group, async_op=a), "all_gather")
         return out.view((self.world,) + tuple(t.shape))
 
     def all_reduce_sum(self, t):
-        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
+        self._run(lambda a: self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group, async_op=a),
+                  "all_reduce(sum)")
         return t
 
     def all_reduce_max(self, t):
-        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group)
+        self._run(lambda a: self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group, async_op=a),
+                  "all_reduce(max)")
         return t
 
 
@@ -282,6 +302,10 @@ class ShardedChainAcceptor:
         T, tp = float(sampling.temperature), float(sampling.top_p)
         if not (T > 0.0 and tp < 1.0 and comm.world * SHARD_CAND <= 256):
             raise ValueError("ShardedChainAcceptor: needs T > 0, top_p < 1 and at most 8 ranks")
+        if graph and getattr(comm, "timeout", None) is not None:
+            # a host wait cannot be recorded in a CUDA graph: captured
+            # collectives are bounded by the process group's own timeout
+            raise ValueError("ShardedChainAcceptor: a graph needs a comm without a host timeout")
         self.target, self.draft, self.drafts = target, draft, drafts
         self.k, self.v0, self.sampling, self.comm = k, v0, sampling, comm
         dev = target.device
@@ -378,3 +402,116 @@ class ShardedChainAcceptor:
 
     def close(self):
         self.graph = None
+
+
+# ----------------------------------------------------------------------
+# Rank failure detection (host side)
+# ----------------------------------------------------------------------
+# A rank that leaves (an exception between steps, a clean or abrupt exit) or
+# stops answering must not leave the others waiting for ever.  Two mechanisms,
+# both on the host, neither touching a GPU kernel:
+#   * guarded collectives: TorchComm(timeout=...) issues each collective
+#     asynchronously and waits at most `timeout` seconds for it; a collective
+#     that a peer never joins, or whose peer connection closed, raises
+#     RankLost (status ETIMEOUT) instead of blocking.  Under NCCL the process
+#     group's own watchdog (which polls the communicator's asynchronous error
+#     and aborts it after the group timeout) is the outer bound; collectives
+#     captured in a CUDA graph cannot take a host wait and rely on it alone;
+#   * a step heartbeat through the process group's key-value store
+#     (PeerMonitor): before launching step s a rank publishes s and waits, at
+#     most `timeout` seconds, until every peer has published s too.  A peer
+#     that left between steps has published a "left" mark and is reported at
+#     once; a peer that stalled or died silently is reported when the wait
+#     runs out.  Either way the rank learns of it before its next launch, with
+#     none of its kernels or collectives in flight.
+# The reference server has no multi-process path; the failure semantics follow
+# its error convention for the new ABI (status codes, here ETIMEOUT).
+
+
+class RankLost(RuntimeError):
+    """A peer rank left, died or did not answer within the timeout.  `code` is
+    the library status SPECDEC_ETIMEOUT; `rank` the peer when it is known."""
+
+    def __init__(self, msg: str, rank: int | None = None):
+        from specdec import ETIMEOUT
+
+        super().__init__(f"specdec error {ETIMEOUT}: {msg}")
+        self.code = ETIMEOUT
+        self.rank = rank
+
+
+def guarded_wait(work, timeout: float, what: str):
+    """Waits for an asynchronous collective at most `timeout` seconds; a
+    timeout or a closed peer connection becomes RankLost."""
+    import datetime
+
+    try:
+        work.wait(timeout=datetime.timedelta(seconds=float(timeout)))
+    except RuntimeError as e:
+        raise RankLost(f"{what}: {e}") from e
+
+
+class PeerMonitor:
+    """Step heartbeat of the ranks through a torch.distributed Store (the one
+    the process group was created with: TCPStore, FileStore, ...).
+
+    begin_step(s) publishes s and returns once every peer has published s;
+    leave() marks this rank gone (call it when leaving between steps, e.g.
+    from an exception handler, or use `with monitor.member(): ...`).  Raises
+    RankLost naming the peer that left, or the first one still behind when
+    `timeout` seconds have passed."""
+
+    def __init__(self, store, rank: int, world: int, timeout: float = 5.0, prefix: str = "specdec/hb",
+                 poll: float = 0.005):
+        if world <= 0 or not 0 <= rank < world:
+            raise ValueError(f"bad monitor: rank={rank} world={world}")
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout, self.prefix, self.poll = float(timeout), prefix, float(poll)
+        self.step = -1
+
+    def _key(self, kind: str, r: int) -> str:
+        return f"{self.prefix}/{kind}/{r}"
+
+    def leave(self):
+        self.store.set(self._key("left", self.rank), "1")
+
+    def peer_left(self, r: int) -> bool:
+        return self.store.check([self._key("left", r)])
+
+    def begin_step(self, step: int):
+        import time
+
+        step = int(step)
+        self.store.set(self._key("step", self.rank), str(step))
+        self.step = step
+        deadline = time.monotonic() + self.timeout
+        waiting = [r for r in range(self.world) if r != self.rank]
+        while waiting:
+            behind = []
+            for r in waiting:
+                if self.peer_left(r):
+                    raise RankLost(f"rank {r} left before step {step}", r)
+                k = self._key("step", r)
+                if not (self.store.check([k]) and int(self.store.get(k)) >= step):
+                    behind.append(r)
+            waiting = behind
+            if not waiting:
+                break
+            if time.monotonic() > deadline:
+                r = waiting[0]
+                raise RankLost(f"rank {r} did not reach step {step} within {self.timeout:g} s", r)
+            time.sleep(self.poll)
+
+    def member(self):
+        """Context manager: marks this rank gone if the body raises."""
+        import contextlib
+
+        @contextlib.contextmanager
+        def _cm():
+            try:
+                yield self
+            except BaseException:
+                self.leave()
+                raise
+
+        return _cm()
