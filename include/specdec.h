@@ -412,6 +412,24 @@ int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const i
 /* Releases slot `seq`: its KV blocks (shared blocks survive while another
  * slot holds them) and, with an index, its prefix references. */
 int specdec_engine_retire(specdec_engine* e, int seq, specdec_radix* cache);
+/* One chunk of slot `seq`'s prompt, for a scheduler that interleaves prompt
+ * chunks with decode steps (ChunkedPrefillState::get_next_chunk,
+ * server/chunked_prefill.cpp:4-24, consumed in
+ * server/continuous_scheduler.cpp:160-176 and server/main.cpp:385-398).
+ * The n tokens follow the K/V the slot already holds (none after
+ * specdec_engine_retire); they run through the forward in 64-row chunks and
+ * their K/V is appended, except that with final_chunk set the last token
+ * becomes the pending token instead.  The draft state h0 becomes the hidden
+ * state of the last token processed.  Fed in 64-token chunks from a retired
+ * slot, the slot ends bit-identical to specdec_engine_admit of the whole
+ * prompt.  Keep the slot inactive (specdec_engine_set_active) while its
+ * prompt is incomplete: steps leave an inactive slot's K/V, pending token
+ * and h0 as they were.  request_id >= 0 records the slot's request (the
+ * source rule of prefix sharing); insert the prompt into a prefix index when
+ * it is complete.  EINVAL when the prompt would exceed max_ctx or the final
+ * chunk leaves no K/V token.  Synchronises the engine stream. */
+int specdec_engine_prefill_chunk(specdec_engine* e, int seq, int32_t request_id, const int32_t* tokens, int n,
+                                 int final_chunk);
 /* Synthetic state: every sequence gets ctx_len[b] tokens of seeded random
  * fp16 K/V, a random pending token and a random draft hidden state. */
 int specdec_engine_seed_state(specdec_engine* e, const int32_t* ctx_len, uint32_t seed);

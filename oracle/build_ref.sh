@@ -3,7 +3,8 @@
 # infrastructure: the result is a checker, never part of the product).
 #
 #   server/paged_attention.cpp, server/speculative_decoder.cpp,
-#   server/mtp_heads.cpp                 compiled in place, unmodified;
+#   server/mtp_heads.cpp, server/chunked_prefill.cpp
+#                                        compiled in place, unmodified;
 #   server/radix_kv_cache.cpp            compiled in place, unmodified, with
 #                                        <functional> force-included;
 #   server/paged_kv_cache.cpp            compiled unmodified from a scratch copy
@@ -38,6 +39,7 @@ CFLAGS="-O2 -fPIC -fopenmp -ffp-contract=off -std=gnu11 -w"
 $CXX $CXXFLAGS -c "$REF/server/paged_attention.cpp" -o "$OUT/obj/paged_attention.o"
 $CXX $CXXFLAGS -c "$REF/server/speculative_decoder.cpp" -o "$OUT/obj/speculative_decoder.o"
 $CXX $CXXFLAGS -c "$REF/server/mtp_heads.cpp" -o "$OUT/obj/mtp_heads.o"
+$CXX $CXXFLAGS -c "$REF/server/chunked_prefill.cpp" -o "$OUT/obj/chunked_prefill.o"
 $CXX $CXXFLAGS -c "$OUT/src/paged_kv_cache.cpp" -o "$OUT/obj/paged_kv_cache.o"
 # radix_kv_cache.cpp uses std::function without including <functional>; the
 # header is supplied on the command line (-include), the source is unmodified

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <vector>
 
+#include "chunked_prefill.h"
 #include "mtp_heads.h"
 #include "paged_attention.h"
 #include "paged_kv_cache.h"
@@ -111,4 +112,25 @@ extern "C" void ref_radix_match(void* h, const int32_t* t, int n, int32_t* match
     auto r = static_cast<RadixKVCache*>(h)->match_prefix(std::vector<int>(t, t + n));
     *matched = r.first;
     *source = r.second;
+}
+
+// ChunkedPrefillState (server/chunked_prefill.cpp), driven call by call: up
+// to `cap` calls of get_next_chunk, with reset() after call `reset_after`
+// (-1: never), each recorded as (chunk length, first token or -1,
+// get_remaining_tokens(), is_prefill_complete) in out4[4 * call].  Returns
+// the number of calls made (the last one returned an empty chunk, or cap).
+extern "C" int ref_chunked_prefill(const int32_t* t, int n, int chunk, int reset_after, int32_t* out4, int cap) {
+    ChunkedPrefillState st(std::vector<int>(t, t + n), chunk);
+    int calls = 0;
+    while (calls < cap) {
+        const std::vector<int> c = st.get_next_chunk();
+        out4[4 * calls + 0] = (int32_t)c.size();
+        out4[4 * calls + 1] = c.empty() ? -1 : c[0];
+        out4[4 * calls + 2] = st.get_remaining_tokens();
+        out4[4 * calls + 3] = st.is_prefill_complete ? 1 : 0;
+        if (calls == reset_after) st.reset();
+        ++calls;
+        if (c.empty()) break;
+    }
+    return calls;
 }

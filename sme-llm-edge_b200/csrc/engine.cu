@@ -420,11 +420,15 @@ __global__ void prefill_rows_kernel(const int32_t* __restrict__ prompts, int P, 
     slot[i] = ctx[b] + r;
 }
 
+// Per sequence b: h0 = the hidden state of its last prefill row (Rp rows per
+// sequence in x; none when Rp = 0) and, unless pending is null, the pending
+// token = the prompt's last token.
 __global__ void prefill_finish_kernel(const int32_t* __restrict__ prompts, int P, const float* __restrict__ x, int Rp,
                                       int H, int32_t* __restrict__ pending, float* __restrict__ h0) {
     const int b = blockIdx.x;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) h0[(size_t)b * H + i] = x[((size_t)b * Rp + Rp - 1) * H + i];
-    if (threadIdx.x == 0) pending[b] = prompts[(size_t)b * P + P - 1];
+    if (Rp > 0)
+        for (int i = threadIdx.x; i < H; i += blockDim.x) h0[(size_t)b * H + i] = x[((size_t)b * Rp + Rp - 1) * H + i];
+    if (threadIdx.x == 0 && pending) pending[b] = prompts[(size_t)b * P + P - 1];
 }
 
 // Seeded random fp16 K/V for slots [0, ctx_len[b]) of every layer.
@@ -1151,12 +1155,56 @@ extern "C" int specdec_engine_retire(specdec_engine* e, int seq, specdec_radix* 
     return specdec_kv_free_request(e->kvm, seq, e->stream);
 }
 
+namespace {
+// Prompt tokens [c_begin, c_end) of slot seq (d_tok[0, T) on the device)
+// through the forward in chunks of at most 64 rows under the chain mask, each
+// chunk's K/V appended after the slot's context; then h0[seq] = the hidden
+// state of the last row processed (when there was one) and, for the final
+// chunk of a prompt, pending[seq] = d_tok[T - 1].  A tree engine's node mask
+// is saved and put back.  Queued on the engine stream; the caller syncs.
+int prefill_slot(specdec_engine* e, int seq, const int32_t* d_tok, int T, int c_begin, int c_end, bool final_chunk) {
+    cudaStream_t s = e->stream;
+    const int H = e->mc.hidden;
+    std::vector<uint64_t> chain(64);
+    for (int r = 0; r < 64; ++r) chain[r] = (r == 63) ? ~0ull : ((1ull << (r + 1)) - 1);
+    uint64_t* saved_mask = nullptr;
+    if (e->tree) {
+        SD_CUDA(cudaMallocAsync(&saved_mask, 8 * 64, s));
+        SD_CUDA(cudaMemcpyAsync(saved_mask, e->mask, 8 * 64, cudaMemcpyDeviceToDevice, s));
+    }
+    SD_CUDA(cudaMemcpyAsync(e->mask, chain.data(), 8 * 64, cudaMemcpyHostToDevice, s));
+    KVState& kvs = kv_state(e->kvm);
+    int rc = SPECDEC_OK, last_rp = 0;
+    for (int c0 = c_begin; c0 < c_end && !rc; c0 += 64) {
+        const int Rp = std::min(64, c_end - c0);
+        if ((rc = kv_append_uniform(e->kvm, 1, Rp, s, seq))) break;
+        prefill_rows_kernel<<<(Rp + 127) / 128, 128, 0, s>>>(d_tok, T, c0, Rp, kvs.ctx + seq, 1, e->tokens, e->pos,
+                                                            e->slot);
+        if (cudaGetLastError() != cudaSuccess) {
+            rc = SPECDEC_ECUDA;
+            break;
+        }
+        rc = forward(e, Rp, false, seq, 1);
+        last_rp = Rp;
+    }
+    if (!rc && (last_rp > 0 || final_chunk)) {
+        prefill_finish_kernel<<<1, 256, 0, s>>>(d_tok, T, e->x, last_rp, H, final_chunk ? e->pending + seq : nullptr,
+                                                e->h0 + (size_t)seq * H);
+        if (cudaGetLastError() != cudaSuccess) rc = SPECDEC_ECUDA;
+    }
+    if (e->tree) {
+        cudaMemcpyAsync(e->mask, saved_mask, 8 * 64, cudaMemcpyDeviceToDevice, s);
+        cudaFreeAsync(saved_mask, s);
+    }
+    return rc;
+}
+}  // namespace
+
 extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt, int P,
                                     specdec_radix* cache, int32_t* shared_tokens) {
     SD_CHECK(e && prompt && seq >= 0 && seq < e->B && P >= 2 && P <= e->rc.max_ctx, SPECDEC_EINVAL,
              "engine_admit: bad argument");
     cudaStream_t s = e->stream;
-    const int H = e->mc.hidden;
     int rc = specdec_engine_retire(e, seq, cache);
     if (rc) return rc;
     // longest indexed prefix of the prompt's KV tokens whose source still holds a slot
@@ -1175,38 +1223,9 @@ extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_
     int32_t* d_prompt = nullptr;
     SD_CUDA(cudaMallocAsync(&d_prompt, sizeof(int32_t) * (size_t)P, s));
     SD_CUDA(cudaMemcpyAsync(d_prompt, prompt, sizeof(int32_t) * (size_t)P, cudaMemcpyHostToDevice, s));
-    std::vector<uint64_t> chain(64);
-    for (int r = 0; r < 64; ++r) chain[r] = (r == 63) ? ~0ull : ((1ull << (r + 1)) - 1);
-    uint64_t* saved_mask = nullptr;
-    if (e->tree) {
-        SD_CUDA(cudaMallocAsync(&saved_mask, 8 * 64, s));
-        SD_CUDA(cudaMemcpyAsync(saved_mask, e->mask, 8 * 64, cudaMemcpyDeviceToDevice, s));
-    }
-    SD_CUDA(cudaMemcpyAsync(e->mask, chain.data(), 8 * 64, cudaMemcpyHostToDevice, s));
     KVState& kvs = kv_state(e->kvm);
-    const int n_end = P - 1;  // the last prompt token becomes the pending token
-    int last_rp = 0;
-    for (int c0 = shared; c0 < n_end && !rc; c0 += 64) {
-        const int Rp = std::min(64, n_end - c0);
-        if ((rc = kv_append_uniform(e->kvm, 1, Rp, s, seq))) break;
-        prefill_rows_kernel<<<(Rp + 127) / 128, 128, 0, s>>>(d_prompt, P, c0, Rp, kvs.ctx + seq, 1, e->tokens, e->pos,
-                                                            e->slot);
-        if (cudaGetLastError() != cudaSuccess) {
-            rc = SPECDEC_ECUDA;
-            break;
-        }
-        rc = forward(e, Rp, false, seq, 1);
-        last_rp = Rp;
-    }
-    if (!rc) {
-        prefill_finish_kernel<<<1, 256, 0, s>>>(d_prompt, P, e->x, last_rp, H, e->pending + seq,
-                                                e->h0 + (size_t)seq * H);
-        if (cudaGetLastError() != cudaSuccess) rc = SPECDEC_ECUDA;
-    }
-    if (e->tree) {
-        cudaMemcpyAsync(e->mask, saved_mask, 8 * 64, cudaMemcpyDeviceToDevice, s);
-        cudaFreeAsync(saved_mask, s);
-    }
+    // the last prompt token becomes the pending token
+    rc = prefill_slot(e, seq, d_prompt, P, shared, P - 1, true);
     cudaFreeAsync(d_prompt, s);
     SD_CUDA(cudaStreamSynchronize(s));
     if (rc) return rc;
@@ -1217,6 +1236,34 @@ extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_
     if (cache && (rc = specdec_radix_insert(cache, request_id, prompt, P - 1))) return rc;
     e->slot_request[seq] = request_id;
     if (shared_tokens) *shared_tokens = shared;
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_engine_prefill_chunk(specdec_engine* e, int seq, int32_t request_id, const int32_t* tokens,
+                                            int n, int final_chunk) {
+    SD_CHECK(e && tokens && seq >= 0 && seq < e->B && n >= 1, SPECDEC_EINVAL, "engine_prefill_chunk: bad argument");
+    cudaStream_t s = e->stream;
+    KVState& kvs = kv_state(e->kvm);
+    int32_t len = 0, nblk = 0;
+    SD_CUDA(cudaMemcpyAsync(&len, kvs.len + seq, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    SD_CUDA(cudaMemcpyAsync(&nblk, kvs.nblk + seq, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    SD_CUDA(cudaStreamSynchronize(s));
+    const int have = nblk < 0 ? 0 : len;  // K/V tokens the slot holds (a retired slot: none)
+    const int n_kv = final_chunk ? n - 1 : n;
+    SD_CHECK(have + n <= e->rc.max_ctx, SPECDEC_EINVAL, "engine_prefill_chunk: prompt longer than max_ctx");
+    SD_CHECK(have + n_kv >= 1, SPECDEC_EINVAL, "engine_prefill_chunk: a prompt needs a token before the pending one");
+    int32_t* d_tok = nullptr;
+    SD_CUDA(cudaMallocAsync(&d_tok, sizeof(int32_t) * (size_t)n, s));
+    SD_CUDA(cudaMemcpyAsync(d_tok, tokens, sizeof(int32_t) * (size_t)n, cudaMemcpyHostToDevice, s));
+    int rc = prefill_slot(e, seq, d_tok, n, 0, n_kv, final_chunk != 0);
+    cudaFreeAsync(d_tok, s);
+    SD_CUDA(cudaStreamSynchronize(s));
+    if (rc) return rc;
+    int st = 0;
+    SD_CUDA(cudaMemcpy(&st, kvs.status, sizeof(int), cudaMemcpyDeviceToHost));
+    SD_CHECK(!st, SPECDEC_ENOMEM, "engine_prefill_chunk: KV block pool exhausted");
+    if ((rc = check_device_status(s))) return rc;
+    if (request_id >= 0) e->slot_request[seq] = request_id;
     return SPECDEC_OK;
 }
 

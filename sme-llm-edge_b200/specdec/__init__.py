@@ -129,6 +129,7 @@ _SIGS = {
     "specdec_engine_load_sme": (I, [P, P, U32]),
     "specdec_engine_admit": (I, [P, I, C.c_int32, P, I, P, C.POINTER(C.c_int32)]),
     "specdec_engine_retire": (I, [P, I, P]),
+    "specdec_engine_prefill_chunk": (I, [P, I, C.c_int32, P, I, I]),
     "specdec_radix_create": (I, [C.POINTER(P)]),
     "specdec_radix_destroy": (I, [P]),
     "specdec_radix_match": (I, [P, P, I, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
@@ -193,6 +194,43 @@ def sampling(temperature: float, top_p: float = 1.0, seed: int = 0, step: int = 
 # ======================================================================
 # Reference operator surface
 # ======================================================================
+class ChunkedPrefillState:
+    """server/chunked_prefill.h: a prompt handed out in chunks of
+    `prefill_chunk_size` tokens (get_next_chunk, chunked_prefill.cpp:4-24),
+    with the `advance_offset` the reference scheduler calls after a prefix
+    match (continuous_scheduler.cpp:83).  Feed each chunk to
+    Engine.prefill_chunk(seq, chunk, final=state.is_prefill_complete)."""
+
+    def __init__(self, prompt_tokens=(), prefill_chunk_size: int = 64):
+        self.prompt_tokens = [int(x) for x in prompt_tokens]
+        self.prefill_chunk_size = int(prefill_chunk_size)
+        self.prefill_offset = 0
+        self.is_prefill_complete = False
+
+    def get_next_chunk(self) -> list[int]:
+        if self.is_prefill_complete or not self.prompt_tokens:
+            return []
+        n = min(len(self.prompt_tokens) - self.prefill_offset, self.prefill_chunk_size)
+        chunk = self.prompt_tokens[self.prefill_offset:self.prefill_offset + n]
+        self.prefill_offset += n
+        if self.prefill_offset >= len(self.prompt_tokens):
+            self.is_prefill_complete = True
+        return chunk
+
+    def get_remaining_tokens(self) -> int:
+        return 0 if not self.prompt_tokens else len(self.prompt_tokens) - self.prefill_offset
+
+    def reset(self):
+        self.prefill_offset = 0
+        self.is_prefill_complete = False
+
+    def advance_offset(self, n: int):
+        """Skips n prompt tokens already present (a shared prefix)."""
+        self.prefill_offset = min(len(self.prompt_tokens), self.prefill_offset + int(n))
+        if self.prompt_tokens and self.prefill_offset >= len(self.prompt_tokens):
+            self.is_prefill_complete = True
+
+
 class SpeculativeDecoder:
     """server/speculative_decoder.h: n-gram drafting on the host, verification on the GPU."""
 
@@ -606,6 +644,13 @@ class Engine:
 
     def retire(self, seq: int, cache: "RadixKVCache | None" = None):
         check(_lib.specdec_engine_retire(self._h, seq, cache.handle if cache is not None else None))
+
+    def prefill_chunk(self, seq: int, tokens, final: bool, request_id: int = -1):
+        """Feeds the next chunk of slot `seq`'s prompt (after a retire, the
+        first chunk); with `final` the chunk's last token becomes the pending
+        token.  See ChunkedPrefillState for the scheduler-side chunking."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        check(_lib.specdec_engine_prefill_chunk(self._h, seq, int(request_id), _p(t), t.size, int(bool(final))))
 
     def seed_state(self, ctx_len, seed: int):
         c = np.ascontiguousarray(ctx_len, dtype=np.int32)
