@@ -473,15 +473,25 @@ class PeerMonitor:
         return f"{self.prefix}/{kind}/{r}"
 
     def leave(self):
-        self.store.set(self._key("left", self.rank), "1")
+        try:
+            self.store.set(self._key("left", self.rank), "1")
+        except RuntimeError:
+            pass  # the store is gone too: the peers find out from their own waits
 
     def peer_left(self, r: int) -> bool:
         return self.store.check([self._key("left", r)])
 
     def begin_step(self, step: int):
+        try:
+            self._begin_step(int(step))
+        except RankLost:
+            raise
+        except RuntimeError as e:  # the store itself is unreachable (its host rank is gone)
+            raise RankLost(f"step store unreachable at step {int(step)}: {e}") from e
+
+    def _begin_step(self, step: int):
         import time
 
-        step = int(step)
         self.store.set(self._key("step", self.rank), str(step))
         self.step = step
         deadline = time.monotonic() + self.timeout
