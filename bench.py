@@ -39,8 +39,8 @@ METRIC = "accepted tokens/s, 8B-shape W4A16 MTP spec-decode, 1/2/4/8 B200; verif
 # DRAM bytes read + written by one launch, from the ncu captures summarised
 # under profiles/: (traffic, launch, algorithmic bytes of that launch)
 TRAFFIC = {
-    "lm_head": (334.4e6, "lm_head M=160 N=128256 K=4096", 271.3e6),
-    "attention": (277.6e6, "attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048", 269.1e6),
+    "lm_head": (332.8e6, "lm_head M=160 N=128256 K=4096", 271.3e6),
+    "attention": (275.5e6, "attention B=32 R=5 Hq=32 Hkv=8 hd=128 ctx=2048", 269.1e6),
 }
 
 
