@@ -446,7 +446,8 @@ int specdec_engine_set_active(specdec_engine* e, const int32_t* active);
 void* specdec_engine_stream(specdec_engine* e);
 /* Read back state / intermediate buffers ("logits", "draft_logits", "drafts",
  * "accepted", "out_tokens", "pending", "h0", "hidden", "lens", "tables", "kv",
- * "step", "emitted", ...) and overwrite state ("h0", "pending", "drafts",
+ * "step", "emitted", "mask": the 64 per-row visibility masks of the new
+ * rows, ...) and overwrite state ("h0", "pending", "drafts",
  * "kv").  Both synchronise the engine stream. */
 int specdec_engine_read(specdec_engine* e, const char* what, void* host, size_t bytes);
 int specdec_engine_write(specdec_engine* e, const char* what, const void* host, size_t bytes);

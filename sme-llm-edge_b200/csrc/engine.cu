@@ -1367,6 +1367,7 @@ View engine_view(specdec_engine* e, const char* what) {
     if (w == "refcounts") return {kvs.ref, 4 * (size_t)e->num_blocks};
     if (w == "kv") return {e->kv, 2 * e->layer_stride * (size_t)c.layers};
     if (w == "step") return {e->step, 4};
+    if (w == "mask") return {e->mask, 8 * 64};
     if (w == "emitted") return {e->emitted, 8};
     if (w == "emb") return {e->emb, 2 * V * H};
     if (w == "w_lm") return {e->lm, e->sz_lm};

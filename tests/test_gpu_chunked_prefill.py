@@ -151,3 +151,31 @@ def test_prefill_chunk_rejects_bad_prompts(cuda_device):
             eng.prefill_chunk(3, [1, 2], final=True)
     finally:
         eng.close()
+
+
+def test_tree_engine_chunked_prefill_keeps_the_tree_mask(cuda_device):
+    """A tree engine prefills under the chain mask and puts its node mask
+    back: chunk-fed slots equal admitted ones, and the tree steps after them
+    agree exactly."""
+    kw = dict(batch=2, draft_len=0, max_ctx=512, temperature=1.0, seed=2, tree_branching=[4, 4, 2, 2],
+              tree_nodes=64, use_graph=True)
+    ref, eng = S.Engine(TINY, **kw), S.Engine(TINY, **kw)
+    try:
+        for e in (ref, eng):
+            e.init_weights(0)
+        prompts = _prompts()[:2]
+        mask_before = eng.read("mask", np.uint64, (64,)).copy()
+        for b, p in enumerate(prompts):
+            ref.admit(b, 100 + b, p)
+            eng.retire(b)
+            _feed(eng, b, p, 64, 100 + b)
+        assert np.array_equal(eng.read("mask", np.uint64, (64,)), mask_before)
+        for b, p in enumerate(prompts):
+            kv_r, len_r, pend_r, h_r = _state(ref, b, len(p) - 1)
+            kv_e, len_e, pend_e, h_e = _state(eng, b, len(p) - 1)
+            assert (len_e, pend_e) == (len_r, pend_r) and np.array_equal(kv_e, kv_r) and np.array_equal(h_e, h_r)
+        for _ in range(2):
+            assert [x.tolist() for x in eng.step_host()] == [x.tolist() for x in ref.step_host()]
+    finally:
+        eng.close()
+        ref.close()
