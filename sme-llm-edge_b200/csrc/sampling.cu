@@ -399,9 +399,8 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
                               DevRowStats* st, uint32_t* whist = nullptr) {
     float m;
     int am = -1;
-    bool finite = true;
     if (need_mass) {
-        m = cta_max(z, V, sm, tp < (1ull << 32) ? &finite : nullptr);
+        m = cta_max(z, V, sm);
     } else {
         cta_argmax(z, V, sm, &m, &am);
     }
@@ -419,18 +418,14 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
             s = cta_mass_sum(z, V, m, c, sm);
             r.sum = s;
             r.nuc = s;
-        } else if (!finite) {
-            // NaN / infinite logits: exp2_fx31's handling of a NaN exponent and
-            // the keys' order decide, so the general path
-            s = cta_mass_sum(z, V, m, c, sm);
-            uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
-            if (thr < 1) thr = 1;
-            row_topp_select(z, V, m, c, thr, sm, whist, &r.tau, &r.nuc);
-            r.sum = s;
         } else {
             uint2* list = reinterpret_cast<uint2*>(whist + kWarpHistWords);
             int* list_n = reinterpret_cast<int*>(list + kNucleusList);
-            if (threadIdx.x == 0) *list_n = 0;
+            int* nan_seen = list_n + 1;  // a NaN exponent: NaN logits, or an infinite maximum
+            if (threadIdx.x == 0) {
+                *list_n = 0;
+                *nan_seen = 0;
+            }
             __syncthreads();
             uint64_t ls = 0;
             // the masses of a group of values first (independent, branch-free),
@@ -442,13 +437,14 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
                 for (int u = 0; u < 16; ++u) {
                     if (u < nv) {
                         t[u] = __fmul_rn(__fsub_rn(v[u], m), c);
-                        e[u] = exp2_fx31_neg(t[u]);  // finite row: t <= 0
+                        e[u] = exp2_fx31_neg(t[u]);  // t <= 0 or -inf; a NaN exponent: general path below
                         s += e[u];
                     }
                 }
 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
-                    if (u < nv && t[u] >= kTList) {
+                    if (u < nv && !(t[u] < kTList)) {  // NaN exponents come here too
+                        if (t[u] != t[u]) *nan_seen = 1;
                         ls += e[u];
                         const int at = atomicAdd(list_n, 1);
                         if (at < kNucleusList) list[at] = make_uint2(logit_key(v[u]), e[u]);
@@ -479,12 +475,19 @@ __device__ void cta_row_stats(const float* __restrict__ z, int V, float c, uint6
             }
             s = block_sum<uint64_t>(s, sm.red64);
             ls = block_sum<uint64_t>(ls, sm.red64);
+            const int n = *list_n;
+            const bool nan_row = *nan_seen != 0;
+            __syncthreads();
+            if (nan_row) {
+                // exp2_fx31's handling of a NaN exponent (the pass above used the
+                // finite-only form) and the keys' order decide: the general path.
+                // -inf logits under a finite maximum stay on the list path: their
+                // exponent is -inf, their mass 0 in both forms.
+                s = cta_mass_sum(z, V, m, c, sm);
+            }
             uint64_t thr = (uint64_t)(((u128)s * tp) >> 32);
             if (thr < 1) thr = 1;
-            const int n = *list_n;
-            const bool in_list = n <= kNucleusList && ls >= thr;
-            __syncthreads();
-            if (in_list) {
+            if (!nan_row && n <= kNucleusList && ls >= thr) {
                 list_topp_select(list, n, thr, sm, whist, &r.tau, &r.nuc);
             } else {
                 row_topp_select(z, V, m, c, thr, sm, whist, &r.tau, &r.nuc);

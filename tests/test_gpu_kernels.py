@@ -84,8 +84,9 @@ def test_accept_chain_topp_both_threshold_paths(cuda_device, scale, T, tp):
 
 
 def test_sample_rows_topp_nonfinite_rows(cuda_device):
-    """Rows with NaN or infinite logits take the general top-p path (the
-    exponent of a NaN logit counts as 0, as in the oracle): draws bit-exact."""
+    """Rows with NaN or +inf logits (a NaN exponent) take the general top-p
+    path (the exponent of a NaN logit counts as 0, as in the oracle); -inf
+    logits under a finite maximum stay on the listed path: draws bit-exact."""
     rng = np.random.default_rng(31)
     rows, k, V = 6, 3, 20000
     z = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
@@ -101,6 +102,40 @@ def test_sample_rows_topp_nonfinite_rows(cuda_device):
     S.check(S.lib().specdec_sample_rows(ptr(d_z), rows, k, V, C.byref(sp), ptr(out), None, 0, stream_ptr()))
     sync()
     assert out.cpu().numpy().tolist() == ref.tolist()
+
+
+@pytest.mark.parametrize("keep", [0.9, 0.1, 0.001])
+def test_topp_on_masked_vocabulary_rows(cuda_device, keep):
+    """Masked vocabulary (-inf outside an allowed set, as with padded or
+    constrained vocabularies): the top-p acceptance and draft draws stay
+    bit-exact with the oracle, down to a handful of allowed tokens."""
+    rng = np.random.default_rng(int(keep * 1000) + 3)
+    B, k, V = 4, 3, 32000
+    tgt = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    dr = (tgt[:, :k] + rng.standard_normal((B, k, V)) * 0.5).astype(np.float32)
+    allowed = rng.random(V) < keep
+    allowed[:2] = True
+    tgt[:, :, ~allowed] = -np.inf
+    dr[:, :, ~allowed] = -np.inf
+    drafts = O.sample_rows(dr.reshape(B * k, V), k, 0.8, 0.9, 9, 0).reshape(B, k)
+    out = _i32(B * k)
+    sp = S.sampling(0.8, 0.9, 9, 0)
+    S.check(S.lib().specdec_sample_rows(ptr(dev(dr.reshape(B * k, V))), B * k, k, V, C.byref(sp), ptr(out), None, 0,
+                                        stream_ptr()))
+    sync()
+    assert out.cpu().numpy().reshape(B, k).tolist() == drafts.tolist()
+    acc_o, out_o = O.accept_chain(tgt, dr, drafts, 0.8, 0.9, 1234, 7)
+    import torch
+
+    acc, outt = _i32(B), _i32((B, k + 1))
+    ws_b = S.lib().specdec_accept_workspace_bytes(B * (2 * k + 1))
+    ws = empty(ws_b, torch.uint8)
+    sp = S.sampling(0.8, 0.9, 1234, 7)
+    S.check(S.lib().specdec_accept_chain(ptr(dev(tgt)), ptr(dev(dr)), ptr(dev(drafts)), B, k, V, C.byref(sp), ptr(acc),
+                                         ptr(outt), ptr(ws), ws_b, stream_ptr()))
+    sync()
+    assert acc.cpu().numpy().tolist() == acc_o.tolist()
+    assert outt.cpu().numpy().tolist() == out_o.tolist()
 
 
 @pytest.mark.parametrize("k", [0, 3])
