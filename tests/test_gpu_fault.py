@@ -31,10 +31,10 @@ def _accept_greedy_matches_oracle():
     acc, out = empty(B, torch.int32), empty((B, k + 1), torch.int32)
     ws_b = S.lib().specdec_accept_workspace_bytes(B * (2 * k + 1))
     ws = empty(ws_b, torch.uint8)
-    d_t = dev(tgt)
+    d_t, d_dr = dev(tgt), dev(drafts)  # held until the kernels have run
     sp = S.sampling(0.0, 1.0, 0, 0)
-    S.check(S.lib().specdec_accept_chain(ptr(d_t), ptr(d_t), ptr(dev(drafts)), B, k, V, C.byref(sp), ptr(acc),
-                                         ptr(out), ptr(ws), ws_b, stream_ptr()))
+    S.check(S.lib().specdec_accept_chain(ptr(d_t), ptr(d_t), ptr(d_dr), B, k, V, C.byref(sp), ptr(acc), ptr(out),
+                                         ptr(ws), ws_b, stream_ptr()))
     sync()
     return acc.cpu().numpy().tolist() == acc_o.tolist() and out.cpu().numpy().tolist() == out_o.tolist()
 

@@ -120,8 +120,8 @@ def test_topp_on_masked_vocabulary_rows(cuda_device, keep):
     drafts = O.sample_rows(dr.reshape(B * k, V), k, 0.8, 0.9, 9, 0).reshape(B, k)
     out = _i32(B * k)
     sp = S.sampling(0.8, 0.9, 9, 0)
-    S.check(S.lib().specdec_sample_rows(ptr(dev(dr.reshape(B * k, V))), B * k, k, V, C.byref(sp), ptr(out), None, 0,
-                                        stream_ptr()))
+    d_t, d_d, d_dr = dev(tgt), dev(dr), dev(drafts)  # held until the kernels have run
+    S.check(S.lib().specdec_sample_rows(ptr(d_d), B * k, k, V, C.byref(sp), ptr(out), None, 0, stream_ptr()))
     sync()
     assert out.cpu().numpy().reshape(B, k).tolist() == drafts.tolist()
     acc_o, out_o = O.accept_chain(tgt, dr, drafts, 0.8, 0.9, 1234, 7)
@@ -131,8 +131,8 @@ def test_topp_on_masked_vocabulary_rows(cuda_device, keep):
     ws_b = S.lib().specdec_accept_workspace_bytes(B * (2 * k + 1))
     ws = empty(ws_b, torch.uint8)
     sp = S.sampling(0.8, 0.9, 1234, 7)
-    S.check(S.lib().specdec_accept_chain(ptr(dev(tgt)), ptr(dev(dr)), ptr(dev(drafts)), B, k, V, C.byref(sp), ptr(acc),
-                                         ptr(outt), ptr(ws), ws_b, stream_ptr()))
+    S.check(S.lib().specdec_accept_chain(ptr(d_t), ptr(d_d), ptr(d_dr), B, k, V, C.byref(sp), ptr(acc), ptr(outt),
+                                         ptr(ws), ws_b, stream_ptr()))
     sync()
     assert acc.cpu().numpy().tolist() == acc_o.tolist()
     assert outt.cpu().numpy().tolist() == out_o.tolist()
