@@ -412,6 +412,17 @@ int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const i
 /* Releases slot `seq`: its KV blocks (shared blocks survive while another
  * slot holds them) and, with an index, its prefix references. */
 int specdec_engine_retire(specdec_engine* e, int seq, specdec_radix* cache);
+/* The first half of specdec_engine_admit, for chunked admission: retires the
+ * slot, shares the indexed prefix of the prompt's K/V tokens whose source
+ * request holds a slot (whole blocks, at most prompt_len - 2 tokens) and
+ * records request_id for the slot.  *shared_tokens receives the number of
+ * shared tokens: feed the rest of the prompt from there with
+ * specdec_engine_prefill_chunk (the reference scheduler's match_prefix,
+ * share_prefix and advance_offset, server/continuous_scheduler.cpp:77-86),
+ * and insert the prompt's K/V tokens into the index when the prompt is
+ * complete (as mark_completed does, :399-409). */
+int specdec_engine_share_prefix(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt,
+                                int prompt_len, specdec_radix* cache, int32_t* shared_tokens);
 /* One chunk of slot `seq`'s prompt, for a scheduler that interleaves prompt
  * chunks with decode steps (ChunkedPrefillState::get_next_chunk,
  * server/chunked_prefill.cpp:4-24, consumed in

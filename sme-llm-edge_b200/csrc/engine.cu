@@ -1200,11 +1200,10 @@ int prefill_slot(specdec_engine* e, int seq, const int32_t* d_tok, int T, int c_
 }
 }  // namespace
 
-extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt, int P,
-                                    specdec_radix* cache, int32_t* shared_tokens) {
+extern "C" int specdec_engine_share_prefix(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt,
+                                           int P, specdec_radix* cache, int32_t* shared_tokens) {
     SD_CHECK(e && prompt && seq >= 0 && seq < e->B && P >= 2 && P <= e->rc.max_ctx, SPECDEC_EINVAL,
-             "engine_admit: bad argument");
-    cudaStream_t s = e->stream;
+             "engine_share_prefix: bad argument");
     int rc = specdec_engine_retire(e, seq, cache);
     if (rc) return rc;
     // longest indexed prefix of the prompt's KV tokens whose source still holds a slot
@@ -1217,9 +1216,23 @@ extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_
             if (b != seq && e->slot_request[b] == src) src_slot = b;
         if (src_slot >= 0) {
             shared = std::min<int>(m, P - 2) / 16 * 16;  // whole blocks; the last KV token is recomputed
-            if (shared > 0 && (rc = specdec_kv_share_prefix(e->kvm, seq, src_slot, shared, s))) return rc;
+            if (shared > 0 && (rc = specdec_kv_share_prefix(e->kvm, seq, src_slot, shared, e->stream))) return rc;
         }
     }
+    e->slot_request[seq] = request_id;
+    if (shared_tokens) *shared_tokens = shared;
+    return SPECDEC_OK;
+}
+
+extern "C" int specdec_engine_admit(specdec_engine* e, int seq, int32_t request_id, const int32_t* prompt, int P,
+                                    specdec_radix* cache, int32_t* shared_tokens) {
+    SD_CHECK(e && prompt && seq >= 0 && seq < e->B && P >= 2 && P <= e->rc.max_ctx, SPECDEC_EINVAL,
+             "engine_admit: bad argument");
+    cudaStream_t s = e->stream;
+    int32_t shared = 0;
+    int rc = specdec_engine_share_prefix(e, seq, request_id, prompt, P, cache, &shared);
+    if (rc) return rc;
+    e->slot_request[seq] = -1;  // a source only once its prompt is in
     int32_t* d_prompt = nullptr;
     SD_CUDA(cudaMallocAsync(&d_prompt, sizeof(int32_t) * (size_t)P, s));
     SD_CUDA(cudaMemcpyAsync(d_prompt, prompt, sizeof(int32_t) * (size_t)P, cudaMemcpyHostToDevice, s));

@@ -130,6 +130,7 @@ _SIGS = {
     "specdec_engine_admit": (I, [P, I, C.c_int32, P, I, P, C.POINTER(C.c_int32)]),
     "specdec_engine_retire": (I, [P, I, P]),
     "specdec_engine_prefill_chunk": (I, [P, I, C.c_int32, P, I, I]),
+    "specdec_engine_share_prefix": (I, [P, I, C.c_int32, P, I, P, C.POINTER(C.c_int32)]),
     "specdec_radix_create": (I, [C.POINTER(P)]),
     "specdec_radix_destroy": (I, [P]),
     "specdec_radix_match": (I, [P, P, I, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
@@ -644,6 +645,18 @@ class Engine:
 
     def retire(self, seq: int, cache: "RadixKVCache | None" = None):
         check(_lib.specdec_engine_retire(self._h, seq, cache.handle if cache is not None else None))
+
+    def share_prefix(self, seq: int, request_id: int, prompt, cache: "RadixKVCache | None" = None) -> int:
+        """Starts slot `seq` on a new request for chunked admission: shares
+        the indexed prefix (whole blocks) and returns the number of shared
+        tokens; feed the rest with prefill_chunk (ChunkedPrefillState.
+        advance_offset(shared)) and insert the prompt into the index when it
+        is complete."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32).reshape(-1)
+        shared = C.c_int32(0)
+        check(_lib.specdec_engine_share_prefix(self._h, seq, int(request_id), _p(p), p.size,
+                                               cache.handle if cache is not None else None, C.byref(shared)))
+        return int(shared.value)
 
     def prefill_chunk(self, seq: int, tokens, final: bool, request_id: int = -1):
         """Feeds the next chunk of slot `seq`'s prompt (after a retire, the

@@ -179,3 +179,46 @@ def test_tree_engine_chunked_prefill_keeps_the_tree_mask(cuda_device):
     finally:
         eng.close()
         ref.close()
+
+
+def test_chunked_admission_with_prefix_sharing_equals_admit(cuda_device):
+    """The reference scheduler's admission (continuous_scheduler.cpp:77-86):
+    match the prompt in the prefix index, share the source's blocks, advance
+    the chunked state past them and prefill the rest chunk by chunk; insert
+    the prompt when it is complete (mark_completed, :399-409).  Against
+    specdec_engine_admit with the same index: the same shared token counts,
+    tables that share the same source blocks, bit-identical state and steps."""
+    rng = np.random.default_rng(11)
+    V = TINY["vocab"]
+    p0 = rng.integers(0, V, 200).astype(np.int32)
+    p1 = np.concatenate([p0[:150], rng.integers(0, V, 60)]).astype(np.int32)
+    p2 = np.concatenate([p1[:180], rng.integers(0, V, 21)]).astype(np.int32)
+    prompts = [p0, p1, p2]
+    ref, eng = _engine(), _engine()
+    c_ref, c_eng = S.RadixKVCache(), S.RadixKVCache()
+    try:
+        shared_ref = [ref.admit(b, 100 + b, prompts[b], c_ref) for b in range(3)]
+        shared_eng = []
+        for b, p in enumerate(prompts):
+            sh = eng.share_prefix(b, 100 + b, p, c_eng)
+            st = S.ChunkedPrefillState(p.tolist(), 64)
+            st.advance_offset(sh)
+            while not st.is_prefill_complete:
+                eng.prefill_chunk(b, st.get_next_chunk(), final=st.is_prefill_complete, request_id=100 + b)
+            c_eng.insert_prefix(100 + b, p[:-1])
+            shared_eng.append(sh)
+        assert shared_eng == shared_ref == [0, 144, 176]
+        mb = eng.info("max_blocks")
+        tab = eng.read("tables", np.int32, (eng.batch, mb))
+        assert tab[1, :9].tolist() == tab[0, :9].tolist() and tab[2, :11].tolist() == tab[1, :11].tolist()
+        for b, p in enumerate(prompts):
+            kv_r, len_r, pend_r, h_r = _state(ref, b, len(p) - 1)
+            kv_e, len_e, pend_e, h_e = _state(eng, b, len(p) - 1)
+            assert (len_e, pend_e) == (len_r, pend_r) and np.array_equal(kv_e, kv_r) and np.array_equal(h_e, h_r)
+        for _ in range(2):
+            assert [x.tolist() for x in eng.step_host()] == [x.tolist() for x in ref.step_host()]
+    finally:
+        eng.close()
+        ref.close()
+        c_ref.close()
+        c_eng.close()
