@@ -454,6 +454,23 @@ int specdec_engine_step_host(specdec_engine* e, int32_t* out_len, int32_t* out_t
 /* Per-sequence active flags used by the next specdec_engine_step_host
  * (inactive sequences keep their state; their reserved slots roll back). */
 int specdec_engine_set_active(specdec_engine* e, const int32_t* active);
+/* The step's four stages as separate calls on the engine stream (no host
+ * synchronisation), in this order; together they queue exactly what
+ * specdec_engine_step does (eagerly, without its CUDA graph):
+ *   draft             MTP heads -> draft logits -> drafted tokens ("drafts";
+ *                     the tree engine's top-k candidates); uploads the active
+ *                     flags set by specdec_engine_set_active;
+ *   verify_forward    reserves R K/V slots per sequence, builds the verify
+ *                     rows and runs the target forward ("logits");
+ *   accept            acceptance -> "accepted", "out_tokens";
+ *   kv_commit_rollback keeps the accepted rows' K/V, sets the next pending
+ *                     token and draft state, rolls the rest back.
+ * Between stages the drafts or logits may be read or replaced
+ * (specdec_engine_read / _write). */
+int specdec_engine_draft(specdec_engine* e);
+int specdec_engine_verify_forward(specdec_engine* e);
+int specdec_engine_accept(specdec_engine* e);
+int specdec_engine_kv_commit_rollback(specdec_engine* e);
 void* specdec_engine_stream(specdec_engine* e);
 /* Read back state / intermediate buffers ("logits", "draft_logits", "drafts",
  * "accepted", "out_tokens", "pending", "h0", "hidden", "lens", "tables", "kv",

@@ -704,13 +704,13 @@ int draft_hidden_and_logits(specdec_engine* e, int levels) {
     return SPECDEC_OK;
 }
 
-int record_step(specdec_engine* e) {
-    const auto& c = e->mc;
-    const int B = e->B, R = e->R, V = c.vocab;
+// The four stages of a speculative step, queued on the engine stream.
+// draft: MTP heads -> draft logits -> drafted tokens (chain: sampled, with
+// their row statistics kept for the acceptance; tree: top-k candidates).
+int record_draft(specdec_engine* e) {
+    const int B = e->B, V = e->mc.vocab;
     cudaStream_t s = e->stream;
-    KVState& kvs = kv_state(e->kvm);
     const auto& sp = e->rc.sampling;
-    e->kernels_per_step = 0;
     prof_mark(e, CAT_OTHER);  // step start
     if (!e->tree) {
         const int k = e->k;
@@ -719,43 +719,74 @@ int record_step(specdec_engine* e) {
         // the draft rows' statistics go where the acceptance reads them: after the B*(k+1) target rows
         ENG_TRY(launch_sample_rows_dev(e->dlogits, B * k, k, V, sp.temperature, sp.top_p, sp.seed, e->step, e->drafts,
                                        static_cast<char*>(e->acc_ws) + (size_t)B * (k + 1) * kAcceptStatsBytes, s));
-        prof_mark(e, CAT_ACCEPT);
-        ++e->kernels_per_step;
-        ENG_TRY(kv_append_uniform(e->kvm, B, R, s));
-        prof_mark(e, CAT_OTHER);
-        build_chain_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->drafts, kvs.ctx, B, k, e->tokens,
-                                                                   e->pos, e->slot);
-        ENG_LAUNCH("build_chain_rows_kernel");
-        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 0);
-        ENG_TRY(forward(e, R, true));
-        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 1);
-        e->kernels_per_step += 2;
-        ENG_TRY(launch_accept_chain_dev(e->logits, e->dlogits, e->drafts, B, k, V, sp.temperature, sp.top_p, sp.seed,
-                                        e->step, e->acc, e->out_tokens, e->acc_ws, true, s));
-        prof_mark(e, CAT_ACCEPT);
-        commit_chain_kernel<<<B, 256, 0, s>>>(e->acc, e->out_tokens, R, kvs.ctx, e->active, e->x, c.hidden, e->new_len,
-                                              e->pending, e->h0, e->emitted, e->step);
-        ENG_LAUNCH("commit_chain_kernel");
     } else {
         const int levels = e->rc.tree_levels;
         ENG_TRY(draft_hidden_and_logits(e, levels));
         ++e->kernels_per_step;
         ENG_TRY(launch_topk(e->dlogits, B * levels, V, e->topk_w, e->topk, s));
-        prof_mark(e, CAT_ACCEPT);
-        ++e->kernels_per_step;
-        ENG_TRY(kv_append_uniform(e->kvm, B, R, s));
-        prof_mark(e, CAT_OTHER);
-        build_tree_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->topk, e->topk_w, levels, e->depth,
-                                                                  e->rank, kvs.ctx, B, R, e->tokens, e->node_tokens,
-                                                                  e->pos, e->slot);
+    }
+    prof_mark(e, CAT_ACCEPT);
+    ++e->kernels_per_step;
+    return SPECDEC_OK;
+}
+
+// verify: reserve the R new K/V slots per sequence, build the verify rows
+// (pending token + drafts, or the tree's nodes) and run the target forward
+// with logits for every row.
+int record_verify(specdec_engine* e) {
+    const int B = e->B, R = e->R;
+    cudaStream_t s = e->stream;
+    KVState& kvs = kv_state(e->kvm);
+    ENG_TRY(kv_append_uniform(e->kvm, B, R, s));
+    prof_mark(e, CAT_OTHER);
+    if (!e->tree) {
+        build_chain_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->drafts, kvs.ctx, B, e->k, e->tokens,
+                                                                   e->pos, e->slot);
+        ENG_LAUNCH("build_chain_rows_kernel");
+    } else {
+        build_tree_rows_kernel<<<(B * R + 127) / 128, 128, 0, s>>>(e->pending, e->topk, e->topk_w, e->rc.tree_levels,
+                                                                  e->depth, e->rank, kvs.ctx, B, R, e->tokens,
+                                                                  e->node_tokens, e->pos, e->slot);
         ENG_LAUNCH("build_tree_rows_kernel");
-        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 0);
-        ENG_TRY(forward(e, R, true));
-        if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 1);
-        ++e->kernels_per_step;
+    }
+    if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 0);
+    ENG_TRY(forward(e, R, true));
+    if (e->stamp_on) stamp_kernel<<<1, 32, 0, s>>>(e->stamps, 1);
+    e->kernels_per_step += e->tree ? 1 : 2;
+    return SPECDEC_OK;
+}
+
+// accept: the acceptance over the verify logits -> accepted lengths and
+// emitted tokens (and the tree's accepted path).
+int record_accept(specdec_engine* e) {
+    const int B = e->B, R = e->R, V = e->mc.vocab;
+    cudaStream_t s = e->stream;
+    const auto& sp = e->rc.sampling;
+    if (!e->tree) {
+        ENG_TRY(launch_accept_chain_dev(e->logits, e->dlogits, e->drafts, B, e->k, V, sp.temperature, sp.top_p,
+                                        sp.seed, e->step, e->acc, e->out_tokens, e->acc_ws, true, s));
+    } else {
         ENG_TRY(launch_accept_tree_dev(e->logits, e->node_tokens, e->parent, B, R, V, sp.temperature, sp.top_p,
                                        sp.seed, e->step, e->acc, e->path, e->out_tokens, s));
-        prof_mark(e, CAT_ACCEPT);
+    }
+    prof_mark(e, CAT_ACCEPT);
+    return SPECDEC_OK;
+}
+
+// commit: keep the accepted rows' K/V (the tree moves its accepted path's
+// K/V into place), set the next pending token and draft state, advance the
+// step counter, and roll the unaccepted reserved slots back.
+int record_commit(specdec_engine* e) {
+    const auto& c = e->mc;
+    const int B = e->B, R = e->R;
+    cudaStream_t s = e->stream;
+    KVState& kvs = kv_state(e->kvm);
+    if (!e->tree) {
+        commit_chain_kernel<<<B, 256, 0, s>>>(e->acc, e->out_tokens, R, kvs.ctx, e->active, e->x, c.hidden, e->new_len,
+                                              e->pending, e->h0, e->emitted, e->step);
+        ENG_LAUNCH("commit_chain_kernel");
+    } else {
+        const int levels = e->rc.tree_levels;
         const int per = 2 * c.n_kv_heads * c.head_dim;
         const size_t sm = sizeof(__half) * (size_t)levels * per;
         tree_compact_kernel<<<dim3(B, c.layers), 256, sm, s>>>(e->acc, e->path, R, kvs.ctx, kvs.tables, e->max_blocks,
@@ -769,6 +800,14 @@ int record_step(specdec_engine* e) {
     ENG_TRY(kv_truncate_dev(e->kvm, e->new_len, B, s));
     prof_mark(e, CAT_OTHER);
     return SPECDEC_OK;
+}
+
+int record_step(specdec_engine* e) {
+    e->kernels_per_step = 0;
+    ENG_TRY(record_draft(e));
+    ENG_TRY(record_verify(e));
+    ENG_TRY(record_accept(e));
+    return record_commit(e);
 }
 
 int synth_tiled(cudaStream_t s, uint32_t seed, RowSegs segs, int N, int K, uint8_t* dst) {
@@ -1343,6 +1382,34 @@ extern "C" int specdec_engine_step_host(specdec_engine* e, int32_t* out_len, int
     if (out_len) std::memcpy(out_len, e->h_out, sizeof(int32_t) * B);
     if (out_tokens) std::memcpy(out_tokens, e->h_out + B, sizeof(int32_t) * B * R);
     return SPECDEC_OK;
+}
+
+// The step's stages one call at a time (eager launches on the engine stream,
+// no host synchronisation): draft, verify forward, accept, K/V commit /
+// rollback.  Called in that order they queue exactly what specdec_engine_step
+// does; between them a caller may read or replace the drafts
+// (specdec_engine_read / _write) or the verify logits.
+extern "C" int specdec_engine_draft(specdec_engine* e) {
+    SD_CHECK(e, SPECDEC_EINVAL, "engine_draft: null");
+    // per-step control input, as specdec_engine_step_host
+    SD_CUDA(cudaMemcpyAsync(e->active, e->h_ctrl, sizeof(int32_t) * e->B, cudaMemcpyHostToDevice, e->stream));
+    e->kernels_per_step = 0;
+    return record_draft(e);
+}
+
+extern "C" int specdec_engine_verify_forward(specdec_engine* e) {
+    SD_CHECK(e, SPECDEC_EINVAL, "engine_verify_forward: null");
+    return record_verify(e);
+}
+
+extern "C" int specdec_engine_accept(specdec_engine* e) {
+    SD_CHECK(e, SPECDEC_EINVAL, "engine_accept: null");
+    return record_accept(e);
+}
+
+extern "C" int specdec_engine_kv_commit_rollback(specdec_engine* e) {
+    SD_CHECK(e, SPECDEC_EINVAL, "engine_kv_commit_rollback: null");
+    return record_commit(e);
 }
 
 extern "C" int specdec_engine_set_active(specdec_engine* e, const int32_t* active) {

@@ -131,6 +131,10 @@ _SIGS = {
     "specdec_engine_retire": (I, [P, I, P]),
     "specdec_engine_prefill_chunk": (I, [P, I, C.c_int32, P, I, I]),
     "specdec_engine_share_prefix": (I, [P, I, C.c_int32, P, I, P, C.POINTER(C.c_int32)]),
+    "specdec_engine_draft": (I, [P]),
+    "specdec_engine_verify_forward": (I, [P]),
+    "specdec_engine_accept": (I, [P]),
+    "specdec_engine_kv_commit_rollback": (I, [P]),
     "specdec_radix_create": (I, [C.POINTER(P)]),
     "specdec_radix_destroy": (I, [P]),
     "specdec_radix_match": (I, [P, P, I, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
@@ -671,6 +675,22 @@ class Engine:
 
     def step(self):
         check(_lib.specdec_engine_step(self._h))
+
+    def draft(self):
+        """Stage 1 of a step: drafted tokens (no host synchronisation)."""
+        check(_lib.specdec_engine_draft(self._h))
+
+    def verify_forward(self):
+        """Stage 2: the verify forward over pending token + drafts."""
+        check(_lib.specdec_engine_verify_forward(self._h))
+
+    def accept(self):
+        """Stage 3: acceptance -> read("accepted") / read("out_tokens")."""
+        check(_lib.specdec_engine_accept(self._h))
+
+    def kv_commit_rollback(self):
+        """Stage 4: commit the accepted rows' K/V, roll the rest back."""
+        check(_lib.specdec_engine_kv_commit_rollback(self._h))
 
     def step_host(self):
         acc = np.zeros(self.batch, np.int32)
