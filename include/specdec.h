@@ -466,7 +466,10 @@ int specdec_engine_set_active(specdec_engine* e, const int32_t* active);
  *   kv_commit_rollback keeps the accepted rows' K/V, sets the next pending
  *                     token and draft state, rolls the rest back.
  * Between stages the drafts or logits may be read or replaced
- * (specdec_engine_read / _write). */
+ * (specdec_engine_read / _write).  Under sampling (temperature > 0) the
+ * acceptance tests drafts against the MTP heads' draft distribution, so
+ * replaced drafts belong under greedy decoding, where acceptance is the
+ * longest prefix equal to the verify logits' arg-max. */
 int specdec_engine_draft(specdec_engine* e);
 int specdec_engine_verify_forward(specdec_engine* e);
 int specdec_engine_accept(specdec_engine* e);
