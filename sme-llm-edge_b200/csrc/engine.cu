@@ -1414,6 +1414,9 @@ extern "C" int specdec_engine_kv_commit_rollback(specdec_engine* e) {
 
 extern "C" int specdec_engine_set_active(specdec_engine* e, const int32_t* active) {
     SD_CHECK(e && active, SPECDEC_EINVAL, "engine_set_active: bad argument");
+    // a copy of the previous flags queued by a step or a draft stage reads this
+    // pinned buffer when the stream reaches it: let it finish first
+    SD_CUDA(cudaStreamSynchronize(e->stream));
     std::memcpy(e->h_ctrl, active, sizeof(int32_t) * e->B);
     return SPECDEC_OK;
 }
